@@ -1,0 +1,409 @@
+"""CPU oracle for the gated-delta path -- TEST INFRASTRUCTURE ONLY.
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
+leg may import this module, and only as the checker: the product path
+(``gdn_b200``) never calls it and has no CPU fallback.
+
+Every function restates one piece of the reference (conferencebeefwood46/
+mlx-lean-moe) in numpy, citing the file:line it follows. Paths are relative to
+the reference project root; ``qw/`` stands for
+``src/mlx_lean_moe/model/qwen3_5/``.
+
+Parity pin: ``tests/golden/make_golden.py`` runs the reference's own modules
+(``qw/gated_delta.py``, ``qw/linear_attention.py``,
+``src/mlx_lean_moe/cache/recurrent_cache.py``) unchanged on a numpy stand-in
+for MLX, plus the reference's own float64 test recurrence
+(``tests/test_gated_delta_metal.py:10-39``), and commits the outputs under
+``tests/golden/``. ``tests/test_oracle_golden.py`` checks every function here
+against those vectors.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+# ---------------------------------------------------------------------------
+# Input generators (restated from the reference's tests, same seeds/shapes)
+# ---------------------------------------------------------------------------
+
+
+def metal_test_inputs(length, key_dim=128, value_dim=17, key_heads=2, value_heads=4):
+    """``_inputs`` of ``tests/test_gated_delta_metal.py:10-23``: seed 42,
+    q L2-normalised and divided by sqrt(Dk), k L2-normalised, v ~ N(0,1),
+    g ~ U(0.98, 1) with head 0 forced to 1, beta ~ U(0, 1), state ~ 0.1 N(0,1).
+    Returns float32 arrays (q, k, v, g, beta, state)."""
+
+    rng = np.random.default_rng(42)
+    q = rng.normal(size=(length, key_heads, key_dim))
+    k = rng.normal(size=q.shape)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True) * key_dim**0.5
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.normal(size=(length, value_heads, value_dim))
+    g = rng.uniform(0.98, 1, size=(length, value_heads))
+    g[:, 0] = 1
+    beta = rng.uniform(0, 1, size=g.shape)
+    state = rng.normal(size=(value_heads, value_dim, key_dim)) * 0.1
+    return [a.astype(np.float32) for a in (q, k, v, g, beta, state)]
+
+
+def gdn_test_inputs(seed, seq_len, hk=2, hv=6, dk=16, dv=8):
+    """``_inputs`` of ``tests/test_qwen3_5_gated_delta.py:26-38``: standard
+    normals drawn in the order q, k, v, a, b, A_log, dt_bias."""
+
+    rng = np.random.default_rng(seed)
+
+    def f32(*shape):
+        return rng.standard_normal(shape).astype(np.float32)
+
+    return {
+        "q": f32(seq_len, hk, dk),
+        "k": f32(seq_len, hk, dk),
+        "v": f32(seq_len, hv, dv),
+        "a": f32(seq_len, hv),
+        "b": f32(seq_len, hv),
+        "A_log": f32(hv),
+        "dt_bias": f32(hv),
+    }
+
+
+# ---------------------------------------------------------------------------
+# The op (qw/gated_delta.py)
+# ---------------------------------------------------------------------------
+
+
+def softplus(x):
+    """``nn.softplus``: log(1 + exp(x)), evaluated without overflow."""
+    return np.logaddexp(np.zeros((), dtype=x.dtype), x).astype(x.dtype)
+
+
+def forget_gate(a, A_log, dt_bias):
+    """``qw/gated_delta.py:14-21``: exp(-exp(A_log) * softplus(a + dt_bias)),
+    all in float32."""
+
+    a32 = np.asarray(a, np.float32)
+    return np.exp(
+        -np.exp(np.asarray(A_log, np.float32))
+        * softplus(a32 + np.asarray(dt_bias, np.float32))
+    ).astype(np.float32)
+
+
+def forget_gate_log(a, A_log, dt_bias):
+    """The log of :func:`forget_gate`, -exp(A_log) * softplus(a + dt_bias),
+    float32 (the log-decay form the chunked prefill consumes)."""
+
+    a32 = np.asarray(a, np.float32)
+    return (
+        -np.exp(np.asarray(A_log, np.float32))
+        * softplus(a32 + np.asarray(dt_bias, np.float32))
+    ).astype(np.float32)
+
+
+def gated_delta_step(q, k, v, g, beta, state):
+    """``qw/gated_delta.py:24-41``. q/k ``(Hv, Dk)`` already repeated out to
+    the value heads; v ``(Hv, Dv)``; g, beta ``(Hv,)``; state
+    ``(Hv, Dv, Dk)``. Same operation order as the reference."""
+
+    state = state * g[:, None, None]
+    read = (state * k[:, None, :]).sum(axis=-1)
+    delta = (v - read) * beta[:, None]
+    state = state + k[:, None, :] * delta[:, :, None]
+    y = (state * q[:, None, :]).sum(axis=-1)
+    return y, state
+
+
+def validate_scan(q, k, v, g, beta, state):
+    """The shape checks of ``qw/gated_delta.py:57-79``, with the reference's
+    messages; raises ValueError."""
+
+    if q.ndim != 3 or k.shape != q.shape or v.ndim != 3:
+        raise ValueError(
+            "q/k must have matching (L, key_heads, key_dim) shapes; v must be 3-D"
+        )
+    length, key_heads, key_dim = q.shape
+    _, value_heads, value_dim = v.shape
+    if min(length, key_heads, key_dim, value_heads, value_dim) <= 0:
+        raise ValueError(
+            "gated_delta_scan requires nonempty sequence and head dimensions"
+        )
+    if v.shape[0] != length or value_heads % key_heads:
+        raise ValueError(
+            "v must match q's sequence length and have a multiple of its head count"
+        )
+    if g.shape != (length, value_heads) or beta.shape != g.shape:
+        raise ValueError("g and beta must have shape (L, value_heads)")
+    if state.shape != (value_heads, value_dim, key_dim):
+        raise ValueError("state must have shape (value_heads, value_dim, key_dim)")
+
+
+def gated_delta_scan(q, k, v, g, beta, state, dtype=np.float64):
+    """``qw/gated_delta.py:44-109`` (validation, then ``_gated_delta_scan_ops``):
+    GQA by repeat-interleave of q/k over the value heads (``:97-101``), then
+    :func:`gated_delta_step` for each position in order (``:105-107``).
+
+    ``g`` is the multiplicative decay in (0, 1]. Computes in ``dtype``
+    (float64 by default, the precision of the reference's own test recurrence
+    ``tests/test_gated_delta_metal.py:26-39``). The input state is not
+    mutated. Returns ``(y (L, Hv, Dv), state (Hv, Dv, Dk))`` in ``dtype``."""
+
+    validate_scan(q, k, v, g, beta, state)
+    q, k, v, g, beta, state = (np.asarray(a).astype(dtype) for a in (q, k, v, g, beta, state))
+    repeat = v.shape[-2] // q.shape[-2]
+    if repeat > 1:
+        q = np.repeat(q, repeat, axis=-2)
+        k = np.repeat(k, repeat, axis=-2)
+    outputs = []
+    for t in range(q.shape[0]):
+        y, state = gated_delta_step(q[t], k[t], v[t], g[t], beta[t], state)
+        outputs.append(y)
+    return np.stack(outputs), state
+
+
+def reference_f64(inputs):
+    """The reference's independent float64 recurrence,
+    ``tests/test_gated_delta_metal.py:26-39``, restated (einsum form)."""
+
+    q, k, v, g, beta, state = [np.array(a).astype(np.float64) for a in inputs]
+    repeat = v.shape[1] // q.shape[1]
+    q, k = np.repeat(q, repeat, axis=1), np.repeat(k, repeat, axis=1)
+    output = []
+    for t in range(len(q)):
+        state *= g[t, :, None, None]
+        read = np.einsum("hvk,hk->hv", state, k[t])
+        correction = (v[t] - read) * beta[t, :, None]
+        state += np.einsum("hv,hk->hvk", correction, k[t])
+        output.append(np.einsum("hvk,hk->hv", state, q[t]))
+    return np.stack(output), state
+
+
+def scan_varlen(q, k, v, g, beta, cu_seqlens, states, dtype=np.float64, g_is_log=False):
+    """Packed variable-length form: sequence ``i`` owns rows
+    ``cu_seqlens[i]:cu_seqlens[i+1]`` of q/k/v/g/beta and ``states[i]``.
+    Each sequence is an independent call of :func:`gated_delta_scan` (the
+    reference has no batch axis, ``qw/gated_delta.py:5``). A sequence of
+    length 0 keeps its state. ``g_is_log`` feeds ``exp(g)`` to the reference
+    semantics. Returns ``(y (N, Hv, Dv), states (B, Hv, Dv, Dk))``."""
+
+    n_seq = len(cu_seqlens) - 1
+    hv, dv = v.shape[1], v.shape[2]
+    y = np.zeros((v.shape[0], hv, dv), dtype=dtype)
+    out_states = np.array(states, dtype=dtype, copy=True)
+    for i in range(n_seq):
+        s, e = int(cu_seqlens[i]), int(cu_seqlens[i + 1])
+        if e == s:
+            continue
+        gi = np.exp(np.asarray(g[s:e], np.float64)) if g_is_log else g[s:e]
+        yi, st = gated_delta_scan(q[s:e], k[s:e], v[s:e], gi, beta[s:e], states[i], dtype)
+        y[s:e] = yi
+        out_states[i] = st
+    return y, out_states
+
+
+# ---------------------------------------------------------------------------
+# The layer's prologue / epilogue (qw/linear_attention.py)
+# ---------------------------------------------------------------------------
+
+
+def rms_norm(x, weight, eps):
+    """``mx.fast.rms_norm`` over the last axis: x / sqrt(mean(x^2) + eps) * w,
+    computed in float32 and returned in x's dtype."""
+
+    x32 = np.asarray(x, np.float32)
+    out = x32 / np.sqrt(np.mean(x32 * x32, axis=-1, keepdims=True) + np.float32(eps))
+    if weight is not None:
+        out = out * np.asarray(weight, np.float32)
+    return out.astype(np.asarray(x).dtype)
+
+
+def silu(x):
+    x = np.asarray(x)
+    return (x / (1.0 + np.exp(-x))).astype(x.dtype)
+
+
+def sigmoid(x):
+    x = np.asarray(x)
+    return (1.0 / (1.0 + np.exp(-x))).astype(x.dtype)
+
+
+def causal_conv_silu(qkv, conv_state, conv_w):
+    """``qw/linear_attention.py:61-79``: depthwise cross-correlation of
+    ``[conv_state ; qkv]`` (no padding, so L outputs) with weight ``(C, K)``
+    (the reference's ``(C, K, 1)`` squeezed), then SiLU. Returns
+    ``(silu(out) (L, C), new_tail (K-1, C))``; the tail is taken from the front
+    index (``:75-77``), so K=1 keeps nothing."""
+
+    qkv = np.asarray(qkv)
+    w = np.asarray(conv_w).reshape(conv_w.shape[0], -1)
+    kernel = w.shape[1]
+    conv_in = np.concatenate([np.asarray(conv_state).astype(qkv.dtype), qkv], axis=0)
+    length = qkv.shape[0]
+    out = np.zeros((length, qkv.shape[1]), dtype=np.result_type(conv_in, w))
+    for j in range(kernel):
+        out += conv_in[j : j + length] * w[None, :, j]
+    tail_start = conv_in.shape[0] - (kernel - 1)
+    return silu(out), conv_in[tail_start:]
+
+
+def qk_norm(q, k):
+    """``qw/linear_attention.py:109-113``: q <- Dk^-1 rms_norm(q, eps=1e-6),
+    k <- Dk^-1/2 rms_norm(k, eps=1e-6), no weight; eps is hard-coded."""
+
+    inv_scale = q.shape[-1] ** -0.5
+    qn = (inv_scale**2) * rms_norm(q, None, 1e-6)
+    kn = inv_scale * rms_norm(k, None, 1e-6)
+    return qn.astype(q.dtype), kn.astype(k.dtype)
+
+
+def gated_rms_norm(x, gate, weight, eps):
+    """``qw/linear_attention.py:22-32``: silu(gate_f32) * rms_norm(x, w, eps)
+    in float32, cast back to x's dtype."""
+
+    normed = rms_norm(x, weight, eps)
+    return (silu(np.asarray(gate, np.float32)) * normed.astype(np.float32)).astype(
+        np.asarray(x).dtype
+    )
+
+
+def split_mixed(mixed, hk, hv, dk, dv):
+    """Split the mixed projection row layout ``[q | k | v | z | b | a]``
+    (widths Hk*Dk, Hk*Dk, Hv*Dv, Hv*Dv, Hv, Hv) into (qkv, z, b, a): the
+    outputs of in_proj_qkv / in_proj_z / in_proj_b / in_proj_a
+    (``qw/linear_attention.py:96-101``)."""
+
+    key_dim, value_dim = hk * dk, hv * dv
+    conv_dim = 2 * key_dim + value_dim
+    qkv = mixed[:, :conv_dim]
+    z = mixed[:, conv_dim : conv_dim + value_dim]
+    b = mixed[:, conv_dim + value_dim : conv_dim + value_dim + hv]
+    a = mixed[:, conv_dim + value_dim + hv : conv_dim + value_dim + 2 * hv]
+    return qkv, z, b, a
+
+
+def linear_attention_core(
+    mixed, conv_w, conv_state, A_log, dt_bias, norm_w, ssm_state, eps, hk, hv, dk, dv,
+    scan_dtype=np.float64,
+):
+    """``qw/linear_attention.py:81-124`` from the projections on, for one
+    sequence: conv+SiLU (``:103``), q/k/v split (``:104-107``), q/k norm
+    (``:109-113``), gates (``:115-116``), scan (``:118-119``), gated RMSNorm
+    of ``y`` cast to z's dtype (``:122-124``). ``out_proj`` is not applied.
+
+    Returns ``(out (L, Hv, Dv) in mixed's dtype, new_conv_state, new_ssm_state,
+    y)``."""
+
+    length = mixed.shape[0]
+    qkv, z, b, a = split_mixed(mixed, hk, hv, dk, dv)
+    conv_out, new_conv = causal_conv_silu(qkv, conv_state, conv_w)
+    key_dim = hk * dk
+    q = conv_out[:, :key_dim].reshape(length, hk, dk)
+    k = conv_out[:, key_dim : 2 * key_dim].reshape(length, hk, dk)
+    v = conv_out[:, 2 * key_dim :].reshape(length, hv, dv)
+    q, k = qk_norm(q, k)
+    g = forget_gate(a, A_log, dt_bias)
+    beta = sigmoid(b)
+    y, new_ssm = gated_delta_scan(q, k, v, g, beta, ssm_state, scan_dtype)
+    zr = z.reshape(length, hv, dv)
+    out = gated_rms_norm(y.astype(zr.dtype), zr, norm_w, eps)
+    return out, new_conv, new_ssm, y
+
+
+# ---------------------------------------------------------------------------
+# Synthetic BASELINE configurations (seeded; value distributions as stated)
+# ---------------------------------------------------------------------------
+
+
+def _l2n(x):
+    return x / np.linalg.norm(x, axis=-1, keepdims=True)
+
+
+def config1_inputs(seed=0):
+    """Config 1: fp32, B=1, T=64, Hk=4, Hv=8, Dk=Dv=64. q,k ~ N(0,1) then
+    L2-normalised per head; v ~ N(0,1); beta = sigmoid(N); log-decay
+    g = -softplus(N); S0 = 0. Returns float32 (q, k, v, g_log, beta, S0)."""
+
+    rng = np.random.default_rng(seed)
+    t, hk, hv, d = 64, 4, 8, 64
+    q = _l2n(rng.standard_normal((t, hk, d)))
+    k = _l2n(rng.standard_normal((t, hk, d)))
+    v = rng.standard_normal((t, hv, d))
+    beta = 1.0 / (1.0 + np.exp(-rng.standard_normal((t, hv))))
+    g_log = -np.logaddexp(0.0, rng.standard_normal((t, hv)))
+    s0 = np.zeros((hv, d, d))
+    return [a.astype(np.float32) for a in (q, k, v, g_log, beta, s0)]
+
+
+def decode_inputs(seed, batch, hk, hv, dk, dv, state_std=0.02, with_state=True):
+    """Config 2 generator for ONE decode step of ``batch`` sequences:
+    q,k ~ N(0,1) L2-normalised, v ~ N(0,1) (all to be rounded to bf16 by the
+    caller), beta = sigmoid(N), g_log = -softplus(N), state ~ N(0, state_std)
+    float32 ``(B, Hv, Dv, Dk)``."""
+
+    rng = np.random.default_rng(seed)
+    q = _l2n(rng.standard_normal((batch, hk, dk))).astype(np.float32)
+    k = _l2n(rng.standard_normal((batch, hk, dk))).astype(np.float32)
+    v = rng.standard_normal((batch, hv, dv)).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-rng.standard_normal((batch, hv))))).astype(np.float32)
+    g_log = (-np.logaddexp(0.0, rng.standard_normal((batch, hv)))).astype(np.float32)
+    state = None
+    if with_state:
+        state = (rng.standard_normal((batch, hv, dv, dk), dtype=np.float32) * state_std)
+    return q, k, v, g_log, beta, state
+
+
+def prefill_inputs(seed, total, hk, hv, dk, dv):
+    """Configs 3 and 5 per-token draws: q,k ~ N(0,1) L2-normalised,
+    v ~ N(0,1), beta = sigmoid(N), g_log = -softplus(N); float32 arrays of
+    ``total`` packed tokens (to be rounded to bf16 by the caller for q/k/v)."""
+
+    rng = np.random.default_rng(seed)
+    q = _l2n(rng.standard_normal((total, hk, dk), dtype=np.float32))
+    k = _l2n(rng.standard_normal((total, hk, dk), dtype=np.float32))
+    v = rng.standard_normal((total, hv, dv), dtype=np.float32)
+    beta = 1.0 / (1.0 + np.exp(-rng.standard_normal((total, hv), dtype=np.float32)))
+    g_log = -np.logaddexp(np.float32(0.0), rng.standard_normal((total, hv), dtype=np.float32))
+    return q, k, v, g_log.astype(np.float32), beta.astype(np.float32)
+
+
+def config5_lengths(n_seq=64, lo=256, hi=16384, seed=1):
+    """Config 5 sequence lengths: ``default_rng(1).integers(256, 16384,
+    size=64, endpoint=True)``."""
+
+    return np.random.default_rng(seed).integers(lo, hi, size=n_seq, endpoint=True)
+
+
+def block_inputs(seed, batch, length, hk=16, hv=32, dk=128, dv=128, kernel=4):
+    """Config 4 generator: mixed projection ``(B*T, 2HkDk + 2HvDv + 2Hv)``
+    ~ N(0,1) (rounded to bf16 by the caller), conv_w ~ N(0, 0.1) ``(C, K)``,
+    A_log ~ U(0, 1.5), dt_bias ~ N(0, 0.1), norm_w = 1."""
+
+    rng = np.random.default_rng(seed)
+    width = 2 * hk * dk + 2 * hv * dv + 2 * hv
+    conv_dim = 2 * hk * dk + hv * dv
+    mixed = rng.standard_normal((batch * length, width), dtype=np.float32)
+    conv_w = (rng.standard_normal((conv_dim, kernel), dtype=np.float32) * 0.1)
+    A_log = rng.uniform(0.0, 1.5, size=hv).astype(np.float32)
+    dt_bias = (rng.standard_normal(hv) * 0.1).astype(np.float32)
+    norm_w = np.ones(dv, np.float32)
+    return mixed, conv_w, A_log, dt_bias, norm_w
+
+
+def bf16_round(x):
+    """Round float32 to the nearest bfloat16 (ties to even), returned as
+    float32: the values a bf16 tensor holds."""
+
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    rounded = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    out = rounded.astype(np.uint32).view(np.float32)
+    return np.where(np.isnan(x), x, out)
+
+
+def rel_l2(actual, expected):
+    """||actual - expected||_2 / ||expected||_2 in float64 (0 if both are 0)."""
+
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    den = math.sqrt(float(np.sum(e * e)))
+    num = math.sqrt(float(np.sum((a - e) ** 2)))
+    return num / den if den > 0 else num
