@@ -1,0 +1,370 @@
+"""Benchmark of the gated-delta hot path on B200 (one JSON line on rank 0).
+
+Default workload: config 2, the decode step at the Qwen3.5-MoE linear-attention
+shape (B=64 sequences x 1 token, 16 key / 32 value heads, d=128, bf16 q/k/v,
+fp32 state [64, 32, 128, 128]), state carried from step to step. A step is
+one decode launch over the batch; ``value`` is the state HBM traffic
+(algorithmic bytes) per second over all ranks. The same line carries the
+prefill number of config 3 (T=8192) under ``"prefill"``.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the reference's CPU path (its ops-path recurrence,
+restated on torch's CPU backend with every host thread; MLX is not
+installable here) on the same workload, rank 0 only.
+
+Multi-GPU (torchrun, one rank per GPU): each rank decodes its own batch of 64
+sequences (sequence sharding, no collective on the data path), timing is the
+max over ranks, ``scaling`` is weak.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "mlx-lean-moe_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "GDN prefill tok/s & decode state HBM GB/s (% peak) at 1/2/4/8 B200 vs MLX CPU"
+B, HK, HV, D = 64, 16, 32, 128
+STATE_BYTES = 2 * B * HV * D * D * 4  # read + write of the fp32 state
+DECODE_BYTES = STATE_BYTES + 2 * B * HK * D * 2 + B * HV * D * 2 + 2 * B * HV * 4 + B * HV * D * 4
+PREFILL_T = 8192
+PREFILL_FLOP = 182_955 * PREFILL_T * HV  # chunked WY count per token-head, see DESIGN.md
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def bf16_round(x):
+    return torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16).float().numpy()
+
+
+def decode_step_inputs(seed):
+    """Config 2 per-step draws (q, k L2-normalised, v ~ N(0,1), beta =
+    sigmoid(N), g = -softplus(N)), q/k/v as bf16."""
+    rng = np.random.default_rng(seed)
+    l2n = lambda x: x / np.linalg.norm(x, axis=-1, keepdims=True)
+    q = torch.from_numpy(l2n(rng.standard_normal((B, HK, D), dtype=np.float32))).to(torch.bfloat16)
+    k = torch.from_numpy(l2n(rng.standard_normal((B, HK, D), dtype=np.float32))).to(torch.bfloat16)
+    v = torch.from_numpy(rng.standard_normal((B, HV, D), dtype=np.float32)).to(torch.bfloat16)
+    beta = torch.from_numpy(1 / (1 + np.exp(-rng.standard_normal((B, HV), dtype=np.float32))))
+    g = torch.from_numpy(-np.logaddexp(np.float32(0), rng.standard_normal((B, HV), dtype=np.float32)))
+    return q, k, v, g.float(), beta.float()
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index):
+        self.proc = None
+        self.bus = None
+        try:
+            props = torch.cuda.get_device_properties(device_index)
+            self.bus = getattr(props, "pci_bus_id", None)
+        except Exception:
+            pass
+        self.local = device_index
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.rows = []
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 10:
+                continue
+            self.rows.append(parts)
+
+    def summary(self):
+        rows = getattr(self, "rows", [])
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        mine = [r for r in rows if self.bus and self.bus.lower()[-12:] in r[1].lower()] or \
+               [r for r in rows if r[0] == str(self.local)] or rows
+        sm = [float(r[2]) for r in mine if r[2].replace(".", "").isdigit()]
+        loaded = [s for s in sm if s > 0.5 * max(sm)] if sm else []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in mine for i, x in enumerate(r[6:10]) if x.lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None,
+                "sm_max_mhz": float(mine[0][3]) if mine[0][3].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(mine)}
+
+
+def cpu_decode_sample(budget_s=10.0):
+    """The reference's CPU path for config 2: per sequence, the ops-path
+    recurrence for one token (torch CPU, all threads). Runs whole steps over
+    all 64 sequences until ~budget_s has passed (at least one)."""
+    from oracle.gdn_torch_cpu import gated_delta_scan_ops
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    rng = np.random.default_rng(0)
+    state = torch.from_numpy((rng.standard_normal((B, HV, D, D), dtype=np.float32) * 0.02))
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        q, k, v, g_log, beta = decode_step_inputs(100 + steps)
+        q, k, v = q.float(), k.float(), v.float()
+        g = torch.exp(g_log)
+        for b in range(B):
+            _, state[b] = gated_delta_scan_ops(q[b : b + 1], k[b : b + 1], v[b : b + 1], g[b : b + 1],
+                                               beta[b : b + 1], state[b])
+        steps += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= budget_s:
+            break
+    return steps, elapsed
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_reference(args, world, rank):
+    """``--impl reference``: the reference's CPU path on the decode workload,
+    rank 0 only (other ranks exit without work)."""
+    if rank == 0:
+        cores = os.cpu_count() or 1
+        torch.set_num_threads(cores)
+        from oracle.gdn_torch_cpu import gated_delta_scan_ops
+
+        rng = np.random.default_rng(0)
+        state = torch.from_numpy(rng.standard_normal((B, HV, D, D), dtype=np.float32) * 0.02)
+        times = []
+        for step in range(args.warmup + args.steps):
+            q, k, v, g_log, beta = decode_step_inputs(100 + step)
+            q, k, v = q.float(), k.float(), v.float()
+            g = torch.exp(g_log)
+            t0 = time.perf_counter()
+            for b in range(B):
+                _, state[b] = gated_delta_scan_ops(q[b : b + 1], k[b : b + 1], v[b : b + 1], g[b : b + 1],
+                                                   beta[b : b + 1], state[b])
+            if step >= args.warmup:
+                times.append(time.perf_counter() - t0)
+        total = sum(times)
+        value = DECODE_BYTES * len(times) / total / 1e9
+        line = {
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, config 2 distributions)",
+            "config": {"workload": "decode, config 2: B=64 x 1 token, 16/32 heads, d=128, fp32 state, "
+                                   "state carried", "global_batch": B, "seq_len": 1, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{args.steps} full decode steps of 64 sequences (torch-CPU restatement "
+                                       "of the reference's ops path; MLX unavailable on this box)"},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+
+
+def measure_prefill(device, iters=3):
+    """Config 3: one sequence of 8192 tokens, bf16 q/k/v, fp32 state from 0."""
+    import gdn_b200
+
+    rng = np.random.default_rng(3)
+    l2n = lambda x: x / np.linalg.norm(x, axis=-1, keepdims=True)
+    q = torch.from_numpy(l2n(rng.standard_normal((PREFILL_T, HK, D), dtype=np.float32))).to(device, torch.bfloat16)
+    k = torch.from_numpy(l2n(rng.standard_normal((PREFILL_T, HK, D), dtype=np.float32))).to(device, torch.bfloat16)
+    v = torch.from_numpy(rng.standard_normal((PREFILL_T, HV, D), dtype=np.float32)).to(device, torch.bfloat16)
+    beta = torch.sigmoid(torch.randn(PREFILL_T, HV, device=device, generator=torch.Generator(device).manual_seed(1)))
+    g = -torch.nn.functional.softplus(torch.randn(PREFILL_T, HV, device=device,
+                                                  generator=torch.Generator(device).manual_seed(2)))
+    state = torch.zeros(1, HV, D, D, device=device)
+    out = torch.empty(PREFILL_T, HV, D, device=device)
+    st_out = torch.empty_like(state)
+    for _ in range(2):
+        gdn_b200.gated_delta_scan_varlen(q, k, v, g, beta, state, g_is_log=True, state_out=st_out, out=out)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * iters)]
+    for i in range(iters):
+        ev[2 * i].record()
+        gdn_b200.gated_delta_scan_varlen(q, k, v, g, beta, state, g_is_log=True, state_out=st_out, out=out)
+        ev[2 * i + 1].record()
+    torch.cuda.synchronize()
+    ms = statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(iters))
+    return ms
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode only: no e2e, prefill or CPU legs (for profiler runs)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        return run_reference(args, world, rank)
+
+    import gdn_b200
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    hbm_peak, tc_peak, peak_kind = peaks()
+
+    # --- device-resident decode (value) --------------------------------
+    rng = np.random.default_rng(1000 + rank)
+    state = torch.from_numpy(rng.standard_normal((B, HV, D, D), dtype=np.float32) * 0.02).to(device)
+    n_inputs = 8
+    dev_inputs = [tuple(x.to(device) for x in decode_step_inputs(rank * 1000 + i)) for i in range(n_inputs)]
+    out = torch.empty(B, HV, D, device=device)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)  # > L2 (126 MB)
+
+    def step(i):
+        q, k, v, g, beta = dev_inputs[i % n_inputs]
+        gdn_b200.gated_delta_decode(q, k, v, g, beta, state, g_is_log=True, out=out)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    with sampler:
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)  # evict the state from L2 between timed steps
+            starts[i].record()
+            step(i)
+            ends[i].record()
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = world * DECODE_BYTES * args.steps / (total_ms / 1e3) / 1e9
+    mean_ms = total_ms / args.steps
+    achieved = DECODE_BYTES / (statistics.mean(step_ms) / 1e3) / 1e9
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 state / bf16 q,k,v",
+        "data": "synthetic (seeded; config 2 value distributions)",
+        "config": {"workload": "decode, config 2: B=64 sequences x 1 token per rank, 16/32 heads, d=128, "
+                               "fp32 state [64,32,128,128] carried in place",
+                   "global_batch": B * world, "seq_len": 1, "parallelism": f"sequence-sharded x{world}",
+                   "l2": "flushed (256 MiB write) before every timed step"},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "traffic": None,
+                     "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6.65 TB/s",
+                     "bytes_per_launch": DECODE_BYTES, "kernel": "decode_kernel<128, bf16>"},
+        "clocks": sampler.summary(),
+    }
+
+    if not args.no_extras:
+        # --- end to end through the public API with host buffers ---------
+        host = [tuple(x.pin_memory() for x in decode_step_inputs(rank * 1000 + 500 + i)) for i in range(n_inputs)]
+        y_host = torch.empty(B, HV, D).pin_memory()
+        h2d = sum(x.numel() * x.element_size() for x in host[0])
+        d2h = y_host.numel() * y_host.element_size()
+        stream = torch.cuda.current_stream(device)
+
+        def e2e_step(i):
+            q, k, v, g, beta = (x.to(device, non_blocking=True) for x in host[i % n_inputs])
+            y, _ = gdn_b200.gated_delta_decode(q, k, v, g, beta, state, g_is_log=True)
+            y_host.copy_(y, non_blocking=True)
+            stream.synchronize()  # the step's result is on the host
+            return y_host
+
+        for i in range(args.warmup):
+            e2e_step(i)
+        if world > 1:
+            torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.steps):
+            e2e_step(i)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([e2e_ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            e2e_ms = float(t.item())
+        line["e2e"] = {"value": world * DECODE_BYTES * args.steps / (e2e_ms / 1e3) / 1e9, "unit": "GB/s",
+                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                       "ms_per_step": e2e_ms / args.steps,
+                       "api": "gdn_b200.gated_delta_decode (pinned host inputs -> device -> host y)"}
+        line["gpu_launches"] = 2 * args.steps
+
+        # --- config 3 prefill (secondary metric) --------------------------
+        pf_ms = measure_prefill(device)
+        line["prefill"] = {"value": PREFILL_T / (pf_ms / 1e3), "unit": "tok/s", "ms": pf_ms,
+                           "config": "config 3: B=1, T=8192, 16/32 heads, d=128, bf16 q/k/v, fp32 state from 0",
+                           "achieved_tflops": PREFILL_FLOP / (pf_ms / 1e3) / 1e12,
+                           "frac_of_bf16_peak": PREFILL_FLOP / (pf_ms / 1e3) / 1e12 / tc_peak,
+                           "algo": "auto"}
+
+        # --- CPU baseline (rank 0, N=1 only) --------------------------------
+        if rank == 0 and world == 1:
+            steps_cpu, secs = cpu_decode_sample()
+            line["cpu_baseline"] = {
+                "value": DECODE_BYTES * steps_cpu / secs / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1,
+                "kind": "port",
+                "sample": f"{steps_cpu} decode steps x 64 sequences in {secs:.1f} s: torch-CPU restatement of the "
+                          "reference's ops path (qw/gated_delta.py:24-41,93-109), one call per sequence; "
+                          "MLX CPU unavailable on this box"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

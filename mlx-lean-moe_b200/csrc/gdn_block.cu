@@ -1,0 +1,275 @@
+// The linear-attention layer's prologue and epilogue around the scan, and
+// the forget gate.
+//
+// Reference (qw/ = src/mlx_lean_moe/model/qwen3_5/):
+//   forget_gate           qw/gated_delta.py:14-21
+//   _convolve             qw/linear_attention.py:61-79
+//   q/k norm, gates       qw/linear_attention.py:104-116
+//   _gated_rms_norm       qw/linear_attention.py:22-32, applied at :122-124
+//
+// Rounding points.  With bfloat16 activations the reference materialises, in
+// bfloat16: the conv weight and the conv state cast to the input dtype
+// (:69, :72), the conv output, its SiLU (nn.silu is one fused function), the
+// rms-normed q/k and their rescaled values (:112-113), beta = sigmoid(b)
+// (:116), y cast to z's dtype (:123), the rms-norm output (:28) and the final
+// product (:30-32).  The forget gate is computed in float32 (gated_delta.py:18-
+// 20) and the scan in float32 (the state is float32).  These kernels compute
+// in float32 and round to the activation type at exactly those points (a no-op
+// for float32 activations).
+#include "gdn_common.cuh"
+
+namespace gdn {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+  return x;
+}
+
+__global__ void forget_gate_kernel(const void* a, gdn_dtype dt, int64_t a_st, int64_t n, int hv,
+                                   const float* A_log, const float* dt_bias, float* g, gdn_gate_kind kind) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (idx >= n * hv) return;
+  const int64_t t = idx / hv;
+  const int h = (int)(idx % hv);
+  const int64_t ai = t * a_st + h;
+  float av;
+  if (dt == GDN_BF16)
+    av = __bfloat162float(static_cast<const __nv_bfloat16*>(a)[ai]);
+  else if (dt == GDN_F16)
+    av = __half2float(static_cast<const __half*>(a)[ai]);
+  else
+    av = static_cast<const float*>(a)[ai];
+  const float lg = -expf(A_log[h]) * softplus_f(av + dt_bias[h]);
+  g[idx] = kind == GDN_GATE_LOG ? lg : expf(lg);
+}
+
+constexpr int TT = 16;          // tokens per prologue CTA
+constexpr int MAXC = 8;         // channels per lane (head width <= 256)
+constexpr int MAXK = 8;         // conv kernel width supported
+
+// Sequence containing token t (cu_seqlens sorted, B + 1 entries).
+__device__ __forceinline__ int64_t find_seq(const int64_t* cu, int64_t n_tokens, int64_t n_seqs, int64_t t) {
+  if (!cu) return t / (n_tokens / n_seqs);
+  int64_t lo = 0, hi = n_seqs - 1;
+  while (lo < hi) {  // last b with cu[b] <= t, skipping empty sequences
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+template <typename T, typename TS>
+__device__ __forceinline__ float conv_src(const BlockParams& p, int64_t b, int64_t start, int64_t pos, int c) {
+  // pos: absolute token index; positions before the sequence start come from
+  // that sequence's conv state rows (row K-1 - (start - pos)).
+  if (pos >= start) return to_f(static_cast<const T*>(p.mixed)[pos * p.mixed_st + c]);
+  if (!p.conv_state_in) return 0.f;
+  const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
+  const int64_t row = p.kernel - 1 - (start - pos);
+  const float x = to_f(static_cast<const TS*>(p.conv_state_in)[(b * (p.kernel - 1) + row) * conv_dim + c]);
+  return round_to<T>(x);
+}
+
+// Grid: x = token tiles of TT, y = groups of 4 conv heads (+1 for the gates).
+// A conv head is Dk channels of q or k, or Dv channels of v; one warp each.
+template <typename T, typename TS>
+__global__ void __launch_bounds__(128) block_prologue_kernel(const BlockParams p) {
+  const int64_t t0 = blockIdx.x * (int64_t)TT;
+  const int n_heads = 2 * p.hk + p.hv;
+  const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
+  const int64_t off_b = conv_dim + (int64_t)p.hv * p.dv, off_a = off_b + p.hv;
+
+  if (blockIdx.y == gridDim.y - 1) {  // gates
+    for (int idx = threadIdx.x; idx < TT * p.hv; idx += blockDim.x) {
+      const int64_t t = t0 + idx / p.hv;
+      const int h = idx % p.hv;
+      if (t >= p.n_tokens) break;
+      const T* row = static_cast<const T*>(p.mixed) + t * p.mixed_st;
+      const float av = to_f(row[off_a + h]), bv = to_f(row[off_b + h]);
+      p.g_log[t * p.hv + h] = -expf(p.A_log[h]) * softplus_f(av + p.dt_bias[h]);
+      p.beta[t * p.hv + h] = round_to<T>(sigmoid_f(bv));
+    }
+    return;
+  }
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ch = blockIdx.y * 4 + warp;
+  if (ch >= n_heads) return;
+  const bool is_q = ch < p.hk, is_k = !is_q && ch < 2 * p.hk;
+  const int width = (is_q || is_k) ? p.dk : p.dv;
+  const int64_t c0 = ch < 2 * p.hk ? (int64_t)ch * p.dk : 2LL * p.hk * p.dk + (int64_t)(ch - 2 * p.hk) * p.dv;
+  const int K = p.kernel;
+
+  float w[MAXC][MAXK];
+#pragma unroll
+  for (int m = 0; m < MAXC; ++m) {
+    const int d = lane + 32 * m;
+#pragma unroll
+    for (int j = 0; j < MAXK; ++j)
+      w[m][j] = (d < width && j < K) ? round_to<T>(p.conv_w[(c0 + d) * K + j]) : 0.f;
+  }
+
+  const int64_t t_end = min(t0 + TT, p.n_tokens);
+  int64_t b = find_seq(p.cu_seqlens, p.n_tokens, p.n_seqs, t0);
+  int64_t s_start, s_end;
+  seq_range(p.cu_seqlens, p.n_tokens, p.n_seqs, b, s_start, s_end);
+  for (int64_t t = t0; t < t_end; ++t) {
+    while (t >= s_end) {  // next non-empty sequence
+      ++b;
+      seq_range(p.cu_seqlens, p.n_tokens, p.n_seqs, b, s_start, s_end);
+    }
+    float x[MAXC];
+    float ss = 0.f;
+#pragma unroll
+    for (int m = 0; m < MAXC; ++m) {
+      const int d = lane + 32 * m;
+      float acc = 0.f;
+      if (d < width) {
+#pragma unroll
+        for (int j = 0; j < MAXK; ++j)
+          if (j < K) acc += w[m][j] * conv_src<T, TS>(p, b, s_start, t - (K - 1) + j, (int)(c0 + d));
+      }
+      const float conv = round_to<T>(acc);
+      x[m] = d < width ? round_to<T>(silu_f(conv)) : 0.f;
+      ss += x[m] * x[m];
+    }
+    if (is_q || is_k) {
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / (float)width + 1e-6f);
+      const float scale = is_q ? 1.f / (float)p.dk : rsqrtf((float)p.dk);
+      T* dst = static_cast<T*>(is_q ? p.q : p.k) + (t * p.hk + (is_q ? ch : ch - p.hk)) * (int64_t)p.dk;
+#pragma unroll
+      for (int m = 0; m < MAXC; ++m) {
+        const int d = lane + 32 * m;
+        if (d < width) dst[d] = from_f<T>(round_to<T>(x[m] * inv) * scale);
+      }
+    } else {
+      T* dst = static_cast<T*>(p.v) + (t * p.hv + (ch - 2 * p.hk)) * (int64_t)p.dv;
+#pragma unroll
+      for (int m = 0; m < MAXC; ++m) {
+        const int d = lane + 32 * m;
+        if (d < width) dst[d] = from_f<T>(x[m]);
+      }
+    }
+  }
+}
+
+// New conv tail per sequence: the last K-1 rows of [conv_state ; qkv_b]
+// (qw/linear_attention.py:75-79), in the state's dtype.  One thread per
+// (sequence, channel); rows are written in increasing order, and each read
+// index is >= the written one, so the update is safe in place.
+template <typename T, typename TS>
+__global__ void block_conv_tail_kernel(const BlockParams p) {
+  const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
+  const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t b = blockIdx.y;
+  if (c >= conv_dim) return;
+  int64_t start, end;
+  seq_range(p.cu_seqlens, p.n_tokens, p.n_seqs, b, start, end);
+  const int64_t len = end - start;
+  const int km1 = p.kernel - 1;
+  TS* out = static_cast<TS*>(p.conv_state_out) + b * km1 * conv_dim;
+  const TS* in = static_cast<const TS*>(p.conv_state_in);
+  for (int i = 0; i < km1; ++i) {
+    const int64_t pos = len - km1 + i;  // position within [conv_state ; qkv] minus (K-1)
+    float x;
+    if (pos >= 0)
+      x = to_f(static_cast<const T*>(p.mixed)[(start + pos) * p.mixed_st + c]);
+    else
+      x = in ? round_to<T>(to_f(in[(b * km1 + km1 + pos) * conv_dim + c])) : 0.f;
+    out[i * conv_dim + c] = from_f<TS>(x);
+  }
+}
+
+// out = silu(z) * rms_norm(y -> T, norm_w, eps); one warp per (token, head).
+template <typename T>
+__global__ void __launch_bounds__(256) block_epilogue_kernel(const BlockParams p) {
+  const int64_t row = blockIdx.x * 8LL + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= p.n_tokens * p.hv) return;
+  const int64_t t = row / p.hv;
+  const int h = (int)(row % p.hv);
+  const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
+  const T* z = static_cast<const T*>(p.mixed) + t * p.mixed_st + conv_dim + (int64_t)h * p.dv;
+  const float* y = p.y + row * p.dv;
+  float yb[MAXC];
+  float ss = 0.f;
+#pragma unroll
+  for (int m = 0; m < MAXC; ++m) {
+    const int d = lane + 32 * m;
+    yb[m] = d < p.dv ? round_to<T>(y[d]) : 0.f;
+    ss += yb[m] * yb[m];
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)p.dv + p.eps);
+  T* out = static_cast<T*>(p.out) + row * p.dv;
+#pragma unroll
+  for (int m = 0; m < MAXC; ++m) {
+    const int d = lane + 32 * m;
+    if (d < p.dv) {
+      const float normed = round_to<T>(yb[m] * inv * p.norm_w[d]);
+      out[d] = from_f<T>(silu_f(to_f(z[d])) * normed);
+    }
+  }
+}
+
+template <typename T, typename TS>
+cudaError_t prologue_t(const BlockParams& p, cudaStream_t s) {
+  const int n_heads = 2 * p.hk + p.hv;
+  const int64_t gx = (p.n_tokens + TT - 1) / TT;
+  if (gx == 0) return cudaSuccess;
+  dim3 grid((unsigned)gx, (unsigned)((n_heads + 3) / 4 + 1));
+  block_prologue_kernel<T, TS><<<grid, 128, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, typename TS>
+cudaError_t tail_t(const BlockParams& p, cudaStream_t s) {
+  const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
+  if (p.kernel <= 1 || p.n_seqs == 0) return cudaSuccess;
+  dim3 grid((unsigned)((conv_dim + 255) / 256), (unsigned)p.n_seqs);
+  block_conv_tail_kernel<T, TS><<<grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_forget_gate(const void* a, gdn_dtype dt, int64_t a_st, int64_t n, int hv, const float* A_log,
+                               const float* dt_bias, float* g, gdn_gate_kind kind, cudaStream_t s) {
+  const int64_t total = n * hv;
+  if (total == 0) return cudaSuccess;
+  forget_gate_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(a, dt, a_st, n, hv, A_log, dt_bias, g, kind);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_block_prologue(const BlockParams& p, cudaStream_t s) {
+  const bool st_bf = p.conv_state_dtype == GDN_BF16;
+  if (p.act_dtype == GDN_BF16)
+    return st_bf ? prologue_t<__nv_bfloat16, __nv_bfloat16>(p, s) : prologue_t<__nv_bfloat16, float>(p, s);
+  return st_bf ? prologue_t<float, __nv_bfloat16>(p, s) : prologue_t<float, float>(p, s);
+}
+
+cudaError_t launch_block_conv_tail(const BlockParams& p, cudaStream_t s) {
+  const bool st_bf = p.conv_state_dtype == GDN_BF16;
+  if (p.act_dtype == GDN_BF16)
+    return st_bf ? tail_t<__nv_bfloat16, __nv_bfloat16>(p, s) : tail_t<__nv_bfloat16, float>(p, s);
+  return st_bf ? tail_t<float, __nv_bfloat16>(p, s) : tail_t<float, float>(p, s);
+}
+
+cudaError_t launch_block_epilogue(const BlockParams& p, cudaStream_t s) {
+  const int64_t rows = p.n_tokens * p.hv;
+  if (rows == 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  if (p.act_dtype == GDN_BF16)
+    block_epilogue_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);
+  else
+    block_epilogue_kernel<float><<<grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace gdn

@@ -1,0 +1,113 @@
+// Shared device helpers and the internal launch interface of libgdn_b200.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "gdn_api.h"
+
+namespace gdn {
+
+// ---------------------------------------------------------------------------
+// Element loads/stores with conversion to/from float
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float x);
+template <>
+__device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
+
+// Round a float to the precision of T and back (identity for float).
+template <typename T>
+__device__ __forceinline__ float round_to(float x) { return to_f(from_f<T>(x)); }
+
+__device__ __forceinline__ float4 operator*(float4 a, float s) { return make_float4(a.x * s, a.y * s, a.z * s, a.w * s); }
+__device__ __forceinline__ float dot4(float4 a, float4 b) { return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w; }
+
+// Token range of sequence b.
+__device__ __forceinline__ void seq_range(const int64_t* cu, int64_t n_tokens, int64_t n_seqs, int64_t b,
+                                          int64_t& start, int64_t& end) {
+  if (cu) {
+    start = cu[b];
+    end = cu[b + 1];
+  } else {
+    const int64_t len = n_tokens / n_seqs;
+    start = b * len;
+    end = start + len;
+  }
+}
+
+// softplus(x) = log(1 + exp(x)) without overflow.
+__device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
+__device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
+
+// ---------------------------------------------------------------------------
+// Internal launch interface (one struct, filled by gdn_api.cu after checks)
+// ---------------------------------------------------------------------------
+struct ScanParams {
+  int64_t n_tokens, n_seqs;
+  const int64_t* cu_seqlens;
+  int hk, hv, dk, dv;
+  const void *q, *k, *v, *g, *beta;
+  int64_t q_st, q_sh, k_st, k_sh, v_st, v_sh, g_st, beta_st;
+  const float* state_in;
+  float* state_out;
+  void* out;
+  gdn_dtype qkv_dtype, gate_dtype, out_dtype;
+  gdn_gate_kind gate_kind;
+  // decode only
+  const int32_t* state_slots;
+  // chunked only
+  void* workspace;
+  size_t workspace_bytes;
+};
+
+struct BlockParams {
+  int64_t n_tokens, n_seqs;
+  const int64_t* cu_seqlens;
+  int hk, hv, dk, dv, kernel;
+  const void* mixed;
+  int64_t mixed_st;
+  gdn_dtype act_dtype;
+  const float* conv_w;
+  const void* conv_state_in;
+  void* conv_state_out;
+  gdn_dtype conv_state_dtype;
+  const float *A_log, *dt_bias, *norm_w;
+  float eps;
+  // prologue outputs (workspace)
+  void *q, *k, *v;   // act dtype, [N, Hk, Dk], [N, Hk, Dk], [N, Hv, Dv]
+  float *g_log, *beta;  // [N, Hv]
+  float* y;          // [N, Hv, Dv] scan output (float32)
+  void* out;         // [N, Hv, Dv] act dtype
+};
+
+cudaError_t launch_decode(const ScanParams& p, cudaStream_t s);
+cudaError_t launch_serial_scan(const ScanParams& p, cudaStream_t s);
+bool serial_supported(int dk);
+
+cudaError_t launch_forget_gate(const void* a, gdn_dtype dt, int64_t a_st, int64_t n, int hv, const float* A_log,
+                               const float* dt_bias, float* g, gdn_gate_kind kind, cudaStream_t s);
+
+cudaError_t launch_block_prologue(const BlockParams& p, cudaStream_t s);
+cudaError_t launch_block_conv_tail(const BlockParams& p, cudaStream_t s);
+cudaError_t launch_block_epilogue(const BlockParams& p, cudaStream_t s);
+
+// Chunked (tensor-core) prefill.
+bool chunked_supported(const ScanParams& p);
+size_t chunked_workspace_bytes(const ScanParams& p);
+cudaError_t launch_chunked_scan(const ScanParams& p, cudaStream_t s);
+// Reads and clears the device error word of the chunked kernels (0 = none).
+cudaError_t read_and_clear_device_error(unsigned* code);
+
+}  // namespace gdn

@@ -1,0 +1,32 @@
+"""gdn_b200: the Qwen3.5 gated-delta (GatedDeltaNet) operator on NVIDIA B200.
+
+Python host side of libgdn_b200.so (hand-written sm_100a CUDA behind the C
+ABI in include/gdn_api.h). The public API mirrors the reference
+conferencebeefwood46/mlx-lean-moe's ``qwen3_5.gated_delta`` module and its
+``RecurrentCache``; CUDA tensors replace MLX arrays.
+"""
+
+from .gated_delta import (
+    check_device_errors,
+    forget_gate,
+    gated_delta_decode,
+    gated_delta_scan,
+    gated_delta_scan_varlen,
+    gated_delta_step,
+)
+from .linear_attention import LinearAttentionShape, Qwen3_5LinearAttention, gated_delta_block
+from .recurrent_cache import BatchedRecurrentCache, RecurrentCache
+
+__all__ = [
+    "BatchedRecurrentCache",
+    "LinearAttentionShape",
+    "Qwen3_5LinearAttention",
+    "RecurrentCache",
+    "check_device_errors",
+    "forget_gate",
+    "gated_delta_block",
+    "gated_delta_decode",
+    "gated_delta_scan",
+    "gated_delta_scan_varlen",
+    "gated_delta_step",
+]

@@ -1,0 +1,181 @@
+"""The gated-delta linear-attention block on B200.
+
+``gated_delta_block`` is the fused part of the reference's
+``Qwen3_5LinearAttention.__call__`` (``qw/linear_attention.py:103-124``, with
+``qw/`` = ``src/mlx_lean_moe/model/qwen3_5/``): from the input projections
+to the gated RMSNorm, as one call into libgdn_b200 (``gdn_fused_block``):
+causal depthwise conv + SiLU, q/k rms-norm, forget gate and beta, the scan,
+and ``silu(z) * rms_norm(y)``. The conv and ssm states are advanced in
+place.
+
+``Qwen3_5LinearAttention`` wraps it with the layer's dense projections
+(``in_proj_qkv/z/b/a`` and ``out_proj`` run as torch matmuls) so the layer
+is a drop-in for the reference's class with a ``RecurrentCache``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .gated_delta import _DTYPES, _require_cuda, _stream
+from .recurrent_cache import RecurrentCache
+
+
+@dataclass(frozen=True)
+class LinearAttentionShape:
+    """``qw/config.py:10-32``: head counts/dims and conv kernel width."""
+
+    num_key_heads: int
+    num_value_heads: int
+    key_head_dim: int
+    value_head_dim: int
+    conv_kernel_dim: int
+
+    @property
+    def key_dim(self) -> int:
+        return self.num_key_heads * self.key_head_dim
+
+    @property
+    def value_dim(self) -> int:
+        return self.num_value_heads * self.value_head_dim
+
+    @property
+    def conv_dim(self) -> int:
+        return 2 * self.key_dim + self.value_dim
+
+    @property
+    def mixed_width(self) -> int:
+        """Row width of the mixed projection ``q | k | v | z | b | a``."""
+        return self.conv_dim + self.value_dim + 2 * self.num_value_heads
+
+
+def gated_delta_block(
+    mixed: torch.Tensor,
+    shape: LinearAttentionShape,
+    conv_w: torch.Tensor,
+    A_log: torch.Tensor,
+    dt_bias: torch.Tensor,
+    norm_w: torch.Tensor,
+    eps: float,
+    conv_state: torch.Tensor | None,
+    ssm_state: torch.Tensor,
+    *,
+    cu_seqlens: torch.Tensor | None = None,
+    n_seqs: int | None = None,
+    conv_state_out: torch.Tensor | None = None,
+    ssm_state_out: torch.Tensor | None = None,
+    algo: str = "auto",
+    out: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
+    """Run the fused block over B packed sequences.
+
+    ``mixed``: ``(N, W)`` float32 or bfloat16, rows ``q | k | v | z | b | a``.
+    ``conv_w``: ``(C, K)`` or ``(C, K, 1)``. ``conv_state``: ``(B, K-1, C)``
+    float32/bfloat16 or None (zeros); ``ssm_state``: float32 ``(B, Hv, Dv,
+    Dk)``. Outputs default to in-place updates of the given states. Returns
+    ``(out (N, Hv, Dv) in mixed's dtype, conv_state_out, ssm_state_out)``."""
+
+    device = _require_cuda(mixed, conv_w, A_log, dt_bias, norm_w, conv_state, ssm_state, cu_seqlens)
+    if mixed.ndim != 2 or mixed.shape[1] != shape.mixed_width or mixed.stride(1) != 1:
+        raise ValueError(f"mixed must be (N, {shape.mixed_width}) with contiguous rows")
+    if mixed.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("mixed must be float32 or bfloat16")
+    if n_seqs is None:
+        n_seqs = 1 if cu_seqlens is None else cu_seqlens.numel() - 1
+    K = shape.conv_kernel_dim
+    hv, dv, dk = shape.num_value_heads, shape.value_head_dim, shape.key_head_dim
+    if tuple(ssm_state.shape) != (n_seqs, hv, dv, dk) or ssm_state.dtype != torch.float32:
+        raise ValueError("ssm_state must be float32 (B, Hv, Dv, Dk)")
+    if conv_state is not None and (tuple(conv_state.shape) != (n_seqs, K - 1, shape.conv_dim)
+                                   or conv_state.dtype not in (torch.float32, torch.bfloat16)):
+        raise ValueError("conv_state must be (B, K-1, conv_dim) float32 or bfloat16")
+    conv_w2 = conv_w.reshape(shape.conv_dim, K).float().contiguous()
+    A = A_log.float().contiguous()
+    dt = dt_bias.float().contiguous()
+    nw = norm_w.float().contiguous()
+    ssm_in = ssm_state.contiguous()
+    if ssm_state_out is None:
+        ssm_state_out = ssm_in
+    if conv_state_out is None and K > 1:
+        conv_state_out = (conv_state if conv_state is not None
+                          else torch.zeros((n_seqs, K - 1, shape.conv_dim), dtype=torch.float32, device=device))
+    if out is None:
+        out = torch.empty((mixed.shape[0], hv, dv), dtype=mixed.dtype, device=device)
+
+    a = _lib.BlockArgs()
+    a.n_tokens, a.n_seqs = mixed.shape[0], n_seqs
+    a.cu_seqlens = cu_seqlens.data_ptr() if cu_seqlens is not None else None
+    a.hk, a.hv, a.dk, a.dv, a.conv_kernel = shape.num_key_heads, hv, dk, dv, K
+    a.mixed, a.mixed_stride_t, a.act_dtype = mixed.data_ptr(), mixed.stride(0), _DTYPES[mixed.dtype]
+    a.conv_w = conv_w2.data_ptr()
+    a.conv_state_in = conv_state.data_ptr() if conv_state is not None else None
+    a.conv_state_out = conv_state_out.data_ptr() if conv_state_out is not None else None
+    st_dtype = conv_state_out.dtype if conv_state_out is not None else torch.float32
+    if conv_state is not None and conv_state.dtype != st_dtype:
+        raise ValueError("conv_state and conv_state_out must share a dtype")
+    a.conv_state_dtype = _DTYPES[st_dtype]
+    a.A_log, a.dt_bias, a.norm_w, a.eps = A.data_ptr(), dt.data_ptr(), nw.data_ptr(), float(eps)
+    a.state_in, a.state_out, a.out = ssm_in.data_ptr(), ssm_state_out.data_ptr(), out.data_ptr()
+    a.algo = _lib.ALGOS[algo]
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(lib.gdn_block_workspace_size(ctypes.byref(a), ctypes.byref(nbytes)), "gated_delta_block")
+        workspace = torch.empty(max(nbytes.value, 1), dtype=torch.uint8, device=device)
+        a.workspace, a.workspace_bytes = workspace.data_ptr(), nbytes.value
+        _lib.check(lib.gdn_fused_block(ctypes.byref(a), _stream(device)), "gated_delta_block")
+    return out, conv_state_out, ssm_state_out
+
+
+class Qwen3_5LinearAttention:
+    """``qw/linear_attention.py:35-127`` with dense projection weights
+    ``(out, in)``: projections as torch matmuls, everything between them in
+    one fused call. ``__call__(x, cache)`` takes ``(hidden,)`` for one decode
+    step or ``(L, hidden)`` and returns the same rank, advancing ``cache``."""
+
+    def __init__(
+        self,
+        shape: LinearAttentionShape,
+        rms_norm_eps: float,
+        in_proj_qkv: torch.Tensor,
+        in_proj_z: torch.Tensor,
+        in_proj_a: torch.Tensor,
+        in_proj_b: torch.Tensor,
+        conv1d_weight: torch.Tensor,
+        A_log: torch.Tensor,
+        dt_bias: torch.Tensor,
+        norm_weight: torch.Tensor,
+        out_proj: torch.Tensor,
+        algo: str = "auto",
+    ) -> None:
+        self.shape = shape
+        self.eps = rms_norm_eps
+        # One matmul produces the mixed row q|k|v|z|b|a.
+        self.in_proj = torch.cat([in_proj_qkv, in_proj_z, in_proj_b, in_proj_a], dim=0)
+        self.conv_w = conv1d_weight.reshape(shape.conv_dim, shape.conv_kernel_dim)
+        self.A_log, self.dt_bias, self.norm_weight = A_log, dt_bias, norm_weight
+        self.out_proj = out_proj
+        self.algo = algo
+
+    def __call__(self, x: torch.Tensor, cache: RecurrentCache) -> torch.Tensor:
+        if x.ndim not in (1, 2):
+            raise ValueError(f"Qwen3_5LinearAttention expects 1-D or 2-D x, got shape {tuple(x.shape)}")
+        squeeze = x.ndim == 1
+        rows = x[None, :] if squeeze else x
+        seq_len = rows.shape[0]
+        mixed = (rows @ self.in_proj.T).contiguous()
+        conv_state, ssm_state = cache.state()
+        new_conv = conv_state.clone()
+        new_ssm = ssm_state.clone()
+        out, _, _ = gated_delta_block(
+            mixed, self.shape, self.conv_w, self.A_log, self.dt_bias, self.norm_weight, self.eps,
+            conv_state[None], ssm_state[None], conv_state_out=new_conv[None], ssm_state_out=new_ssm[None],
+            algo=self.algo,
+        )
+        cache.update(new_conv, new_ssm, advance=seq_len)
+        result = out.reshape(seq_len, -1) @ self.out_proj.T
+        return result[0] if squeeze else result

@@ -226,43 +226,52 @@ def sigmoid(x):
     return (1.0 / (1.0 + np.exp(-x))).astype(x.dtype)
 
 
-def causal_conv_silu(qkv, conv_state, conv_w):
+def _ident(x):
+    return x
+
+
+def causal_conv_silu(qkv, conv_state, conv_w, rnd=_ident):
     """``qw/linear_attention.py:61-79``: depthwise cross-correlation of
     ``[conv_state ; qkv]`` (no padding, so L outputs) with weight ``(C, K)``
     (the reference's ``(C, K, 1)`` squeezed), then SiLU. Returns
     ``(silu(out) (L, C), new_tail (K-1, C))``; the tail is taken from the front
-    index (``:75-77``), so K=1 keeps nothing."""
+    index (``:75-77``), so K=1 keeps nothing.
 
-    qkv = np.asarray(qkv)
-    w = np.asarray(conv_w).reshape(conv_w.shape[0], -1)
+    ``rnd`` rounds to the activation dtype where the reference materialises
+    an array in it: the conv state and weight cast to the input dtype
+    (``:69, :72``), the conv output and its SiLU (identity for float32)."""
+
+    qkv = np.asarray(qkv, np.float32)
+    w = rnd(np.asarray(conv_w, np.float32).reshape(conv_w.shape[0], -1))
     kernel = w.shape[1]
-    conv_in = np.concatenate([np.asarray(conv_state).astype(qkv.dtype), qkv], axis=0)
+    conv_in = np.concatenate([rnd(np.asarray(conv_state, np.float32)), qkv], axis=0)
     length = qkv.shape[0]
-    out = np.zeros((length, qkv.shape[1]), dtype=np.result_type(conv_in, w))
+    out = np.zeros((length, qkv.shape[1]), dtype=np.float64)
     for j in range(kernel):
-        out += conv_in[j : j + length] * w[None, :, j]
+        out += conv_in[j : j + length].astype(np.float64) * w[None, :, j]
+    out = rnd(out.astype(np.float32))
     tail_start = conv_in.shape[0] - (kernel - 1)
-    return silu(out), conv_in[tail_start:]
+    return rnd(silu(out)), conv_in[tail_start:]
 
 
-def qk_norm(q, k):
+def qk_norm(q, k, rnd=_ident):
     """``qw/linear_attention.py:109-113``: q <- Dk^-1 rms_norm(q, eps=1e-6),
-    k <- Dk^-1/2 rms_norm(k, eps=1e-6), no weight; eps is hard-coded."""
+    k <- Dk^-1/2 rms_norm(k, eps=1e-6), no weight; eps is hard-coded. ``rnd``
+    rounds the rms-norm output and the rescaled value, as the reference
+    materialises both."""
 
     inv_scale = q.shape[-1] ** -0.5
-    qn = (inv_scale**2) * rms_norm(q, None, 1e-6)
-    kn = inv_scale * rms_norm(k, None, 1e-6)
-    return qn.astype(q.dtype), kn.astype(k.dtype)
+    qn = rnd(np.float32(inv_scale**2) * rnd(rms_norm(q, None, 1e-6)))
+    kn = rnd(np.float32(inv_scale) * rnd(rms_norm(k, None, 1e-6)))
+    return qn.astype(np.float32), kn.astype(np.float32)
 
 
-def gated_rms_norm(x, gate, weight, eps):
+def gated_rms_norm(x, gate, weight, eps, rnd=_ident):
     """``qw/linear_attention.py:22-32``: silu(gate_f32) * rms_norm(x, w, eps)
-    in float32, cast back to x's dtype."""
+    in float32, cast back to x's dtype (``rnd``)."""
 
-    normed = rms_norm(x, weight, eps)
-    return (silu(np.asarray(gate, np.float32)) * normed.astype(np.float32)).astype(
-        np.asarray(x).dtype
-    )
+    normed = rnd(rms_norm(x, weight, eps))
+    return rnd(silu(np.asarray(gate, np.float32)) * normed.astype(np.float32))
 
 
 def split_mixed(mixed, hk, hv, dk, dv):
@@ -280,32 +289,45 @@ def split_mixed(mixed, hk, hv, dk, dv):
     return qkv, z, b, a
 
 
+def block_prologue(mixed, conv_w, conv_state, A_log, dt_bias, hk, hv, dk, dv, rnd=_ident):
+    """``qw/linear_attention.py:103-116`` for one sequence: conv + SiLU, q/k/v
+    split, q/k norm, log forget gate and beta. Returns float32
+    ``(q, k, v, g_log, beta, new_conv_state)`` (values rounded by ``rnd``
+    where the reference rounds)."""
+
+    length = mixed.shape[0]
+    qkv, _, b, a = split_mixed(np.asarray(mixed, np.float32), hk, hv, dk, dv)
+    conv_out, new_conv = causal_conv_silu(qkv, conv_state, conv_w, rnd)
+    key_dim = hk * dk
+    q = conv_out[:, :key_dim].reshape(length, hk, dk)
+    k = conv_out[:, key_dim : 2 * key_dim].reshape(length, hk, dk)
+    v = conv_out[:, 2 * key_dim :].reshape(length, hv, dv)
+    q, k = qk_norm(q, k, rnd)
+    g_log = forget_gate_log(a, A_log, dt_bias)
+    beta = rnd(sigmoid(np.asarray(b, np.float32)))
+    return q, k, v, g_log, beta, new_conv
+
+
 def linear_attention_core(
     mixed, conv_w, conv_state, A_log, dt_bias, norm_w, ssm_state, eps, hk, hv, dk, dv,
-    scan_dtype=np.float64,
+    scan_dtype=np.float64, rnd=_ident,
 ):
     """``qw/linear_attention.py:81-124`` from the projections on, for one
     sequence: conv+SiLU (``:103``), q/k/v split (``:104-107``), q/k norm
     (``:109-113``), gates (``:115-116``), scan (``:118-119``), gated RMSNorm
     of ``y`` cast to z's dtype (``:122-124``). ``out_proj`` is not applied.
+    ``rnd`` is the activation-dtype rounding (bf16_round for bfloat16).
 
-    Returns ``(out (L, Hv, Dv) in mixed's dtype, new_conv_state, new_ssm_state,
-    y)``."""
+    Returns ``(out (L, Hv, Dv), new_conv_state, new_ssm_state, y)``."""
 
     length = mixed.shape[0]
-    qkv, z, b, a = split_mixed(mixed, hk, hv, dk, dv)
-    conv_out, new_conv = causal_conv_silu(qkv, conv_state, conv_w)
-    key_dim = hk * dk
-    q = conv_out[:, :key_dim].reshape(length, hk, dk)
-    k = conv_out[:, key_dim : 2 * key_dim].reshape(length, hk, dk)
-    v = conv_out[:, 2 * key_dim :].reshape(length, hv, dv)
-    q, k = qk_norm(q, k)
-    g = forget_gate(a, A_log, dt_bias)
-    beta = sigmoid(b)
+    q, k, v, g_log, beta, new_conv = block_prologue(mixed, conv_w, conv_state, A_log, dt_bias, hk, hv, dk, dv, rnd)
+    g = np.exp(g_log.astype(np.float64)) if scan_dtype == np.float64 else np.exp(g_log)
     y, new_ssm = gated_delta_scan(q, k, v, g, beta, ssm_state, scan_dtype)
+    _, z, _, _ = split_mixed(np.asarray(mixed, np.float32), hk, hv, dk, dv)
     zr = z.reshape(length, hv, dv)
-    out = gated_rms_norm(y.astype(zr.dtype), zr, norm_w, eps)
-    return out, new_conv, new_ssm, y
+    out = gated_rms_norm(rnd(y.astype(np.float32)), zr, norm_w, eps, rnd)
+    return out, new_conv, new_ssm.astype(np.float32), y
 
 
 # ---------------------------------------------------------------------------

@@ -1,0 +1,124 @@
+"""The C ABI: the library loads on a CPU-only host, exports every function
+include/gdn_api.h declares, its ctypes structs match the C layout, and
+argument errors come back as status codes before any CUDA call."""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+from conftest import ROOT
+from gdn_b200 import _lib
+
+HEADER = os.path.join(ROOT, "include", "gdn_api.h")
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gdn_[a-z_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_function():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 9
+    for name in names:
+        assert hasattr(lib, name), name
+    assert set(names) == set(_lib.EXPORTS)
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True, text=True).stdout
+    for name in names:
+        assert re.search(rf"\bT {name}\b", out), f"{name} not exported"
+
+
+def test_version():
+    assert _lib.load().gdn_version() == 1
+
+
+def _c_layout(tmp_path, struct: str, fields: list[str]) -> list[int]:
+    src = tmp_path / "layout.c"
+    lines = [f'#include "{HEADER}"', "#include <stdio.h>", "#include <stddef.h>", "int main(void){"]
+    lines.append(f'printf("%zu\\n", sizeof({struct}));')
+    for f in fields:
+        lines.append(f'printf("%zu\\n", offsetof({struct}, {f}));')
+    lines.append("return 0;}")
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-o", str(exe), str(src)], check=True)
+    return [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+
+
+@pytest.mark.parametrize("py,c", [(_lib.ScanArgs, "gdn_scan_args"), (_lib.DecodeArgs, "gdn_decode_args"),
+                                  (_lib.BlockArgs, "gdn_block_args")])
+def test_ctypes_structs_match_c_layout(tmp_path, py, c):
+    fields = [f[0] for f in py._fields_]
+    got = [ctypes.sizeof(py)] + [getattr(py, f).offset for f in fields]
+    assert got == _c_layout(tmp_path, c, fields)
+
+
+def _valid_args():
+    a = _lib.ScanArgs()
+    a.n_tokens, a.n_seqs = 4, 1
+    a.hk, a.hv, a.dk, a.dv = 2, 4, 16, 8
+    for name in ("q", "k", "v", "g", "beta", "out"):
+        setattr(a, name, 0x1000)
+    a.state_out = 0x2000
+    return a
+
+
+@pytest.mark.parametrize(
+    "mutate,fragment",
+    [
+        (lambda a: setattr(a, "hv", 3), "multiple of its head count"),
+        (lambda a: setattr(a, "dk", 0), "nonempty"),
+        (lambda a: setattr(a, "n_seqs", 3), "multiple of n_seqs"),
+        (lambda a: setattr(a, "state_out", 0x2004), "16-byte aligned"),
+        (lambda a: setattr(a, "q", None), "non-NULL"),
+        (lambda a: setattr(a, "q_stride_t", -1), "non-negative"),
+        (lambda a: (setattr(a, "state_in", 0x2000 + 64)), "overlaps"),
+        (lambda a: setattr(a, "out_dtype", _lib.GDN_F16), "out_dtype"),
+        (lambda a: setattr(a, "dk", 18), "dk"),
+        (lambda a: (setattr(a, "algo", _lib.GDN_ALGO_CHUNKED), setattr(a, "dk", 64)), "chunked"),
+    ],
+)
+def test_scan_rejects_bad_arguments_on_the_host(mutate, fragment):
+    lib = _lib.load()
+    a = _valid_args()
+    mutate(a)
+    size = ctypes.c_size_t(0)
+    st = lib.gdn_scan_workspace_size(ctypes.byref(a), ctypes.byref(size))
+    assert st in (_lib.GDN_EINVAL, _lib.GDN_EUNSUPPORTED)
+    assert fragment in lib.gdn_last_error().decode()
+
+
+def test_null_args_and_decode_checks():
+    lib = _lib.load()
+    assert lib.gdn_scan(None, None) == _lib.GDN_EINVAL
+    assert lib.gdn_decode(None, None) == _lib.GDN_EINVAL
+    d = _lib.DecodeArgs()
+    d.base = _valid_args()
+    assert lib.gdn_decode(ctypes.byref(d), None) == _lib.GDN_EINVAL  # 4 tokens for 1 sequence
+    assert "one token per sequence" in lib.gdn_last_error().decode()
+    b = _lib.BlockArgs()
+    assert lib.gdn_fused_block(ctypes.byref(b), None) == _lib.GDN_EINVAL
+    assert lib.gdn_forget_gate(None, 0, 0, 4, 0, None, None, None, 0, None) == _lib.GDN_EINVAL
+
+
+def test_block_workspace_size_is_host_only():
+    lib = _lib.load()
+    b = _lib.BlockArgs()
+    b.n_tokens, b.n_seqs = 64, 2
+    b.hk, b.hv, b.dk, b.dv, b.conv_kernel = 2, 4, 32, 32, 4
+    b.mixed, b.mixed_stride_t = 0x1000, 2 * 64 + 2 * 128 + 8
+    b.act_dtype, b.conv_state_dtype = _lib.GDN_BF16, _lib.GDN_F32
+    b.conv_w = b.A_log = b.dt_bias = b.norm_w = 0x3000
+    b.state_out, b.conv_state_out, b.out = 0x4000, 0x5000, 0x6000
+    b.eps = 1e-6
+    size = ctypes.c_size_t(0)
+    assert lib.gdn_block_workspace_size(ctypes.byref(b), ctypes.byref(size)) == _lib.GDN_OK
+    # q, k, v (bf16) + g, beta, y (fp32), each 256-byte aligned
+    assert size.value >= 64 * (2 * 64 * 2 + 128 * 2 + 4 * 4 * 2 + 128 * 4)
