@@ -142,10 +142,15 @@ __global__ void __launch_bounds__(128) decode_kernel(const ScanParams p) {
 // Token-serial scan over packed sequences.  Grid: x = B * row tiles, y = Hv.
 // q/k/v/g/beta of TB tokens are staged in shared memory (as float), then each
 // thread advances its rows through those tokens with the state in registers.
+// The next block of TB tokens is loaded into registers while the current one
+// is processed, so global-memory latency stays off the token loop.
 template <int DKP, typename T>
 __global__ void __launch_bounds__(128) serial_scan_kernel(const ScanParams p) {
   using L = Layout<DKP>;
   constexpr int TB = DKP >= 256 ? 16 : 32;
+  constexpr int NK = TB * DKP / 128;                       // k (and q) values staged per thread
+  constexpr int NV = (TB * L::ROWS + 127) / 128;           // v values staged per thread
+  static_assert(TB * DKP % 128 == 0, "staging layout");
   __shared__ __align__(16) float sk[TB][DKP];
   __shared__ __align__(16) float sq[TB][DKP];
   __shared__ float sv[TB][L::ROWS];
@@ -184,27 +189,53 @@ __global__ void __launch_bounds__(128) serial_scan_kernel(const ScanParams p) {
   const T* qbase = static_cast<const T*>(p.q) + kh * p.q_sh;
   const T* vbase = static_cast<const T*>(p.v) + h * p.v_sh;
 
+  // Registers holding the next block of tokens.
+  float pk[NK], pq[NK], pv[NV], pg = 0.f, pb = 0.f;
+  auto prefetch = [&](int64_t t0) {
+    const int64_t nt = end - t0 < TB ? end - t0 : TB;
+#pragma unroll
+    for (int e = 0; e < NK; ++e) {
+      const int idx = threadIdx.x + 128 * e;
+      const int tt = idx / DKP, c = idx % DKP;
+      const bool ok = tt < nt && c < dk;
+      pk[e] = ok ? to_f(kbase[(t0 + tt) * p.k_st + c]) : 0.f;
+      pq[e] = ok ? to_f(qbase[(t0 + tt) * p.q_st + c]) : 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < NV; ++e) {
+      const int idx = threadIdx.x + 128 * e;
+      const int tt = idx / L::ROWS, r = idx % L::ROWS;
+      const int row = tile_row0 + r;
+      pv[e] = (tt < nt && row < dv) ? to_f(vbase[(t0 + tt) * p.v_st + row]) : 0.f;
+    }
+    if (threadIdx.x < nt) {
+      pg = load_gate(p.g, p.gate_dtype, (t0 + threadIdx.x) * p.g_st + h);
+      if (p.gate_kind == GDN_GATE_LOG) pg = expf(pg);
+      pb = load_gate(p.beta, p.gate_dtype, (t0 + threadIdx.x) * p.beta_st + h);
+    }
+  };
+
+  if (start < end) prefetch(start);
   for (int64_t t0 = start; t0 < end; t0 += TB) {
     const int nt = (int)((end - t0) < TB ? (end - t0) : TB);
     __syncthreads();  // the previous block of tokens has been consumed
-    for (int idx = threadIdx.x; idx < nt * DKP; idx += blockDim.x) {
-      const int tt = idx / DKP, c = idx % DKP;
-      const int64_t tok = t0 + tt;
-      sk[tt][c] = c < dk ? to_f(kbase[tok * p.k_st + c]) : 0.f;
-      sq[tt][c] = c < dk ? to_f(qbase[tok * p.q_st + c]) : 0.f;
+#pragma unroll
+    for (int e = 0; e < NK; ++e) {
+      const int idx = threadIdx.x + 128 * e;
+      sk[idx / DKP][idx % DKP] = pk[e];
+      sq[idx / DKP][idx % DKP] = pq[e];
     }
-    for (int idx = threadIdx.x; idx < nt * L::ROWS; idx += blockDim.x) {
-      const int tt = idx / L::ROWS, r = idx % L::ROWS;
-      const int row = tile_row0 + r;
-      sv[tt][r] = row < dv ? to_f(vbase[(t0 + tt) * p.v_st + row]) : 0.f;
+#pragma unroll
+    for (int e = 0; e < NV; ++e) {
+      const int idx = threadIdx.x + 128 * e;
+      if (idx < TB * L::ROWS) sv[idx / L::ROWS][idx % L::ROWS] = pv[e];
     }
-    for (int tt = threadIdx.x; tt < nt; tt += blockDim.x) {
-      float gv = load_gate(p.g, p.gate_dtype, (t0 + tt) * p.g_st + h);
-      if (p.gate_kind == GDN_GATE_LOG) gv = expf(gv);
-      sg[tt] = gv;
-      sb[tt] = load_gate(p.beta, p.gate_dtype, (t0 + tt) * p.beta_st + h);
+    if (threadIdx.x < TB) {
+      sg[threadIdx.x] = pg;
+      sb[threadIdx.x] = pb;
     }
     __syncthreads();
+    if (t0 + TB < end) prefetch(t0 + TB);
 
     for (int tt = 0; tt < nt; ++tt) {
       const float gv = sg[tt], bv = sb[tt];
