@@ -184,6 +184,40 @@ gdn_status gdn_block_workspace_size(const gdn_block_args *args, size_t *bytes);
  * linear_attention.py:103-124, and its RecurrentCache.update (:120). */
 gdn_status gdn_fused_block(const gdn_block_args *args, gdn_stream_t stream);
 
+/* Size of the device scratch array behind gdn_fused_block_noalloc: 16 MiB
+ * (about 500 tokens of scratch at the Qwen3.5 linear-attention shape, 16/32
+ * heads of 128, bf16 activations). */
+#define GDN_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* gdn_fused_block for callers that cannot allocate device memory.  It has no
+ * counterpart in the reference (MLX allocates internally).
+ *
+ * Some callers cannot hand the library a workspace: a host bound to this
+ * library through a plain C FFI (Go, Java, Rust, a game or embedded engine)
+ * has no device allocator of its own and would need a cudaMalloc/cudaFree
+ * per call, which synchronises the whole device and stalls every stream in a
+ * serving loop; a server that reserves its entire device budget at start-up
+ * (weights, state pools) has no headroom for a per-call allocation at all.
+ * This entry point takes the same arguments as gdn_fused_block, ignores
+ * args->workspace / workspace_bytes, and instead uses one scratch array of
+ * GDN_NOALLOC_SCRATCH_BYTES compiled into the library as a __device__
+ * variable.  Every GPU on which the library is loaded holds that array until
+ * the process exits.  The call allocates nothing: no cudaMalloc, no cudaFree,
+ * no allocating library routine.
+ *
+ *  - Calls whose scratch need (gdn_block_workspace_size) exceeds
+ *    GDN_NOALLOC_SCRATCH_BYTES are rejected with GDN_EUNSUPPORTED before
+ *    anything runs; split them into calls over fewer tokens.
+ *  - The first call on each device looks up the array's device address
+ *    (cudaGetSymbolAddress, with that device current) and caches it; make
+ *    that first call before any stream capture.
+ *  - All calls share the one array.  Calls that can overlap on the GPU
+ *    (different streams, or several host threads) race on it: serialise them,
+ *    e.g. on one stream.  The array keeps the last call's data; nothing in it
+ *    needs to start at zero, since every scratch value is written before it
+ *    is read within a call. */
+gdn_status gdn_fused_block_noalloc(const gdn_block_args *args, gdn_stream_t stream);
+
 /* Synchronises `stream`, then reports and clears any error a bounded
  * device-side wait recorded since the last call (GDN_ETIMEOUT), or a CUDA
  * error (GDN_ECUDA). */

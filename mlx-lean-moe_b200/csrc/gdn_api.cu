@@ -130,6 +130,18 @@ gdn_status pick_algo(const gdn_scan_args* a, const gdn::ScanParams& p, bool* chu
 
 }  // namespace
 
+namespace gdn {
+gdn_status set_error(gdn_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return st;
+}
+}  // namespace gdn
+
 extern "C" {
 
 int gdn_version(void) { return GDN_API_VERSION; }

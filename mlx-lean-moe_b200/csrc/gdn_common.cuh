@@ -92,6 +92,9 @@ struct BlockParams {
   void* out;         // [N, Hv, Dv] act dtype
 };
 
+// Records a printf-style message for gdn_last_error() and returns st.
+gdn_status set_error(gdn_status st, const char* fmt, ...);
+
 cudaError_t launch_decode(const ScanParams& p, cudaStream_t s);
 cudaError_t launch_serial_scan(const ScanParams& p, cudaStream_t s);
 bool serial_supported(int dk);

@@ -71,6 +71,7 @@ EXPORTS = {
     "gdn_forget_gate": (_enum, [_p, _enum, _i64, _i64, _i32, _p, _p, _p, _enum, _p]),
     "gdn_block_workspace_size": (_enum, [ctypes.POINTER(BlockArgs), ctypes.POINTER(ctypes.c_size_t)]),
     "gdn_fused_block": (_enum, [ctypes.POINTER(BlockArgs), _p]),
+    "gdn_fused_block_noalloc": (_enum, [ctypes.POINTER(BlockArgs), _p]),
     "gdn_check_device_errors": (_enum, [_p]),
 }
 
