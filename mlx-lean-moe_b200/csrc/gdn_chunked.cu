@@ -1,14 +1,808 @@
-// Chunked (WY/UT, chunk 64) prefill on the tensor cores.
+// Chunked gated-delta prefill on the sm_100a tensor cores (chunk C = 64,
+// Dk = Dv = 128, bf16 q/k/v, float32 state).
+//
+// The recurrence of the reference (qw/gated_delta.py:24-41, qw/ =
+// src/mlx_lean_moe/model/qwen3_5/) run token by token is, over a chunk of C
+// tokens with inclusive log-decay cumsum G (gamma = exp(G_last)):
+//   A[t,s] = beta_t exp(G_t - G_s) k_t.k_s  (s < t),   T = (I + A)^-1
+//   R      = diag(beta) (V - diag(exp G) K S^T)          (C x Dv)
+//   Delta  = T R                                         (the d_t of every token)
+//   Y      = diag(exp G) Q S^T + P Delta,  P[t,s] = exp(G_t - G_s) q_t.k_s (s <= t)
+//   S'     = gamma S + Delta^T diag(exp(G_last - G)) K
+// Every decay factor is exp of a difference G_t - G_s with t >= s (never a
+// ratio of exponentials), so strong decays cannot overflow.
+//
+// Two kernels:
+//  * chunk_prep_kernel, parallel over (chunk, value head): one tcgen05 MMA
+//    [K;Q] K^T (M=128, N=64, K=128) gives K K^T and Q K^T in TMEM; the
+//    epilogue builds A and P, a forward substitution gives T, and T and P are
+//    written to the workspace as bf16 hi/lo pairs in the SW128 operand layout.
+//  * chunk_scan_kernel, one CTA per (sequence, value head), serial over the
+//    chunks with the float32 state S resident in TMEM.  Warp roles: warp 0
+//    loads (TMA tensor loads of K, Q, V; bulk copies of T, P), warp 1 issues
+//    the MMAs, warps 2-5 run the epilogues (one TMEM lane quarter each, one
+//    state row per thread).  Per chunk, in the transposed orientation
+//    (M = Dv state rows):
+//      [X | Y] = S [K | Q]^T       (N = 128, K = Dk)    2 passes (S hi, lo)
+//      Delta^T = R^T T^T           (N = 64,  K = C)     3 passes (hi*hi, hi*lo, lo*hi)
+//      O^T     = Delta^T P^T       (N = 64,  K = C)     3 passes
+//      U       = Delta'^T K        (N = 128, K = C)     2 passes (Delta' hi, lo)
+//    then Y^T = diag(exp G)-scaled Y + O and S <- gamma S + U.
+//  Operands that are not exact in bf16 (S, R, T, Delta, P) are split into
+//  bf16 hi + lo parts; the products then carry ~16 mantissa bits (rel-L2
+//  ~5e-6 against the float64 recurrence at T = 4096, versus ~3e-3 with plain
+//  bf16 operands and ~4e-4 with tf32).
+//
+// Every wait is bounded (2 s): on a timeout the kernel records an error in
+// g_device_error (read by gdn_check_device_errors), stops issuing work, lets
+// its own copies and MMAs in flight finish (again bounded), frees its TMEM
+// and returns.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
 #include "gdn_common.cuh"
+#include "gdn_sm100.cuh"
 
 namespace gdn {
 
 // Error word written by bounded device-side waits (0 = no error).
 __device__ unsigned g_device_error = 0;
 
-bool chunked_supported(const ScanParams&) { return false; }
-size_t chunked_workspace_bytes(const ScanParams&) { return 0; }
-cudaError_t launch_chunked_scan(const ScanParams&, cudaStream_t) { return cudaErrorNotSupported; }
+namespace {
+
+using namespace sm100;
+
+constexpr int CH = 64;   // chunk length
+constexpr int DH = 128;  // head dim (Dk = Dv)
+constexpr uint64_t kWaitNs = 2000000000ull;
+constexpr uint32_t kTile64 = 64 * 64 * 2;          // 64 x 64 bf16 operand tile (8 KB)
+constexpr size_t kRecBytes = 4 * (size_t)kTile64;  // T hi, T lo, P hi, P lo per (chunk, head)
+
+struct ChunkParams {
+  int64_t n_tokens, n_seqs;
+  const int64_t* cu;
+  int hk, hv;
+  const void* g;
+  const void* beta;
+  int64_t g_st, beta_st;
+  gdn_dtype gate_dtype;
+  gdn_gate_kind gate_kind;
+  const float* state_in;
+  float* state_out;
+  void* out;
+  gdn_dtype out_dtype;
+  unsigned char* ws;  // kRecBytes per (chunk slot, value head)
+};
+
+__device__ __forceinline__ float load_gate_f(const void* base, gdn_dtype dt, int64_t idx) {
+  return dt == GDN_BF16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[idx])
+                        : static_cast<const float*>(base)[idx];
+}
+
+// Log-decay of token t, head h (clamped so that cumulative sums stay finite).
+__device__ __forceinline__ float log_decay(const ChunkParams& p, int64_t t, int h) {
+  float x = load_gate_f(p.g, p.gate_dtype, t * p.g_st + h);
+  if (p.gate_kind == GDN_GATE_MULT) x = logf(x);
+  return fmaxf(x, -1.0e4f);
+}
+
+__device__ __forceinline__ int64_t nchunks_of(int64_t len) { return (len + CH - 1) / CH; }
+
+// Chunk slot -> (sequence, chunk index within it); false past the last chunk.
+__device__ bool slot_to_chunk(const ChunkParams& p, int64_t slot, int64_t& b, int64_t& j) {
+  int64_t base = 0;
+  for (int64_t s = 0; s < p.n_seqs; ++s) {
+    int64_t st, en;
+    seq_range(p.cu, p.n_tokens, p.n_seqs, s, st, en);
+    const int64_t nc = nchunks_of(en - st);
+    if (slot < base + nc) {
+      b = s;
+      j = slot - base;
+      return true;
+    }
+    base += nc;
+  }
+  return false;
+}
+
+__device__ int64_t chunk_base_of(const ChunkParams& p, int64_t b) {
+  int64_t base = 0;
+  for (int64_t s = 0; s < b; ++s) {
+    int64_t st, en;
+    seq_range(p.cu, p.n_tokens, p.n_seqs, s, st, en);
+    base += nchunks_of(en - st);
+  }
+  return base;
+}
+
+__device__ __forceinline__ void record_error(volatile int* abort_flag) {
+  *abort_flag = 1;
+  atomicOr(&g_device_error, kErrTimeout);
+}
+
+// Inclusive prefix sum of sl[0..63] into sG by one warp (2 values per lane);
+// also exp(G), exp(G_last - G) and gamma = exp(G_last).
+__device__ __forceinline__ void chunk_cumsum(int lane, const float* sl, float* sG, float* seG, float* sdG,
+                                             float* sgamma) {
+  float a = sl[2 * lane], b = sl[2 * lane + 1];
+  float s = a + b;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const float o = __shfl_up_sync(0xffffffffu, s, off);
+    if (lane >= off) s += o;
+  }
+  const float g1 = s, g0 = s - b;
+  const float last = __shfl_sync(0xffffffffu, s, 31);
+  sG[2 * lane] = g0;
+  sG[2 * lane + 1] = g1;
+  seG[2 * lane] = expf(g0);
+  seG[2 * lane + 1] = expf(g1);
+  sdG[2 * lane] = expf(last - g0);
+  sdG[2 * lane + 1] = expf(last - g1);
+  if (lane == 0) *sgamma = expf(last);
+}
+
+// ===========================================================================
+// Kernel A: per (chunk, value head) -- T = (I + A)^-1 and P, as bf16 hi/lo.
+// ===========================================================================
+constexpr int kPrepAStride = 68;  // floats per row of the A / T scratch (16-byte rows)
+constexpr size_t kPrepSmem = 1024 + 32768 + 2 * 64 * kPrepAStride * 4;
+
+__global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                         const __grid_constant__ CUtensorMap kmap,
+                                                         const ChunkParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sKQ = base;                                        // [K;Q] 128 rows x 128, SW128
+  float* sA = reinterpret_cast<float*>(base + 32768);               // 64 x kPrepAStride
+  float* sT = sA + 64 * kPrepAStride;                               // 64 x kPrepAStride
+  __shared__ float sl[CH], sb[CH], sG[CH], seG[CH], sdG[CH], sgamma;
+  __shared__ __align__(8) uint64_t bar_load, bar_mma;
+  __shared__ uint32_t tmem_base;
+  __shared__ int64_t s_t0;
+  __shared__ int s_n, s_valid;
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.y;
+  const int kh = h / (p.hv / p.hk);
+  const int64_t slot = blockIdx.x;
+
+  if (tid == 0) {
+    int64_t b, j;
+    s_valid = slot_to_chunk(p, slot, b, j) ? 1 : 0;
+    if (s_valid) {
+      int64_t st, en;
+      seq_range(p.cu, p.n_tokens, p.n_seqs, b, st, en);
+      s_t0 = st + j * CH;
+      s_n = (int)(en - s_t0 < CH ? en - s_t0 : CH);
+    }
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (!s_valid) return;
+  const int64_t t0 = s_t0;
+  const int n = s_n;
+
+  if (warp == 0) tmem_alloc(&tmem_base, 64);
+  if (tid == 0) {
+    mbar_init(&bar_load, 1);
+    mbar_init(&bar_mma, 1);
+    fence_mbar_init();
+  }
+  if (tid < CH) {
+    const bool ok = tid < n;
+    sl[tid] = ok ? log_decay(p, t0 + tid, h) : 0.f;
+    sb[tid] = ok ? load_gate_f(p.beta, p.gate_dtype, (t0 + tid) * p.beta_st + h) : 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bar_load, 32768);
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb) {
+      tma_load_3d(sKQ + kb * 16384, &kmap, &bar_load, kb * 64, kh, (int)t0);
+      tma_load_3d(sKQ + kb * 16384 + 8192, &qmap, &bar_load, kb * 64, kh, (int)t0);
+    }
+  }
+  if (warp == 1) chunk_cumsum(lane, sl, sG, seG, sdG, &sgamma);
+
+  bool mma_issued = false;
+  if (tid == 0) {
+    if (mbar_wait(&bar_load, 0, kWaitNs)) {
+      tc_fence_after();
+      const uint32_t idesc = idesc_bf16_f32(128, 64);
+#pragma unroll
+      for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint32_t a = smem_u32(sKQ + kb * 16384 + ks * 32);
+          mma_bf16(tmem, sdesc_sw128(a), sdesc_sw128(a), idesc, kb + ks > 0);
+        }
+      mma_commit(&bar_mma);
+      mma_issued = true;
+    } else {
+      record_error(&abort_flag);
+    }
+  }
+  __syncthreads();
+  const bool ok = !abort_flag && mbar_wait(&bar_mma, 0, kWaitNs);
+  if (!ok && tid == 0) record_error(&abort_flag);
+  __syncthreads();
+  if (abort_flag) {
+    if (tid == 0 && mma_issued) mbar_wait(&bar_mma, 0, kWaitNs);
+    if (tid == 0) mbar_wait(&bar_load, 0, kWaitNs);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 64);
+    return;
+  }
+  tc_fence_after();
+
+  // Row r of [KK^T ; QK^T]: warps 0-1 hold K K^T rows, warps 2-3 Q K^T rows.
+  const int row = warp * 32 + lane;
+  float v[64];
+  {
+    float r0[32], r1[32];
+    const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16);
+    tmem_ld32(ta, r0);
+    tmem_ld32(ta + 32, r1);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      v[i] = r0[i];
+      v[32 + i] = r1[i];
+    }
+  }
+  if (row < CH) {
+    const int t = row;
+    const float gt = sG[t], bt = sb[t];
+    float* arow = sA + t * kPrepAStride;
+#pragma unroll
+    for (int s = 0; s < CH; ++s) arow[s] = (s < t && t < n) ? bt * expf(gt - sG[s]) * v[s] : 0.f;
+  } else {
+    const int t = row - CH;
+    const float gt = sG[t];
+    float pv[64];
+#pragma unroll
+    for (int s = 0; s < CH; ++s) pv[s] = (s <= t && t < n) ? expf(gt - sG[s]) * v[s] : 0.f;
+    unsigned char* rec = p.ws + ((size_t)slot * p.hv + h) * kRecBytes;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      uint4 hi, lo;
+      split8(pv + 8 * c, hi, lo);
+      *reinterpret_cast<uint4*>(rec + 2 * kTile64 + sw128_chunk(64, t, 0, c)) = hi;
+      *reinterpret_cast<uint4*>(rec + 3 * kTile64 + sw128_chunk(64, t, 0, c)) = lo;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 64);
+
+  // Forward substitution: thread c < 64 owns column c of T = (I + A)^-1.
+  if (tid < CH) {
+    const int c = tid;
+    float x[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float* arow = sA + i * kPrepAStride;
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < i; ++j) acc = fmaf(arow[j], x[j], acc);
+      x[i] = i < c ? 0.f : (i == c ? 1.f : -acc);
+    }
+#pragma unroll
+    for (int i = 0; i < 64; ++i) sT[i * kPrepAStride + c] = x[i];
+  }
+  __syncthreads();
+  {
+    const int t = tid & 63;
+    const bool lo_half = tid >= 64;
+    unsigned char* rec = p.ws + ((size_t)slot * p.hv + h) * kRecBytes + (lo_half ? kTile64 : 0);
+    const float* trow = sT + t * kPrepAStride;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float x8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x8[i] = trow[8 * c + i];
+      uint4 hi, lo;
+      split8(x8, hi, lo);
+      *reinterpret_cast<uint4*>(rec + sw128_chunk(64, t, 0, c)) = lo_half ? lo : hi;
+    }
+  }
+}
+
+// ===========================================================================
+// Kernel B: per (sequence, value head) -- serial over chunks, S in TMEM.
+// ===========================================================================
+// Dynamic shared memory map (offsets from the 1024-aligned base).
+constexpr uint32_t OFF_SHI = 0, OFF_SLO = 32768;   // S hi/lo: 128 x 128, two K-blocks
+constexpr uint32_t OFF_KQ = 65536;                 // [K;Q]: 128 x 128, two K-blocks
+constexpr uint32_t OFF_V = 98304;                  // V: [64][128] bf16 row-major
+constexpr uint32_t OFF_T = 114688;                 // T hi, T lo: 64 x 64 each
+constexpr uint32_t OFF_P = 131072;                 // P hi, P lo
+constexpr uint32_t OFF_R = 147456;                 // R (then Delta') hi, lo: 128 x 64 each
+constexpr uint32_t OFF_D = 180224;                 // Delta hi, lo: 128 x 64 each
+constexpr uint32_t OFF_KT = 212992;                // K^T: 128 (dk) x 64 (t)
+constexpr uint32_t SCAN_SMEM_USED = 229376;
+constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
+
+// TMEM columns.
+constexpr uint32_t TM_S = 0, TM_XY = 128, TM_D = 256, TM_O = 320, TM_U = 384;
+
+enum Bar {
+  B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
+  B_S_READY, B_XY_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_KT_READY, B_OU_DONE, B_DRAIN, N_BARS
+};
+
+__global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                            const __grid_constant__ CUtensorMap kmap,
+                                                            const __grid_constant__ CUtensorMap vmap,
+                                                            const ChunkParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bars[N_BARS];
+  __shared__ float sl[CH], sb[CH], sG[CH], seG[CH], sdG[CH], sgamma;
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int abort_flag;
+  __shared__ int64_t s_start, s_end, s_cbase;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x % p.hv;
+  const int64_t b = blockIdx.x / p.hv;
+  const int kh = h / (p.hv / p.hk);
+
+  if (tid == 0) {
+    int64_t st, en;
+    seq_range(p.cu, p.n_tokens, p.n_seqs, b, st, en);
+    s_start = st;
+    s_end = en;
+    s_cbase = chunk_base_of(p, b);
+    abort_flag = 0;
+    for (int i = 0; i < N_BARS; ++i) mbar_init(&bars[i], (i == B_KQ_EMPTY) ? 2 : 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+  const int64_t start = s_start, end = s_end;
+  const int64_t nch = nchunks_of(end - start);
+  const size_t head_off = ((size_t)b * p.hv + h) * DH * DH;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && nch > 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      // Loads issued per full barrier (each barrier has at most one in flight).
+      uint32_t n_kq = 0, n_v = 0, n_t = 0, n_p = 0;
+      for (int64_t c = 0; c < nch; ++c) {
+        const uint32_t par = (uint32_t)((c - 1) & 1);
+        const int t0 = (int)(start + c * CH);
+        const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
+        if (c > 0 && !mbar_wait(&bars[B_KQ_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+        if (abort_flag) break;
+        mbar_arrive_expect_tx(&bars[B_KQ_FULL], 32768);
+        for (int kb = 0; kb < 2; ++kb) {
+          tma_load_3d(base + OFF_KQ + kb * 16384, &kmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
+          tma_load_3d(base + OFF_KQ + kb * 16384 + 8192, &qmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
+        }
+        ++n_kq;
+        if (c > 0 && !mbar_wait(&bars[B_V_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+        if (abort_flag) break;
+        mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
+        tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
+        ++n_v;
+        if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+        if (abort_flag) break;
+        mbar_arrive_expect_tx(&bars[B_T_FULL], 2 * kTile64);
+        bulk_load(base + OFF_T, rec, 2 * kTile64, &bars[B_T_FULL]);
+        ++n_t;
+        if (c > 0 && !mbar_wait(&bars[B_P_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+        if (abort_flag) break;
+        mbar_arrive_expect_tx(&bars[B_P_FULL], 2 * kTile64);
+        bulk_load(base + OFF_P, rec + 2 * kTile64, 2 * kTile64, &bars[B_P_FULL]);
+        ++n_p;
+      }
+      // After an abort, let the copies this thread started land (bounded)
+      // before the CTA releases its shared memory.
+      if (abort_flag) {
+        if (n_kq) mbar_wait(&bars[B_KQ_FULL], (n_kq - 1) & 1, kWaitNs);
+        if (n_v) mbar_wait(&bars[B_V_FULL], (n_v - 1) & 1, kWaitNs);
+        if (n_t) mbar_wait(&bars[B_T_FULL], (n_t - 1) & 1, kWaitNs);
+        if (n_p) mbar_wait(&bars[B_P_FULL], (n_p - 1) & 1, kWaitNs);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && nch > 0) {
+      const uint32_t id128 = idesc_bf16_f32(128, 128);
+      const uint32_t id64 = idesc_bf16_f32(128, 64);
+      const uint32_t sS[2] = {smem_u32(base + OFF_SHI), smem_u32(base + OFF_SLO)};
+      const uint32_t sKQ = smem_u32(base + OFF_KQ);
+      const uint32_t sT[2] = {smem_u32(base + OFF_T), smem_u32(base + OFF_T + kTile64)};
+      const uint32_t sP[2] = {smem_u32(base + OFF_P), smem_u32(base + OFF_P + kTile64)};
+      const uint32_t sR[2] = {smem_u32(base + OFF_R), smem_u32(base + OFF_R + 16384)};
+      const uint32_t sD[2] = {smem_u32(base + OFF_D), smem_u32(base + OFF_D + 16384)};
+      const uint32_t sKt = smem_u32(base + OFF_KT);
+      // (a operand part, b operand part) of the three-pass split products
+      const int pa[3] = {0, 0, 1}, pb[3] = {0, 1, 0};
+      for (int64_t c = 0; c < nch; ++c) {
+        const uint32_t par = (uint32_t)(c & 1);
+        if (!mbar_wait(&bars[B_KQ_FULL], par, kWaitNs) || !mbar_wait(&bars[B_S_READY], par, kWaitNs)) {
+          record_error(&abort_flag);
+          break;
+        }
+        if (abort_flag) break;
+        tc_fence_after();
+        {  // [X | Y] = S [K | Q]^T
+          int n = 0;
+          for (int part = 0; part < 2; ++part)
+            for (int kb = 0; kb < 2; ++kb)
+              for (int ks = 0; ks < 4; ++ks, ++n)
+                mma_bf16(tmem + TM_XY, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
+                         sdesc_sw128(sKQ + kb * 16384 + ks * 32), id128, n > 0);
+        }
+        mma_commit(&bars[B_XY_DONE]);
+        mma_commit(&bars[B_KQ_EMPTY]);
+        if (!mbar_wait(&bars[B_R_READY], par, kWaitNs) || !mbar_wait(&bars[B_T_FULL], par, kWaitNs)) {
+          record_error(&abort_flag);
+          break;
+        }
+        if (abort_flag) break;
+        tc_fence_after();
+        {  // Delta^T = R^T T^T
+          int n = 0;
+          for (int pass = 0; pass < 3; ++pass)
+            for (int ks = 0; ks < 4; ++ks, ++n)
+              mma_bf16(tmem + TM_D, sdesc_sw128(sR[pa[pass]] + ks * 32), sdesc_sw128(sT[pb[pass]] + ks * 32), id64,
+                       n > 0);
+        }
+        mma_commit(&bars[B_D_DONE]);
+        mma_commit(&bars[B_T_EMPTY]);
+        if (!mbar_wait(&bars[B_DD_READY], par, kWaitNs) || !mbar_wait(&bars[B_P_FULL], par, kWaitNs) ||
+            !mbar_wait(&bars[B_KT_READY], par, kWaitNs)) {
+          record_error(&abort_flag);
+          break;
+        }
+        if (abort_flag) break;
+        tc_fence_after();
+        {  // O^T = Delta^T P^T
+          int n = 0;
+          for (int pass = 0; pass < 3; ++pass)
+            for (int ks = 0; ks < 4; ++ks, ++n)
+              mma_bf16(tmem + TM_O, sdesc_sw128(sD[pa[pass]] + ks * 32), sdesc_sw128(sP[pb[pass]] + ks * 32), id64,
+                       n > 0);
+        }
+        {  // U = Delta'^T K   (Delta' lives in the R buffer)
+          int n = 0;
+          for (int part = 0; part < 2; ++part)
+            for (int ks = 0; ks < 4; ++ks, ++n)
+              mma_bf16(tmem + TM_U, sdesc_sw128(sR[part] + ks * 32), sdesc_sw128(sKt + ks * 32), id128, n > 0);
+        }
+        mma_commit(&bars[B_OU_DONE]);
+        mma_commit(&bars[B_P_EMPTY]);
+      }
+      // Wait for every MMA issued so far before the CTA winds down.
+      mma_commit(&bars[B_DRAIN]);
+      mbar_wait(&bars[B_DRAIN], 0, kWaitNs);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int e = tid - 64;              // 0..127
+    const int q = warp & 3;              // TMEM lane quarter of this warp
+    const int dv = q * 32 + lane;        // state row
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    const bool leader = e == 0;
+    unsigned char* sm = base;
+
+    // S_0 -> TMEM and its bf16 hi/lo operand.
+    {
+      const float* srow = p.state_in ? p.state_in + head_off + (size_t)dv * DH : nullptr;
+      for (int cb = 0; cb < 4; ++cb) {
+        float x[32];
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          float4 v4 = srow ? *reinterpret_cast<const float4*>(srow + cb * 32 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          x[i] = v4.x;
+          x[i + 1] = v4.y;
+          x[i + 2] = v4.z;
+          x[i + 3] = v4.w;
+        }
+        tmem_st32(tq + TM_S + cb * 32, x);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint4 hi, lo;
+          split8(x + 8 * c4, hi, lo);
+          const int kb = cb >> 1, c = (cb & 1) * 4 + c4;
+          *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, kb, c)) = hi;
+          *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, kb, c)) = lo;
+        }
+      }
+      tmem_wait_st();
+      fence_async_smem();
+      tc_fence_before();
+      named_sync(1, 128);
+      if (leader) mbar_arrive(&bars[B_S_READY]);
+    }
+
+    for (int64_t c = 0; c < nch; ++c) {
+      const uint32_t par = (uint32_t)(c & 1);
+      const int64_t t0 = start + c * CH;
+      const int n = (int)(end - t0 < CH ? end - t0 : CH);
+      // gates of this chunk
+      if (e < CH) {
+        const bool ok = e < n;
+        sl[e] = ok ? log_decay(p, t0 + e, h) : 0.f;
+        sb[e] = ok ? load_gate_f(p.beta, p.gate_dtype, (t0 + e) * p.beta_st + h) : 0.f;
+      }
+      named_sync(1, 128);
+      if (e < 32) chunk_cumsum(lane, sl, sG, seG, sdG, &sgamma);
+      // K^T for the state update, from the K rows of the [K;Q] tile.
+      bool ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(1, 128, !ok)) break;
+      {
+        const int dk = e;  // this thread builds row dk of K^T
+        const int kb = dk >> 6, cc = (dk & 63) >> 3, wi = dk & 7;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int ta = 8 * c8 + 2 * i, tb = ta + 1;
+            const unsigned short lo_b =
+                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, ta, kb, cc) + wi * 2);
+            const unsigned short hi_b =
+                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, tb, kb, cc) + wi * 2);
+            w[i] = (uint32_t)lo_b | ((uint32_t)hi_b << 16);
+          }
+          *reinterpret_cast<uint4*>(sm + OFF_KT + sw128_chunk(128, dk, 0, c8)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      fence_async_smem();
+      named_sync(1, 128);
+      if (leader) {
+        mbar_arrive(&bars[B_KT_READY]);
+        mbar_arrive(&bars[B_KQ_EMPTY]);
+      }
+
+      // R = beta (V - X exp(G))
+      ok = mbar_wait(&bars[B_XY_DONE], par, kWaitNs) && mbar_wait(&bars[B_V_FULL], par, kWaitNs);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(1, 128, !ok)) break;
+      tc_fence_after();
+      {
+        const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_V);
+        for (int half = 0; half < 2; ++half) {
+          float x[32];
+          tmem_ld32(tq + TM_XY + half * 32, x);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int t = half * 32 + i;
+            x[i] = sb[t] * (__bfloat162float(V[t * DH + dv]) - x[i] * seG[t]);
+          }
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint4 hi, lo;
+            split8(x + 8 * c4, hi, lo);
+            const int cidx = half * 4 + c4;
+            *reinterpret_cast<uint4*>(sm + OFF_R + sw128_chunk(128, dv, 0, cidx)) = hi;
+            *reinterpret_cast<uint4*>(sm + OFF_R + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
+          }
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      named_sync(1, 128);
+      if (leader) {
+        mbar_arrive(&bars[B_R_READY]);
+        mbar_arrive(&bars[B_V_EMPTY]);
+      }
+
+      // Delta (for the output) and Delta' = Delta exp(G_last - G) (for the state)
+      ok = mbar_wait(&bars[B_D_DONE], par, kWaitNs);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(1, 128, !ok)) break;
+      tc_fence_after();
+      for (int half = 0; half < 2; ++half) {
+        float x[32], y[32];
+        tmem_ld32(tq + TM_D + half * 32, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) y[i] = x[i] * sdG[half * 32 + i];
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint4 hi, lo;
+          const int cidx = half * 4 + c4;
+          split8(x + 8 * c4, hi, lo);
+          *reinterpret_cast<uint4*>(sm + OFF_D + sw128_chunk(128, dv, 0, cidx)) = hi;
+          *reinterpret_cast<uint4*>(sm + OFF_D + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
+          split8(y + 8 * c4, hi, lo);
+          *reinterpret_cast<uint4*>(sm + OFF_R + sw128_chunk(128, dv, 0, cidx)) = hi;
+          *reinterpret_cast<uint4*>(sm + OFF_R + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      named_sync(1, 128);
+      if (leader) mbar_arrive(&bars[B_DD_READY]);
+
+      // y_t = exp(G_t) Y_t + O_t ; S <- gamma S + U
+      ok = mbar_wait(&bars[B_OU_DONE], par, kWaitNs);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(1, 128, !ok)) break;
+      tc_fence_after();
+      for (int half = 0; half < 2; ++half) {
+        float yv[32], ov[32];
+        tmem_ld32(tq + TM_XY + 64 + half * 32, yv);
+        tmem_ld32(tq + TM_O + half * 32, ov);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int t = half * 32 + i;
+          if (t < n) {
+            const float yo = fmaf(yv[i], seG[t], ov[i]);
+            const size_t oi = ((size_t)(t0 + t) * p.hv + h) * DH + dv;
+            if (p.out_dtype == GDN_BF16)
+              static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(yo);
+            else
+              static_cast<float*>(p.out)[oi] = yo;
+          }
+        }
+      }
+      const float gamma = sgamma;
+      for (int cb = 0; cb < 4; ++cb) {
+        float s[32], u[32];
+        tmem_ld32(tq + TM_S + cb * 32, s);
+        tmem_ld32(tq + TM_U + cb * 32, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[i] = fmaf(gamma, s[i], u[i]);
+        tmem_st32(tq + TM_S + cb * 32, s);
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint4 hi, lo;
+          split8(s + 8 * c4, hi, lo);
+          const int kb = cb >> 1, cidx = (cb & 1) * 4 + c4;
+          *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, kb, cidx)) = hi;
+          *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, kb, cidx)) = lo;
+        }
+      }
+      tmem_wait_st();
+      fence_async_smem();
+      tc_fence_before();
+      named_sync(1, 128);
+      if (leader) mbar_arrive(&bars[B_S_READY]);
+    }
+
+    // Final state (or the initial one for an empty sequence) -> state_out.
+    if (!named_sync_or(1, 128, abort_flag != 0)) {
+      tc_fence_after();
+      float* orow = p.state_out + head_off + (size_t)dv * DH;
+      for (int cb = 0; cb < 4; ++cb) {
+        float s[32];
+        tmem_ld32(tq + TM_S + cb * 32, s);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(orow + cb * 32 + i) = make_float4(s[i], s[i + 1], s[i + 2], s[i + 3]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// 3-D map over a [N, H, 128] bf16 tensor with element strides (st, sh, 1);
+// box {box_x, 1, 64}.
+bool make_map(CUtensorMap* map, const void* ptr, int64_t n_tokens, int heads, int64_t st, int64_t sh, int box_x,
+              bool swizzle) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  std::memset(map, 0, sizeof(*map));
+  cuuint64_t dims[3] = {(cuuint64_t)DH, (cuuint64_t)heads, (cuuint64_t)n_tokens};
+  cuuint64_t strides[2] = {(cuuint64_t)sh * 2, (cuuint64_t)st * 2};
+  cuuint32_t box[3] = {(cuuint32_t)box_x, 1, (cuuint32_t)CH};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int64_t max_slots(const ScanParams& p) { return (p.n_tokens + CH - 1) / CH + p.n_seqs; }
+
+bool aligned_elems(int64_t s) { return s >= 0 && s % 8 == 0; }
+bool aligned_ptr16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace
+
+bool chunked_supported(const ScanParams& p) {
+  return p.qkv_dtype == GDN_BF16 && p.dk == DH && p.dv == DH && p.hv % p.hk == 0 && aligned_elems(p.q_st) &&
+         aligned_elems(p.q_sh) && aligned_elems(p.k_st) && aligned_elems(p.k_sh) && aligned_elems(p.v_st) &&
+         aligned_elems(p.v_sh) && p.n_tokens < (int64_t)1 << 31 && tensor_map_encoder() != nullptr;
+}
+
+size_t chunked_workspace_bytes(const ScanParams& p) { return (size_t)max_slots(p) * p.hv * kRecBytes; }
+
+cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
+  if (!aligned_ptr16(sp.q) || !aligned_ptr16(sp.k) || !aligned_ptr16(sp.v) || !aligned_ptr16(sp.workspace))
+    return cudaErrorMisalignedAddress;
+  CUtensorMap qmap, kmap, vmap;
+  const int64_t N = sp.n_tokens;
+  if (N > 0) {
+    if (!make_map(&qmap, sp.q, N, sp.hk, sp.q_st, sp.q_sh, 64, true) ||
+        !make_map(&kmap, sp.k, N, sp.hk, sp.k_st, sp.k_sh, 64, true) ||
+        !make_map(&vmap, sp.v, N, sp.hv, sp.v_st, sp.v_sh, 128, false))
+      return cudaErrorInvalidValue;
+  } else {
+    std::memset(&qmap, 0, sizeof(qmap));
+    kmap = vmap = qmap;
+  }
+  ChunkParams p;
+  p.n_tokens = N;
+  p.n_seqs = sp.n_seqs;
+  p.cu = sp.cu_seqlens;
+  p.hk = sp.hk;
+  p.hv = sp.hv;
+  p.g = sp.g;
+  p.beta = sp.beta;
+  p.g_st = sp.g_st;
+  p.beta_st = sp.beta_st;
+  p.gate_dtype = sp.gate_dtype;
+  p.gate_kind = sp.gate_kind;
+  p.state_in = sp.state_in;
+  p.state_out = sp.state_out;
+  p.out = sp.out;
+  p.out_dtype = sp.out_dtype;
+  p.ws = static_cast<unsigned char*>(sp.workspace);
+
+  static bool attrs_set = false;
+  if (!attrs_set) {
+    cudaError_t e = cudaFuncSetAttribute(chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
+    if (e != cudaSuccess) return e;
+    attrs_set = true;
+  }
+  const int64_t slots = max_slots(sp);
+  if (N > 0 && slots > 0) {
+    if (slots > 0x7fffffffLL || sp.hv > 65535) return cudaErrorInvalidConfiguration;
+    chunk_prep_kernel<<<dim3((unsigned)slots, (unsigned)sp.hv), 128, kPrepSmem, s>>>(qmap, kmap, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  const int64_t ctas = sp.n_seqs * sp.hv;
+  if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  chunk_scan_kernel<<<(unsigned)ctas, 192, kScanSmem, s>>>(qmap, kmap, vmap, p);
+  return cudaGetLastError();
+}
 
 cudaError_t read_and_clear_device_error(unsigned* code) {
   cudaError_t e = cudaMemcpyFromSymbol(code, g_device_error, sizeof(unsigned));
