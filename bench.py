@@ -238,6 +238,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true",
                     help="decode only: no e2e, prefill or CPU legs (for profiler runs)")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiler runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
@@ -359,7 +360,7 @@ def main():
                            "algo": "auto"}
 
         # --- CPU baseline (rank 0, N=1 only) --------------------------------
-        if rank == 0 and world == 1:
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
             steps_cpu, secs = cpu_decode_sample()
             line["cpu_baseline"] = {
                 "value": DECODE_BYTES * steps_cpu / secs / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1,
