@@ -17,18 +17,23 @@
 //    [K;Q] K^T (M=128, N=64, K=128) gives K K^T and Q K^T in TMEM; the
 //    epilogue builds A and P, a forward substitution gives T, and T and P are
 //    written to the workspace as bf16 hi/lo pairs in the SW128 operand layout.
+//    The same kernel stores the chunk's gate vectors (beta, exp G,
+//    exp(G_last - G), gamma) next to T and P.
 //  * chunk_scan_kernel, one CTA per (sequence, value head), serial over the
 //    chunks with the float32 state S resident in TMEM.  Warp roles: warp 0
-//    loads (TMA tensor loads of K, Q, V; bulk copies of T, P), warp 1 issues
-//    the MMAs, warps 2-5 run the epilogues (one TMEM lane quarter each, one
-//    state row per thread).  Per chunk, in the transposed orientation
-//    (M = Dv state rows):
-//      [X | Y] = S [K | Q]^T       (N = 128, K = Dk)    2 passes (S hi, lo)
+//    loads (TMA tensor loads of K, Q, V; bulk copies of T, P and the gates),
+//    warp 1 issues the MMAs, warps 2-9 run the epilogues (two per TMEM lane
+//    quarter: each thread owns one state row and half of its columns).  Per
+//    chunk, in the transposed orientation (M = Dv state rows):
+//      X       = S K^T             (N = 64,  K = Dk)    2 passes (S hi, lo)
+//      Y       = S Q^T             (N = 64,  K = Dk)    2 passes
 //      Delta^T = R^T T^T           (N = 64,  K = C)     3 passes (hi*hi, hi*lo, lo*hi)
+//      U       = Delta^T Kd        (N = 128, K = C)     3 passes, Kd = diag(exp(G_last - G)) K
 //      O^T     = Delta^T P^T       (N = 64,  K = C)     3 passes
-//      U       = Delta'^T K        (N = 128, K = C)     2 passes (Delta' hi, lo)
-//    then Y^T = diag(exp G)-scaled Y + O and S <- gamma S + U.
-//  Operands that are not exact in bf16 (S, R, T, Delta, P) are split into
+//    then S <- gamma S + U (the chain into the next chunk) and, off that
+//    chain, y = exp(G) Y + O.  Delta reuses the S lo operand buffer, which is
+//    dead between the X/Y MMAs and the state update.
+//  Operands that are not exact in bf16 (S, R, T, Delta, P, Kd) are split into
 //  bf16 hi + lo parts; the products then carry ~16 mantissa bits (rel-L2
 //  ~5e-6 against the float64 recurrence at T = 4096, versus ~3e-3 with plain
 //  bf16 operands and ~4e-4 with tf32).
@@ -57,7 +62,10 @@ constexpr int CH = 64;   // chunk length
 constexpr int DH = 128;  // head dim (Dk = Dv)
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr uint32_t kTile64 = 64 * 64 * 2;          // 64 x 64 bf16 operand tile (8 KB)
-constexpr size_t kRecBytes = 4 * (size_t)kTile64;  // T hi, T lo, P hi, P lo per (chunk, head)
+constexpr uint32_t kGateBytes = 1024;               // beta[64], exp G[64], exp(G_last - G)[64], gamma
+// Per (chunk, head): T hi, T lo, P hi, P lo, gates.
+constexpr size_t kRecBytes = 4 * (size_t)kTile64 + kGateBytes;
+constexpr uint32_t GATE_BETA = 0, GATE_EG = 64, GATE_DG = 128, GATE_GAMMA = 192;  // float offsets
 
 struct ChunkParams {
   int64_t n_tokens, n_seqs;
@@ -209,7 +217,17 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
       tma_load_3d(sKQ + kb * 16384 + 8192, &qmap, &bar_load, kb * 64, kh, (int)t0);
     }
   }
-  if (warp == 1) chunk_cumsum(lane, sl, sG, seG, sdG, &sgamma);
+  if (warp == 1) {
+    chunk_cumsum(lane, sl, sG, seG, sdG, &sgamma);
+    __syncwarp();
+    float* gates = reinterpret_cast<float*>(p.ws + ((size_t)slot * p.hv + h) * kRecBytes + 4 * kTile64);
+    for (int i = lane; i < CH; i += 32) {
+      gates[GATE_BETA + i] = sb[i];
+      gates[GATE_EG + i] = seG[i];
+      gates[GATE_DG + i] = sdG[i];
+    }
+    for (int i = GATE_GAMMA + lane; i < (int)(kGateBytes / 4); i += 32) gates[i] = i == GATE_GAMMA ? sgamma : 0.f;
+  }
 
   bool mma_issued = false;
   if (tid == 0) {
@@ -283,17 +301,19 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 64);
 
-  // Forward substitution: thread c < 64 owns column c of T = (I + A)^-1.
+  // Forward substitution: thread c < 64 owns column c of T = (I + A)^-1
+  // (four partial sums per row keep the FMA chain short).
   if (tid < CH) {
     const int c = tid;
     float x[64];
 #pragma unroll
     for (int i = 0; i < 64; ++i) {
       const float* arow = sA + i * kPrepAStride;
-      float acc = 0.f;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int j = 0; j < i; ++j) acc = fmaf(arow[j], x[j], acc);
-      x[i] = i < c ? 0.f : (i == c ? 1.f : -acc);
+      for (int j = 0; j < i; ++j) acc[j & 3] = fmaf(arow[j], x[j], acc[j & 3]);
+      const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      x[i] = i < c ? 0.f : (i == c ? 1.f : -sum);
     }
 #pragma unroll
     for (int i = 0; i < 64; ++i) sT[i * kPrepAStride + c] = x[i];
@@ -320,33 +340,35 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
 // Kernel B: per (sequence, value head) -- serial over chunks, S in TMEM.
 // ===========================================================================
 // Dynamic shared memory map (offsets from the 1024-aligned base).
-constexpr uint32_t OFF_SHI = 0, OFF_SLO = 32768;   // S hi/lo: 128 x 128, two K-blocks
+constexpr uint32_t OFF_SHI = 0, OFF_SLO = 32768;   // S hi/lo: 128 x 128, two K-blocks each
+constexpr uint32_t OFF_D = OFF_SLO;                // Delta hi, lo (128 x 64 each) while S lo is dead
 constexpr uint32_t OFF_KQ = 65536;                 // [K;Q]: 128 x 128, two K-blocks
 constexpr uint32_t OFF_V = 98304;                  // V: [64][128] bf16 row-major
 constexpr uint32_t OFF_T = 114688;                 // T hi, T lo: 64 x 64 each
 constexpr uint32_t OFF_P = 131072;                 // P hi, P lo
-constexpr uint32_t OFF_R = 147456;                 // R (then Delta') hi, lo: 128 x 64 each
-constexpr uint32_t OFF_D = 180224;                 // Delta hi, lo: 128 x 64 each
-constexpr uint32_t OFF_KT = 212992;                // K^T: 128 (dk) x 64 (t)
-constexpr uint32_t SCAN_SMEM_USED = 229376;
+constexpr uint32_t OFF_KT = 147456;                // Kd^T hi, lo: 128 (dk) x 64 (t) each
+constexpr uint32_t OFF_GATES = 180224;             // two 1 KB gate buffers (chunk parity)
+constexpr uint32_t OFF_R = OFF_GATES + 2 * kGateBytes;  // R hi, lo: 128 x 64 each
+constexpr uint32_t SCAN_SMEM_USED = OFF_R + 32768;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
+constexpr int kEpiThreads = 256;                   // warps 2-9
 
 // TMEM columns.
-constexpr uint32_t TM_S = 0, TM_XY = 128, TM_D = 256, TM_O = 320, TM_U = 384;
+constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y = 192, TM_D = 256, TM_O = 320, TM_U = 384;
 
 enum Bar {
   B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
-  B_S_READY, B_XY_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_KT_READY, B_OU_DONE, B_DRAIN, N_BARS
+  B_S_READY, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_KT_READY, B_OU_DONE, B_O_FREE, B_DRAIN,
+  N_BARS
 };
 
-__global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                                                             const __grid_constant__ CUtensorMap kmap,
                                                             const __grid_constant__ CUtensorMap vmap,
                                                             const ChunkParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t bars[N_BARS];
-  __shared__ float sl[CH], sb[CH], sG[CH], seG[CH], sdG[CH], sgamma;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
   __shared__ int64_t s_start, s_end, s_cbase;
@@ -389,11 +411,12 @@ __global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constan
         const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
         if (c > 0 && !mbar_wait(&bars[B_KQ_EMPTY], par, kWaitNs)) record_error(&abort_flag);
         if (abort_flag) break;
-        mbar_arrive_expect_tx(&bars[B_KQ_FULL], 32768);
+        mbar_arrive_expect_tx(&bars[B_KQ_FULL], 32768 + kGateBytes);
         for (int kb = 0; kb < 2; ++kb) {
           tma_load_3d(base + OFF_KQ + kb * 16384, &kmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
           tma_load_3d(base + OFF_KQ + kb * 16384 + 8192, &qmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
         }
+        bulk_load(base + OFF_GATES + (c & 1) * kGateBytes, rec + 4 * kTile64, kGateBytes, &bars[B_KQ_FULL]);
         ++n_kq;
         if (c > 0 && !mbar_wait(&bars[B_V_EMPTY], par, kWaitNs)) record_error(&abort_flag);
         if (abort_flag) break;
@@ -426,13 +449,13 @@ __global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constan
       const uint32_t id128 = idesc_bf16_f32(128, 128);
       const uint32_t id64 = idesc_bf16_f32(128, 64);
       const uint32_t sS[2] = {smem_u32(base + OFF_SHI), smem_u32(base + OFF_SLO)};
-      const uint32_t sKQ = smem_u32(base + OFF_KQ);
+      const uint32_t sK = smem_u32(base + OFF_KQ), sQ = sK + 8192;
       const uint32_t sT[2] = {smem_u32(base + OFF_T), smem_u32(base + OFF_T + kTile64)};
       const uint32_t sP[2] = {smem_u32(base + OFF_P), smem_u32(base + OFF_P + kTile64)};
       const uint32_t sR[2] = {smem_u32(base + OFF_R), smem_u32(base + OFF_R + 16384)};
       const uint32_t sD[2] = {smem_u32(base + OFF_D), smem_u32(base + OFF_D + 16384)};
-      const uint32_t sKt = smem_u32(base + OFF_KT);
-      // (a operand part, b operand part) of the three-pass split products
+      const uint32_t sKt[2] = {smem_u32(base + OFF_KT), smem_u32(base + OFF_KT + 16384)};
+      // (a part, b part) of the three-pass split products hi*hi + hi*lo + lo*hi
       const int pa[3] = {0, 0, 1}, pb[3] = {0, 1, 0};
       for (int64_t c = 0; c < nch; ++c) {
         const uint32_t par = (uint32_t)(c & 1);
@@ -442,15 +465,30 @@ __global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constan
         }
         if (abort_flag) break;
         tc_fence_after();
-        {  // [X | Y] = S [K | Q]^T
+        {  // X = S K^T: the only product of S on the state chain
           int n = 0;
           for (int part = 0; part < 2; ++part)
             for (int kb = 0; kb < 2; ++kb)
               for (int ks = 0; ks < 4; ++ks, ++n)
-                mma_bf16(tmem + TM_XY, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
-                         sdesc_sw128(sKQ + kb * 16384 + ks * 32), id128, n > 0);
+                mma_bf16(tmem + TM_X, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
+                         sdesc_sw128(sK + kb * 16384 + ks * 32), id64, n > 0);
         }
-        mma_commit(&bars[B_XY_DONE]);
+        mma_commit(&bars[B_X_DONE]);
+        // Y = S Q^T, once the previous chunk's output stage has read Y and O.
+        if (c > 0 && !mbar_wait(&bars[B_O_FREE], (uint32_t)((c - 1) & 1), kWaitNs)) {
+          record_error(&abort_flag);
+          break;
+        }
+        if (abort_flag) break;
+        tc_fence_after();
+        {
+          int n = 0;
+          for (int part = 0; part < 2; ++part)
+            for (int kb = 0; kb < 2; ++kb)
+              for (int ks = 0; ks < 4; ++ks, ++n)
+                mma_bf16(tmem + TM_Y, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
+                         sdesc_sw128(sQ + kb * 16384 + ks * 32), id64, n > 0);
+        }
         mma_commit(&bars[B_KQ_EMPTY]);
         if (!mbar_wait(&bars[B_R_READY], par, kWaitNs) || !mbar_wait(&bars[B_T_FULL], par, kWaitNs)) {
           record_error(&abort_flag);
@@ -467,8 +505,20 @@ __global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constan
         }
         mma_commit(&bars[B_D_DONE]);
         mma_commit(&bars[B_T_EMPTY]);
-        if (!mbar_wait(&bars[B_DD_READY], par, kWaitNs) || !mbar_wait(&bars[B_P_FULL], par, kWaitNs) ||
-            !mbar_wait(&bars[B_KT_READY], par, kWaitNs)) {
+        if (!mbar_wait(&bars[B_DD_READY], par, kWaitNs) || !mbar_wait(&bars[B_KT_READY], par, kWaitNs)) {
+          record_error(&abort_flag);
+          break;
+        }
+        if (abort_flag) break;
+        tc_fence_after();
+        {  // U = Delta^T Kd   (state chain first)
+          int n = 0;
+          for (int pass = 0; pass < 3; ++pass)
+            for (int ks = 0; ks < 4; ++ks, ++n)
+              mma_bf16(tmem + TM_U, sdesc_sw128(sD[pa[pass]] + ks * 32), sdesc_sw128(sKt[pb[pass]] + ks * 32),
+                       id128, n > 0);
+        }
+        if (!mbar_wait(&bars[B_P_FULL], par, kWaitNs)) {
           record_error(&abort_flag);
           break;
         }
@@ -481,12 +531,8 @@ __global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constan
               mma_bf16(tmem + TM_O, sdesc_sw128(sD[pa[pass]] + ks * 32), sdesc_sw128(sP[pb[pass]] + ks * 32), id64,
                        n > 0);
         }
-        {  // U = Delta'^T K   (Delta' lives in the R buffer)
-          int n = 0;
-          for (int part = 0; part < 2; ++part)
-            for (int ks = 0; ks < 4; ++ks, ++n)
-              mma_bf16(tmem + TM_U, sdesc_sw128(sR[part] + ks * 32), sdesc_sw128(sKt + ks * 32), id128, n > 0);
-        }
+        // One commit for U and O: Delta (in the S lo buffer) is free only
+        // once both have read it.
         mma_commit(&bars[B_OU_DONE]);
         mma_commit(&bars[B_P_EMPTY]);
       }
@@ -496,40 +542,42 @@ __global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constan
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int e = tid - 64;              // 0..127
-    const int q = warp & 3;              // TMEM lane quarter of this warp
-    const int dv = q * 32 + lane;        // state row
+    const int e = tid - 64;                   // 0..255
+    const int q = warp & 3;                   // TMEM lane quarter of this warp
+    const int half = (warp - 2) >> 2;         // which half of the columns this thread owns
+    const int dv = q * 32 + lane;             // state row
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     const bool leader = e == 0;
     unsigned char* sm = base;
 
-    // S_0 -> TMEM and its bf16 hi/lo operand.
+    // S_0 -> TMEM and its bf16 hi/lo operand (columns 64*half .. +64).
     {
       const float* srow = p.state_in ? p.state_in + head_off + (size_t)dv * DH : nullptr;
-      for (int cb = 0; cb < 4; ++cb) {
+      for (int cc = 0; cc < 2; ++cc) {
+        const int col = half * 64 + cc * 32;
         float x[32];
 #pragma unroll
         for (int i = 0; i < 32; i += 4) {
-          float4 v4 = srow ? *reinterpret_cast<const float4*>(srow + cb * 32 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float4 v4 = srow ? *reinterpret_cast<const float4*>(srow + col + i) : make_float4(0.f, 0.f, 0.f, 0.f);
           x[i] = v4.x;
           x[i + 1] = v4.y;
           x[i + 2] = v4.z;
           x[i + 3] = v4.w;
         }
-        tmem_st32(tq + TM_S + cb * 32, x);
+        tmem_st32(tq + TM_S + col, x);
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint4 hi, lo;
           split8(x + 8 * c4, hi, lo);
-          const int kb = cb >> 1, c = (cb & 1) * 4 + c4;
-          *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, kb, c)) = hi;
-          *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, kb, c)) = lo;
+          const int cidx = cc * 4 + c4;
+          *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, half, cidx)) = hi;
+          *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, half, cidx)) = lo;
         }
       }
       tmem_wait_st();
       fence_async_smem();
       tc_fence_before();
-      named_sync(1, 128);
+      named_sync(1, kEpiThreads);
       if (leader) mbar_arrive(&bars[B_S_READY]);
     }
 
@@ -537,120 +585,140 @@ __global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constan
       const uint32_t par = (uint32_t)(c & 1);
       const int64_t t0 = start + c * CH;
       const int n = (int)(end - t0 < CH ? end - t0 : CH);
-      // gates of this chunk
-      if (e < CH) {
-        const bool ok = e < n;
-        sl[e] = ok ? log_decay(p, t0 + e, h) : 0.f;
-        sb[e] = ok ? load_gate_f(p.beta, p.gate_dtype, (t0 + e) * p.beta_st + h) : 0.f;
-      }
-      named_sync(1, 128);
-      if (e < 32) chunk_cumsum(lane, sl, sG, seG, sdG, &sgamma);
-      // K^T for the state update, from the K rows of the [K;Q] tile.
+      const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
+
+      // Kd^T = (diag(exp(G_last - G)) K)^T as bf16 hi/lo, from the K rows.
       bool ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
-      if (named_sync_or(1, 128, !ok)) break;
+      if (named_sync_or(1, kEpiThreads, !ok)) break;
       {
-        const int dk = e;  // this thread builds row dk of K^T
+        const int dk = e & 127, th = e >> 7;  // row dk of Kd^T, tokens 32*th .. +32
         const int kb = dk >> 6, cc = (dk & 63) >> 3, wi = dk & 7;
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          uint32_t w[4];
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float x[8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int ta = 8 * c8 + 2 * i, tb = ta + 1;
-            const unsigned short lo_b =
-                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, ta, kb, cc) + wi * 2);
-            const unsigned short hi_b =
-                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, tb, kb, cc) + wi * 2);
-            w[i] = (uint32_t)lo_b | ((uint32_t)hi_b << 16);
+          for (int i = 0; i < 8; ++i) {
+            const int t = th * 32 + c8 * 8 + i;
+            const unsigned short kbits =
+                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, t, kb, cc) + wi * 2);
+            x[i] = __uint_as_float((uint32_t)kbits << 16) * gates[GATE_DG + t];
           }
-          *reinterpret_cast<uint4*>(sm + OFF_KT + sw128_chunk(128, dk, 0, c8)) = make_uint4(w[0], w[1], w[2], w[3]);
+          uint4 hi, lo;
+          split8(x, hi, lo);
+          const int cidx = th * 4 + c8;
+          *reinterpret_cast<uint4*>(sm + OFF_KT + sw128_chunk(128, dk, 0, cidx)) = hi;
+          *reinterpret_cast<uint4*>(sm + OFF_KT + 16384 + sw128_chunk(128, dk, 0, cidx)) = lo;
         }
       }
       fence_async_smem();
-      named_sync(1, 128);
+      named_sync(1, kEpiThreads);
       if (leader) {
         mbar_arrive(&bars[B_KT_READY]);
         mbar_arrive(&bars[B_KQ_EMPTY]);
       }
 
-      // R = beta (V - X exp(G))
-      ok = mbar_wait(&bars[B_XY_DONE], par, kWaitNs) && mbar_wait(&bars[B_V_FULL], par, kWaitNs);
+      // R = beta (V - X exp(G)), tokens 32*half .. +32 of row dv.
+      ok = mbar_wait(&bars[B_X_DONE], par, kWaitNs) && mbar_wait(&bars[B_V_FULL], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
-      if (named_sync_or(1, 128, !ok)) break;
+      if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
       {
         const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_V);
-        for (int half = 0; half < 2; ++half) {
-          float x[32];
-          tmem_ld32(tq + TM_XY + half * 32, x);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int t = half * 32 + i;
-            x[i] = sb[t] * (__bfloat162float(V[t * DH + dv]) - x[i] * seG[t]);
-          }
-#pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            uint4 hi, lo;
-            split8(x + 8 * c4, hi, lo);
-            const int cidx = half * 4 + c4;
-            *reinterpret_cast<uint4*>(sm + OFF_R + sw128_chunk(128, dv, 0, cidx)) = hi;
-            *reinterpret_cast<uint4*>(sm + OFF_R + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
-          }
-        }
-      }
-      fence_async_smem();
-      tc_fence_before();
-      named_sync(1, 128);
-      if (leader) {
-        mbar_arrive(&bars[B_R_READY]);
-        mbar_arrive(&bars[B_V_EMPTY]);
-      }
-
-      // Delta (for the output) and Delta' = Delta exp(G_last - G) (for the state)
-      ok = mbar_wait(&bars[B_D_DONE], par, kWaitNs);
-      if (!ok) record_error(&abort_flag);
-      if (named_sync_or(1, 128, !ok)) break;
-      tc_fence_after();
-      for (int half = 0; half < 2; ++half) {
-        float x[32], y[32];
-        tmem_ld32(tq + TM_D + half * 32, x);
+        float x[32];
+        tmem_ld32(tq + TM_X + half * 32, x);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) y[i] = x[i] * sdG[half * 32 + i];
+        for (int i = 0; i < 32; ++i) {
+          const int t = half * 32 + i;
+          x[i] = gates[GATE_BETA + t] * (__bfloat162float(V[t * DH + dv]) - x[i] * gates[GATE_EG + t]);
+        }
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint4 hi, lo;
-          const int cidx = half * 4 + c4;
           split8(x + 8 * c4, hi, lo);
-          *reinterpret_cast<uint4*>(sm + OFF_D + sw128_chunk(128, dv, 0, cidx)) = hi;
-          *reinterpret_cast<uint4*>(sm + OFF_D + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
-          split8(y + 8 * c4, hi, lo);
+          const int cidx = half * 4 + c4;
           *reinterpret_cast<uint4*>(sm + OFF_R + sw128_chunk(128, dv, 0, cidx)) = hi;
           *reinterpret_cast<uint4*>(sm + OFF_R + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
         }
       }
       fence_async_smem();
       tc_fence_before();
-      named_sync(1, 128);
+      named_sync(1, kEpiThreads);
+      if (leader) {
+        mbar_arrive(&bars[B_R_READY]);
+        mbar_arrive(&bars[B_V_EMPTY]);
+      }
+
+      // Delta -> bf16 hi/lo operand.
+      ok = mbar_wait(&bars[B_D_DONE], par, kWaitNs);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(1, kEpiThreads, !ok)) break;
+      tc_fence_after();
+      {
+        float x[32];
+        tmem_ld32(tq + TM_D + half * 32, x);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint4 hi, lo;
+          split8(x + 8 * c4, hi, lo);
+          const int cidx = half * 4 + c4;
+          *reinterpret_cast<uint4*>(sm + OFF_D + sw128_chunk(128, dv, 0, cidx)) = hi;
+          *reinterpret_cast<uint4*>(sm + OFF_D + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
+        }
+      }
+      fence_async_smem();
+      tc_fence_before();
+      named_sync(1, kEpiThreads);
       if (leader) mbar_arrive(&bars[B_DD_READY]);
 
-      // y_t = exp(G_t) Y_t + O_t ; S <- gamma S + U
+      // S <- gamma S + U, then its hi/lo operand for the next chunk.
       ok = mbar_wait(&bars[B_OU_DONE], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
-      if (named_sync_or(1, 128, !ok)) break;
+      if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
-      for (int half = 0; half < 2; ++half) {
+      {
+        const float gamma = gates[GATE_GAMMA];
+        for (int cc = 0; cc < 2; ++cc) {
+          const int col = half * 64 + cc * 32;
+          float sv[32], u[32];
+          tmem_ld32(tq + TM_S + col, sv);
+          tmem_ld32(tq + TM_U + col, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[i] = fmaf(gamma, sv[i], u[i]);
+          tmem_st32(tq + TM_S + col, sv);
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            uint4 hi, lo;
+            split8(sv + 8 * c4, hi, lo);
+            const int cidx = cc * 4 + c4;
+            *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, half, cidx)) = hi;
+            *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, half, cidx)) = lo;
+          }
+        }
+      }
+      tmem_wait_st();
+      fence_async_smem();
+      tc_fence_before();
+      named_sync(1, kEpiThreads);
+      if (leader) mbar_arrive(&bars[B_S_READY]);
+
+      // Output, off the state chain: y_t = exp(G_t) Y_t + O_t.
+      {
         float yv[32], ov[32];
-        tmem_ld32(tq + TM_XY + 64 + half * 32, yv);
+        tmem_ld32(tq + TM_Y + half * 32, yv);
         tmem_ld32(tq + TM_O + half * 32, ov);
         tmem_wait_ld();
+        tc_fence_before();
+        named_sync(1, kEpiThreads);
+        if (leader) mbar_arrive(&bars[B_O_FREE]);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int t = half * 32 + i;
           if (t < n) {
-            const float yo = fmaf(yv[i], seG[t], ov[i]);
+            const float yo = fmaf(yv[i], gates[GATE_EG + t], ov[i]);
             const size_t oi = ((size_t)(t0 + t) * p.hv + h) * DH + dv;
             if (p.out_dtype == GDN_BF16)
               static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(yo);
@@ -659,42 +727,20 @@ __global__ void __launch_bounds__(192, 1) chunk_scan_kernel(const __grid_constan
           }
         }
       }
-      const float gamma = sgamma;
-      for (int cb = 0; cb < 4; ++cb) {
-        float s[32], u[32];
-        tmem_ld32(tq + TM_S + cb * 32, s);
-        tmem_ld32(tq + TM_U + cb * 32, u);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = fmaf(gamma, s[i], u[i]);
-        tmem_st32(tq + TM_S + cb * 32, s);
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint4 hi, lo;
-          split8(s + 8 * c4, hi, lo);
-          const int kb = cb >> 1, cidx = (cb & 1) * 4 + c4;
-          *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, kb, cidx)) = hi;
-          *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, kb, cidx)) = lo;
-        }
-      }
-      tmem_wait_st();
-      fence_async_smem();
-      tc_fence_before();
-      named_sync(1, 128);
-      if (leader) mbar_arrive(&bars[B_S_READY]);
     }
 
     // Final state (or the initial one for an empty sequence) -> state_out.
-    if (!named_sync_or(1, 128, abort_flag != 0)) {
+    if (!named_sync_or(1, kEpiThreads, abort_flag != 0)) {
       tc_fence_after();
       float* orow = p.state_out + head_off + (size_t)dv * DH;
-      for (int cb = 0; cb < 4; ++cb) {
-        float s[32];
-        tmem_ld32(tq + TM_S + cb * 32, s);
+      for (int cc = 0; cc < 2; ++cc) {
+        const int col = half * 64 + cc * 32;
+        float sv[32];
+        tmem_ld32(tq + TM_S + col, sv);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
-          *reinterpret_cast<float4*>(orow + cb * 32 + i) = make_float4(s[i], s[i + 1], s[i + 2], s[i + 3]);
+          *reinterpret_cast<float4*>(orow + col + i) = make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]);
       }
     }
   }
@@ -800,7 +846,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   }
   const int64_t ctas = sp.n_seqs * sp.hv;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  chunk_scan_kernel<<<(unsigned)ctas, 192, kScanSmem, s>>>(qmap, kmap, vmap, p);
+  chunk_scan_kernel<<<(unsigned)ctas, 320, kScanSmem, s>>>(qmap, kmap, vmap, p);
   return cudaGetLastError();
 }
 
