@@ -124,6 +124,18 @@ __device__ int64_t chunk_base_of(const ChunkParams& p, int64_t b) {
   return base;
 }
 
+// 32 consecutive gate values from shared memory (16-byte aligned) as float4s.
+__device__ __forceinline__ void load_gate32(const float* src, float (&dst)[32]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 v = reinterpret_cast<const float4*>(src)[i];
+    dst[4 * i] = v.x;
+    dst[4 * i + 1] = v.y;
+    dst[4 * i + 2] = v.z;
+    dst[4 * i + 3] = v.w;
+  }
+}
+
 __device__ __forceinline__ void record_error(volatile int* abort_flag) {
   *abort_flag = 1;
   atomicOr(&g_device_error, kErrTimeout);
@@ -354,7 +366,9 @@ constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
 constexpr int kEpiThreads = 256;                   // warps 2-9
 
 // TMEM columns.
-constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y = 192, TM_D = 256, TM_O = 320, TM_U = 384;
+// The state update accumulates straight onto S (S is scaled by gamma in TMEM
+// while the Delta MMA runs), so there is no separate U accumulator.
+constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y = 192, TM_D = 256, TM_O = 320;
 
 enum Bar {
   B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
@@ -511,12 +525,11 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
         }
         if (abort_flag) break;
         tc_fence_after();
-        {  // U = Delta^T Kd   (state chain first)
-          int n = 0;
+        {  // S <- (gamma S) + Delta^T Kd   (state chain first)
           for (int pass = 0; pass < 3; ++pass)
-            for (int ks = 0; ks < 4; ++ks, ++n)
-              mma_bf16(tmem + TM_U, sdesc_sw128(sD[pa[pass]] + ks * 32), sdesc_sw128(sKt[pb[pass]] + ks * 32),
-                       id128, n > 0);
+            for (int ks = 0; ks < 4; ++ks)
+              mma_bf16(tmem + TM_S, sdesc_sw128(sD[pa[pass]] + ks * 32), sdesc_sw128(sKt[pb[pass]] + ks * 32),
+                       id128, true);
         }
         if (!mbar_wait(&bars[B_P_FULL], par, kWaitNs)) {
           record_error(&abort_flag);
@@ -594,6 +607,8 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
       {
         const int dk = e & 127, th = e >> 7;  // row dk of Kd^T, tokens 32*th .. +32
         const int kb = dk >> 6, cc = (dk & 63) >> 3, wi = dk & 7;
+        float dg[32];
+        load_gate32(gates + GATE_DG + th * 32, dg);
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
           float x[8];
@@ -602,7 +617,7 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
             const int t = th * 32 + c8 * 8 + i;
             const unsigned short kbits =
                 *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, t, kb, cc) + wi * 2);
-            x[i] = __uint_as_float((uint32_t)kbits << 16) * gates[GATE_DG + t];
+            x[i] = __uint_as_float((uint32_t)kbits << 16) * dg[c8 * 8 + i];
           }
           uint4 hi, lo;
           split8(x, hi, lo);
@@ -628,10 +643,13 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
         float x[32];
         tmem_ld32(tq + TM_X + half * 32, x);
         tmem_wait_ld();
+        float bt[32], eg[32];
+        load_gate32(gates + GATE_BETA + half * 32, bt);
+        load_gate32(gates + GATE_EG + half * 32, eg);
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const int t = half * 32 + i;
-          x[i] = gates[GATE_BETA + t] * (__bfloat162float(V[t * DH + dv]) - x[i] * gates[GATE_EG + t]);
+          x[i] = bt[i] * (__bfloat162float(V[t * DH + dv]) - x[i] * eg[i]);
         }
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
@@ -648,6 +666,22 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
       if (leader) {
         mbar_arrive(&bars[B_R_READY]);
         mbar_arrive(&bars[B_V_EMPTY]);
+      }
+
+      // While the Delta MMA runs: S <- gamma S in TMEM (the state update MMA
+      // then accumulates onto it).  Ordered before the U MMA by DD_READY.
+      {
+        const float gamma = gates[GATE_GAMMA];
+        for (int cc = 0; cc < 2; ++cc) {
+          const int col = half * 64 + cc * 32;
+          float sv[32];
+          tmem_ld32(tq + TM_S + col, sv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) sv[i] *= gamma;
+          tmem_st32(tq + TM_S + col, sv);
+        }
+        tmem_wait_st();
       }
 
       // Delta -> bf16 hi/lo operand.
@@ -673,22 +707,17 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
       named_sync(1, kEpiThreads);
       if (leader) mbar_arrive(&bars[B_DD_READY]);
 
-      // S <- gamma S + U, then its hi/lo operand for the next chunk.
+      // The updated S -> its hi/lo operand for the next chunk.
       ok = mbar_wait(&bars[B_OU_DONE], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
       {
-        const float gamma = gates[GATE_GAMMA];
         for (int cc = 0; cc < 2; ++cc) {
           const int col = half * 64 + cc * 32;
-          float sv[32], u[32];
+          float sv[32];
           tmem_ld32(tq + TM_S + col, sv);
-          tmem_ld32(tq + TM_U + col, u);
           tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sv[i] = fmaf(gamma, sv[i], u[i]);
-          tmem_st32(tq + TM_S + col, sv);
 #pragma unroll
           for (int c4 = 0; c4 < 4; ++c4) {
             uint4 hi, lo;
@@ -699,7 +728,6 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
           }
         }
       }
-      tmem_wait_st();
       fence_async_smem();
       tc_fence_before();
       named_sync(1, kEpiThreads);
@@ -714,17 +742,22 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
         tc_fence_before();
         named_sync(1, kEpiThreads);
         if (leader) mbar_arrive(&bars[B_O_FREE]);
+        const int tb = half * 32;
+        const int cnt = n - tb < 0 ? 0 : (n - tb < 32 ? n - tb : 32);
+        const size_t ostride = (size_t)p.hv * DH;
+        const size_t obase = ((size_t)(t0 + tb) * p.hv + h) * DH + dv;
+        float eg[32];
+        load_gate32(gates + GATE_EG + tb, eg);
+        if (p.out_dtype == GDN_BF16) {
+          __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + obase;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int t = half * 32 + i;
-          if (t < n) {
-            const float yo = fmaf(yv[i], gates[GATE_EG + t], ov[i]);
-            const size_t oi = ((size_t)(t0 + t) * p.hv + h) * DH + dv;
-            if (p.out_dtype == GDN_BF16)
-              static_cast<__nv_bfloat16*>(p.out)[oi] = __float2bfloat16_rn(yo);
-            else
-              static_cast<float*>(p.out)[oi] = yo;
-          }
+          for (int i = 0; i < 32; ++i)
+            if (i < cnt) op[i * ostride] = __float2bfloat16_rn(fmaf(yv[i], eg[i], ov[i]));
+        } else {
+          float* op = static_cast<float*>(p.out) + obase;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < cnt) op[i * ostride] = fmaf(yv[i], eg[i], ov[i]);
         }
       }
     }
