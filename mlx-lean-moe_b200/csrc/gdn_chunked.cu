@@ -22,8 +22,9 @@
 //  * chunk_scan_kernel, one CTA per (sequence, value head), serial over the
 //    chunks with the float32 state S resident in TMEM.  Warp roles: warp 0
 //    loads (TMA tensor loads of K, Q, V; bulk copies of T, P and the gates),
-//    warp 1 issues the MMAs, warps 2-9 run the epilogues (two per TMEM lane
-//    quarter: each thread owns one state row and half of its columns).  Per
+//    warp 1 issues the MMAs, warps 2-9 run the state-chain epilogues (two
+//    per TMEM lane quarter: each thread owns one state row and half of its
+//    columns), warps 10-13 build Kd^T and write the output, off the chain.  Per
 //    chunk, in the transposed orientation (M = Dv state rows):
 //      X       = S K^T             (N = 64,  K = Dk)    2 passes (S hi, lo)
 //      Y       = S Q^T             (N = 64,  K = Dk)    2 passes
@@ -363,7 +364,8 @@ constexpr uint32_t OFF_GATES = 180224;             // two 1 KB gate buffers (chu
 constexpr uint32_t OFF_R = OFF_GATES + 2 * kGateBytes;  // R hi, lo: 128 x 64 each
 constexpr uint32_t SCAN_SMEM_USED = OFF_R + 32768;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
-constexpr int kEpiThreads = 256;                   // warps 2-9
+constexpr int kEpiThreads = 256;                   // warps 2-9: the state chain
+constexpr int kAuxThreads = 128;                   // warps 10-13: Kd^T and the output
 
 // TMEM columns.
 // The state update accumulates straight onto S (S is scaled by gamma in TMEM
@@ -376,7 +378,7 @@ enum Bar {
   N_BARS
 };
 
-__global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                                                             const __grid_constant__ CUtensorMap kmap,
                                                             const __grid_constant__ CUtensorMap vmap,
                                                             const ChunkParams p) {
@@ -553,8 +555,8 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
       mma_commit(&bars[B_DRAIN]);
       mbar_wait(&bars[B_DRAIN], 0, kWaitNs);
     }
-  } else {
-    // ------------------------------------------------------------ epilogue
+  } else if (warp < 10) {
+    // ------------------------------------------------------- state-chain epilogue
     const int e = tid - 64;                   // 0..255
     const int q = warp & 3;                   // TMEM lane quarter of this warp
     const int half = (warp - 2) >> 2;         // which half of the columns this thread owns
@@ -596,42 +598,12 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
 
     for (int64_t c = 0; c < nch; ++c) {
       const uint32_t par = (uint32_t)(c & 1);
-      const int64_t t0 = start + c * CH;
-      const int n = (int)(end - t0 < CH ? end - t0 : CH);
       const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
 
-      // Kd^T = (diag(exp(G_last - G)) K)^T as bf16 hi/lo, from the K rows.
+      // Gates of this chunk arrive with K and Q.
       bool ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
-      {
-        const int dk = e & 127, th = e >> 7;  // row dk of Kd^T, tokens 32*th .. +32
-        const int kb = dk >> 6, cc = (dk & 63) >> 3, wi = dk & 7;
-        float dg[32];
-        load_gate32(gates + GATE_DG + th * 32, dg);
-#pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          float x[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int t = th * 32 + c8 * 8 + i;
-            const unsigned short kbits =
-                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, t, kb, cc) + wi * 2);
-            x[i] = __uint_as_float((uint32_t)kbits << 16) * dg[c8 * 8 + i];
-          }
-          uint4 hi, lo;
-          split8(x, hi, lo);
-          const int cidx = th * 4 + c8;
-          *reinterpret_cast<uint4*>(sm + OFF_KT + sw128_chunk(128, dk, 0, cidx)) = hi;
-          *reinterpret_cast<uint4*>(sm + OFF_KT + 16384 + sw128_chunk(128, dk, 0, cidx)) = lo;
-        }
-      }
-      fence_async_smem();
-      named_sync(1, kEpiThreads);
-      if (leader) {
-        mbar_arrive(&bars[B_KT_READY]);
-        mbar_arrive(&bars[B_KQ_EMPTY]);
-      }
 
       // R = beta (V - X exp(G)), tokens 32*half .. +32 of row dv.
       ok = mbar_wait(&bars[B_X_DONE], par, kWaitNs) && mbar_wait(&bars[B_V_FULL], par, kWaitNs);
@@ -732,34 +704,6 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
       tc_fence_before();
       named_sync(1, kEpiThreads);
       if (leader) mbar_arrive(&bars[B_S_READY]);
-
-      // Output, off the state chain: y_t = exp(G_t) Y_t + O_t.
-      {
-        float yv[32], ov[32];
-        tmem_ld32(tq + TM_Y + half * 32, yv);
-        tmem_ld32(tq + TM_O + half * 32, ov);
-        tmem_wait_ld();
-        tc_fence_before();
-        named_sync(1, kEpiThreads);
-        if (leader) mbar_arrive(&bars[B_O_FREE]);
-        const int tb = half * 32;
-        const int cnt = n - tb < 0 ? 0 : (n - tb < 32 ? n - tb : 32);
-        const size_t ostride = (size_t)p.hv * DH;
-        const size_t obase = ((size_t)(t0 + tb) * p.hv + h) * DH + dv;
-        float eg[32];
-        load_gate32(gates + GATE_EG + tb, eg);
-        if (p.out_dtype == GDN_BF16) {
-          __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + obase;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < cnt) op[i * ostride] = __float2bfloat16_rn(fmaf(yv[i], eg[i], ov[i]));
-        } else {
-          float* op = static_cast<float*>(p.out) + obase;
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (i < cnt) op[i * ostride] = fmaf(yv[i], eg[i], ov[i]);
-        }
-      }
     }
 
     // Final state (or the initial one for an empty sequence) -> state_out.
@@ -774,6 +718,98 @@ __global__ void __launch_bounds__(320, 1) chunk_scan_kernel(const __grid_constan
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
           *reinterpret_cast<float4*>(orow + col + i) = make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]);
+      }
+    }
+  } else {
+    // ------------------------------------------------- Kd^T and output (aux)
+    const int e = tid - 320;                  // 0..127 (warps 10-13)
+    const int q = warp & 3;                   // TMEM lane quarter of this warp
+    const int dv = q * 32 + lane;             // output row (value dim)
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    const bool leader = e == 0;
+    unsigned char* sm = base;
+    for (int64_t c = 0; c < nch; ++c) {
+      const uint32_t par = (uint32_t)(c & 1);
+      const int64_t t0 = start + c * CH;
+      const int n = (int)(end - t0 < CH ? end - t0 : CH);
+      const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
+
+      // Kd^T = (diag(exp(G_last - G)) K)^T as bf16 hi/lo, row dk = e, all 64 tokens.
+      bool ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(2, kAuxThreads, !ok)) break;
+      {
+        const int dk = e;
+        const int kb = dk >> 6, cc = (dk & 63) >> 3, wi = dk & 7;
+        for (int th = 0; th < 2; ++th) {
+          float dg[32];
+          load_gate32(gates + GATE_DG + th * 32, dg);
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            float x[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int t = th * 32 + c8 * 8 + i;
+              const unsigned short kbits =
+                  *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, t, kb, cc) + wi * 2);
+              x[i] = __uint_as_float((uint32_t)kbits << 16) * dg[c8 * 8 + i];
+            }
+            uint4 hi, lo;
+            split8(x, hi, lo);
+            const int cidx = th * 4 + c8;
+            *reinterpret_cast<uint4*>(sm + OFF_KT + sw128_chunk(128, dk, 0, cidx)) = hi;
+            *reinterpret_cast<uint4*>(sm + OFF_KT + 16384 + sw128_chunk(128, dk, 0, cidx)) = lo;
+          }
+        }
+      }
+      fence_async_smem();
+      named_sync(2, kAuxThreads);
+      if (leader) {
+        mbar_arrive(&bars[B_KT_READY]);
+        mbar_arrive(&bars[B_KQ_EMPTY]);
+      }
+
+      // Output: y_t = exp(G_t) Y_t + O_t for row dv, all tokens of the chunk.
+      ok = mbar_wait(&bars[B_OU_DONE], par, kWaitNs);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(2, kAuxThreads, !ok)) break;
+      tc_fence_after();
+      {
+        // y = exp(G) Y + O for all 64 tokens of row dv, read out of TMEM
+        // before O_FREE lets the next chunk's Y and O MMAs overwrite them.
+        float y[64];
+        tmem_ld32(tq + TM_Y, *reinterpret_cast<float(*)[32]>(y));
+        tmem_ld32(tq + TM_Y + 32, *reinterpret_cast<float(*)[32]>(y + 32));
+        tmem_wait_ld();
+        for (int hh = 0; hh < 2; ++hh) {
+          float o[32];
+          tmem_ld32(tq + TM_O + hh * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 g4 = *reinterpret_cast<const float4*>(gates + GATE_EG + hh * 32 + i);
+            y[hh * 32 + i] = fmaf(y[hh * 32 + i], g4.x, o[i]);
+            y[hh * 32 + i + 1] = fmaf(y[hh * 32 + i + 1], g4.y, o[i + 1]);
+            y[hh * 32 + i + 2] = fmaf(y[hh * 32 + i + 2], g4.z, o[i + 2]);
+            y[hh * 32 + i + 3] = fmaf(y[hh * 32 + i + 3], g4.w, o[i + 3]);
+          }
+        }
+        tc_fence_before();
+        named_sync(2, kAuxThreads);
+        if (leader) mbar_arrive(&bars[B_O_FREE]);
+        const size_t ostride = (size_t)p.hv * DH;
+        const size_t obase = ((size_t)t0 * p.hv + h) * DH + dv;
+        if (p.out_dtype == GDN_BF16) {
+          __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + obase;
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i < n) op[i * ostride] = __float2bfloat16_rn(y[i]);
+        } else {
+          float* op = static_cast<float*>(p.out) + obase;
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i < n) op[i * ostride] = y[i];
+        }
       }
     }
   }
@@ -879,7 +915,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   }
   const int64_t ctas = sp.n_seqs * sp.hv;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  chunk_scan_kernel<<<(unsigned)ctas, 320, kScanSmem, s>>>(qmap, kmap, vmap, p);
+  chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, p);
   return cudaGetLastError();
 }
 
