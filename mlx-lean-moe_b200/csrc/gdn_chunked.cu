@@ -26,11 +26,12 @@
 //    per TMEM lane quarter: each thread owns one state row and half of its
 //    columns), warps 10-13 build Kd^T and write the output, off the chain.  Per
 //    chunk, in the transposed orientation (M = Dv state rows):
-//      X       = S K^T             (N = 64,  K = Dk)    2 passes (S hi, lo)
-//      Y       = S Q^T             (N = 64,  K = Dk)    2 passes
-//      Delta^T = R^T T^T           (N = 64,  K = C)     3 passes (hi*hi, hi*lo, lo*hi)
+//      [X | Y] = S [K | Q]^T       (N = 128, K = Dk)    2 passes (S hi, lo)
+//      Delta^T = R^T T^T           (N = 128 + 64, K = C) R_hi [T_hi; T_lo]^T + R_lo T_hi^T
 //      U       = Delta^T Kd        (N = 128, K = C)     3 passes, Kd = diag(exp(G_last - G)) K
-//      O^T     = Delta^T P^T       (N = 64,  K = C)     3 passes
+//      O^T     = Delta^T P^T       (N = 128 + 64, K = C) as Delta
+//    (an M = 128 MMA costs about the same for N = 64 and N = 128, so the
+//    hi*lo term rides along as the second half of a 128-wide product).
 //    then S <- gamma S + U (the chain into the next chunk) and, off that
 //    chain, y = exp(G) Y + O.  Delta reuses the S lo operand buffer, which is
 //    dead between the X/Y MMAs and the state update.
@@ -359,6 +360,9 @@ constexpr uint32_t OFF_KQ = 65536;                 // [K;Q]: 128 x 128, two K-bl
 constexpr uint32_t OFF_V = 98304;                  // V: [64][128] bf16 row-major
 constexpr uint32_t OFF_T = 114688;                 // T hi, T lo: 64 x 64 each
 constexpr uint32_t OFF_P = 131072;                 // P hi, P lo
+// Output staging for the TMA store: [64 t][128 dv] in the output dtype, in
+// the T and P tiles (dead once the Delta and O MMAs of the chunk are done).
+constexpr uint32_t OFF_OSTAGE = OFF_T;
 constexpr uint32_t OFF_KT = 147456;                // Kd^T hi, lo: 128 (dk) x 64 (t) each
 constexpr uint32_t OFF_GATES = 180224;             // two 1 KB gate buffers (chunk parity)
 constexpr uint32_t OFF_R = OFF_GATES + 2 * kGateBytes;  // R hi, lo: 128 x 64 each
@@ -370,17 +374,20 @@ constexpr int kAuxThreads = 128;                   // warps 10-13: Kd^T and the 
 // TMEM columns.
 // The state update accumulates straight onto S (S is scaled by gamma in TMEM
 // while the Delta MMA runs), so there is no separate U accumulator.
-constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y = 192, TM_D = 256, TM_O = 320;
+// Delta and O take 128 columns each: their hi*hi + lo*hi part in the first 64,
+// the hi*lo part (one N = 128 MMA against [hi; lo] of T or P) in the second.
+constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y = 192, TM_D = 256, TM_O = 384;
 
 enum Bar {
-  B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
-  B_S_READY, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_KT_READY, B_OU_DONE, B_O_FREE, B_DRAIN,
+  B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_P_FULL,
+  B_S_READY, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_KT_READY, B_OU_DONE, B_O_FREE, B_OSTAGE_FREE, B_DRAIN,
   N_BARS
 };
 
 __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                                                             const __grid_constant__ CUtensorMap kmap,
                                                             const __grid_constant__ CUtensorMap vmap,
+                                                            const __grid_constant__ CUtensorMap omap,
                                                             const ChunkParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -439,13 +446,12 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
         tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
         ++n_v;
-        if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+        // T and P share their tiles with the previous chunk's output staging.
+        if (c > 0 && !mbar_wait(&bars[B_OSTAGE_FREE], par, kWaitNs)) record_error(&abort_flag);
         if (abort_flag) break;
         mbar_arrive_expect_tx(&bars[B_T_FULL], 2 * kTile64);
         bulk_load(base + OFF_T, rec, 2 * kTile64, &bars[B_T_FULL]);
         ++n_t;
-        if (c > 0 && !mbar_wait(&bars[B_P_EMPTY], par, kWaitNs)) record_error(&abort_flag);
-        if (abort_flag) break;
         mbar_arrive_expect_tx(&bars[B_P_FULL], 2 * kTile64);
         bulk_load(base + OFF_P, rec + 2 * kTile64, 2 * kTile64, &bars[B_P_FULL]);
         ++n_p;
@@ -465,7 +471,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       const uint32_t id128 = idesc_bf16_f32(128, 128);
       const uint32_t id64 = idesc_bf16_f32(128, 64);
       const uint32_t sS[2] = {smem_u32(base + OFF_SHI), smem_u32(base + OFF_SLO)};
-      const uint32_t sK = smem_u32(base + OFF_KQ), sQ = sK + 8192;
+      const uint32_t sK = smem_u32(base + OFF_KQ);
       const uint32_t sT[2] = {smem_u32(base + OFF_T), smem_u32(base + OFF_T + kTile64)};
       const uint32_t sP[2] = {smem_u32(base + OFF_P), smem_u32(base + OFF_P + kTile64)};
       const uint32_t sR[2] = {smem_u32(base + OFF_R), smem_u32(base + OFF_R + 16384)};
@@ -481,16 +487,8 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         }
         if (abort_flag) break;
         tc_fence_after();
-        {  // X = S K^T: the only product of S on the state chain
-          int n = 0;
-          for (int part = 0; part < 2; ++part)
-            for (int kb = 0; kb < 2; ++kb)
-              for (int ks = 0; ks < 4; ++ks, ++n)
-                mma_bf16(tmem + TM_X, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
-                         sdesc_sw128(sK + kb * 16384 + ks * 32), id64, n > 0);
-        }
-        mma_commit(&bars[B_X_DONE]);
-        // Y = S Q^T, once the previous chunk's output stage has read Y and O.
+        // [X | Y] = S [K | Q]^T; Y is free to overwrite once the previous
+        // chunk's output stage has read it.
         if (c > 0 && !mbar_wait(&bars[B_O_FREE], (uint32_t)((c - 1) & 1), kWaitNs)) {
           record_error(&abort_flag);
           break;
@@ -502,9 +500,10 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           for (int part = 0; part < 2; ++part)
             for (int kb = 0; kb < 2; ++kb)
               for (int ks = 0; ks < 4; ++ks, ++n)
-                mma_bf16(tmem + TM_Y, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
-                         sdesc_sw128(sQ + kb * 16384 + ks * 32), id64, n > 0);
+                mma_bf16(tmem + TM_X, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
+                         sdesc_sw128(sK + kb * 16384 + ks * 32), id128, n > 0);
         }
+        mma_commit(&bars[B_X_DONE]);
         mma_commit(&bars[B_KQ_EMPTY]);
         if (!mbar_wait(&bars[B_R_READY], par, kWaitNs) || !mbar_wait(&bars[B_T_FULL], par, kWaitNs)) {
           record_error(&abort_flag);
@@ -512,15 +511,13 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         }
         if (abort_flag) break;
         tc_fence_after();
-        {  // Delta^T = R^T T^T
-          int n = 0;
-          for (int pass = 0; pass < 3; ++pass)
-            for (int ks = 0; ks < 4; ++ks, ++n)
-              mma_bf16(tmem + TM_D, sdesc_sw128(sR[pa[pass]] + ks * 32), sdesc_sw128(sT[pb[pass]] + ks * 32), id64,
-                       n > 0);
+        {  // Delta^T = R_hi [T_hi; T_lo]^T (N = 128) + R_lo T_hi^T (N = 64)
+          for (int ks = 0; ks < 4; ++ks)
+            mma_bf16(tmem + TM_D, sdesc_sw128(sR[0] + ks * 32), sdesc_sw128(sT[0] + ks * 32), id128, ks > 0);
+          for (int ks = 0; ks < 4; ++ks)
+            mma_bf16(tmem + TM_D, sdesc_sw128(sR[1] + ks * 32), sdesc_sw128(sT[0] + ks * 32), id64, true);
         }
         mma_commit(&bars[B_D_DONE]);
-        mma_commit(&bars[B_T_EMPTY]);
         if (!mbar_wait(&bars[B_DD_READY], par, kWaitNs) || !mbar_wait(&bars[B_KT_READY], par, kWaitNs)) {
           record_error(&abort_flag);
           break;
@@ -539,17 +536,15 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         }
         if (abort_flag) break;
         tc_fence_after();
-        {  // O^T = Delta^T P^T
-          int n = 0;
-          for (int pass = 0; pass < 3; ++pass)
-            for (int ks = 0; ks < 4; ++ks, ++n)
-              mma_bf16(tmem + TM_O, sdesc_sw128(sD[pa[pass]] + ks * 32), sdesc_sw128(sP[pb[pass]] + ks * 32), id64,
-                       n > 0);
+        {  // O^T = Delta_hi [P_hi; P_lo]^T (N = 128) + Delta_lo P_hi^T (N = 64)
+          for (int ks = 0; ks < 4; ++ks)
+            mma_bf16(tmem + TM_O, sdesc_sw128(sD[0] + ks * 32), sdesc_sw128(sP[0] + ks * 32), id128, ks > 0);
+          for (int ks = 0; ks < 4; ++ks)
+            mma_bf16(tmem + TM_O, sdesc_sw128(sD[1] + ks * 32), sdesc_sw128(sP[0] + ks * 32), id64, true);
         }
         // One commit for U and O: Delta (in the S lo buffer) is free only
         // once both have read it.
         mma_commit(&bars[B_OU_DONE]);
-        mma_commit(&bars[B_P_EMPTY]);
       }
       // Wait for every MMA issued so far before the CTA winds down.
       mma_commit(&bars[B_DRAIN]);
@@ -662,9 +657,12 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
       {
-        float x[32];
+        float x[32], x2[32];
         tmem_ld32(tq + TM_D + half * 32, x);
+        tmem_ld32(tq + TM_D + 64 + half * 32, x2);
         tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] += x2[i];
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
           uint4 hi, lo;
@@ -793,25 +791,54 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
             y[hh * 32 + i + 2] = fmaf(y[hh * 32 + i + 2], g4.z, o[i + 2]);
             y[hh * 32 + i + 3] = fmaf(y[hh * 32 + i + 3], g4.w, o[i + 3]);
           }
+          tmem_ld32(tq + TM_O + 64 + hh * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) y[hh * 32 + i] += o[i];
         }
         tc_fence_before();
         named_sync(2, kAuxThreads);
         if (leader) mbar_arrive(&bars[B_O_FREE]);
-        const size_t ostride = (size_t)p.hv * DH;
-        const size_t obase = ((size_t)t0 * p.hv + h) * DH + dv;
-        if (p.out_dtype == GDN_BF16) {
-          __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + obase;
+        if (n == CH) {
+          // Whole chunk: stage [t][dv] in shared memory, one TMA tensor store.
+          if (p.out_dtype == GDN_BF16) {
+            __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i < n) op[i * ostride] = __float2bfloat16_rn(y[i]);
+            for (int i = 0; i < 64; ++i) st[i * DH + dv] = __float2bfloat16_rn(y[i]);
+          } else {
+            float* st = reinterpret_cast<float*>(sm + OFF_OSTAGE);
+#pragma unroll
+            for (int i = 0; i < 64; ++i) st[i * DH + dv] = y[i];
+          }
+          fence_async_smem();
+          named_sync(2, kAuxThreads);
+          if (leader) {
+            tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
+            bulk_commit_group();
+            bulk_wait_group_read0();
+            mbar_arrive(&bars[B_OSTAGE_FREE]);
+          }
         } else {
-          float* op = static_cast<float*>(p.out) + obase;
+          // Ragged last chunk of a sequence: plain stores of the valid rows.
+          const size_t ostride = (size_t)p.hv * DH;
+          const size_t obase = ((size_t)t0 * p.hv + h) * DH + dv;
+          if (p.out_dtype == GDN_BF16) {
+            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + obase;
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i < n) op[i * ostride] = y[i];
+            for (int i = 0; i < 64; ++i)
+              if (i < n) op[i * ostride] = __float2bfloat16_rn(y[i]);
+          } else {
+            float* op = static_cast<float*>(p.out) + obase;
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              if (i < n) op[i * ostride] = y[i];
+          }
+          named_sync(2, kAuxThreads);
+          if (leader) mbar_arrive(&bars[B_OSTAGE_FREE]);
         }
       }
     }
+    if (leader) bulk_wait_group0();  // every output tile has reached global memory
   }
 
   tc_fence_before();
@@ -851,6 +878,22 @@ bool make_map(CUtensorMap* map, const void* ptr, int64_t n_tokens, int heads, in
   return r == CUDA_SUCCESS;
 }
 
+// 3-D map over the contiguous output [N, Hv, 128] (fp32 or bf16), box {128, 1, 64}.
+bool make_out_map(CUtensorMap* map, void* ptr, int64_t n_tokens, int heads, gdn_dtype dt) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  std::memset(map, 0, sizeof(*map));
+  const cuuint64_t es = dt == GDN_BF16 ? 2 : 4;
+  cuuint64_t dims[3] = {(cuuint64_t)DH, (cuuint64_t)heads, (cuuint64_t)n_tokens};
+  cuuint64_t strides[2] = {DH * es, (cuuint64_t)heads * DH * es};
+  cuuint32_t box[3] = {(cuuint32_t)DH, 1, (cuuint32_t)CH};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt == GDN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr,
+                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 int64_t max_slots(const ScanParams& p) { return (p.n_tokens + CH - 1) / CH + p.n_seqs; }
 
 bool aligned_elems(int64_t s) { return s >= 0 && s % 8 == 0; }
@@ -869,16 +912,17 @@ size_t chunked_workspace_bytes(const ScanParams& p) { return (size_t)max_slots(p
 cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   if (!aligned_ptr16(sp.q) || !aligned_ptr16(sp.k) || !aligned_ptr16(sp.v) || !aligned_ptr16(sp.workspace))
     return cudaErrorMisalignedAddress;
-  CUtensorMap qmap, kmap, vmap;
+  CUtensorMap qmap, kmap, vmap, omap;
   const int64_t N = sp.n_tokens;
   if (N > 0) {
     if (!make_map(&qmap, sp.q, N, sp.hk, sp.q_st, sp.q_sh, 64, true) ||
         !make_map(&kmap, sp.k, N, sp.hk, sp.k_st, sp.k_sh, 64, true) ||
-        !make_map(&vmap, sp.v, N, sp.hv, sp.v_st, sp.v_sh, 128, false))
+        !make_map(&vmap, sp.v, N, sp.hv, sp.v_st, sp.v_sh, 128, false) ||
+        !make_out_map(&omap, sp.out, N, sp.hv, sp.out_dtype))
       return cudaErrorInvalidValue;
   } else {
     std::memset(&qmap, 0, sizeof(qmap));
-    kmap = vmap = qmap;
+    kmap = vmap = omap = qmap;
   }
   ChunkParams p;
   p.n_tokens = N;
@@ -915,7 +959,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   }
   const int64_t ctas = sp.n_seqs * sp.hv;
   if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, p);
+  chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p);
   return cudaGetLastError();
 }
 
