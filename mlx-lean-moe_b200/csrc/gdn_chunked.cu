@@ -355,7 +355,6 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
 // ===========================================================================
 // Dynamic shared memory map (offsets from the 1024-aligned base).
 constexpr uint32_t OFF_SHI = 0, OFF_SLO = 32768;   // S hi/lo: 128 x 128, two K-blocks each
-constexpr uint32_t OFF_D = OFF_SLO;                // Delta hi, lo (128 x 64 each) while S lo is dead
 constexpr uint32_t OFF_KQ = 65536;                 // [K;Q]: 128 x 128, two K-blocks
 constexpr uint32_t OFF_V = 98304;                  // V: [64][128] bf16 row-major
 constexpr uint32_t OFF_T = 114688;                 // T hi, T lo: 64 x 64 each
@@ -365,8 +364,7 @@ constexpr uint32_t OFF_P = 131072;                 // P hi, P lo
 constexpr uint32_t OFF_OSTAGE = OFF_T;
 constexpr uint32_t OFF_KT = 147456;                // Kd^T hi, lo: 128 (dk) x 64 (t) each
 constexpr uint32_t OFF_GATES = 180224;             // two 1 KB gate buffers (chunk parity)
-constexpr uint32_t OFF_R = OFF_GATES + 2 * kGateBytes;  // R hi, lo: 128 x 64 each
-constexpr uint32_t SCAN_SMEM_USED = OFF_R + 32768;
+constexpr uint32_t SCAN_SMEM_USED = OFF_GATES + 2 * kGateBytes;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
 constexpr int kEpiThreads = 256;                   // warps 2-9: the state chain
 constexpr int kAuxThreads = 128;                   // warps 10-13: Kd^T and the output
@@ -376,11 +374,16 @@ constexpr int kAuxThreads = 128;                   // warps 10-13: Kd^T and the 
 // while the Delta MMA runs), so there is no separate U accumulator.
 // Delta and O take 128 columns each: their hi*hi + lo*hi part in the first 64,
 // the hi*lo part (one N = 128 MMA against [hi; lo] of T or P) in the second.
+// R and Delta, the A operands of the next MMAs, are written back as packed
+// bf16 hi/lo in place of the accumulators they come from (X, Delta).
 constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y = 192, TM_D = 256, TM_O = 384;
+constexpr uint32_t TM_RHI = TM_X, TM_RLO = TM_X + 32;   // 64 tokens -> 32 packed columns each
+constexpr uint32_t TM_DHI = TM_D, TM_DLO = TM_D + 32;
 
 enum Bar {
   B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_P_FULL,
-  B_S_READY, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_KT_READY, B_OU_DONE, B_O_FREE, B_OSTAGE_FREE, B_DRAIN,
+  B_S_READY, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_O_FREE, B_OSTAGE_FREE,
+  B_DRAIN,
   N_BARS
 };
 
@@ -474,8 +477,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       const uint32_t sK = smem_u32(base + OFF_KQ);
       const uint32_t sT[2] = {smem_u32(base + OFF_T), smem_u32(base + OFF_T + kTile64)};
       const uint32_t sP[2] = {smem_u32(base + OFF_P), smem_u32(base + OFF_P + kTile64)};
-      const uint32_t sR[2] = {smem_u32(base + OFF_R), smem_u32(base + OFF_R + 16384)};
-      const uint32_t sD[2] = {smem_u32(base + OFF_D), smem_u32(base + OFF_D + 16384)};
+      const uint32_t tD[2] = {tmem + TM_DHI, tmem + TM_DLO};
       const uint32_t sKt[2] = {smem_u32(base + OFF_KT), smem_u32(base + OFF_KT + 16384)};
       // (a part, b part) of the three-pass split products hi*hi + hi*lo + lo*hi
       const int pa[3] = {0, 0, 1}, pb[3] = {0, 1, 0};
@@ -511,11 +513,11 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         }
         if (abort_flag) break;
         tc_fence_after();
-        {  // Delta^T = R_hi [T_hi; T_lo]^T (N = 128) + R_lo T_hi^T (N = 64)
+        {  // Delta^T = R_hi [T_hi; T_lo]^T (N = 128) + R_lo T_hi^T (N = 64), R from TMEM
           for (int ks = 0; ks < 4; ++ks)
-            mma_bf16(tmem + TM_D, sdesc_sw128(sR[0] + ks * 32), sdesc_sw128(sT[0] + ks * 32), id128, ks > 0);
+            mma_bf16_ts(tmem + TM_D, tmem + TM_RHI + ks * 8, sdesc_sw128(sT[0] + ks * 32), id128, ks > 0);
           for (int ks = 0; ks < 4; ++ks)
-            mma_bf16(tmem + TM_D, sdesc_sw128(sR[1] + ks * 32), sdesc_sw128(sT[0] + ks * 32), id64, true);
+            mma_bf16_ts(tmem + TM_D, tmem + TM_RLO + ks * 8, sdesc_sw128(sT[0] + ks * 32), id64, true);
         }
         mma_commit(&bars[B_D_DONE]);
         if (!mbar_wait(&bars[B_DD_READY], par, kWaitNs) || !mbar_wait(&bars[B_KT_READY], par, kWaitNs)) {
@@ -524,12 +526,12 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         }
         if (abort_flag) break;
         tc_fence_after();
-        {  // S <- (gamma S) + Delta^T Kd   (state chain first)
+        {  // S <- (gamma S) + Delta^T Kd   (state chain first), Delta from TMEM
           for (int pass = 0; pass < 3; ++pass)
             for (int ks = 0; ks < 4; ++ks)
-              mma_bf16(tmem + TM_S, sdesc_sw128(sD[pa[pass]] + ks * 32), sdesc_sw128(sKt[pb[pass]] + ks * 32),
-                       id128, true);
+              mma_bf16_ts(tmem + TM_S, tD[pa[pass]] + ks * 8, sdesc_sw128(sKt[pb[pass]] + ks * 32), id128, true);
         }
+        mma_commit(&bars[B_U_DONE]);
         if (!mbar_wait(&bars[B_P_FULL], par, kWaitNs)) {
           record_error(&abort_flag);
           break;
@@ -538,12 +540,10 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         tc_fence_after();
         {  // O^T = Delta_hi [P_hi; P_lo]^T (N = 128) + Delta_lo P_hi^T (N = 64)
           for (int ks = 0; ks < 4; ++ks)
-            mma_bf16(tmem + TM_O, sdesc_sw128(sD[0] + ks * 32), sdesc_sw128(sP[0] + ks * 32), id128, ks > 0);
+            mma_bf16_ts(tmem + TM_O, tD[0] + ks * 8, sdesc_sw128(sP[0] + ks * 32), id128, ks > 0);
           for (int ks = 0; ks < 4; ++ks)
-            mma_bf16(tmem + TM_O, sdesc_sw128(sD[1] + ks * 32), sdesc_sw128(sP[0] + ks * 32), id64, true);
+            mma_bf16_ts(tmem + TM_O, tD[1] + ks * 8, sdesc_sw128(sP[0] + ks * 32), id64, true);
         }
-        // One commit for U and O: Delta (in the S lo buffer) is free only
-        // once both have read it.
         mma_commit(&bars[B_OU_DONE]);
       }
       // Wait for every MMA issued so far before the CTA winds down.
@@ -618,16 +618,14 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           const int t = half * 32 + i;
           x[i] = bt[i] * (__bfloat162float(V[t * DH + dv]) - x[i] * eg[i]);
         }
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint4 hi, lo;
-          split8(x + 8 * c4, hi, lo);
-          const int cidx = half * 4 + c4;
-          *reinterpret_cast<uint4*>(sm + OFF_R + sw128_chunk(128, dv, 0, cidx)) = hi;
-          *reinterpret_cast<uint4*>(sm + OFF_R + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
-        }
+        uint32_t hi[16], lo[16];
+        split32_packed(x, hi, lo);
+        // R hi/lo overwrite X in place: every X column must be read first.
+        named_sync(1, kEpiThreads);
+        tmem_st16(tq + TM_RHI + half * 16, hi);
+        tmem_st16(tq + TM_RLO + half * 16, lo);
+        tmem_wait_st();
       }
-      fence_async_smem();
       tc_fence_before();
       named_sync(1, kEpiThreads);
       if (leader) {
@@ -663,22 +661,20 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[i] += x2[i];
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint4 hi, lo;
-          split8(x + 8 * c4, hi, lo);
-          const int cidx = half * 4 + c4;
-          *reinterpret_cast<uint4*>(sm + OFF_D + sw128_chunk(128, dv, 0, cidx)) = hi;
-          *reinterpret_cast<uint4*>(sm + OFF_D + 16384 + sw128_chunk(128, dv, 0, cidx)) = lo;
-        }
+        uint32_t hi[16], lo[16];
+        split32_packed(x, hi, lo);
+        // Delta hi/lo overwrite the accumulator in place: read it all first.
+        named_sync(1, kEpiThreads);
+        tmem_st16(tq + TM_DHI + half * 16, hi);
+        tmem_st16(tq + TM_DLO + half * 16, lo);
+        tmem_wait_st();
       }
-      fence_async_smem();
       tc_fence_before();
       named_sync(1, kEpiThreads);
       if (leader) mbar_arrive(&bars[B_DD_READY]);
 
       // The updated S -> its hi/lo operand for the next chunk.
-      ok = mbar_wait(&bars[B_OU_DONE], par, kWaitNs);
+      ok = mbar_wait(&bars[B_U_DONE], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();

@@ -232,6 +232,28 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&r)[32]) 
       : "memory");
 }
 
+// 32 lanes x 16 columns of 32-bit TMEM <- 16 registers per thread.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&u)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(u[0]), "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7]), "r"(u[8]),
+      "r"(u[9]), "r"(u[10]), "r"(u[11]), "r"(u[12]), "r"(u[13]), "r"(u[14]), "r"(u[15])
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T: A packed bf16 in TMEM (lane = row, column
+// j holds K elements 2j (low half) and 2j + 1), B a K-major bf16 smem tile.
+__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -265,6 +287,16 @@ __device__ __forceinline__ void split8(const float* x, uint4& hi, uint4& lo) {
   }
   hi = make_uint4(h[0], h[1], h[2], h[3]);
   lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
+// Splits 32 floats into packed bf16 hi words and packed bf16 lo (x - hi)
+// words, 16 each (element 2j in the low half of word j).
+__device__ __forceinline__ void split32_packed(const float (&x)[32], uint32_t (&hi)[16], uint32_t (&lo)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    hi[j] = pack_bf16(x[2 * j], x[2 * j + 1]);
+    lo[j] = pack_bf16(x[2 * j] - bf16_lo_f(hi[j]), x[2 * j + 1] - bf16_hi_f(hi[j]));
+  }
 }
 
 }  // namespace sm100
