@@ -218,8 +218,227 @@ __global__ void __launch_bounds__(256) block_epilogue_kernel(const BlockParams p
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Vectorized prologue/epilogue for the common shapes (conv kernel <= 4, head
+// dims a power of two in [8, 256]).  Same arithmetic and rounding points as
+// the general kernels above.
+// ---------------------------------------------------------------------------
+constexpr int VT = 64;  // tokens per prologue CTA
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* src, float (&x)[8]);
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* src, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = __uint_as_float(w[i] << 16);
+    x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* src, float (&x)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(src);
+  const float4 b = *reinterpret_cast<const float4*>(src + 4);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T* dst, const float (&x)[8]);
+template <>
+__device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* dst, const float (&x)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <>
+__device__ __forceinline__ void store8<float>(float* dst, const float (&x)[8]) {
+  *reinterpret_cast<float4*>(dst) = make_float4(x[0], x[1], x[2], x[3]);
+  *reinterpret_cast<float4*>(dst + 4) = make_float4(x[4], x[5], x[6], x[7]);
+}
+
+// One row (8 channels starting at c) of the conv input at absolute position
+// pos for sequence b starting at `start`: the projection row, or the
+// sequence's conv state for positions before its start.
+template <typename T, typename TS>
+__device__ __forceinline__ void conv_row(const BlockParams& p, int64_t conv_dim, int64_t b, int64_t start,
+                                         int64_t pos, int c, float (&x)[8]) {
+  if (pos >= start) {
+    load8<T>(static_cast<const T*>(p.mixed) + pos * p.mixed_st + c, x);
+    return;
+  }
+  if (!p.conv_state_in) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x[i] = 0.f;
+    return;
+  }
+  const int64_t row = p.kernel - 1 - (start - pos);
+  const TS* src = static_cast<const TS*>(p.conv_state_in) + (b * (p.kernel - 1) + row) * conv_dim + c;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = round_to<T>(to_f(src[i]));
+}
+
+// Grid: x = token tiles of VT, y = channel blocks of 2048 (+1 for the gates).
+// Thread: 8 consecutive channels; a warp covers 256 channels, so a q/k head
+// of Dk channels is Dk/8 consecutive lanes (Dk a power of two <= 256).
+template <typename T, typename TS, int K>
+__global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockParams p) {
+  const int64_t t0 = blockIdx.x * (int64_t)VT;
+  const int64_t t_end = min(t0 + VT, p.n_tokens);
+  const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
+  if (blockIdx.y == gridDim.y - 1) {  // gates
+    const int64_t off_b = conv_dim + (int64_t)p.hv * p.dv, off_a = off_b + p.hv;
+    for (int idx = threadIdx.x; idx < VT * p.hv; idx += blockDim.x) {
+      const int64_t t = t0 + idx / p.hv;
+      const int h = idx % p.hv;
+      if (t >= p.n_tokens) break;
+      const T* row = static_cast<const T*>(p.mixed) + t * p.mixed_st;
+      const float av = to_f(row[off_a + h]), bv = to_f(row[off_b + h]);
+      p.g_log[t * p.hv + h] = -expf(p.A_log[h]) * softplus_f(av + p.dt_bias[h]);
+      p.beta[t * p.hv + h] = round_to<T>(sigmoid_f(bv));
+    }
+    return;
+  }
+  // Lanes past the last channel stay in the loop (without loads or stores)
+  // so that every shuffle below has its full warp.
+  const int c_raw = (int)(blockIdx.y * 2048 + threadIdx.x * 8);
+  const bool active = c_raw < conv_dim;  // whole 8-groups only (conv_dim % 8 == 0)
+  const int c = active ? c_raw : 0;
+  const int64_t key_dim = (int64_t)p.hk * p.dk;
+  const bool is_q = c < key_dim, is_k = !is_q && c < 2 * key_dim;
+  const int group = (is_q || is_k) ? p.dk / 8 : 32;  // lanes sharing one q/k head
+
+  float w[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) w[i][j] = j < K ? round_to<T>(p.conv_w[(int64_t)(c + i) * K + j]) : 0.f;
+
+  int64_t b = find_seq(p.cu_seqlens, p.n_tokens, p.n_seqs, t0);
+  int64_t s_start, s_end;
+  seq_range(p.cu_seqlens, p.n_tokens, p.n_seqs, b, s_start, s_end);
+  // win[j] = conv input at position t - (K-1) + j, j < K-1 (the history)
+  float win[K > 1 ? K - 1 : 1][8];
+  auto reset = [&](int64_t t) {
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) conv_row<T, TS>(p, conv_dim, b, s_start, t - (K - 1) + j, c, win[j]);
+  };
+  reset(t0);
+  const float qscale = 1.f / (float)p.dk, kscale = rsqrtf((float)p.dk);
+  for (int64_t t = t0; t < t_end; ++t) {
+    if (t >= s_end) {  // next (non-empty) sequence: fresh history from its conv state
+      do {
+        ++b;
+        seq_range(p.cu_seqlens, p.n_tokens, p.n_seqs, b, s_start, s_end);
+      } while (t >= s_end);
+      reset(t);
+    }
+    float cur[8];
+    load8<T>(static_cast<const T*>(p.mixed) + t * p.mixed_st + c, cur);
+    float x[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < K - 1; ++j) acc += w[i][j] * win[j][i];
+      acc += w[i][K - 1] * cur[i];
+      x[i] = round_to<T>(silu_f(round_to<T>(acc)));
+      ss += x[i] * x[i];
+    }
+    // q/k rms-norm: reduce over the lanes of this head (all lanes shuffle).
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float o = __shfl_xor_sync(0xffffffffu, ss, off);
+      if (off < group) ss += o;
+    }
+    if (is_q || is_k) {
+      const float inv = rsqrtf(ss / (float)p.dk + 1e-6f);
+      const float scale = is_q ? qscale : kscale;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = round_to<T>(round_to<T>(x[i] * inv) * scale);
+      T* dst = static_cast<T*>(is_q ? p.q : p.k) + t * key_dim + (is_q ? c : c - key_dim);
+      if (active) store8<T>(dst, x);
+    } else {
+      T* dst = static_cast<T*>(p.v) + t * (int64_t)p.hv * p.dv + (c - 2 * key_dim);
+      if (active) store8<T>(dst, x);
+    }
+    // slide the history window
+#pragma unroll
+    for (int j = 0; j + 1 < K - 1; ++j)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) win[j][i] = win[j + 1][i];
+    if constexpr (K > 1) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) win[K - 2][i] = cur[i];
+    }
+  }
+}
+
+// out = silu(z) * rms_norm(y -> T, norm_w, eps); Dv/8 lanes per (token, head)
+// row, 8 values per lane.
+template <typename T>
+__global__ void __launch_bounds__(256) block_epilogue_fast_kernel(const BlockParams p) {
+  const int lanes = p.dv / 8;
+  const int64_t gtid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t row = gtid / lanes;
+  const int d0 = (int)(gtid % lanes) * 8;
+  const bool valid = row < p.n_tokens * p.hv;
+  const int64_t rr = valid ? row : 0;
+  const int64_t t = rr / p.hv;
+  const int h = (int)(rr % p.hv);
+  const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
+  float y[8], z[8], w[8];
+  load8<float>(p.y + rr * p.dv + d0, y);
+  load8<T>(static_cast<const T*>(p.mixed) + t * p.mixed_st + conv_dim + (int64_t)h * p.dv + d0, z);
+  load8<float>(p.norm_w + d0, w);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    y[i] = round_to<T>(y[i]);
+    ss += y[i] * y[i];
+  }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, ss, off);
+    if (off < lanes) ss += o;
+  }
+  const float inv = rsqrtf(ss / (float)p.dv + p.eps);
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = silu_f(z[i]) * round_to<T>(y[i] * inv * w[i]);
+  if (valid) store8<T>(static_cast<T*>(p.out) + rr * p.dv + d0, o);
+}
+
+bool pow2_in(int x, int lo, int hi) { return x >= lo && x <= hi && (x & (x - 1)) == 0; }
+
+bool fast_shapes(const BlockParams& p) {
+  return p.kernel >= 1 && p.kernel <= 4 && pow2_in(p.dk, 8, 256) && pow2_in(p.dv, 8, 256) && p.mixed_st % 8 == 0 &&
+         (reinterpret_cast<uintptr_t>(p.mixed) & 15u) == 0 && (reinterpret_cast<uintptr_t>(p.norm_w) & 15u) == 0;
+}
+
 template <typename T, typename TS>
 cudaError_t prologue_t(const BlockParams& p, cudaStream_t s) {
+  if (fast_shapes(p)) {
+    const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
+    const int64_t gx = (p.n_tokens + VT - 1) / VT;
+    if (gx == 0) return cudaSuccess;
+    dim3 grid((unsigned)gx, (unsigned)((conv_dim + 2047) / 2048 + 1));
+    switch (p.kernel) {
+      case 1: block_prologue_fast_kernel<T, TS, 1><<<grid, 256, 0, s>>>(p); break;
+      case 2: block_prologue_fast_kernel<T, TS, 2><<<grid, 256, 0, s>>>(p); break;
+      case 3: block_prologue_fast_kernel<T, TS, 3><<<grid, 256, 0, s>>>(p); break;
+      default: block_prologue_fast_kernel<T, TS, 4><<<grid, 256, 0, s>>>(p); break;
+    }
+    return cudaGetLastError();
+  }
   const int n_heads = 2 * p.hk + p.hv;
   const int64_t gx = (p.n_tokens + TT - 1) / TT;
   if (gx == 0) return cudaSuccess;
@@ -264,6 +483,15 @@ cudaError_t launch_block_conv_tail(const BlockParams& p, cudaStream_t s) {
 cudaError_t launch_block_epilogue(const BlockParams& p, cudaStream_t s) {
   const int64_t rows = p.n_tokens * p.hv;
   if (rows == 0) return cudaSuccess;
+  if (fast_shapes(p)) {
+    const int64_t threads = rows * (p.dv / 8);
+    const unsigned grid = (unsigned)((threads + 255) / 256);
+    if (p.act_dtype == GDN_BF16)
+      block_epilogue_fast_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);
+    else
+      block_epilogue_fast_kernel<float><<<grid, 256, 0, s>>>(p);
+    return cudaGetLastError();
+  }
   const unsigned grid = (unsigned)((rows + 7) / 8);
   if (p.act_dtype == GDN_BF16)
     block_epilogue_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);

@@ -114,6 +114,9 @@ def gated_delta_block(
     a.conv_w = conv_w2.data_ptr()
     a.conv_state_in = conv_state.data_ptr() if conv_state is not None else None
     a.conv_state_out = conv_state_out.data_ptr() if conv_state_out is not None else None
+    if K == 1:  # no conv history at all
+        conv_state = conv_state_out = None
+        a.conv_state_in = a.conv_state_out = None
     st_dtype = conv_state_out.dtype if conv_state_out is not None else torch.float32
     if conv_state is not None and conv_state.dtype != st_dtype:
         raise ValueError("conv_state and conv_state_out must share a dtype")

@@ -68,18 +68,18 @@ def test_layer_stepwise_and_chunked_calls_carry_both_states(golden):
     assert len(shapes) == 1 and cache.size == 12
 
 
-def _bf16_block_case(lengths, hk, hv, dk, dv, seed, algo="auto"):
+def _bf16_block_case(lengths, hk, hv, dk, dv, seed, algo="auto", kernel=4):
     B = len(lengths)
     cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
     N = int(cu[-1])
-    shape = LinearAttentionShape(hk, hv, dk, dv, 4)
+    shape = LinearAttentionShape(hk, hv, dk, dv, kernel)
     rng = np.random.default_rng(seed)
     mixed = O.bf16_round(rng.standard_normal((N, shape.mixed_width)).astype(np.float32))
-    conv_w = (rng.standard_normal((shape.conv_dim, 4)) * 0.1).astype(np.float32)
+    conv_w = (rng.standard_normal((shape.conv_dim, kernel)) * 0.1).astype(np.float32)
     A_log = rng.uniform(0, 1.5, hv).astype(np.float32)
     dt_bias = (rng.standard_normal(hv) * 0.1).astype(np.float32)
     norm_w = (1 + 0.1 * rng.standard_normal(dv)).astype(np.float32)
-    conv_state = O.bf16_round((rng.standard_normal((B, 3, shape.conv_dim))).astype(np.float32))
+    conv_state = O.bf16_round((rng.standard_normal((B, kernel - 1, shape.conv_dim))).astype(np.float32))
     ssm = (rng.standard_normal((B, hv, dv, dk)) * 0.02).astype(np.float32)
     eps = 1e-6
 
@@ -115,6 +115,24 @@ def test_bf16_block_matches_oracle(lengths):
 
 def test_bf16_block_at_model_head_shape():
     go, eo, gc, ec, gs, es = _bf16_block_case([96, 160], 16, 32, 128, 128, seed=4)
+    assert O.rel_l2(go, eo) < 2e-3
+    assert O.rel_l2(gs, es) < 2e-3
+    np.testing.assert_array_equal(gc, ec)
+
+
+@pytest.mark.parametrize("kernel", [1, 2, 3])
+def test_bf16_block_other_conv_widths(kernel):
+    go, eo, gc, ec, gs, es = _bf16_block_case([5, 70], 2, 4, 32, 64, seed=10 + kernel, kernel=kernel)
+    assert O.rel_l2(go, eo) < 2e-3
+    assert O.rel_l2(gs, es) < 2e-3
+    if kernel > 1:
+        np.testing.assert_array_equal(gc, ec)
+
+
+def test_bf16_block_general_head_dims():
+    """Head dims that are not powers of two take the general prologue and
+    epilogue kernels and the serial scan."""
+    go, eo, gc, ec, gs, es = _bf16_block_case([33, 2], 3, 6, 48, 40, seed=21)
     assert O.rel_l2(go, eo) < 2e-3
     assert O.rel_l2(gs, es) < 2e-3
     np.testing.assert_array_equal(gc, ec)
