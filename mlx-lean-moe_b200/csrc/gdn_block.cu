@@ -264,6 +264,36 @@ __device__ __forceinline__ void store8<float>(float* dst, const float (&x)[8]) {
   *reinterpret_cast<float4*>(dst + 4) = make_float4(x[4], x[5], x[6], x[7]);
 }
 
+// A raw 8-channel row as loaded from global memory (16 bytes of bf16 or 32
+// bytes of float), converted to floats later.
+template <typename T>
+struct Raw8;
+template <>
+struct Raw8<__nv_bfloat16> {
+  uint4 u;
+  __device__ __forceinline__ void load(const __nv_bfloat16* src) { u = __ldg(reinterpret_cast<const uint4*>(src)); }
+  __device__ __forceinline__ void to_float(float (&x)[8]) const {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[2 * i] = __uint_as_float(w[i] << 16);
+      x[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+};
+template <>
+struct Raw8<float> {
+  float4 a, b;
+  __device__ __forceinline__ void load(const float* src) {
+    a = __ldg(reinterpret_cast<const float4*>(src));
+    b = __ldg(reinterpret_cast<const float4*>(src) + 1);
+  }
+  __device__ __forceinline__ void to_float(float (&x)[8]) const {
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+  }
+};
+
 // One row (8 channels starting at c) of the conv input at absolute position
 // pos for sequence b starting at `start`: the projection row, or the
 // sequence's conv state for positions before its start.
@@ -332,52 +362,66 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
   };
   reset(t0);
   const float qscale = 1.f / (float)p.dk, kscale = rsqrtf((float)p.dk);
-  for (int64_t t = t0; t < t_end; ++t) {
-    if (t >= s_end) {  // next (non-empty) sequence: fresh history from its conv state
-      do {
-        ++b;
-        seq_range(p.cu_seqlens, p.n_tokens, p.n_seqs, b, s_start, s_end);
-      } while (t >= s_end);
-      reset(t);
-    }
-    float cur[8];
-    load8<T>(static_cast<const T*>(p.mixed) + t * p.mixed_st + c, cur);
-    float x[8];
-    float ss = 0.f;
+  const T* src = static_cast<const T*>(p.mixed) + c;
+  // Rows t .. t+PF-1 are loaded before row t is used, so the loads run ahead
+  // of the arithmetic and the stores.
+  constexpr int PF = 4;
+  Raw8<T> ring[PF];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float acc = 0.f;
+  for (int u = 0; u < PF; ++u)
+    if (active && t0 + u < t_end) ring[u].load(src + (t0 + u) * p.mixed_st);
+  for (int64_t tb = t0; tb < t_end; tb += PF) {
 #pragma unroll
-      for (int j = 0; j < K - 1; ++j) acc += w[i][j] * win[j][i];
-      acc += w[i][K - 1] * cur[i];
-      x[i] = round_to<T>(silu_f(round_to<T>(acc)));
-      ss += x[i] * x[i];
-    }
-    // q/k rms-norm: reduce over the lanes of this head (all lanes shuffle).
+    for (int u = 0; u < PF; ++u) {
+      const int64_t t = tb + u;
+      if (t >= t_end) break;
+      if (t >= s_end) {  // next (non-empty) sequence: fresh history from its conv state
+        do {
+          ++b;
+          seq_range(p.cu_seqlens, p.n_tokens, p.n_seqs, b, s_start, s_end);
+        } while (t >= s_end);
+        reset(t);
+      }
+      float cur[8];
+      ring[u].to_float(cur);
+      if (active && t + PF < t_end) ring[u].load(src + (t + PF) * p.mixed_st);
+      float x[8];
+      float ss = 0.f;
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      const float o = __shfl_xor_sync(0xffffffffu, ss, off);
-      if (off < group) ss += o;
-    }
-    if (is_q || is_k) {
-      const float inv = rsqrtf(ss / (float)p.dk + 1e-6f);
-      const float scale = is_q ? qscale : kscale;
+      for (int i = 0; i < 8; ++i) {
+        float acc = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = round_to<T>(round_to<T>(x[i] * inv) * scale);
-      T* dst = static_cast<T*>(is_q ? p.q : p.k) + t * key_dim + (is_q ? c : c - key_dim);
-      if (active) store8<T>(dst, x);
-    } else {
-      T* dst = static_cast<T*>(p.v) + t * (int64_t)p.hv * p.dv + (c - 2 * key_dim);
-      if (active) store8<T>(dst, x);
-    }
-    // slide the history window
+        for (int j = 0; j < K - 1; ++j) acc += w[i][j] * win[j][i];
+        acc += w[i][K - 1] * cur[i];
+        x[i] = round_to<T>(silu_f(round_to<T>(acc)));
+        ss += x[i] * x[i];
+      }
+      // q/k rms-norm: reduce over the lanes of this head (all lanes shuffle).
 #pragma unroll
-    for (int j = 0; j + 1 < K - 1; ++j)
+      for (int off = 16; off >= 1; off >>= 1) {
+        const float o = __shfl_xor_sync(0xffffffffu, ss, off);
+        if (off < group) ss += o;
+      }
+      if (is_q || is_k) {
+        const float inv = rsqrtf(ss / (float)p.dk + 1e-6f);
+        const float scale = is_q ? qscale : kscale;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) win[j][i] = win[j + 1][i];
-    if constexpr (K > 1) {
+        for (int i = 0; i < 8; ++i) x[i] = round_to<T>(round_to<T>(x[i] * inv) * scale);
+        T* dst = static_cast<T*>(is_q ? p.q : p.k) + t * key_dim + (is_q ? c : c - key_dim);
+        if (active) store8<T>(dst, x);
+      } else {
+        T* dst = static_cast<T*>(p.v) + t * (int64_t)p.hv * p.dv + (c - 2 * key_dim);
+        if (active) store8<T>(dst, x);
+      }
+      // slide the history window
 #pragma unroll
-      for (int i = 0; i < 8; ++i) win[K - 2][i] = cur[i];
+      for (int j = 0; j + 1 < K - 1; ++j)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) win[j][i] = win[j + 1][i];
+      if constexpr (K > 1) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) win[K - 2][i] = cur[i];
+      }
     }
   }
 }

@@ -315,14 +315,17 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 64);
 
-  // Forward substitution: thread c < 64 owns column c of T = (I + A)^-1
-  // (four partial sums per row keep the FMA chain short).
-  if (tid < CH) {
-    const int c = tid;
-    float x[64];
+  // T = (I + A)^-1 by 2 x 2 blocks of 32: T11 = (I + A11)^-1 and
+  // T22 = (I + A22)^-1 by forward substitution (warp 0 / warp 1, one column
+  // per thread, four partial sums per row), then T21 = -T22 (A21 T11) on all
+  // four warps; T12 = 0.
+  if (warp < 2) {
+    const int off = warp * 32;  // block (off, off)
+    const int c = lane;
+    float x[32];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const float* arow = sA + i * kPrepAStride;
+    for (int i = 0; i < 32; ++i) {
+      const float* arow = sA + (off + i) * kPrepAStride + off;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int j = 0; j < i; ++j) acc[j & 3] = fmaf(arow[j], x[j], acc[j & 3]);
@@ -330,7 +333,41 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
       x[i] = i < c ? 0.f : (i == c ? 1.f : -sum);
     }
 #pragma unroll
-    for (int i = 0; i < 64; ++i) sT[i * kPrepAStride + c] = x[i];
+    for (int i = 0; i < 32; ++i) {
+      sT[(off + i) * kPrepAStride + off + c] = x[i];
+      sT[(off + i) * kPrepAStride + (32 - off) + c] = 0.f;  // T12 (and T21, overwritten below)
+    }
+  }
+  __syncthreads();
+  {  // M = A21 T11 into the (now unused) A11 block
+    const int i = tid >> 2, j0 = (tid & 3) * 8;
+    float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const float* arow = sA + (32 + i) * kPrepAStride;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float a = arow[k];
+      const float* trow = sT + k * kPrepAStride + j0;
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) m[jj] = fmaf(a, trow[jj], m[jj]);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) sA[i * kPrepAStride + j0 + jj] = m[jj];
+  }
+  __syncthreads();
+  {  // T21 = -T22 M
+    const int i = tid >> 2, j0 = (tid & 3) * 8;
+    float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const float* trow = sT + (32 + i) * kPrepAStride + 32;
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float tv = trow[k];
+      const float* mrow = sA + k * kPrepAStride + j0;
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) m[jj] = fmaf(tv, mrow[jj], m[jj]);
+    }
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) sT[(32 + i) * kPrepAStride + j0 + jj] = -m[jj];
   }
   __syncthreads();
   {
