@@ -8,6 +8,14 @@ one decode launch over the batch; ``value`` is the state HBM traffic
 prefill number of config 3 (T=8192) under ``"prefill"``.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload decode|varlen]
+
+``--workload varlen`` is config 5 instead: 64 packed sequences (lengths
+``default_rng(1).integers(256, 16384, 64, endpoint=True)``, 516,496 tokens)
+split across the ranks by longest-processing-time bin packing, one prefill
+over each rank's sequences followed by 256 decode steps; ``value`` is the
+prefill rate in tokens/s over all ranks (strong scaling: the total is fixed),
+and the decode phase is reported beside it.
 
 ``--impl reference`` times the reference's CPU path (its ops-path recurrence,
 restated on torch's CPU backend with every host thread; MLX is not
@@ -165,8 +173,25 @@ def dist_setup(args):
 
 
 def run_reference(args, world, rank):
-    """``--impl reference``: the reference's CPU path on the decode workload,
+    """``--impl reference``: the reference's CPU path on the same workload,
     rank 0 only (other ranks exit without work)."""
+    if rank == 0 and args.workload == "varlen":
+        cores = os.cpu_count() or 1
+        rates = [cpu_prefill_sample() for _ in range(args.warmup + args.steps)][args.warmup:]
+        value = statistics.mean(rates)
+        line = {
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 512 / value * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, config 5)",
+            "config": {"workload": "config 5 prefill, sampled: 512 tokens of one sequence per step",
+                       "global_batch": 1, "seq_len": 512, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                             "sample": "512 tokens of one config-5 sequence per step (torch-CPU restatement of the "
+                                       "reference's ops path; MLX unavailable on this box)"},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
     if rank == 0:
         cores = os.cpu_count() or 1
         torch.set_num_threads(cores)
@@ -265,6 +290,120 @@ def measure_block(device, iters=3):
     return statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(iters)), Bb * T
 
 
+def cpu_prefill_sample(n_tokens=512):
+    """The reference's CPU path on the first ``n_tokens`` tokens of config 5's
+    first sequence (all host threads); returns tokens/s."""
+    from oracle.gdn_torch_cpu import gated_delta_scan_ops
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(5)
+    q = torch.nn.functional.normalize(torch.randn(n_tokens, HK, D, generator=g), dim=-1).bfloat16().float()
+    k = torch.nn.functional.normalize(torch.randn(n_tokens, HK, D, generator=g), dim=-1).bfloat16().float()
+    v = torch.randn(n_tokens, HV, D, generator=g).bfloat16().float()
+    beta = torch.sigmoid(torch.randn(n_tokens, HV, generator=g))
+    gm = torch.exp(-torch.nn.functional.softplus(torch.randn(n_tokens, HV, generator=g)))
+    s0 = torch.randn(HV, D, D, generator=g) * 0.02
+    t0 = time.perf_counter()
+    gated_delta_scan_ops(q, k, v, gm, beta, s0)
+    return n_tokens / (time.perf_counter() - t0)
+
+
+def run_varlen(args, world, rank, local):
+    """Config 5 on this rank's share of the sequences (see module docstring)."""
+    import gdn_b200
+    from gdn_b200.sharding import lpt_partition
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    lengths = np.random.default_rng(1).integers(256, 16384, size=64, endpoint=True)
+    mine = lpt_partition(lengths, world)[rank]
+    my_len = [int(lengths[i]) for i in mine]
+    n_loc = len(my_len)
+    n_tok = int(sum(my_len))
+    gen = torch.Generator(device).manual_seed(100 + rank)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(my_len)]), dtype=torch.int64, device=device)
+    q = torch.nn.functional.normalize(torch.randn(n_tok, HK, D, device=device, generator=gen), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(n_tok, HK, D, device=device, generator=gen), dim=-1).bfloat16()
+    v = torch.randn(n_tok, HV, D, device=device, generator=gen).bfloat16()
+    beta = torch.sigmoid(torch.randn(n_tok, HV, device=device, generator=gen))
+    g_log = -torch.nn.functional.softplus(torch.randn(n_tok, HV, device=device, generator=gen))
+    s_init = torch.randn(max(n_loc, 1), HV, D, D, device=device, generator=gen) * 0.02
+    state = torch.empty_like(s_init)
+    out = torch.empty(n_tok, HV, D, device=device)
+    dq = torch.nn.functional.normalize(torch.randn(4, max(n_loc, 1), HK, D, device=device, generator=gen), dim=-1).bfloat16()
+    dk = torch.nn.functional.normalize(torch.randn(4, max(n_loc, 1), HK, D, device=device, generator=gen), dim=-1).bfloat16()
+    dv = torch.randn(4, max(n_loc, 1), HV, D, device=device, generator=gen).bfloat16()
+    db = torch.sigmoid(torch.randn(4, max(n_loc, 1), HV, device=device, generator=gen))
+    dg = -torch.nn.functional.softplus(torch.randn(4, max(n_loc, 1), HV, device=device, generator=gen))
+    dout = torch.empty(max(n_loc, 1), HV, D, device=device)
+    n_decode = 256
+
+    def prefill():
+        state.copy_(s_init)
+        if n_loc:
+            gdn_b200.gated_delta_scan_varlen(q, k, v, g_log, beta, state, cu, g_is_log=True, state_out=state,
+                                             out=out)
+
+    def decode():
+        for i in range(n_decode):
+            if n_loc:
+                gdn_b200.gated_delta_decode(dq[i % 4, :n_loc], dk[i % 4, :n_loc], dv[i % 4, :n_loc],
+                                            dg[i % 4, :n_loc], db[i % 4, :n_loc], state[:n_loc], g_is_log=True,
+                                            out=dout[:n_loc])
+
+    for _ in range(args.warmup):
+        prefill()
+        decode()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    pf_ms, dec_ms = 0.0, 0.0
+    sampler = ClockSampler(local)
+    with sampler:
+        for _ in range(args.steps):
+            ev[0].record()
+            prefill()
+            ev[1].record()
+            decode()
+            ev[2].record()
+            torch.cuda.synchronize()
+            pf_ms += ev[0].elapsed_time(ev[1])
+            dec_ms += ev[1].elapsed_time(ev[2])
+    if world > 1:
+        t = torch.tensor([pf_ms, dec_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        pf_ms, dec_ms = float(t[0]), float(t[1])
+        torch.distributed.barrier()
+    total_tok = int(lengths.sum())
+    dec_bytes = n_decode * (2 * 64 * HV * D * D * 4)  # state read + write of all 64 sequences per step
+    hbm_peak, tc_peak, peak_kind = peaks()
+    pf_s = pf_ms / 1e3 / args.steps
+    line = {
+        "metric": METRIC, "value": total_tok / pf_s, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": (pf_ms + dec_ms) / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32 state / bf16 q,k,v",
+        "data": "synthetic (seeded; config 5 lengths and value distributions)",
+        "config": {"workload": "config 5: 64 packed sequences, 516,496 tokens, LPT-sharded by sequence; prefill "
+                               "then 256 decode steps per sequence, no cross-GPU exchange",
+                   "global_batch": 64, "seq_len": "256..16384 (packed)", "parallelism": f"sequence-sharded x{world}",
+                   "l2": "inputs (4.2 GB of q/k/v) far larger than L2"},
+        "prefill": {"ms": pf_ms / args.steps, "achieved_tflops": PREFILL_FLOP / PREFILL_T * total_tok / pf_s / 1e12,
+                    "frac_of_bf16_peak": PREFILL_FLOP / PREFILL_T * total_tok / pf_s / 1e12 / tc_peak},
+        "decode": {"value": dec_bytes / (dec_ms / 1e3 / args.steps) / 1e9, "unit": "GB/s", "steps": n_decode,
+                   "ms": dec_ms / args.steps, "peak": hbm_peak, "peak_kind": peak_kind},
+        "clocks": sampler.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = {"value": cpu_prefill_sample(), "unit": "tok/s", "cores": os.cpu_count() or 1,
+                                "kind": "port", "sample": "first 512 tokens of one config-5 sequence (torch-CPU "
+                                "restatement of the reference's ops path, all threads); MLX CPU unavailable"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -274,11 +413,14 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="decode only: no e2e, prefill or CPU legs (for profiler runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiler runs)")
+    ap.add_argument("--workload", choices=["decode", "varlen"], default="decode")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)
+    if args.workload == "varlen":
+        return run_varlen(args, world, rank, local)
 
     import gdn_b200
 
