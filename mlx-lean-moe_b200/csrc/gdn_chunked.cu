@@ -24,18 +24,18 @@
 //    loads (TMA tensor loads of K, Q, V; bulk copies of T, P and the gates),
 //    warp 1 issues the MMAs, warps 2-9 run the state-chain epilogues (two
 //    per TMEM lane quarter: each thread owns one state row and half of its
-//    columns), warps 10-13 build Kd^T and write the output, off the chain.  Per
+//    columns), warps 10-13 transpose K and write the output, off the chain.  Per
 //    chunk, in the transposed orientation (M = Dv state rows):
 //      [X | Y] = S [K | Q]^T       (N = 128, K = Dk)    2 passes (S hi, lo)
 //      Delta^T = R^T T^T           (N = 128 + 64, K = C) R_hi [T_hi; T_lo]^T + R_lo T_hi^T
-//      U       = Delta^T Kd        (N = 128, K = C)     3 passes, Kd = diag(exp(G_last - G)) K
+//      U       = Delta'^T K        (N = 128, K = C)     2 passes, Delta' = Delta diag(exp(G_last - G))
 //      O^T     = Delta^T P^T       (N = 128 + 64, K = C) as Delta
 //    (an M = 128 MMA costs about the same for N = 64 and N = 128, so the
 //    hi*lo term rides along as the second half of a 128-wide product).
 //    then S <- gamma S + U (the chain into the next chunk) and, off that
 //    chain, y = exp(G) Y + O.  Delta reuses the S lo operand buffer, which is
 //    dead between the X/Y MMAs and the state update.
-//  Operands that are not exact in bf16 (S, R, T, Delta, P, Kd) are split into
+//  Operands that are not exact in bf16 (S, R, T, Delta, Delta', P) are split into
 //  bf16 hi + lo parts; the products then carry ~16 mantissa bits (rel-L2
 //  ~5e-6 against the float64 recurrence at T = 4096, versus ~3e-3 with plain
 //  bf16 operands and ~4e-4 with tf32).
@@ -399,12 +399,12 @@ constexpr uint32_t OFF_P = 131072;                 // P hi, P lo
 // Output staging for the TMA store: [64 t][128 dv] in the output dtype, in
 // the T and P tiles (dead once the Delta and O MMAs of the chunk are done).
 constexpr uint32_t OFF_OSTAGE = OFF_T;
-constexpr uint32_t OFF_KT = 147456;                // Kd^T hi, lo: 128 (dk) x 64 (t) each
-constexpr uint32_t OFF_GATES = 180224;             // two 1 KB gate buffers (chunk parity)
+constexpr uint32_t OFF_KT = 147456;                // K^T: 128 (dk) x 64 (t), exact in bf16
+constexpr uint32_t OFF_GATES = OFF_KT + 16384;     // two 1 KB gate buffers (chunk parity)
 constexpr uint32_t SCAN_SMEM_USED = OFF_GATES + 2 * kGateBytes;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
 constexpr int kEpiThreads = 256;                   // warps 2-9: the state chain
-constexpr int kAuxThreads = 128;                   // warps 10-13: Kd^T and the output
+constexpr int kAuxThreads = 128;                   // warps 10-13: K^T and the output
 
 // TMEM columns.
 // The state update accumulates straight onto S (S is scaled by gamma in TMEM
@@ -416,6 +416,9 @@ constexpr int kAuxThreads = 128;                   // warps 10-13: Kd^T and the 
 constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y = 192, TM_D = 256, TM_O = 384;
 constexpr uint32_t TM_RHI = TM_X, TM_RLO = TM_X + 32;   // 64 tokens -> 32 packed columns each
 constexpr uint32_t TM_DHI = TM_D, TM_DLO = TM_D + 32;
+// Delta' = Delta diag(exp(G_last - G)) for the state update, in the second
+// half of the Delta region (its hi*lo accumulator part is read first).
+constexpr uint32_t TM_DPHI = TM_D + 64, TM_DPLO = TM_D + 96;
 
 enum Bar {
   B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_P_FULL,
@@ -515,9 +518,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       const uint32_t sT[2] = {smem_u32(base + OFF_T), smem_u32(base + OFF_T + kTile64)};
       const uint32_t sP[2] = {smem_u32(base + OFF_P), smem_u32(base + OFF_P + kTile64)};
       const uint32_t tD[2] = {tmem + TM_DHI, tmem + TM_DLO};
-      const uint32_t sKt[2] = {smem_u32(base + OFF_KT), smem_u32(base + OFF_KT + 16384)};
-      // (a part, b part) of the three-pass split products hi*hi + hi*lo + lo*hi
-      const int pa[3] = {0, 0, 1}, pb[3] = {0, 1, 0};
+      const uint32_t sKt = smem_u32(base + OFF_KT);
       for (int64_t c = 0; c < nch; ++c) {
         const uint32_t par = (uint32_t)(c & 1);
         if (!mbar_wait(&bars[B_KQ_FULL], par, kWaitNs) || !mbar_wait(&bars[B_S_READY], par, kWaitNs)) {
@@ -563,10 +564,11 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         }
         if (abort_flag) break;
         tc_fence_after();
-        {  // S <- (gamma S) + Delta^T Kd   (state chain first), Delta from TMEM
-          for (int pass = 0; pass < 3; ++pass)
+        {  // S <- (gamma S) + Delta'^T K   (state chain first), Delta' from TMEM, K exact
+          const uint32_t tDP[2] = {tmem + TM_DPHI, tmem + TM_DPLO};
+          for (int part = 0; part < 2; ++part)
             for (int ks = 0; ks < 4; ++ks)
-              mma_bf16_ts(tmem + TM_S, tD[pa[pass]] + ks * 8, sdesc_sw128(sKt[pb[pass]] + ks * 32), id128, true);
+              mma_bf16_ts(tmem + TM_S, tDP[part] + ks * 8, sdesc_sw128(sKt + ks * 32), id128, true);
         }
         mma_commit(&bars[B_U_DONE]);
         if (!mbar_wait(&bars[B_P_FULL], par, kWaitNs)) {
@@ -698,12 +700,24 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) x[i] += x2[i];
-        uint32_t hi[16], lo[16];
-        split32_packed(x, hi, lo);
-        // Delta hi/lo overwrite the accumulator in place: read it all first.
+        // Delta and Delta' hi/lo overwrite the accumulator in place: read it all first.
         named_sync(1, kEpiThreads);
-        tmem_st16(tq + TM_DHI + half * 16, hi);
-        tmem_st16(tq + TM_DLO + half * 16, lo);
+        {
+          uint32_t hi[16], lo[16];
+          split32_packed(x, hi, lo);
+          tmem_st16(tq + TM_DHI + half * 16, hi);
+          tmem_st16(tq + TM_DLO + half * 16, lo);
+        }
+        {
+          float dg[32];
+          load_gate32(gates + GATE_DG + half * 32, dg);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) x[i] *= dg[i];
+          uint32_t hi[16], lo[16];
+          split32_packed(x, hi, lo);
+          tmem_st16(tq + TM_DPHI + half * 16, hi);
+          tmem_st16(tq + TM_DPLO + half * 16, lo);
+        }
         tmem_wait_st();
       }
       tc_fence_before();
@@ -752,7 +766,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       }
     }
   } else {
-    // ------------------------------------------------- Kd^T and output (aux)
+    // ------------------------------------------------- K^T and output (aux)
     const int e = tid - 320;                  // 0..127 (warps 10-13)
     const int q = warp & 3;                   // TMEM lane quarter of this warp
     const int dv = q * 32 + lane;             // output row (value dim)
@@ -765,32 +779,26 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       const int n = (int)(end - t0 < CH ? end - t0 : CH);
       const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
 
-      // Kd^T = (diag(exp(G_last - G)) K)^T as bf16 hi/lo, row dk = e, all 64 tokens.
+      // K^T (exact bf16 transpose), row dk = e, all 64 tokens.
       bool ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(2, kAuxThreads, !ok)) break;
       {
         const int dk = e;
         const int kb = dk >> 6, cc = (dk & 63) >> 3, wi = dk & 7;
-        for (int th = 0; th < 2; ++th) {
-          float dg[32];
-          load_gate32(gates + GATE_DG + th * 32, dg);
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            float x[8];
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int t = th * 32 + c8 * 8 + i;
-              const unsigned short kbits =
-                  *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, t, kb, cc) + wi * 2);
-              x[i] = __uint_as_float((uint32_t)kbits << 16) * dg[c8 * 8 + i];
-            }
-            uint4 hi, lo;
-            split8(x, hi, lo);
-            const int cidx = th * 4 + c8;
-            *reinterpret_cast<uint4*>(sm + OFF_KT + sw128_chunk(128, dk, 0, cidx)) = hi;
-            *reinterpret_cast<uint4*>(sm + OFF_KT + 16384 + sw128_chunk(128, dk, 0, cidx)) = lo;
+          for (int i = 0; i < 4; ++i) {
+            const int ta = c8 * 8 + 2 * i, tb = ta + 1;
+            const uint32_t lo_b =
+                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, ta, kb, cc) + wi * 2);
+            const uint32_t hi_b =
+                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, tb, kb, cc) + wi * 2);
+            w[i] = lo_b | (hi_b << 16);
           }
+          *reinterpret_cast<uint4*>(sm + OFF_KT + sw128_chunk(128, dk, 0, c8)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
       fence_async_smem();

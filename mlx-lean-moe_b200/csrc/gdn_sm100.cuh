@@ -242,6 +242,13 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&u)[16
       : "memory");
 }
 
+// 32 lanes x 8 columns of 32-bit TMEM <- 8 registers per thread.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* u) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(u[0]),
+               "r"(u[1]), "r"(u[2]), "r"(u[3]), "r"(u[4]), "r"(u[5]), "r"(u[6]), "r"(u[7])
+               : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]^T: A packed bf16 in TMEM (lane = row, column
 // j holds K elements 2j (low half) and 2j + 1), B a K-major bf16 smem tile.
 __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
