@@ -422,7 +422,7 @@ constexpr uint32_t TM_DPHI = TM_D + 64, TM_DPLO = TM_D + 96;
 
 enum Bar {
   B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_P_FULL,
-  B_S_READY, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_O_FREE, B_OSTAGE_FREE,
+  B_S_READY0, B_S_READY1, B_X_DONE, B_R_READY0, B_R_READY1, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_Y_FREE, B_O_FREE, B_OSTAGE_FREE,
   B_DRAIN,
   N_BARS
 };
@@ -521,41 +521,57 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       const uint32_t sKt = smem_u32(base + OFF_KT);
       for (int64_t c = 0; c < nch; ++c) {
         const uint32_t par = (uint32_t)(c & 1);
-        if (!mbar_wait(&bars[B_KQ_FULL], par, kWaitNs) || !mbar_wait(&bars[B_S_READY], par, kWaitNs)) {
+        // [X | Y] = S [K | Q]^T, one K-block (64 of Dk) at a time as the
+        // epilogue finishes converting it; Y is free to overwrite once the
+        // output warps have read the previous chunk's.
+        if (!mbar_wait(&bars[B_KQ_FULL], par, kWaitNs) ||
+            (c > 0 && !mbar_wait(&bars[B_Y_FREE], (uint32_t)((c - 1) & 1), kWaitNs))) {
           record_error(&abort_flag);
           break;
         }
-        if (abort_flag) break;
-        tc_fence_after();
-        // [X | Y] = S [K | Q]^T; Y is free to overwrite once the previous
-        // chunk's output stage has read it.
-        if (c > 0 && !mbar_wait(&bars[B_O_FREE], (uint32_t)((c - 1) & 1), kWaitNs)) {
-          record_error(&abort_flag);
-          break;
-        }
-        if (abort_flag) break;
-        tc_fence_after();
         {
+          bool stop = false;
           int n = 0;
-          for (int part = 0; part < 2; ++part)
-            for (int kb = 0; kb < 2; ++kb)
+          for (int kb = 0; kb < 2; ++kb) {
+            if (!mbar_wait(&bars[kb == 0 ? B_S_READY0 : B_S_READY1], par, kWaitNs)) {
+              record_error(&abort_flag);
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            for (int part = 0; part < 2; ++part)
               for (int ks = 0; ks < 4; ++ks, ++n)
                 mma_bf16(tmem + TM_X, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
                          sdesc_sw128(sK + kb * 16384 + ks * 32), id128, n > 0);
+          }
+          if (stop || abort_flag) break;
         }
         mma_commit(&bars[B_X_DONE]);
         mma_commit(&bars[B_KQ_EMPTY]);
-        if (!mbar_wait(&bars[B_R_READY], par, kWaitNs) || !mbar_wait(&bars[B_T_FULL], par, kWaitNs)) {
+        // Delta^T = R_hi [T_hi; T_lo]^T (N = 128) + R_lo T_hi^T (N = 64), R from
+        // TMEM: K steps {0, 2} (tokens 0-15, 32-47) once the first half of R is
+        // in, then {1, 3}.
+        if (!mbar_wait(&bars[B_T_FULL], par, kWaitNs)) {
           record_error(&abort_flag);
           break;
         }
-        if (abort_flag) break;
-        tc_fence_after();
-        {  // Delta^T = R_hi [T_hi; T_lo]^T (N = 128) + R_lo T_hi^T (N = 64), R from TMEM
-          for (int ks = 0; ks < 4; ++ks)
-            mma_bf16_ts(tmem + TM_D, tmem + TM_RHI + ks * 8, sdesc_sw128(sT[0] + ks * 32), id128, ks > 0);
-          for (int ks = 0; ks < 4; ++ks)
-            mma_bf16_ts(tmem + TM_D, tmem + TM_RLO + ks * 8, sdesc_sw128(sT[0] + ks * 32), id64, true);
+        {
+          bool stop = false;
+          for (int rh = 0; rh < 2; ++rh) {
+            if (!mbar_wait(&bars[rh == 0 ? B_R_READY0 : B_R_READY1], par, kWaitNs)) {
+              record_error(&abort_flag);
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            for (int kk = 0; kk < 2; ++kk) {
+              const int ks = rh + 2 * kk;
+              mma_bf16_ts(tmem + TM_D, tmem + TM_RHI + ks * 8, sdesc_sw128(sT[0] + ks * 32), id128,
+                          !(rh == 0 && kk == 0));
+              mma_bf16_ts(tmem + TM_D, tmem + TM_RLO + ks * 8, sdesc_sw128(sT[0] + ks * 32), id64, true);
+            }
+          }
+          if (stop || abort_flag) break;
         }
         mma_commit(&bars[B_D_DONE]);
         if (!mbar_wait(&bars[B_DD_READY], par, kWaitNs) || !mbar_wait(&bars[B_KT_READY], par, kWaitNs)) {
@@ -571,7 +587,8 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
               mma_bf16_ts(tmem + TM_S, tDP[part] + ks * 8, sdesc_sw128(sKt + ks * 32), id128, true);
         }
         mma_commit(&bars[B_U_DONE]);
-        if (!mbar_wait(&bars[B_P_FULL], par, kWaitNs)) {
+        if (!mbar_wait(&bars[B_P_FULL], par, kWaitNs) ||
+            (c > 0 && !mbar_wait(&bars[B_O_FREE], (uint32_t)((c - 1) & 1), kWaitNs))) {
           record_error(&abort_flag);
           break;
         }
@@ -599,35 +616,34 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     const bool leader = e == 0;
     unsigned char* sm = base;
 
-    // S_0 -> TMEM and its bf16 hi/lo operand (columns 64*half .. +64).
-    {
+    // S_0 -> TMEM and its bf16 hi/lo operand, one K-block per pass (columns
+    // 64*kb + 32*half .. +32 of row dv in pass kb).
+    for (int kb = 0; kb < 2; ++kb) {
+      const int col = kb * 64 + half * 32;
       const float* srow = p.state_in ? p.state_in + head_off + (size_t)dv * DH : nullptr;
-      for (int cc = 0; cc < 2; ++cc) {
-        const int col = half * 64 + cc * 32;
-        float x[32];
+      float x[32];
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 v4 = srow ? *reinterpret_cast<const float4*>(srow + col + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-          x[i] = v4.x;
-          x[i + 1] = v4.y;
-          x[i + 2] = v4.z;
-          x[i + 3] = v4.w;
-        }
-        tmem_st32(tq + TM_S + col, x);
+      for (int i = 0; i < 32; i += 4) {
+        const float4 v4 = srow ? *reinterpret_cast<const float4*>(srow + col + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x[i] = v4.x;
+        x[i + 1] = v4.y;
+        x[i + 2] = v4.z;
+        x[i + 3] = v4.w;
+      }
+      tmem_st32(tq + TM_S + col, x);
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint4 hi, lo;
-          split8(x + 8 * c4, hi, lo);
-          const int cidx = cc * 4 + c4;
-          *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, half, cidx)) = hi;
-          *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, half, cidx)) = lo;
-        }
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint4 hi, lo;
+        split8(x + 8 * c4, hi, lo);
+        const int cidx = half * 4 + c4;
+        *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, kb, cidx)) = hi;
+        *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, kb, cidx)) = lo;
       }
       tmem_wait_st();
       fence_async_smem();
       tc_fence_before();
       named_sync(1, kEpiThreads);
-      if (leader) mbar_arrive(&bars[B_S_READY]);
+      if (leader) mbar_arrive(&bars[kb == 0 ? B_S_READY0 : B_S_READY1]);
     }
 
     for (int64_t c = 0; c < nch; ++c) {
@@ -649,28 +665,39 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         float x[32];
         tmem_ld32(tq + TM_X + half * 32, x);
         tmem_wait_ld();
-        float bt[32], eg[32];
-        load_gate32(gates + GATE_BETA + half * 32, bt);
-        load_gate32(gates + GATE_EG + half * 32, eg);
+        // Tokens 32*half + [0, 16) first (K steps 0 and 2 of the Delta MMA),
+        // then 32*half + [16, 32).
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int t = half * 32 + i;
-          x[i] = bt[i] * (__bfloat162float(V[t * DH + dv]) - x[i] * eg[i]);
+        for (int rh = 0; rh < 2; ++rh) {
+          float r16[16];
+#pragma unroll
+          for (int i4 = 0; i4 < 16; i4 += 4) {
+            const int j = rh * 16 + i4;
+            const float4 b4 = *reinterpret_cast<const float4*>(gates + GATE_BETA + half * 32 + j);
+            const float4 e4 = *reinterpret_cast<const float4*>(gates + GATE_EG + half * 32 + j);
+            const int t = half * 32 + j;
+            r16[i4] = b4.x * (__bfloat162float(V[t * DH + dv]) - x[j] * e4.x);
+            r16[i4 + 1] = b4.y * (__bfloat162float(V[(t + 1) * DH + dv]) - x[j + 1] * e4.y);
+            r16[i4 + 2] = b4.z * (__bfloat162float(V[(t + 2) * DH + dv]) - x[j + 2] * e4.z);
+            r16[i4 + 3] = b4.w * (__bfloat162float(V[(t + 3) * DH + dv]) - x[j + 3] * e4.w);
+          }
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            hi[j] = pack_bf16(r16[2 * j], r16[2 * j + 1]);
+            lo[j] = pack_bf16(r16[2 * j] - bf16_lo_f(hi[j]), r16[2 * j + 1] - bf16_hi_f(hi[j]));
+          }
+          // R hi/lo overwrite X in place: every X column must be read first.
+          if (rh == 0) named_sync(1, kEpiThreads);
+          tmem_st8(tq + TM_RHI + half * 16 + rh * 8, hi);
+          tmem_st8(tq + TM_RLO + half * 16 + rh * 8, lo);
+          tmem_wait_st();
+          tc_fence_before();
+          named_sync(1, kEpiThreads);
+          if (leader) mbar_arrive(&bars[rh == 0 ? B_R_READY0 : B_R_READY1]);
         }
-        uint32_t hi[16], lo[16];
-        split32_packed(x, hi, lo);
-        // R hi/lo overwrite X in place: every X column must be read first.
-        named_sync(1, kEpiThreads);
-        tmem_st16(tq + TM_RHI + half * 16, hi);
-        tmem_st16(tq + TM_RLO + half * 16, lo);
-        tmem_wait_st();
       }
-      tc_fence_before();
-      named_sync(1, kEpiThreads);
-      if (leader) {
-        mbar_arrive(&bars[B_R_READY]);
-        mbar_arrive(&bars[B_V_EMPTY]);
-      }
+      if (leader) mbar_arrive(&bars[B_V_EMPTY]);
 
       // While the Delta MMA runs: S <- gamma S in TMEM (the state update MMA
       // then accumulates onto it).  Ordered before the U MMA by DD_READY.
@@ -724,31 +751,30 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       named_sync(1, kEpiThreads);
       if (leader) mbar_arrive(&bars[B_DD_READY]);
 
-      // The updated S -> its hi/lo operand for the next chunk.
+      // The updated S -> its hi/lo operand for the next chunk, one K-block per
+      // pass so that the next X/Y MMA can start on the first.
       ok = mbar_wait(&bars[B_U_DONE], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
-      {
-        for (int cc = 0; cc < 2; ++cc) {
-          const int col = half * 64 + cc * 32;
-          float sv[32];
-          tmem_ld32(tq + TM_S + col, sv);
-          tmem_wait_ld();
+      for (int kb = 0; kb < 2; ++kb) {
+        const int col = kb * 64 + half * 32;
+        float sv[32];
+        tmem_ld32(tq + TM_S + col, sv);
+        tmem_wait_ld();
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            uint4 hi, lo;
-            split8(sv + 8 * c4, hi, lo);
-            const int cidx = cc * 4 + c4;
-            *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, half, cidx)) = hi;
-            *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, half, cidx)) = lo;
-          }
+        for (int c4 = 0; c4 < 4; ++c4) {
+          uint4 hi, lo;
+          split8(sv + 8 * c4, hi, lo);
+          const int cidx = half * 4 + c4;
+          *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, kb, cidx)) = hi;
+          *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, kb, cidx)) = lo;
         }
+        fence_async_smem();
+        tc_fence_before();
+        named_sync(1, kEpiThreads);
+        if (leader) mbar_arrive(&bars[kb == 0 ? B_S_READY0 : B_S_READY1]);
       }
-      fence_async_smem();
-      tc_fence_before();
-      named_sync(1, kEpiThreads);
-      if (leader) mbar_arrive(&bars[B_S_READY]);
     }
 
     // Final state (or the initial one for an empty sequence) -> state_out.
@@ -779,26 +805,20 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       const int n = (int)(end - t0 < CH ? end - t0 : CH);
       const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
 
-      // K^T (exact bf16 transpose), row dk = e, all 64 tokens.
+      // K^T (exact bf16 transpose) by 8x8 blocks: 128 blocks of (8 tokens x
+      // 8 dk), four per ldmatrix/stmatrix pair, eight pairs per warp.
       bool ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(2, kAuxThreads, !ok)) break;
       {
-        const int dk = e;
-        const int kb = dk >> 6, cc = (dk & 63) >> 3, wi = dk & 7;
+        const int r = lane & 7, m = lane >> 3;
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          uint32_t w[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int ta = c8 * 8 + 2 * i, tb = ta + 1;
-            const uint32_t lo_b =
-                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, ta, kb, cc) + wi * 2);
-            const uint32_t hi_b =
-                *reinterpret_cast<const unsigned short*>(sm + OFF_KQ + sw128_chunk(128, tb, kb, cc) + wi * 2);
-            w[i] = lo_b | (hi_b << 16);
-          }
-          *reinterpret_cast<uint4*>(sm + OFF_KT + sw128_chunk(128, dk, 0, c8)) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int it = 0; it < 8; ++it) {
+          const int bi = ((e >> 5) * 8 + it) * 4 + m;  // 0..127
+          const int cidx = bi >> 3, tb = bi & 7;      // dk chunk (0..15), token block
+          uint32_t f[4];
+          ldmatrix_x4_trans(smem_u32(sm + OFF_KQ + sw128_chunk(128, tb * 8 + r, cidx >> 3, cidx & 7)), f);
+          stmatrix_x4(smem_u32(sm + OFF_KT + sw128_chunk(128, cidx * 8 + r, 0, tb)), f);
         }
       }
       fence_async_smem();
@@ -808,34 +828,42 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         mbar_arrive(&bars[B_KQ_EMPTY]);
       }
 
-      // Output: y_t = exp(G_t) Y_t + O_t for row dv, all tokens of the chunk.
+      // y = exp(G) Y for all 64 tokens of row dv, read out of TMEM as soon as
+      // the X/Y MMA is done so that the next chunk's can start early.
+      ok = mbar_wait(&bars[B_X_DONE], par, kWaitNs);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(2, kAuxThreads, !ok)) break;
+      tc_fence_after();
+      float y[64];
+      tmem_ld32(tq + TM_Y, *reinterpret_cast<float(*)[32]>(y));
+      tmem_ld32(tq + TM_Y + 32, *reinterpret_cast<float(*)[32]>(y + 32));
+      tmem_wait_ld();
+      tc_fence_before();
+      named_sync(2, kAuxThreads);
+      if (leader) mbar_arrive(&bars[B_Y_FREE]);
+#pragma unroll
+      for (int i = 0; i < 64; i += 4) {
+        const float4 g4 = *reinterpret_cast<const float4*>(gates + GATE_EG + i);
+        y[i] *= g4.x;
+        y[i + 1] *= g4.y;
+        y[i + 2] *= g4.z;
+        y[i + 3] *= g4.w;
+      }
+
+      // Output: y_t += O_t (both accumulator parts), then store.
       ok = mbar_wait(&bars[B_OU_DONE], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(2, kAuxThreads, !ok)) break;
       tc_fence_after();
       {
-        // y = exp(G) Y + O for all 64 tokens of row dv, read out of TMEM
-        // before O_FREE lets the next chunk's Y and O MMAs overwrite them.
-        float y[64];
-        tmem_ld32(tq + TM_Y, *reinterpret_cast<float(*)[32]>(y));
-        tmem_ld32(tq + TM_Y + 32, *reinterpret_cast<float(*)[32]>(y + 32));
-        tmem_wait_ld();
-        for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+        for (int hh = 0; hh < 4; ++hh) {
           float o[32];
           tmem_ld32(tq + TM_O + hh * 32, o);
           tmem_wait_ld();
+          const int yb = (hh & 1) * 32;
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            const float4 g4 = *reinterpret_cast<const float4*>(gates + GATE_EG + hh * 32 + i);
-            y[hh * 32 + i] = fmaf(y[hh * 32 + i], g4.x, o[i]);
-            y[hh * 32 + i + 1] = fmaf(y[hh * 32 + i + 1], g4.y, o[i + 1]);
-            y[hh * 32 + i + 2] = fmaf(y[hh * 32 + i + 2], g4.z, o[i + 2]);
-            y[hh * 32 + i + 3] = fmaf(y[hh * 32 + i + 3], g4.w, o[i + 3]);
-          }
-          tmem_ld32(tq + TM_O + 64 + hh * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) y[hh * 32 + i] += o[i];
+          for (int i = 0; i < 32; ++i) y[yb + i] += o[i];
         }
         tc_fence_before();
         named_sync(2, kAuxThreads);

@@ -249,6 +249,25 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* u) {
                : "memory");
 }
 
+// Four 8x8 b16 matrices, transposed on the way in: lanes 8m..8m+7 give the
+// row addresses (16 B each) of matrix m; lane l gets, in r[m], elements
+// [l/4][2(l%4)], [l/4][2(l%4)+1] of matrix m's transpose.
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t saddr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr)
+               : "memory");
+}
+
+// The inverse placement of ldmatrix (no transpose): r[m] of lane l holds
+// elements [l/4][2(l%4)..+1] of matrix m, whose rows go to the addresses
+// given by lanes 8m..8m+7.
+__device__ __forceinline__ void stmatrix_x4(uint32_t saddr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(saddr), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3])
+               : "memory");
+}
+
 // D[tmem] (+)= A[tmem] * B[smem]^T: A packed bf16 in TMEM (lane = row, column
 // j holds K elements 2j (low half) and 2j + 1), B a K-major bf16 smem tile.
 __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
