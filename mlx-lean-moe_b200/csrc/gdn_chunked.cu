@@ -396,12 +396,13 @@ constexpr uint32_t OFF_KQ = 65536;                 // [K;Q]: 128 x 128, two K-bl
 constexpr uint32_t OFF_V = 98304;                  // V: [64][128] bf16 row-major
 constexpr uint32_t OFF_T = 114688;                 // T hi, T lo: 64 x 64 each
 constexpr uint32_t OFF_P = 131072;                 // P hi, P lo
-// Output staging for the TMA store: [64 t][128 dv] in the output dtype, in
-// the T and P tiles (dead once the Delta and O MMAs of the chunk are done).
-constexpr uint32_t OFF_OSTAGE = OFF_T;
 constexpr uint32_t OFF_KT = 147456;                // K^T: 128 (dk) x 64 (t), exact in bf16
 constexpr uint32_t OFF_GATES = OFF_KT + 16384;     // two 1 KB gate buffers (chunk parity)
-constexpr uint32_t SCAN_SMEM_USED = OFF_GATES + 2 * kGateBytes;
+// Output staging for the TMA store: [64 t][128 dv] in the output dtype (its
+// own buffer, so that the next chunk's T and P loads need not wait for the
+// store to drain).
+constexpr uint32_t OFF_OSTAGE = OFF_GATES + 2 * kGateBytes;
+constexpr uint32_t SCAN_SMEM_USED = OFF_OSTAGE + 64 * DH * 4;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
 constexpr int kEpiThreads = 256;                   // warps 2-9: the state chain
 constexpr int kAuxThreads = 128;                   // warps 10-13: K^T and the output
@@ -422,7 +423,7 @@ constexpr uint32_t TM_DPHI = TM_D + 64, TM_DPLO = TM_D + 96;
 
 enum Bar {
   B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_P_FULL,
-  B_S_READY0, B_S_READY1, B_X_DONE, B_R_READY0, B_R_READY1, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_Y_FREE, B_O_FREE, B_OSTAGE_FREE,
+  B_S_READY0, B_S_READY1, B_X_DONE, B_R_READY0, B_R_READY1, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_Y_FREE, B_O_FREE, B_T_EMPTY, B_P_EMPTY,
   B_DRAIN,
   N_BARS
 };
@@ -489,12 +490,14 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
         tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
         ++n_v;
-        // T and P share their tiles with the previous chunk's output staging.
-        if (c > 0 && !mbar_wait(&bars[B_OSTAGE_FREE], par, kWaitNs)) record_error(&abort_flag);
+        // T and P once the previous chunk's Delta and O MMAs have read theirs.
+        if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, kWaitNs)) record_error(&abort_flag);
         if (abort_flag) break;
         mbar_arrive_expect_tx(&bars[B_T_FULL], 2 * kTile64);
         bulk_load(base + OFF_T, rec, 2 * kTile64, &bars[B_T_FULL]);
         ++n_t;
+        if (c > 0 && !mbar_wait(&bars[B_P_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+        if (abort_flag) break;
         mbar_arrive_expect_tx(&bars[B_P_FULL], 2 * kTile64);
         bulk_load(base + OFF_P, rec + 2 * kTile64, 2 * kTile64, &bars[B_P_FULL]);
         ++n_p;
@@ -574,6 +577,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           if (stop || abort_flag) break;
         }
         mma_commit(&bars[B_D_DONE]);
+        mma_commit(&bars[B_T_EMPTY]);
         if (!mbar_wait(&bars[B_DD_READY], par, kWaitNs) || !mbar_wait(&bars[B_KT_READY], par, kWaitNs)) {
           record_error(&abort_flag);
           break;
@@ -601,6 +605,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
             mma_bf16_ts(tmem + TM_O, tD[1] + ks * 8, sdesc_sw128(sP[0] + ks * 32), id64, true);
         }
         mma_commit(&bars[B_OU_DONE]);
+        mma_commit(&bars[B_P_EMPTY]);
       }
       // Wait for every MMA issued so far before the CTA winds down.
       mma_commit(&bars[B_DRAIN]);
@@ -865,6 +870,8 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
 #pragma unroll
           for (int i = 0; i < 32; ++i) y[yb + i] += o[i];
         }
+        // The previous chunk's tile store must have left the staging buffer.
+        if (leader) bulk_wait_group_read0();
         tc_fence_before();
         named_sync(2, kAuxThreads);
         if (leader) mbar_arrive(&bars[B_O_FREE]);
@@ -884,8 +891,6 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           if (leader) {
             tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
             bulk_commit_group();
-            bulk_wait_group_read0();
-            mbar_arrive(&bars[B_OSTAGE_FREE]);
           }
         } else {
           // Ragged last chunk of a sequence: plain stores of the valid rows.
@@ -902,8 +907,6 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
             for (int i = 0; i < 64; ++i)
               if (i < n) op[i * ostride] = y[i];
           }
-          named_sync(2, kAuxThreads);
-          if (leader) mbar_arrive(&bars[B_OSTAGE_FREE]);
         }
       }
     }
