@@ -100,18 +100,32 @@ __device__ __forceinline__ float log_decay(const ChunkParams& p, int64_t t, int 
 __device__ __forceinline__ int64_t nchunks_of(int64_t len) { return (len + CH - 1) / CH; }
 
 // Chunk slot -> (sequence, chunk index within it); false past the last chunk.
-__device__ bool slot_to_chunk(const ChunkParams& p, int64_t slot, int64_t& b, int64_t& j) {
+// Warp-cooperative (every lane returns the same answer): 32 sequences per step.
+__device__ bool slot_to_chunk(const ChunkParams& p, int64_t slot, int lane, int64_t& b, int64_t& j) {
   int64_t base = 0;
-  for (int64_t s = 0; s < p.n_seqs; ++s) {
-    int64_t st, en;
-    seq_range(p.cu, p.n_tokens, p.n_seqs, s, st, en);
-    const int64_t nc = nchunks_of(en - st);
-    if (slot < base + nc) {
-      b = s;
-      j = slot - base;
+  for (int64_t s0 = 0; s0 < p.n_seqs; s0 += 32) {
+    const int64_t s = s0 + lane;
+    int64_t nc = 0;
+    if (s < p.n_seqs) {
+      int64_t st, en;
+      seq_range(p.cu, p.n_tokens, p.n_seqs, s, st, en);
+      nc = nchunks_of(en - st);
+    }
+    int64_t incl = nc;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    const int64_t excl = incl - nc;
+    const unsigned hit = __ballot_sync(0xffffffffu, nc > 0 && slot >= base + excl && slot < base + incl);
+    if (hit) {
+      const int l = __ffs(hit) - 1;
+      b = s0 + l;
+      j = slot - base - __shfl_sync(0xffffffffu, excl, l);
       return true;
     }
-    base += nc;
+    base += __shfl_sync(0xffffffffu, incl, 31);
   }
   return false;
 }
@@ -143,8 +157,8 @@ __device__ __forceinline__ void record_error(volatile int* abort_flag) {
   atomicOr(&g_device_error, kErrTimeout);
 }
 
-// Inclusive prefix sum of sl[0..63] into sG by one warp (2 values per lane);
-// also exp(G), exp(G_last - G) and gamma = exp(G_last).
+// Inclusive prefix sum of sl[0..63] (log2 units) into sG by one warp (2
+// values per lane); also exp(G), exp(G_last - G) and gamma = exp(G_last).
 __device__ __forceinline__ void chunk_cumsum(int lane, const float* sl, float* sG, float* seG, float* sdG,
                                              float* sgamma) {
   float a = sl[2 * lane], b = sl[2 * lane + 1];
@@ -158,28 +172,67 @@ __device__ __forceinline__ void chunk_cumsum(int lane, const float* sl, float* s
   const float last = __shfl_sync(0xffffffffu, s, 31);
   sG[2 * lane] = g0;
   sG[2 * lane + 1] = g1;
-  seG[2 * lane] = expf(g0);
-  seG[2 * lane + 1] = expf(g1);
-  sdG[2 * lane] = expf(last - g0);
-  sdG[2 * lane + 1] = expf(last - g1);
-  if (lane == 0) *sgamma = expf(last);
+  seG[2 * lane] = exp2f(g0);
+  seG[2 * lane + 1] = exp2f(g1);
+  sdG[2 * lane] = exp2f(last - g0);
+  sdG[2 * lane + 1] = exp2f(last - g1);
+  if (lane == 0) *sgamma = exp2f(last);
 }
 
 // ===========================================================================
 // Kernel A: per (chunk, value head) -- T = (I + A)^-1 and P, as bf16 hi/lo.
 // ===========================================================================
 constexpr int kPrepAStride = 68;  // floats per row of the A / T scratch (16-byte rows)
-constexpr size_t kPrepSmem = 1024 + 32768 + 2 * 64 * kPrepAStride * 4;
+// A and T scratch; it takes the place of the [K;Q] tile once the MMA has read it.
+constexpr size_t kPrepScratch = 2 * 64 * kPrepAStride * 4;
+static_assert(kPrepScratch >= 32768, "the scratch must cover the [K;Q] tile");
+constexpr size_t kPrepSmem = 1024 + kPrepScratch;
+constexpr float kLog2e = 1.4426950408889634f;
 
-__global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                         const __grid_constant__ CUtensorMap kmap,
-                                                         const ChunkParams p) {
+// Level-1 step of the doubling inverse for the 32-blocks (b0, b0+1):
+// T[b1][b0] = -T[b1][b1] (A[b1][b0] T[b0][b0]), 16 x 16 blocks.  Thread tid
+// (0..127) owns row ii, columns j0..j0+3 of one of the two pairs.
+__device__ __forceinline__ void prep_level1(float* sA, float* sT, int tid) {
+  const int pr = tid >> 6, ii = (tid >> 2) & 15, j0 = (tid & 3) * 4;
+  const int r0 = 32 * pr, r1 = r0 + 16;  // first rows of blocks b0 and b1
+  float m[4] = {0.f, 0.f, 0.f, 0.f};
+  const float* arow = sA + (r1 + ii) * kPrepAStride + r0;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float a = arow[k];
+    const float4 t4 = *reinterpret_cast<const float4*>(sT + (r0 + k) * kPrepAStride + r0 + j0);
+    m[0] = fmaf(a, t4.x, m[0]);
+    m[1] = fmaf(a, t4.y, m[1]);
+    m[2] = fmaf(a, t4.z, m[2]);
+    m[3] = fmaf(a, t4.w, m[3]);
+  }
+  // M -> the A[b0][b0] block (read only by the level-0 substitution, done).
+  *reinterpret_cast<float4*>(sA + (r0 + ii) * kPrepAStride + r0 + j0) = make_float4(m[0], m[1], m[2], m[3]);
+  __syncthreads();
+  float t[4] = {0.f, 0.f, 0.f, 0.f};
+  const float* trow = sT + (r1 + ii) * kPrepAStride + r1;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const float tv = trow[k];
+    const float4 m4 = *reinterpret_cast<const float4*>(sA + (r0 + k) * kPrepAStride + r0 + j0);
+    t[0] = fmaf(tv, m4.x, t[0]);
+    t[1] = fmaf(tv, m4.y, t[1]);
+    t[2] = fmaf(tv, m4.z, t[2]);
+    t[3] = fmaf(tv, m4.w, t[3]);
+  }
+  *reinterpret_cast<float4*>(sT + (r1 + ii) * kPrepAStride + r0 + j0) = make_float4(-t[0], -t[1], -t[2], -t[3]);
+}
+
+__global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                            const __grid_constant__ CUtensorMap kmap,
+                                                            const ChunkParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sKQ = base;                                        // [K;Q] 128 rows x 128, SW128
-  float* sA = reinterpret_cast<float*>(base + 32768);               // 64 x kPrepAStride
+  float* sA = reinterpret_cast<float*>(base);                       // 64 x kPrepAStride (after the MMA)
   float* sT = sA + 64 * kPrepAStride;                               // 64 x kPrepAStride
-  __shared__ float sl[CH], sb[CH], sG[CH], seG[CH], sdG[CH], sgamma;
+  __shared__ __align__(16) float sl[CH], sb[CH], sG[CH], seG[CH], sdG[CH];
+  __shared__ float sgamma;
   __shared__ __align__(8) uint64_t bar_load, bar_mma;
   __shared__ uint32_t tmem_base;
   __shared__ int64_t s_t0;
@@ -191,16 +244,19 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
   const int kh = h / (p.hv / p.hk);
   const int64_t slot = blockIdx.x;
 
-  if (tid == 0) {
-    int64_t b, j;
-    s_valid = slot_to_chunk(p, slot, b, j) ? 1 : 0;
-    if (s_valid) {
-      int64_t st, en;
-      seq_range(p.cu, p.n_tokens, p.n_seqs, b, st, en);
-      s_t0 = st + j * CH;
-      s_n = (int)(en - s_t0 < CH ? en - s_t0 : CH);
+  if (warp == 0) {
+    int64_t b = 0, j = 0;
+    const bool valid = slot_to_chunk(p, slot, lane, b, j);
+    if (lane == 0) {
+      s_valid = valid ? 1 : 0;
+      if (valid) {
+        int64_t st, en;
+        seq_range(p.cu, p.n_tokens, p.n_seqs, b, st, en);
+        s_t0 = st + j * CH;
+        s_n = (int)(en - s_t0 < CH ? en - s_t0 : CH);
+      }
+      abort_flag = 0;
     }
-    abort_flag = 0;
   }
   __syncthreads();
   if (!s_valid) return;
@@ -215,7 +271,8 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
   }
   if (tid < CH) {
     const bool ok = tid < n;
-    sl[tid] = ok ? log_decay(p, t0 + tid, h) : 0.f;
+    // Decays in log2 units: every exp below is an exp2 of a difference.
+    sl[tid] = ok ? log_decay(p, t0 + tid, h) * kLog2e : 0.f;
     sb[tid] = ok ? load_gate_f(p.beta, p.gate_dtype, (t0 + tid) * p.beta_st + h) : 0.f;
   }
   tc_fence_before();
@@ -276,37 +333,45 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
   tc_fence_after();
 
   // Row r of [KK^T ; QK^T]: warps 0-1 hold K K^T rows, warps 2-3 Q K^T rows.
+  // The [K;Q] tile is dead from here on: A and T take its place.
   const int row = warp * 32 + lane;
   float v[64];
   {
-    float r0[32], r1[32];
     const uint32_t ta = tmem + ((uint32_t)(warp * 32) << 16);
-    tmem_ld32(ta, r0);
-    tmem_ld32(ta + 32, r1);
+    tmem_ld32(ta, *reinterpret_cast<float(*)[32]>(v));
+    tmem_ld32(ta + 32, *reinterpret_cast<float(*)[32]>(v + 32));
     tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      v[i] = r0[i];
-      v[32 + i] = r1[i];
-    }
   }
   if (row < CH) {
     const int t = row;
     const float gt = sG[t], bt = sb[t];
     float* arow = sA + t * kPrepAStride;
 #pragma unroll
-    for (int s = 0; s < CH; ++s) arow[s] = (s < t && t < n) ? bt * expf(gt - sG[s]) * v[s] : 0.f;
+    for (int s4 = 0; s4 < CH; s4 += 4) {
+      const float4 g4 = *reinterpret_cast<const float4*>(sG + s4);
+      float4 a4;
+      a4.x = (s4 < t && t < n) ? bt * exp2f(gt - g4.x) * v[s4] : 0.f;
+      a4.y = (s4 + 1 < t && t < n) ? bt * exp2f(gt - g4.y) * v[s4 + 1] : 0.f;
+      a4.z = (s4 + 2 < t && t < n) ? bt * exp2f(gt - g4.z) * v[s4 + 2] : 0.f;
+      a4.w = (s4 + 3 < t && t < n) ? bt * exp2f(gt - g4.w) * v[s4 + 3] : 0.f;
+      *reinterpret_cast<float4*>(arow + s4) = a4;
+    }
   } else {
     const int t = row - CH;
     const float gt = sG[t];
-    float pv[64];
 #pragma unroll
-    for (int s = 0; s < CH; ++s) pv[s] = (s <= t && t < n) ? expf(gt - sG[s]) * v[s] : 0.f;
+    for (int s4 = 0; s4 < CH; s4 += 4) {
+      const float4 g4 = *reinterpret_cast<const float4*>(sG + s4);
+      v[s4] = (s4 <= t && t < n) ? exp2f(gt - g4.x) * v[s4] : 0.f;
+      v[s4 + 1] = (s4 + 1 <= t && t < n) ? exp2f(gt - g4.y) * v[s4 + 1] : 0.f;
+      v[s4 + 2] = (s4 + 2 <= t && t < n) ? exp2f(gt - g4.z) * v[s4 + 2] : 0.f;
+      v[s4 + 3] = (s4 + 3 <= t && t < n) ? exp2f(gt - g4.w) * v[s4 + 3] : 0.f;
+    }
     unsigned char* rec = p.ws + ((size_t)slot * p.hv + h) * kRecBytes;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint4 hi, lo;
-      split8(pv + 8 * c, hi, lo);
+      split8(v + 8 * c, hi, lo);
       *reinterpret_cast<uint4*>(rec + 2 * kTile64 + sw128_chunk(64, t, 0, c)) = hi;
       *reinterpret_cast<uint4*>(rec + 3 * kTile64 + sw128_chunk(64, t, 0, c)) = lo;
     }
@@ -315,31 +380,45 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 64);
 
-  // T = (I + A)^-1 by 2 x 2 blocks of 32: T11 = (I + A11)^-1 and
-  // T22 = (I + A22)^-1 by forward substitution (warp 0 / warp 1, one column
-  // per thread, four partial sums per row), then T21 = -T22 (A21 T11) on all
-  // four warps; T12 = 0.
-  if (warp < 2) {
-    const int off = warp * 32;  // block (off, off)
-    const int c = lane;
-    float x[32];
+  // T = (I + A)^-1 by doubling.  Level 0: warp w inverts the diagonal 16-block
+  // w by forward substitution (lane c < 16 owns column c); it also clears the
+  // blocks of T above the diagonal that the later products read.
+  {
+    const int off = warp * 16, c = lane & 15;
+    float x[16];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
+    for (int i = 0; i < 16; ++i) {
       const float* arow = sA + (off + i) * kPrepAStride + off;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      float acc0 = 0.f, acc1 = 0.f;
 #pragma unroll
-      for (int j = 0; j < i; ++j) acc[j & 3] = fmaf(arow[j], x[j], acc[j & 3]);
-      const float sum = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-      x[i] = i < c ? 0.f : (i == c ? 1.f : -sum);
+      for (int j4 = 0; j4 < i; j4 += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(arow + j4);
+        acc0 = fmaf(a4.x, x[j4], acc0);
+        if (j4 + 1 < i) acc1 = fmaf(a4.y, x[j4 + 1], acc1);
+        if (j4 + 2 < i) acc0 = fmaf(a4.z, x[j4 + 2], acc0);
+        if (j4 + 3 < i) acc1 = fmaf(a4.w, x[j4 + 3], acc1);
+      }
+      x[i] = i < c ? 0.f : (i == c ? 1.f : -(acc0 + acc1));
     }
+    if (lane < 16) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      sT[(off + i) * kPrepAStride + off + c] = x[i];
-      sT[(off + i) * kPrepAStride + (32 - off) + c] = 0.f;  // T12 (and T21, overwritten below)
+      for (int i = 0; i < 16; ++i) sT[(off + i) * kPrepAStride + off + c] = x[i];
+      if ((warp & 1) == 0) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sT[(off + i) * kPrepAStride + off + 16 + c] = 0.f;
+      }
+    }
+    if (warp < 2) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) sT[(off + i) * kPrepAStride + 32 + lane] = 0.f;  // T12
     }
   }
   __syncthreads();
-  {  // M = A21 T11 into the (now unused) A11 block
+  // Level 1: the two diagonal 32-blocks.
+  prep_level1(sA, sT, tid);
+  __syncthreads();
+  // Level 2: T21 = -T22 (A21 T11) with M = A21 T11 in the (dead) A11 block.
+  {
     const int i = tid >> 2, j0 = (tid & 3) * 8;
     float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const float* arow = sA + (32 + i) * kPrepAStride;
@@ -355,7 +434,7 @@ __global__ void __launch_bounds__(128) chunk_prep_kernel(const __grid_constant__
     for (int jj = 0; jj < 8; ++jj) sA[i * kPrepAStride + j0 + jj] = m[jj];
   }
   __syncthreads();
-  {  // T21 = -T22 M
+  {
     const int i = tid >> 2, j0 = (tid & 3) * 8;
     float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const float* trow = sT + (32 + i) * kPrepAStride + 32;
