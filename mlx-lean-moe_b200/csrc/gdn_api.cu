@@ -249,7 +249,7 @@ gdn_status check_block(const gdn_block_args* a, gdn::BlockParams* p, gdn::ScanPa
   L->g = round_up(L->v + (size_t)N * a->hv * a->dv * es, 256);
   L->beta = round_up(L->g + (size_t)N * a->hv * 4, 256);
   L->y = round_up(L->beta + (size_t)N * a->hv * 4, 256);
-  L->scan = round_up(L->y + (size_t)N * a->hv * a->dv * 4, 256);
+  L->scan = round_up(L->y + (size_t)N * a->hv * a->dv * es, 256);
 
   char* ws = static_cast<char*>(a->workspace);
   p->n_tokens = N;
@@ -276,7 +276,7 @@ gdn_status check_block(const gdn_block_args* a, gdn::BlockParams* p, gdn::ScanPa
   p->v = ws + L->v;
   p->g_log = reinterpret_cast<float*>(ws + L->g);
   p->beta = reinterpret_cast<float*>(ws + L->beta);
-  p->y = reinterpret_cast<float*>(ws + L->y);
+  p->y = ws + L->y;
   p->out = a->out;
 
   gdn_scan_args sa = {};
@@ -305,7 +305,7 @@ gdn_status check_block(const gdn_block_args* a, gdn::BlockParams* p, gdn::ScanPa
   sa.out = p->y;
   sa.qkv_dtype = a->act_dtype;
   sa.gate_dtype = GDN_F32;
-  sa.out_dtype = GDN_F32;
+  sa.out_dtype = a->act_dtype;  // y rounded to the act dtype, as the reference does before the norm
   sa.gate_kind = GDN_GATE_LOG;
   sa.algo = a->algo;
   gdn_status st = check_scan(&sa, sp, a->n_seqs, /*check_pointers=*/false);

@@ -196,13 +196,13 @@ __global__ void __launch_bounds__(256) block_epilogue_kernel(const BlockParams p
   const int h = (int)(row % p.hv);
   const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
   const T* z = static_cast<const T*>(p.mixed) + t * p.mixed_st + conv_dim + (int64_t)h * p.dv;
-  const float* y = p.y + row * p.dv;
+  const T* y = static_cast<const T*>(p.y) + row * p.dv;  // already in the activation dtype
   float yb[MAXC];
   float ss = 0.f;
 #pragma unroll
   for (int m = 0; m < MAXC; ++m) {
     const int d = lane + 32 * m;
-    yb[m] = d < p.dv ? round_to<T>(y[d]) : 0.f;
+    yb[m] = d < p.dv ? to_f(y[d]) : 0.f;
     ss += yb[m] * yb[m];
   }
   ss = warp_sum(ss);
@@ -393,7 +393,7 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
 #pragma unroll
         for (int j = 0; j < K - 1; ++j) acc += w[i][j] * win[j][i];
         acc += w[i][K - 1] * cur[i];
-        x[i] = round_to<T>(silu_f(round_to<T>(acc)));
+        x[i] = round_to<T>(silu_fast(round_to<T>(acc)));
         ss += x[i] * x[i];
       }
       // q/k rms-norm: reduce over the lanes of this head (all lanes shuffle).
@@ -440,15 +440,12 @@ __global__ void __launch_bounds__(256) block_epilogue_fast_kernel(const BlockPar
   const int h = (int)(rr % p.hv);
   const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
   float y[8], z[8], w[8];
-  load8<float>(p.y + rr * p.dv + d0, y);
+  load8<T>(static_cast<const T*>(p.y) + rr * p.dv + d0, y);  // already in the activation dtype
   load8<T>(static_cast<const T*>(p.mixed) + t * p.mixed_st + conv_dim + (int64_t)h * p.dv + d0, z);
   load8<float>(p.norm_w + d0, w);
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    y[i] = round_to<T>(y[i]);
-    ss += y[i] * y[i];
-  }
+  for (int i = 0; i < 8; ++i) ss += y[i] * y[i];
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) {
     const float o = __shfl_xor_sync(0xffffffffu, ss, off);
@@ -457,7 +454,7 @@ __global__ void __launch_bounds__(256) block_epilogue_fast_kernel(const BlockPar
   const float inv = rsqrtf(ss / (float)p.dv + p.eps);
   float o[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] = silu_f(z[i]) * round_to<T>(y[i] * inv * w[i]);
+  for (int i = 0; i < 8; ++i) o[i] = silu_fast(z[i]) * round_to<T>(y[i] * inv * w[i]);
   if (valid) store8<T>(static_cast<T*>(p.out) + rr * p.dv + d0, o);
 }
 
@@ -468,6 +465,12 @@ bool fast_shapes(const BlockParams& p) {
          (reinterpret_cast<uintptr_t>(p.mixed) & 15u) == 0 && (reinterpret_cast<uintptr_t>(p.norm_w) & 15u) == 0;
 }
 
+template <typename T, typename TS, int K>
+cudaError_t launch_prologue_fast(dim3 grid, const BlockParams& p, cudaStream_t s) {
+  block_prologue_fast_kernel<T, TS, K><<<grid, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
 template <typename T, typename TS>
 cudaError_t prologue_t(const BlockParams& p, cudaStream_t s) {
   if (fast_shapes(p)) {
@@ -476,12 +479,11 @@ cudaError_t prologue_t(const BlockParams& p, cudaStream_t s) {
     if (gx == 0) return cudaSuccess;
     dim3 grid((unsigned)gx, (unsigned)((conv_dim + 2047) / 2048 + 1));
     switch (p.kernel) {
-      case 1: block_prologue_fast_kernel<T, TS, 1><<<grid, 256, 0, s>>>(p); break;
-      case 2: block_prologue_fast_kernel<T, TS, 2><<<grid, 256, 0, s>>>(p); break;
-      case 3: block_prologue_fast_kernel<T, TS, 3><<<grid, 256, 0, s>>>(p); break;
-      default: block_prologue_fast_kernel<T, TS, 4><<<grid, 256, 0, s>>>(p); break;
+      case 1: return launch_prologue_fast<T, TS, 1>(grid, p, s);
+      case 2: return launch_prologue_fast<T, TS, 2>(grid, p, s);
+      case 3: return launch_prologue_fast<T, TS, 3>(grid, p, s);
+      default: return launch_prologue_fast<T, TS, 4>(grid, p, s);
     }
-    return cudaGetLastError();
   }
   const int n_heads = 2 * p.hk + p.hv;
   const int64_t gx = (p.n_tokens + TT - 1) / TT;
