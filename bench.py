@@ -47,6 +47,8 @@ METRIC = "GDN prefill tok/s & decode state HBM GB/s (% peak) at 1/2/4/8 B200 vs 
 B, HK, HV, D = 64, 16, 32, 128
 STATE_BYTES = 2 * B * HV * D * D * 4  # read + write of the fp32 state
 DECODE_BYTES = STATE_BYTES + 2 * B * HK * D * 2 + B * HV * D * 2 + 2 * B * HV * 4 + B * HV * D * 4
+# DRAM bytes of one decode_kernel launch at config 2, from one ncu capture (read + write).
+DECODE_NCU_TRAFFIC = 135_301_120 + 76_251_648
 PREFILL_T = 8192
 PREFILL_FLOP = 182_955 * PREFILL_T * HV  # chunked WY count per token-head, see DESIGN.md
 
@@ -500,7 +502,10 @@ def main():
                          "flush lines remain)"},
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "traffic": None,
+                     "frac": achieved / hbm_peak, "traffic": DECODE_NCU_TRAFFIC,
+                     "traffic_source": "one ncu capture of this kernel at config 2 (dram__bytes_read.sum "
+                                       "135,301,120 + dram__bytes_write.sum 76,251,648; the rest of the "
+                                       "state write-back leaves L2 after the launch)",
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s",
                      "bytes_per_launch": DECODE_BYTES, "kernel": "decode_kernel<128, bf16>"},
