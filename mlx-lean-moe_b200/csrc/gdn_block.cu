@@ -344,6 +344,7 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
   const int64_t key_dim = (int64_t)p.hk * p.dk;
   const bool is_q = c < key_dim, is_k = !is_q && c < 2 * key_dim;
   const int group = (is_q || is_k) ? p.dk / 8 : 32;  // lanes sharing one q/k head
+  const bool qk_warp = __any_sync(0xffffffffu, is_q || is_k);
 
   float w[8][4];
 #pragma unroll
@@ -386,7 +387,6 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
       ring[u].to_float(cur);
       if (active && t + PF < t_end) ring[u].load(src + (t + PF) * p.mixed_st);
       float x[8];
-      float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         float acc = 0.f;
@@ -394,13 +394,18 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
         for (int j = 0; j < K - 1; ++j) acc += w[i][j] * win[j][i];
         acc += w[i][K - 1] * cur[i];
         x[i] = round_to<T>(silu_fast(round_to<T>(acc)));
-        ss += x[i] * x[i];
       }
-      // q/k rms-norm: reduce over the lanes of this head (all lanes shuffle).
+      // q/k rms-norm: reduce over the lanes of this head (all lanes of a
+      // warp holding any q/k channel shuffle; v-only warps skip it).
+      float ss = 0.f;
+      if (qk_warp) {
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float o = __shfl_xor_sync(0xffffffffu, ss, off);
-        if (off < group) ss += o;
+        for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+          const float o = __shfl_xor_sync(0xffffffffu, ss, off);
+          if (off < group) ss += o;
+        }
       }
       if (is_q || is_k) {
         const float inv = rsqrtf(ss / (float)p.dk + 1e-6f);

@@ -50,11 +50,16 @@ __device__ __forceinline__ void seq_range(const int64_t* cu, int64_t n_tokens, i
 __device__ __forceinline__ float softplus_f(float x) { return fmaxf(x, 0.f) + log1pf(expf(-fabsf(x))); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.f / (1.f + expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x / (1.f + expf(-x)); }
-// x * sigmoid(x) as x / (1 + 2^(-x log2 e)) with exp2f and the approximate
-// divide: a few instructions, relative error ~1e-6 (well below the bf16
+// x * sigmoid(x) as x / (1 + 2^(-x log2 e)) with the hardware approximate
+// exp2 (ex2.approx) and the approximate divide: a few instructions, relative error ~1e-6 (well below the bf16
 // rounding that follows it in the fused-block kernels).  For x < -87 the
 // denominator is inf and the result the correct limit -0.
-__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + exp2f(x * -1.4426950408889634f)); }
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + ex2_approx(x * -1.4426950408889634f)); }
 
 // ---------------------------------------------------------------------------
 // Internal launch interface (one struct, filled by gdn_api.cu after checks)
