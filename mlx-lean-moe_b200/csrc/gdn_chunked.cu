@@ -46,6 +46,7 @@
 // and returns.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 
 #include "gdn_common.cuh"
@@ -69,6 +70,19 @@ constexpr uint32_t kGateBytes = 1024;               // beta[64], exp G[64], exp(
 constexpr size_t kRecBytes = 4 * (size_t)kTile64 + kGateBytes;
 constexpr uint32_t GATE_BETA = 0, GATE_EG = 64, GATE_DG = 128, GATE_GAMMA = 192;  // float offsets
 
+// A chain of the serial kernel other than "sequence b from state_in[b]":
+// used to split one long sequence into segments (see launch_chunked_scan).
+constexpr int kChainIdentity = 1;  // no state_in: start from the identity (a transition chain)
+constexpr int kChainZeroV = 2;     // V taken as 0 (no V loads)
+constexpr int kChainNoOut = 4;     // write no output
+constexpr int kMaxChains = 16;
+struct ChainDesc {
+  int64_t seq;              // sequence (segment) of cu this chain runs over
+  const float* state_in;    // [Hv, Dv, Dk] start state, or nullptr (0, or I with kChainIdentity)
+  float* state_out;         // [Hv, Dv, Dk] final state, or nullptr (not written)
+  int flags;
+};
+
 struct ChunkParams {
   int64_t n_tokens, n_seqs;
   const int64_t* cu;
@@ -83,6 +97,10 @@ struct ChunkParams {
   void* out;
   gdn_dtype out_dtype;
   unsigned char* ws;  // kRecBytes per (chunk slot, value head)
+  // n_chains > 0: CTA row blockIdx.x / hv runs chains[row] instead of sequence
+  // blockIdx.x / hv with state_in / state_out.
+  int n_chains;
+  ChainDesc chains[kMaxChains];
 };
 
 __device__ __forceinline__ float load_gate_f(const void* base, gdn_dtype dt, int64_t idx) {
@@ -521,8 +539,30 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x % p.hv;
-  const int64_t b = blockIdx.x / p.hv;
+  const int64_t row = blockIdx.x / p.hv;
   const int kh = h / (p.hv / p.hk);
+  const size_t head_state = (size_t)h * DH * DH;
+  int64_t b;
+  const float* chain_in;
+  float* chain_out;
+  int flags;
+  if (p.n_chains > 0) {
+    const ChainDesc& d = p.chains[row];
+    b = d.seq;
+    chain_in = d.state_in ? d.state_in + head_state : nullptr;
+    chain_out = d.state_out ? d.state_out + head_state : nullptr;
+    flags = d.flags;
+  } else {
+    b = row;
+    const size_t off = (size_t)b * p.hv * DH * DH + head_state;
+    chain_in = p.state_in ? p.state_in + off : nullptr;
+    chain_out = p.state_out + off;
+    flags = 0;
+  }
+  if (flags & kChainZeroV) {  // V = 0 for a transition chain: a zero tile, never loaded
+    for (int i = tid; i < 16384 / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(base + OFF_V)[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
 
   if (tid == 0) {
     int64_t st, en;
@@ -541,7 +581,6 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
   const uint32_t tmem = tmem_base;
   const int64_t start = s_start, end = s_end;
   const int64_t nch = nchunks_of(end - start);
-  const size_t head_off = ((size_t)b * p.hv + h) * DH * DH;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -566,8 +605,12 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         ++n_kq;
         if (c > 0 && !mbar_wait(&bars[B_V_EMPTY], par, kWaitNs)) record_error(&abort_flag);
         if (abort_flag) break;
-        mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
-        tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
+        if (flags & kChainZeroV) {
+          mbar_arrive(&bars[B_V_FULL]);
+        } else {
+          mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
+          tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
+        }
         ++n_v;
         // T and P once the previous chunk's Delta and O MMAs have read theirs.
         if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, kWaitNs)) record_error(&abort_flag);
@@ -704,7 +747,8 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     // 64*kb + 32*half .. +32 of row dv in pass kb).
     for (int kb = 0; kb < 2; ++kb) {
       const int col = kb * 64 + half * 32;
-      const float* srow = p.state_in ? p.state_in + head_off + (size_t)dv * DH : nullptr;
+      const float* srow = chain_in ? chain_in + (size_t)dv * DH : nullptr;
+      const float diag = (flags & kChainIdentity) ? 1.f : 0.f;
       float x[32];
 #pragma unroll
       for (int i = 0; i < 32; i += 4) {
@@ -713,6 +757,10 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         x[i + 1] = v4.y;
         x[i + 2] = v4.z;
         x[i + 3] = v4.w;
+      }
+      if (!srow) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] = (col + i == dv) ? diag : 0.f;
       }
       tmem_st32(tq + TM_S + col, x);
 #pragma unroll
@@ -862,9 +910,9 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     }
 
     // Final state (or the initial one for an empty sequence) -> state_out.
-    if (!named_sync_or(1, kEpiThreads, abort_flag != 0)) {
+    if (!named_sync_or(1, kEpiThreads, abort_flag != 0) && chain_out) {
       tc_fence_after();
-      float* orow = p.state_out + head_off + (size_t)dv * DH;
+      float* orow = chain_out + (size_t)dv * DH;
       for (int cc = 0; cc < 2; ++cc) {
         const int col = half * 64 + cc * 32;
         float sv[32];
@@ -954,7 +1002,9 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         tc_fence_before();
         named_sync(2, kAuxThreads);
         if (leader) mbar_arrive(&bars[B_O_FREE]);
-        if (n == CH) {
+        if (flags & kChainNoOut) {
+          // a transition chain: only its final state is wanted
+        } else if (n == CH) {
           // Whole chunk: stage [t][dv] in shared memory, one TMA tensor store.
           if (p.out_dtype == GDN_BF16) {
             __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
@@ -1045,7 +1095,101 @@ bool make_out_map(CUtensorMap* map, void* ptr, int64_t n_tokens, int heads, gdn_
   return r == CUDA_SUCCESS;
 }
 
-int64_t max_slots(const ScanParams& p) { return (p.n_tokens + CH - 1) / CH + p.n_seqs; }
+// ---------------------------------------------------------------------------
+// One long sequence in segments.  The chunk chain maps a segment's start
+// state affinely, S_end = S_start M + U: M (Dk x Dk) is the same recurrence
+// run with V = 0 from the identity, U its end state from zero.  With P
+// segments, phase 1 runs segment 0 for real (its outputs and end state are
+// final) together with U_i and M_i of segments 1..P-2, all in one launch;
+// phase 2 chains S_start(i+1) = S_start(i) M_i + U_i (fp32, per head); phase 3
+// reruns segments 1..P-1 from their start states.  Every chain is shorter by
+// about P, and phase 1's 1 + 2(P-2) chains per head still fit one wave.
+// ---------------------------------------------------------------------------
+constexpr int kMaxSegs = 8;
+constexpr int kSmCount = 148;      // B200: phase-1 chains are kept within one wave of CTAs
+constexpr int kMinSegChunks = 8;   // shorter segments cost more than they save
+
+struct SegCu {
+  int64_t cu[kMaxSegs + 1];
+};
+
+__global__ void seg_setup_kernel(const SegCu c, int n, int64_t* cu) {
+  if (threadIdx.x <= n) cu[threadIdx.x] = c.cu[threadIdx.x];
+}
+
+// next = prev * M + next for every head (128 x 128 fp32 each).  Grid (Hv, 8):
+// 16 rows of one head per CTA; thread = 1 row x 8 columns.
+__global__ void __launch_bounds__(256) state_combine_kernel(const float* __restrict__ prev, const float* __restrict__ M,
+                                                            float* next) {
+  __shared__ __align__(16) float sa[16][DH];
+  __shared__ __align__(16) float sm[32][DH];
+  const int tid = threadIdx.x, r = tid >> 4, c0 = (tid & 15) * 8;
+  const size_t head = (size_t)blockIdx.x * DH * DH;
+  const int r0 = blockIdx.y * 16;
+  const float* A = prev + head + (size_t)r0 * DH;
+  const float* Mh = M + head;
+  float* C = next + head + (size_t)r0 * DH;
+  for (int i = tid; i < 16 * DH / 4; i += 256)
+    reinterpret_cast<float4*>(&sa[0][0])[i] = reinterpret_cast<const float4*>(A)[i];
+  float acc[8];
+  {
+    const float4 x0 = *reinterpret_cast<const float4*>(C + (size_t)r * DH + c0);
+    const float4 x1 = *reinterpret_cast<const float4*>(C + (size_t)r * DH + c0 + 4);
+    acc[0] = x0.x; acc[1] = x0.y; acc[2] = x0.z; acc[3] = x0.w;
+    acc[4] = x1.x; acc[5] = x1.y; acc[6] = x1.z; acc[7] = x1.w;
+  }
+  for (int k0 = 0; k0 < DH; k0 += 32) {
+    __syncthreads();
+    for (int i = tid; i < 32 * DH / 4; i += 256)
+      reinterpret_cast<float4*>(&sm[0][0])[i] = reinterpret_cast<const float4*>(Mh + (size_t)k0 * DH)[i];
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float a = sa[r][k0 + k];
+      const float4 m0 = *reinterpret_cast<const float4*>(&sm[k][c0]);
+      const float4 m1 = *reinterpret_cast<const float4*>(&sm[k][c0 + 4]);
+      acc[0] = fmaf(a, m0.x, acc[0]);
+      acc[1] = fmaf(a, m0.y, acc[1]);
+      acc[2] = fmaf(a, m0.z, acc[2]);
+      acc[3] = fmaf(a, m0.w, acc[3]);
+      acc[4] = fmaf(a, m1.x, acc[4]);
+      acc[5] = fmaf(a, m1.y, acc[5]);
+      acc[6] = fmaf(a, m1.z, acc[6]);
+      acc[7] = fmaf(a, m1.w, acc[7]);
+    }
+  }
+  *reinterpret_cast<float4*>(C + (size_t)r * DH + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  *reinterpret_cast<float4*>(C + (size_t)r * DH + c0 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
+// Segments for one scan (1 = run it whole): only a single dense sequence whose
+// heads leave most of the GPU idle is split.
+int seg_count(const ScanParams& p) {
+  if (p.n_seqs != 1 || p.cu_seqlens) return 1;
+  const int64_t nch = (p.n_tokens + CH - 1) / CH;
+  int P = 1;
+  for (int q = 3; q <= kMaxSegs; ++q) {
+    if ((int64_t)p.hv * (2 * q - 3) > kSmCount || nch < (int64_t)kMinSegChunks * q) break;
+    P = q;
+  }
+  return P;
+}
+
+struct SegLayout {
+  size_t recs, cu, w, m, total;
+};
+
+SegLayout seg_layout(const ScanParams& p, int P) {
+  SegLayout L;
+  const size_t state = (size_t)p.hv * DH * DH * sizeof(float);
+  const int64_t nseq = P > 1 ? P : p.n_seqs;
+  L.recs = (size_t)((p.n_tokens + CH - 1) / CH + nseq) * p.hv * kRecBytes;
+  L.cu = (L.recs + 255) & ~(size_t)255;
+  L.w = L.cu + (P > 1 ? 256 : 0);
+  L.m = L.w + (P > 1 ? (size_t)(P - 1) * state : 0);
+  L.total = L.m + (P > 1 ? (size_t)(P - 2) * state : 0);
+  return L;
+}
 
 bool aligned_elems(int64_t s) { return s >= 0 && s % 8 == 0; }
 bool aligned_ptr16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -1058,7 +1202,7 @@ bool chunked_supported(const ScanParams& p) {
          aligned_elems(p.v_sh) && p.n_tokens < (int64_t)1 << 31 && tensor_map_encoder() != nullptr;
 }
 
-size_t chunked_workspace_bytes(const ScanParams& p) { return (size_t)max_slots(p) * p.hv * kRecBytes; }
+size_t chunked_workspace_bytes(const ScanParams& p) { return seg_layout(p, seg_count(p)).total; }
 
 cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   if (!aligned_ptr16(sp.q) || !aligned_ptr16(sp.k) || !aligned_ptr16(sp.v) || !aligned_ptr16(sp.workspace))
@@ -1101,16 +1245,59 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     attrs_set = true;
   }
-  const int64_t slots = max_slots(sp);
+  p.n_chains = 0;
+  const int P = seg_count(sp);
+  if (P > 1) {
+    // Segment boundaries on chunk multiples, segment 0 first.
+    const SegLayout L = seg_layout(sp, P);
+    const int64_t nch = (N + CH - 1) / CH;
+    SegCu sc;
+    for (int i = 0; i <= P; ++i) sc.cu[i] = std::min<int64_t>(N, (nch * i / P) * CH);
+    int64_t* cu_dev = reinterpret_cast<int64_t*>(p.ws + L.cu);
+    seg_setup_kernel<<<1, 32, 0, s>>>(sc, P, cu_dev);
+    p.cu = cu_dev;
+    p.n_seqs = P;
+  }
+  const int64_t slots = (N + CH - 1) / CH + p.n_seqs;
   if (N > 0 && slots > 0) {
     if (slots > 0x7fffffffLL || sp.hv > 65535) return cudaErrorInvalidConfiguration;
     chunk_prep_kernel<<<dim3((unsigned)slots, (unsigned)sp.hv), 128, kPrepSmem, s>>>(qmap, kmap, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  const int64_t ctas = sp.n_seqs * sp.hv;
-  if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p);
+  if (P <= 1) {
+    const int64_t ctas = sp.n_seqs * sp.hv;
+    if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p);
+    return cudaGetLastError();
+  }
+  const SegLayout L = seg_layout(sp, P);
+  const size_t hstate = (size_t)sp.hv * DH * DH;
+  float* W = reinterpret_cast<float*>(p.ws + L.w);  // end states of segments 0..P-2, then their start states
+  float* Mt = reinterpret_cast<float*>(p.ws + L.m); // transitions of segments 1..P-2
+  // phase 1: segment 0 for real; U_i and M_i of segments 1..P-2
+  ChunkParams p1 = p;
+  p1.n_chains = 1 + 2 * (P - 2);
+  p1.chains[0] = {0, sp.state_in, W, 0};
+  for (int i = 1; i <= P - 2; ++i) {
+    p1.chains[i] = {i, nullptr, W + i * hstate, kChainNoOut};
+    p1.chains[P - 2 + i] = {i, nullptr, Mt + (i - 1) * hstate, kChainIdentity | kChainZeroV | kChainNoOut};
+  }
+  chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p1);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // phase 2: start states, W[j] = W[j-1] M_j + U_j
+  for (int j = 1; j <= P - 2; ++j) {
+    state_combine_kernel<<<dim3((unsigned)sp.hv, DH / 16), 256, 0, s>>>(W + (j - 1) * hstate, Mt + (j - 1) * hstate,
+                                                                      W + j * hstate);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  // phase 3: segments 1..P-1 from their start states; the last one's end state is the result
+  ChunkParams p3 = p;
+  p3.n_chains = P - 1;
+  for (int i = 1; i <= P - 1; ++i) p3.chains[i - 1] = {i, W + (i - 1) * hstate, i == P - 1 ? sp.state_out : nullptr, 0};
+  chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p3);
   return cudaGetLastError();
 }
 

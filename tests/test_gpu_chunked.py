@@ -106,3 +106,23 @@ def test_chunked_rejects_unsupported_shapes():
     with pytest.raises(ValueError, match="chunked"):
         gdn_b200.gated_delta_scan_varlen(t(q[:, :, :64]), t(k[:, :, :64]), t(v), t(g), t(beta), None,
                                          algo="chunked", g_is_log=True)
+
+
+@pytest.mark.parametrize("hk,hv,T,decay", [(4, 8, 4096, "cfg"), (8, 16, 3072 + 40, "slow"),
+                                           (16, 32, 2048, "strong"), (16, 32, 1600, "cfg")])
+def test_segmented_single_sequence(hk, hv, T, decay):
+    """One dense sequence (no cu_seqlens) whose heads leave the GPU idle is run
+    in time segments (transition chains + start-state combine); it must agree
+    with the oracle's serial recurrence and with the unsegmented chunked run."""
+    q, k, v, g, beta, cu, s0 = _inputs([T], hk, hv, seed=7, decay=decay, state_std=0.05)
+    state = t(s0)
+    y, st = gdn_b200.gated_delta_scan_varlen(
+        t(q, torch.bfloat16), t(k, torch.bfloat16), t(v, torch.bfloat16), t(g), t(beta), state,
+        g_is_log=True, algo="chunked", state_out=state)  # in place
+    gdn_b200.check_device_errors()
+    y, st = n(y), n(st)
+    ey, est = oracle_c.scan_varlen(q, k, v, g, beta, cu, s0, g_is_log=True)
+    assert O.rel_l2(y, ey) <= DESIGN, O.rel_l2(y, ey)
+    assert O.rel_l2(st, est) <= DESIGN, O.rel_l2(st, est)
+    y1, st1 = _run(q, k, v, g, beta, cu, s0)  # with cu_seqlens: one chain per head
+    assert O.rel_l2(y, y1) <= DESIGN and O.rel_l2(st, st1) <= DESIGN
