@@ -1117,49 +1117,52 @@ __global__ void seg_setup_kernel(const SegCu c, int n, int64_t* cu) {
   if (threadIdx.x <= n) cu[threadIdx.x] = c.cu[threadIdx.x];
 }
 
-// next = prev * M + next for every head (128 x 128 fp32 each).  Grid (Hv, 8):
-// 16 rows of one head per CTA; thread = 1 row x 8 columns.
+// next = prev * M + next for every head (128 x 128 fp32 each).  Grid
+// (Hv, 4): 32 rows of one head per CTA, M (64 KB) and the rows (16 KB) staged
+// in shared memory with every load in flight at once; thread = 2 rows x 8
+// columns.
+constexpr size_t kCombineSmem = (size_t)(DH + 32) * DH * sizeof(float);
 __global__ void __launch_bounds__(256) state_combine_kernel(const float* __restrict__ prev, const float* __restrict__ M,
                                                             float* next) {
-  __shared__ __align__(16) float sa[16][DH];
-  __shared__ __align__(16) float sm[32][DH];
-  const int tid = threadIdx.x, r = tid >> 4, c0 = (tid & 15) * 8;
+  extern __shared__ __align__(16) float csm[];
+  float* sm = csm;            // [128][128] M
+  float* sa = csm + DH * DH;  // [32][128] rows of prev
+  const int tid = threadIdx.x, r = (tid >> 4) * 2, c0 = (tid & 15) * 8;
   const size_t head = (size_t)blockIdx.x * DH * DH;
-  const int r0 = blockIdx.y * 16;
-  const float* A = prev + head + (size_t)r0 * DH;
-  const float* Mh = M + head;
-  float* C = next + head + (size_t)r0 * DH;
-  for (int i = tid; i < 16 * DH / 4; i += 256)
-    reinterpret_cast<float4*>(&sa[0][0])[i] = reinterpret_cast<const float4*>(A)[i];
-  float acc[8];
-  {
-    const float4 x0 = *reinterpret_cast<const float4*>(C + (size_t)r * DH + c0);
-    const float4 x1 = *reinterpret_cast<const float4*>(C + (size_t)r * DH + c0 + 4);
-    acc[0] = x0.x; acc[1] = x0.y; acc[2] = x0.z; acc[3] = x0.w;
-    acc[4] = x1.x; acc[5] = x1.y; acc[6] = x1.z; acc[7] = x1.w;
+  const int r0 = blockIdx.y * 32;
+  const float4* Mh = reinterpret_cast<const float4*>(M + head);
+  const float4* A = reinterpret_cast<const float4*>(prev + head + (size_t)r0 * DH);
+#pragma unroll 4
+  for (int i = tid; i < DH * DH / 4; i += 256) reinterpret_cast<float4*>(sm)[i] = Mh[i];
+#pragma unroll 4
+  for (int i = tid; i < 32 * DH / 4; i += 256) reinterpret_cast<float4*>(sa)[i] = A[i];
+  float* C = next + head + (size_t)(r0 + r) * DH + c0;
+  float acc[2][8];
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    const float4 x0 = *reinterpret_cast<const float4*>(C + rr * DH);
+    const float4 x1 = *reinterpret_cast<const float4*>(C + rr * DH + 4);
+    acc[rr][0] = x0.x; acc[rr][1] = x0.y; acc[rr][2] = x0.z; acc[rr][3] = x0.w;
+    acc[rr][4] = x1.x; acc[rr][5] = x1.y; acc[rr][6] = x1.z; acc[rr][7] = x1.w;
   }
-  for (int k0 = 0; k0 < DH; k0 += 32) {
-    __syncthreads();
-    for (int i = tid; i < 32 * DH / 4; i += 256)
-      reinterpret_cast<float4*>(&sm[0][0])[i] = reinterpret_cast<const float4*>(Mh + (size_t)k0 * DH)[i];
-    __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      const float a = sa[r][k0 + k];
-      const float4 m0 = *reinterpret_cast<const float4*>(&sm[k][c0]);
-      const float4 m1 = *reinterpret_cast<const float4*>(&sm[k][c0 + 4]);
-      acc[0] = fmaf(a, m0.x, acc[0]);
-      acc[1] = fmaf(a, m0.y, acc[1]);
-      acc[2] = fmaf(a, m0.z, acc[2]);
-      acc[3] = fmaf(a, m0.w, acc[3]);
-      acc[4] = fmaf(a, m1.x, acc[4]);
-      acc[5] = fmaf(a, m1.y, acc[5]);
-      acc[6] = fmaf(a, m1.z, acc[6]);
-      acc[7] = fmaf(a, m1.w, acc[7]);
+  __syncthreads();
+#pragma unroll 4
+  for (int k = 0; k < DH; ++k) {
+    const float a0 = sa[r * DH + k], a1 = sa[(r + 1) * DH + k];
+    const float4 m0 = *reinterpret_cast<const float4*>(sm + k * DH + c0);
+    const float4 m1 = *reinterpret_cast<const float4*>(sm + k * DH + c0 + 4);
+    const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      acc[0][j] = fmaf(a0, mv[j], acc[0][j]);
+      acc[1][j] = fmaf(a1, mv[j], acc[1][j]);
     }
   }
-  *reinterpret_cast<float4*>(C + (size_t)r * DH + c0) = make_float4(acc[0], acc[1], acc[2], acc[3]);
-  *reinterpret_cast<float4*>(C + (size_t)r * DH + c0 + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+#pragma unroll
+  for (int rr = 0; rr < 2; ++rr) {
+    *reinterpret_cast<float4*>(C + rr * DH) = make_float4(acc[rr][0], acc[rr][1], acc[rr][2], acc[rr][3]);
+    *reinterpret_cast<float4*>(C + rr * DH + 4) = make_float4(acc[rr][4], acc[rr][5], acc[rr][6], acc[rr][7]);
+  }
 }
 
 // Segments for one scan (1 = run it whole): only a single dense sequence whose
@@ -1243,6 +1246,8 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
     if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(state_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCombineSmem);
+    if (e != cudaSuccess) return e;
     attrs_set = true;
   }
   p.n_chains = 0;
@@ -1288,8 +1293,8 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   // phase 2: start states, W[j] = W[j-1] M_j + U_j
   for (int j = 1; j <= P - 2; ++j) {
-    state_combine_kernel<<<dim3((unsigned)sp.hv, DH / 16), 256, 0, s>>>(W + (j - 1) * hstate, Mt + (j - 1) * hstate,
-                                                                      W + j * hstate);
+    state_combine_kernel<<<dim3((unsigned)sp.hv, DH / 32), 256, kCombineSmem, s>>>(
+        W + (j - 1) * hstate, Mt + (j - 1) * hstate, W + j * hstate);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
