@@ -97,6 +97,7 @@ struct ChunkParams {
   void* out;
   gdn_dtype out_dtype;
   unsigned char* ws;  // kRecBytes per (chunk slot, value head)
+  int64_t rec0;       // chunk prep: record index of its first slot (segments prepared apart)
   // n_chains > 0: CTA row blockIdx.x / hv runs chains[row] instead of sequence
   // blockIdx.x / hv with state_in / state_out.
   int n_chains;
@@ -309,7 +310,7 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
   if (warp == 1) {
     chunk_cumsum(lane, sl, sG, seG, sdG, &sgamma);
     __syncwarp();
-    float* gates = reinterpret_cast<float*>(p.ws + ((size_t)slot * p.hv + h) * kRecBytes + 4 * kTile64);
+    float* gates = reinterpret_cast<float*>(p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes + 4 * kTile64);
     for (int i = lane; i < CH; i += 32) {
       gates[GATE_BETA + i] = sb[i];
       gates[GATE_EG + i] = seG[i];
@@ -385,7 +386,7 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
       v[s4 + 2] = (s4 + 2 <= t && t < n) ? exp2f(gt - g4.z) * v[s4 + 2] : 0.f;
       v[s4 + 3] = (s4 + 3 <= t && t < n) ? exp2f(gt - g4.w) * v[s4 + 3] : 0.f;
     }
-    unsigned char* rec = p.ws + ((size_t)slot * p.hv + h) * kRecBytes;
+    unsigned char* rec = p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       uint4 hi, lo;
@@ -470,7 +471,7 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
   {
     const int t = tid & 63;
     const bool lo_half = tid >= 64;
-    unsigned char* rec = p.ws + ((size_t)slot * p.hv + h) * kRecBytes + (lo_half ? kTile64 : 0);
+    unsigned char* rec = p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes + (lo_half ? kTile64 : 0);
     const float* trow = sT + t * kPrepAStride;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -1165,6 +1166,30 @@ __global__ void __launch_bounds__(256) state_combine_kernel(const float* __restr
   }
 }
 
+// A second stream (and its fork / join events) per device, made on first use.
+struct SideStream {
+  cudaStream_t stream;
+  cudaEvent_t fork, join;
+};
+SideStream* side_stream() {
+  constexpr int kMaxDevices = 64;
+  static SideStream streams[kMaxDevices];
+  static bool made[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (!made[dev]) {
+    SideStream& x = streams[dev];
+    int lo = 0, hi = 0;  // numerically greatest = lowest priority
+    if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
+        cudaStreamCreateWithPriority(&x.stream, cudaStreamNonBlocking, lo) != cudaSuccess ||
+        cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming) != cudaSuccess)
+      return nullptr;
+    made[dev] = true;
+  }
+  return &streams[dev];
+}
+
 // Segments for one scan (1 = run it whole): only a single dense sequence whose
 // heads leave most of the GPU idle is split.
 int seg_count(const ScanParams& p) {
@@ -1239,6 +1264,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   p.out = sp.out;
   p.out_dtype = sp.out_dtype;
   p.ws = static_cast<unsigned char*>(sp.workspace);
+  p.rec0 = 0;
 
   static bool attrs_set = false;
   if (!attrs_set) {
@@ -1263,19 +1289,49 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     p.cu = cu_dev;
     p.n_seqs = P;
   }
-  const int64_t slots = (N + CH - 1) / CH + p.n_seqs;
-  if (N > 0 && slots > 0) {
-    if (slots > 0x7fffffffLL || sp.hv > 65535) return cudaErrorInvalidConfiguration;
-    chunk_prep_kernel<<<dim3((unsigned)slots, (unsigned)sp.hv), 128, kPrepSmem, s>>>(qmap, kmap, p);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
   if (P <= 1) {
+    const int64_t slots = (N + CH - 1) / CH + p.n_seqs;
+    if (N > 0 && slots > 0) {
+      if (slots > 0x7fffffffLL || sp.hv > 65535) return cudaErrorInvalidConfiguration;
+      chunk_prep_kernel<<<dim3((unsigned)slots, (unsigned)sp.hv), 128, kPrepSmem, s>>>(qmap, kmap, p);
+      cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+    }
     const int64_t ctas = sp.n_seqs * sp.hv;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p);
     return cudaGetLastError();
   }
+  // Chunk records: segments 0..P-2 before phase 1; the last segment's (needed
+  // only by phase 3) on a low-priority side stream that starts with phase 1,
+  // on the SMs phase 1 leaves free.
+  SideStream* side = side_stream();
+  if (!side) return cudaErrorNotReady;
+  const int64_t nch_all = (N + CH - 1) / CH;
+  const int64_t last0 = (nch_all * (P - 1) / P);  // first chunk of the last segment
+  {
+    ChunkParams pf = p;
+    pf.n_seqs = P - 1;
+    chunk_prep_kernel<<<dim3((unsigned)(last0 + P - 1), (unsigned)sp.hv), 128, kPrepSmem, s>>>(qmap, kmap, pf);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = cudaEventRecord(side->fork, s);
+  if (e != cudaSuccess) return e;
+  e = cudaStreamWaitEvent(side->stream, side->fork, 0);
+  if (e != cudaSuccess) return e;
+  {
+    ChunkParams pl = p;
+    pl.cu = p.cu + (P - 1);
+    pl.n_seqs = 1;
+    pl.rec0 = last0;  // records are numbered by chunk over the segments in order
+    chunk_prep_kernel<<<dim3((unsigned)(nch_all - last0 + 1), (unsigned)sp.hv), 128, kPrepSmem, side->stream>>>(
+        qmap, kmap, pl);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  e = cudaEventRecord(side->join, side->stream);
+  if (e != cudaSuccess) return e;
   const SegLayout L = seg_layout(sp, P);
   const size_t hstate = (size_t)sp.hv * DH * DH;
   float* W = reinterpret_cast<float*>(p.ws + L.w);  // end states of segments 0..P-2, then their start states
@@ -1289,7 +1345,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     p1.chains[P - 2 + i] = {i, nullptr, Mt + (i - 1) * hstate, kChainIdentity | kChainZeroV | kChainNoOut};
   }
   chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p1);
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // phase 2: start states, W[j] = W[j-1] M_j + U_j
   for (int j = 1; j <= P - 2; ++j) {
@@ -1299,6 +1355,8 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     if (e != cudaSuccess) return e;
   }
   // phase 3: segments 1..P-1 from their start states; the last one's end state is the result
+  e = cudaStreamWaitEvent(s, side->join, 0);
+  if (e != cudaSuccess) return e;
   ChunkParams p3 = p;
   p3.n_chains = P - 1;
   for (int i = 1; i <= P - 1; ++i) p3.chains[i - 1] = {i, W + (i - 1) * hstate, i == P - 1 ? sp.state_out : nullptr, 0};
