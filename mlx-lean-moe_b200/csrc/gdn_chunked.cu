@@ -361,18 +361,24 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
     tmem_ld32(ta + 32, *reinterpret_cast<float(*)[32]>(v + 32));
     tmem_wait_ld();
   }
+  // Decay groups of four columns past the warp's last row are all masked
+  // and skipped (warp-uniform).  ex2.approx (relative error ~2^-22) is far
+  // below the bf16 hi/lo resolution of the records.
+  const int s_lim = (warp & 1) * 32 + 32;
   if (row < CH) {
     const int t = row;
     const float gt = sG[t], bt = sb[t];
     float* arow = sA + t * kPrepAStride;
 #pragma unroll
     for (int s4 = 0; s4 < CH; s4 += 4) {
-      const float4 g4 = *reinterpret_cast<const float4*>(sG + s4);
-      float4 a4;
-      a4.x = (s4 < t && t < n) ? bt * exp2f(gt - g4.x) * v[s4] : 0.f;
-      a4.y = (s4 + 1 < t && t < n) ? bt * exp2f(gt - g4.y) * v[s4 + 1] : 0.f;
-      a4.z = (s4 + 2 < t && t < n) ? bt * exp2f(gt - g4.z) * v[s4 + 2] : 0.f;
-      a4.w = (s4 + 3 < t && t < n) ? bt * exp2f(gt - g4.w) * v[s4 + 3] : 0.f;
+      float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (s4 < s_lim) {
+        const float4 g4 = *reinterpret_cast<const float4*>(sG + s4);
+        a4.x = (s4 < t && t < n) ? bt * ex2_approx(gt - g4.x) * v[s4] : 0.f;
+        a4.y = (s4 + 1 < t && t < n) ? bt * ex2_approx(gt - g4.y) * v[s4 + 1] : 0.f;
+        a4.z = (s4 + 2 < t && t < n) ? bt * ex2_approx(gt - g4.z) * v[s4 + 2] : 0.f;
+        a4.w = (s4 + 3 < t && t < n) ? bt * ex2_approx(gt - g4.w) * v[s4 + 3] : 0.f;
+      }
       *reinterpret_cast<float4*>(arow + s4) = a4;
     }
   } else {
@@ -380,11 +386,15 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
     const float gt = sG[t];
 #pragma unroll
     for (int s4 = 0; s4 < CH; s4 += 4) {
-      const float4 g4 = *reinterpret_cast<const float4*>(sG + s4);
-      v[s4] = (s4 <= t && t < n) ? exp2f(gt - g4.x) * v[s4] : 0.f;
-      v[s4 + 1] = (s4 + 1 <= t && t < n) ? exp2f(gt - g4.y) * v[s4 + 1] : 0.f;
-      v[s4 + 2] = (s4 + 2 <= t && t < n) ? exp2f(gt - g4.z) * v[s4 + 2] : 0.f;
-      v[s4 + 3] = (s4 + 3 <= t && t < n) ? exp2f(gt - g4.w) * v[s4 + 3] : 0.f;
+      if (s4 < s_lim) {
+        const float4 g4 = *reinterpret_cast<const float4*>(sG + s4);
+        v[s4] = (s4 <= t && t < n) ? ex2_approx(gt - g4.x) * v[s4] : 0.f;
+        v[s4 + 1] = (s4 + 1 <= t && t < n) ? ex2_approx(gt - g4.y) * v[s4 + 1] : 0.f;
+        v[s4 + 2] = (s4 + 2 <= t && t < n) ? ex2_approx(gt - g4.z) * v[s4 + 2] : 0.f;
+        v[s4 + 3] = (s4 + 3 <= t && t < n) ? ex2_approx(gt - g4.w) * v[s4 + 3] : 0.f;
+      } else {
+        v[s4] = v[s4 + 1] = v[s4 + 2] = v[s4 + 3] = 0.f;
+      }
     }
     unsigned char* rec = p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes;
 #pragma unroll
