@@ -312,6 +312,17 @@ gdn_status check_block(const gdn_block_args* a, gdn::BlockParams* p, gdn::ScanPa
   if (st != GDN_OK) return st;
   st = pick_algo(&sa, *sp, chunked);
   if (st != GDN_OK) return st;
+  // The chunked scan applies the gated norm in its output stage and writes the
+  // layer output directly (bf16 activations, z 16-byte aligned).
+  const int64_t conv_dim = 2LL * a->hk * a->dk + (int64_t)a->hv * a->dv;
+  if (*chunked && a->act_dtype == GDN_BF16 && a->mixed_stride_t % 8 == 0 && conv_dim % 8 == 0 &&
+      aligned16(a->mixed)) {
+    sp->z = static_cast<const __nv_bfloat16*>(a->mixed) + conv_dim;
+    sp->z_st = a->mixed_stride_t;
+    sp->norm_w = a->norm_w;
+    sp->norm_eps = a->eps;
+    sp->out = a->out;
+  }
   const size_t scan_bytes = *chunked ? gdn::chunked_workspace_bytes(*sp) : 0;
   L->total = L->scan + scan_bytes;
   sp->workspace = ws + L->scan;
@@ -352,6 +363,7 @@ gdn_status gdn_fused_block(const gdn_block_args* args, gdn_stream_t stream) {
   if (st != GDN_OK) return st;
   st = cuda_status(chunked ? gdn::launch_chunked_scan(sp, s) : gdn::launch_serial_scan(sp, s), "scan launch");
   if (st != GDN_OK) return st;
+  if (sp.z) return GDN_OK;  // the scan's output stage did the gated norm
   return cuda_status(gdn::launch_block_epilogue(p, s), "block epilogue launch");
 }
 

@@ -98,6 +98,11 @@ struct ChunkParams {
   gdn_dtype out_dtype;
   unsigned char* ws;  // kRecBytes per (chunk slot, value head)
   int64_t rec0;       // chunk prep: record index of its first slot (segments prepared apart)
+  // Fused block: the output stage applies out = silu(z) * rms_norm(y -> bf16,
+  // norm_w, eps) (z tiles by TMA), writing the layer output instead of y.
+  int gated;
+  const float* norm_w;
+  float norm_eps;
   // n_chains > 0: CTA row blockIdx.x / hv runs chains[row] instead of sequence
   // blockIdx.x / hv with state_in / state_out.
   int n_chains;
@@ -510,7 +515,8 @@ constexpr uint32_t OFF_GATES = OFF_KT + 16384;     // two 1 KB gate buffers (chu
 // own buffer, so that the next chunk's T and P loads need not wait for the
 // store to drain).
 constexpr uint32_t OFF_OSTAGE = OFF_GATES + 2 * kGateBytes;
-constexpr uint32_t SCAN_SMEM_USED = OFF_OSTAGE + 64 * DH * 4;
+constexpr uint32_t OFF_Z = OFF_OSTAGE + 64 * DH * 4;  // z tile [64 t][128 dv] bf16 (gated output)
+constexpr uint32_t SCAN_SMEM_USED = OFF_Z + 64 * DH * 2;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
 constexpr int kEpiThreads = 256;                   // warps 2-9: the state chain
 constexpr int kAuxThreads = 128;                   // warps 10-13: K^T and the output
@@ -531,7 +537,7 @@ constexpr uint32_t TM_DPHI = TM_D + 64, TM_DPLO = TM_D + 96;
 
 enum Bar {
   B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_P_FULL,
-  B_S_READY0, B_S_READY1, B_X_DONE, B_R_READY0, B_R_READY1, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_Y_FREE, B_O_FREE, B_T_EMPTY, B_P_EMPTY,
+  B_S_READY0, B_S_READY1, B_X_DONE, B_R_READY0, B_R_READY1, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_Y_FREE, B_O_FREE, B_T_EMPTY, B_P_EMPTY, B_Z_FULL, B_Z_EMPTY,
   B_DRAIN,
   N_BARS
 };
@@ -540,6 +546,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
                                                             const __grid_constant__ CUtensorMap kmap,
                                                             const __grid_constant__ CUtensorMap vmap,
                                                             const __grid_constant__ CUtensorMap omap,
+                                                            const __grid_constant__ CUtensorMap zmap,
                                                             const ChunkParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -600,7 +607,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
       // Loads issued per full barrier (each barrier has at most one in flight).
-      uint32_t n_kq = 0, n_v = 0, n_t = 0, n_p = 0;
+      uint32_t n_kq = 0, n_v = 0, n_t = 0, n_p = 0, n_z = 0;
       for (int64_t c = 0; c < nch; ++c) {
         const uint32_t par = (uint32_t)((c - 1) & 1);
         const int t0 = (int)(start + c * CH);
@@ -634,6 +641,14 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         mbar_arrive_expect_tx(&bars[B_P_FULL], 2 * kTile64);
         bulk_load(base + OFF_P, rec + 2 * kTile64, 2 * kTile64, &bars[B_P_FULL]);
         ++n_p;
+        // z of the gated output stage, last: it is needed only at the end of the chunk.
+        if (p.gated && !(flags & kChainNoOut)) {
+          if (n_z > 0 && !mbar_wait(&bars[B_Z_EMPTY], (n_z - 1) & 1, kWaitNs)) record_error(&abort_flag);
+          if (abort_flag) break;
+          mbar_arrive_expect_tx(&bars[B_Z_FULL], 64 * DH * 2);
+          tma_load_3d(base + OFF_Z, &zmap, &bars[B_Z_FULL], 0, h, t0);
+          ++n_z;
+        }
       }
       // After an abort, let the copies this thread started land (bounded)
       // before the CTA releases its shared memory.
@@ -642,6 +657,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         if (n_v) mbar_wait(&bars[B_V_FULL], (n_v - 1) & 1, kWaitNs);
         if (n_t) mbar_wait(&bars[B_T_FULL], (n_t - 1) & 1, kWaitNs);
         if (n_p) mbar_wait(&bars[B_P_FULL], (n_p - 1) & 1, kWaitNs);
+        if (n_z) mbar_wait(&bars[B_Z_FULL], (n_z - 1) & 1, kWaitNs);
       }
     }
   } else if (warp == 1) {
@@ -942,6 +958,9 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     const bool leader = e == 0;
     unsigned char* sm = base;
+    float nw[8];  // gated output: the norm weights of this lane's 8 dv
+#pragma unroll
+    for (int j = 0; j < 8; ++j) nw[j] = p.gated ? p.norm_w[(e & 15) * 8 + j] : 0.f;
     for (int64_t c = 0; c < nch; ++c) {
       const uint32_t par = (uint32_t)(c & 1);
       const int64_t t0 = start + c * CH;
@@ -1015,6 +1034,63 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         if (leader) mbar_arrive(&bars[B_O_FREE]);
         if (flags & kChainNoOut) {
           // a transition chain: only its final state is wanted
+        } else if (p.gated) {
+          // Fused-block output: y rounded to bf16 is staged [t][dv]; then the
+          // 16 lanes of a token (8 dv each) reduce its row, gate it with z
+          // and overwrite it in place: out = silu(z) * rms_norm(y, w, eps).
+          __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
+#pragma unroll
+          for (int i = 0; i < 64; ++i) st[i * DH + dv] = __float2bfloat16_rn(y[i]);
+          ok = mbar_wait(&bars[B_Z_FULL], par, kWaitNs);
+          if (!ok) record_error(&abort_flag);
+          if (named_sync_or(2, kAuxThreads, !ok)) break;  // every row is staged, z has landed
+          const int g8 = (e & 15) * 8;
+          const __nv_bfloat16* zt = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_Z);
+#pragma unroll 2
+          for (int it = 0; it < 8; ++it) {
+            const int tt = (e >> 4) + 8 * it;
+            const uint4 yu = *reinterpret_cast<const uint4*>(st + tt * DH + g8);
+            const uint4 zu = *reinterpret_cast<const uint4*>(zt + tt * DH + g8);
+            const uint32_t yw[4] = {yu.x, yu.y, yu.z, yu.w}, zw[4] = {zu.x, zu.y, zu.z, zu.w};
+            float yv[8], zv[8], ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              yv[2 * j] = bf16_lo_f(yw[j]);
+              yv[2 * j + 1] = bf16_hi_f(yw[j]);
+              zv[2 * j] = bf16_lo_f(zw[j]);
+              zv[2 * j + 1] = bf16_hi_f(zw[j]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(yv[j], yv[j], ss);
+#pragma unroll
+            for (int off = 8; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+            const float inv = rsqrtf(ss * (1.f / DH) + p.norm_eps);
+            uint32_t ow[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float n0 = __bfloat162float(__float2bfloat16_rn(yv[2 * j] * inv * nw[2 * j]));
+              const float n1 = __bfloat162float(__float2bfloat16_rn(yv[2 * j + 1] * inv * nw[2 * j + 1]));
+              ow[j] = pack_bf16(silu_fast(zv[2 * j]) * n0, silu_fast(zv[2 * j + 1]) * n1);
+            }
+            *reinterpret_cast<uint4*>(st + tt * DH + g8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          }
+          fence_async_smem();
+          named_sync(2, kAuxThreads);
+          if (leader) mbar_arrive(&bars[B_Z_EMPTY]);
+          if (n == CH) {
+            if (leader) {
+              tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
+              bulk_commit_group();
+            }
+          } else {  // ragged last chunk: the valid rows, 16 bytes per lane
+            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + g8;
+            for (int it = 0; it < 8; ++it) {
+              const int tt = (e >> 4) + 8 * it;
+              if (tt < n)
+                *reinterpret_cast<uint4*>(op + (size_t)tt * p.hv * DH) =
+                    *reinterpret_cast<const uint4*>(st + tt * DH + g8);
+            }
+          }
         } else if (n == CH) {
           // Whole chunk: stage [t][dv] in shared memory, one TMA tensor store.
           if (p.out_dtype == GDN_BF16) {
@@ -1245,13 +1321,18 @@ size_t chunked_workspace_bytes(const ScanParams& p) { return seg_layout(p, seg_c
 cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   if (!aligned_ptr16(sp.q) || !aligned_ptr16(sp.k) || !aligned_ptr16(sp.v) || !aligned_ptr16(sp.workspace))
     return cudaErrorMisalignedAddress;
-  CUtensorMap qmap, kmap, vmap, omap;
+  CUtensorMap qmap, kmap, vmap, omap, zmap;
   const int64_t N = sp.n_tokens;
+  const bool gated = sp.z != nullptr;
+  if (gated && (sp.out_dtype != GDN_BF16 || !aligned_ptr16(sp.z) || !aligned_elems(sp.z_st) || !sp.norm_w))
+    return cudaErrorInvalidValue;
+  std::memset(&zmap, 0, sizeof(zmap));
   if (N > 0) {
     if (!make_map(&qmap, sp.q, N, sp.hk, sp.q_st, sp.q_sh, 64, true) ||
         !make_map(&kmap, sp.k, N, sp.hk, sp.k_st, sp.k_sh, 64, true) ||
         !make_map(&vmap, sp.v, N, sp.hv, sp.v_st, sp.v_sh, 128, false) ||
-        !make_out_map(&omap, sp.out, N, sp.hv, sp.out_dtype))
+        !make_out_map(&omap, sp.out, N, sp.hv, sp.out_dtype) ||
+        (gated && !make_map(&zmap, sp.z, N, sp.hv, sp.z_st, DH, 128, false)))
       return cudaErrorInvalidValue;
   } else {
     std::memset(&qmap, 0, sizeof(qmap));
@@ -1275,6 +1356,9 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   p.out_dtype = sp.out_dtype;
   p.ws = static_cast<unsigned char*>(sp.workspace);
   p.rec0 = 0;
+  p.gated = gated ? 1 : 0;
+  p.norm_w = sp.norm_w;
+  p.norm_eps = sp.norm_eps;
 
   static bool attrs_set = false;
   if (!attrs_set) {
@@ -1309,7 +1393,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     }
     const int64_t ctas = sp.n_seqs * sp.hv;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p);
+    chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p);
     return cudaGetLastError();
   }
   // Chunk records: segments 0..P-2 before phase 1; the last segment's (needed
@@ -1354,7 +1438,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     p1.chains[i] = {i, nullptr, W + i * hstate, kChainNoOut};
     p1.chains[P - 2 + i] = {i, nullptr, Mt + (i - 1) * hstate, kChainIdentity | kChainZeroV | kChainNoOut};
   }
-  chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p1);
+  chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // phase 2: start states, W[j] = W[j-1] M_j + U_j
@@ -1370,7 +1454,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   ChunkParams p3 = p;
   p3.n_chains = P - 1;
   for (int i = 1; i <= P - 1; ++i) p3.chains[i - 1] = {i, W + (i - 1) * hstate, i == P - 1 ? sp.state_out : nullptr, 0};
-  chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, p3);
+  chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p3);
   return cudaGetLastError();
 }
 

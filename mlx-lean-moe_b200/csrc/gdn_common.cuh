@@ -80,6 +80,13 @@ struct ScanParams {
   // chunked only
   void* workspace;
   size_t workspace_bytes;
+  // chunked, optional (z != nullptr): out = silu(z) * rms_norm(y -> out dtype,
+  // norm_w, eps) in the output stage (the fused block's gated norm); z is
+  // [N, Hv, Dv] in the out dtype with token stride z_st and head stride Dv.
+  const void* z = nullptr;
+  int64_t z_st = 0;
+  const float* norm_w = nullptr;
+  float norm_eps = 0.f;
 };
 
 struct BlockParams {
