@@ -393,8 +393,12 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
 #pragma unroll
         for (int j = 0; j < K - 1; ++j) acc += w[i][j] * win[j][i];
         acc += w[i][K - 1] * cur[i];
-        x[i] = round_to<T>(silu_fast(round_to<T>(acc)));
+        x[i] = acc;
       }
+      round8<T>(x);  // the conv output, then SiLU of it, in the activation dtype
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = silu_fast(x[i]);
+      round8<T>(x);
       // q/k rms-norm: reduce over the lanes of this head (all lanes of a
       // warp holding any q/k channel shuffle; v-only warps skip it).
       float ss = 0.f;
@@ -411,7 +415,11 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
         const float inv = rsqrtf(ss / (float)p.dk + 1e-6f);
         const float scale = is_q ? qscale : kscale;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = round_to<T>(round_to<T>(x[i] * inv) * scale);
+        for (int i = 0; i < 8; ++i) x[i] *= inv;
+        round8<T>(x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] *= scale;
+        round8<T>(x);
         T* dst = static_cast<T*>(is_q ? p.q : p.k) + t * key_dim + (is_q ? c : c - key_dim);
         if (active) store8<T>(dst, x);
       } else {
@@ -459,7 +467,10 @@ __global__ void __launch_bounds__(256) block_epilogue_fast_kernel(const BlockPar
   const float inv = rsqrtf(ss / (float)p.dv + p.eps);
   float o[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] = silu_fast(z[i]) * round_to<T>(y[i] * inv * w[i]);
+  for (int i = 0; i < 8; ++i) o[i] = y[i] * inv * w[i];
+  round8<T>(o);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] *= silu_fast(z[i]);
   if (valid) store8<T>(static_cast<T*>(p.out) + rr * p.dv + d0, o);
 }
 

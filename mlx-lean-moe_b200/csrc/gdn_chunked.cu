@@ -515,7 +515,11 @@ constexpr uint32_t OFF_GATES = OFF_KT + 16384;     // two 1 KB gate buffers (chu
 // own buffer, so that the next chunk's T and P loads need not wait for the
 // store to drain).
 constexpr uint32_t OFF_OSTAGE = OFF_GATES + 2 * kGateBytes;
-constexpr uint32_t OFF_Z = OFF_OSTAGE + 64 * DH * 4;  // z tile [64 t][128 dv] bf16 (gated output)
+// z tiles [64 t][128 dv] bf16 of the gated output, double-buffered: the
+// second one in the upper half of the staging buffer (the gated output is
+// bf16, so the staging needs only its lower half).
+constexpr uint32_t OFF_Z = OFF_OSTAGE + 64 * DH * 4;
+constexpr uint32_t OFF_Z2 = OFF_OSTAGE + 64 * DH * 2;
 constexpr uint32_t SCAN_SMEM_USED = OFF_Z + 64 * DH * 2;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
 constexpr int kEpiThreads = 256;                   // warps 2-9: the state chain
@@ -537,7 +541,7 @@ constexpr uint32_t TM_DPHI = TM_D + 64, TM_DPLO = TM_D + 96;
 
 enum Bar {
   B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_P_FULL,
-  B_S_READY0, B_S_READY1, B_X_DONE, B_R_READY0, B_R_READY1, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_Y_FREE, B_O_FREE, B_T_EMPTY, B_P_EMPTY, B_Z_FULL, B_Z_EMPTY,
+  B_S_READY0, B_S_READY1, B_X_DONE, B_R_READY0, B_R_READY1, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_Y_FREE, B_O_FREE, B_T_EMPTY, B_P_EMPTY, B_Z_FULL0, B_Z_FULL1,
   B_DRAIN,
   N_BARS
 };
@@ -589,7 +593,8 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     s_end = en;
     s_cbase = chunk_base_of(p, b);
     abort_flag = 0;
-    for (int i = 0; i < N_BARS; ++i) mbar_init(&bars[i], (i == B_KQ_EMPTY) ? 2 : 1);
+    // KQ_EMPTY: the X/Y MMA, the K^T transpose and the output warps (done with the gates).
+    for (int i = 0; i < N_BARS; ++i) mbar_init(&bars[i], (i == B_KQ_EMPTY) ? 3 : 1);
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(&tmem_base, 512);
@@ -602,62 +607,93 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0 && nch > 0) {
-      prefetch_tensormap(&qmap);
-      prefetch_tensormap(&kmap);
-      prefetch_tensormap(&vmap);
+    // Lane 0 issues the loads.  With the gated output (whose norm keeps the
+    // output warps busy) the whole warp then transposes the chunk's K into
+    // K^T (the state update's operand) once it has landed and the previous
+    // state update has read the last K^T: 128 blocks of (8 tokens x 8 dk),
+    // four per ldmatrix/stmatrix pair.  Otherwise the output warps do it.
+    if (nch > 0) {
+      if (lane == 0) {
+        prefetch_tensormap(&qmap);
+        prefetch_tensormap(&kmap);
+        prefetch_tensormap(&vmap);
+      }
       // Loads issued per full barrier (each barrier has at most one in flight).
-      uint32_t n_kq = 0, n_v = 0, n_t = 0, n_p = 0, n_z = 0;
+      uint32_t n_kq = 0, n_v = 0, n_t = 0, n_p = 0;
       for (int64_t c = 0; c < nch; ++c) {
         const uint32_t par = (uint32_t)((c - 1) & 1);
-        const int t0 = (int)(start + c * CH);
-        const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
-        if (c > 0 && !mbar_wait(&bars[B_KQ_EMPTY], par, kWaitNs)) record_error(&abort_flag);
-        if (abort_flag) break;
-        mbar_arrive_expect_tx(&bars[B_KQ_FULL], 32768 + kGateBytes);
-        for (int kb = 0; kb < 2; ++kb) {
-          tma_load_3d(base + OFF_KQ + kb * 16384, &kmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
-          tma_load_3d(base + OFF_KQ + kb * 16384 + 8192, &qmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
+        if (lane == 0) {
+          const int t0 = (int)(start + c * CH);
+          const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
+          do {
+            if (c > 0 && !mbar_wait(&bars[B_KQ_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+            if (abort_flag) break;
+            mbar_arrive_expect_tx(&bars[B_KQ_FULL], 32768 + kGateBytes);
+            for (int kb = 0; kb < 2; ++kb) {
+              tma_load_3d(base + OFF_KQ + kb * 16384, &kmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
+              tma_load_3d(base + OFF_KQ + kb * 16384 + 8192, &qmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
+            }
+            bulk_load(base + OFF_GATES + (c & 1) * kGateBytes, rec + 4 * kTile64, kGateBytes, &bars[B_KQ_FULL]);
+            ++n_kq;
+            if (c > 0 && !mbar_wait(&bars[B_V_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+            if (abort_flag) break;
+            if (flags & kChainZeroV) {
+              mbar_arrive(&bars[B_V_FULL]);
+            } else {
+              mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
+              tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
+            }
+            ++n_v;
+            // T and P once the previous chunk's Delta and O MMAs have read theirs.
+            if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+            if (abort_flag) break;
+            mbar_arrive_expect_tx(&bars[B_T_FULL], 2 * kTile64);
+            bulk_load(base + OFF_T, rec, 2 * kTile64, &bars[B_T_FULL]);
+            ++n_t;
+            if (c > 0 && !mbar_wait(&bars[B_P_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+            if (abort_flag) break;
+            mbar_arrive_expect_tx(&bars[B_P_FULL], 2 * kTile64);
+            bulk_load(base + OFF_P, rec + 2 * kTile64, 2 * kTile64, &bars[B_P_FULL]);
+            ++n_p;
+          } while (false);
         }
-        bulk_load(base + OFF_GATES + (c & 1) * kGateBytes, rec + 4 * kTile64, kGateBytes, &bars[B_KQ_FULL]);
-        ++n_kq;
-        if (c > 0 && !mbar_wait(&bars[B_V_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+        __syncwarp();
         if (abort_flag) break;
-        if (flags & kChainZeroV) {
-          mbar_arrive(&bars[B_V_FULL]);
-        } else {
-          mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
-          tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
+        if (!p.gated) {  // the output warps have the time for K^T
+          if (lane == 0) mbar_arrive(&bars[B_KQ_EMPTY]);
+          continue;
         }
-        ++n_v;
-        // T and P once the previous chunk's Delta and O MMAs have read theirs.
-        if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, kWaitNs)) record_error(&abort_flag);
-        if (abort_flag) break;
-        mbar_arrive_expect_tx(&bars[B_T_FULL], 2 * kTile64);
-        bulk_load(base + OFF_T, rec, 2 * kTile64, &bars[B_T_FULL]);
-        ++n_t;
-        if (c > 0 && !mbar_wait(&bars[B_P_EMPTY], par, kWaitNs)) record_error(&abort_flag);
-        if (abort_flag) break;
-        mbar_arrive_expect_tx(&bars[B_P_FULL], 2 * kTile64);
-        bulk_load(base + OFF_P, rec + 2 * kTile64, 2 * kTile64, &bars[B_P_FULL]);
-        ++n_p;
-        // z of the gated output stage, last: it is needed only at the end of the chunk.
-        if (p.gated && !(flags & kChainNoOut)) {
-          if (n_z > 0 && !mbar_wait(&bars[B_Z_EMPTY], (n_z - 1) & 1, kWaitNs)) record_error(&abort_flag);
-          if (abort_flag) break;
-          mbar_arrive_expect_tx(&bars[B_Z_FULL], 64 * DH * 2);
-          tma_load_3d(base + OFF_Z, &zmap, &bars[B_Z_FULL], 0, h, t0);
-          ++n_z;
+        const bool ok = mbar_wait(&bars[B_KQ_FULL], (uint32_t)(c & 1), kWaitNs) &&
+                        (c == 0 || mbar_wait(&bars[B_U_DONE], par, kWaitNs));
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0) record_error(&abort_flag);
+          break;
+        }
+        {
+          const int r = lane & 7, m = lane >> 3;
+#pragma unroll 4
+          for (int it = 0; it < 32; ++it) {
+            const int bi = it * 4 + m;                  // 0..127
+            const int cidx = bi >> 3, tb = bi & 7;      // dk chunk (0..15), token block
+            uint32_t f[4];
+            ldmatrix_x4_trans(smem_u32(base + OFF_KQ + sw128_chunk(128, tb * 8 + r, cidx >> 3, cidx & 7)), f);
+            stmatrix_x4(smem_u32(base + OFF_KT + sw128_chunk(128, cidx * 8 + r, 0, tb)), f);
+          }
+        }
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bars[B_KT_READY]);
+          mbar_arrive(&bars[B_KQ_EMPTY]);
         }
       }
       // After an abort, let the copies this thread started land (bounded)
       // before the CTA releases its shared memory.
-      if (abort_flag) {
+      if (lane == 0 && abort_flag) {
         if (n_kq) mbar_wait(&bars[B_KQ_FULL], (n_kq - 1) & 1, kWaitNs);
         if (n_v) mbar_wait(&bars[B_V_FULL], (n_v - 1) & 1, kWaitNs);
         if (n_t) mbar_wait(&bars[B_T_FULL], (n_t - 1) & 1, kWaitNs);
         if (n_p) mbar_wait(&bars[B_P_FULL], (n_p - 1) & 1, kWaitNs);
-        if (n_z) mbar_wait(&bars[B_Z_FULL], (n_z - 1) & 1, kWaitNs);
       }
     }
   } else if (warp == 1) {
@@ -951,7 +987,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       }
     }
   } else {
-    // ------------------------------------------------- K^T and output (aux)
+    // ------------------------------------------------- K^T (ungated) and output (aux)
     const int e = tid - 320;                  // 0..127 (warps 10-13)
     const int q = warp & 3;                   // TMEM lane quarter of this warp
     const int dv = q * 32 + lane;             // output row (value dim)
@@ -961,18 +997,35 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     float nw[8];  // gated output: the norm weights of this lane's 8 dv
 #pragma unroll
     for (int j = 0; j < 8; ++j) nw[j] = p.gated ? p.norm_w[(e & 15) * 8 + j] : 0.f;
+    // The z tiles are loaded by this group's leader into two buffers, chunk c
+    // into buffer c & 1, each as soon as chunk c - 2 is done with it.
+    const bool zload = p.gated && !(flags & kChainNoOut);
+    const uint32_t zoff[2] = {OFF_Z2, OFF_Z};
+    int64_t n_z = 0;  // z tiles issued
+    if (zload && leader) {
+      prefetch_tensormap(&zmap);
+      for (; n_z < 2 && n_z < nch; ++n_z) {
+        mbar_arrive_expect_tx(&bars[B_Z_FULL0 + (n_z & 1)], 64 * DH * 2);
+        tma_load_3d(base + zoff[n_z & 1], &zmap, &bars[B_Z_FULL0 + (n_z & 1)], 0, h, (int)(start + n_z * CH));
+      }
+    }
     for (int64_t c = 0; c < nch; ++c) {
       const uint32_t par = (uint32_t)(c & 1);
       const int64_t t0 = start + c * CH;
       const int n = (int)(end - t0 < CH ? end - t0 : CH);
       const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
 
-      // K^T (exact bf16 transpose) by 8x8 blocks: 128 blocks of (8 tokens x
-      // 8 dk), four per ldmatrix/stmatrix pair, eight pairs per warp.
-      bool ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
-      if (!ok) record_error(&abort_flag);
-      if (named_sync_or(2, kAuxThreads, !ok)) break;
-      {
+      // y = exp(G) Y for all 64 tokens of row dv, read out of TMEM as soon as
+      // the X/Y MMA is done so that the next chunk's can start early.
+      bool ok;
+      if (!p.gated) {
+        // K^T (exact bf16 transpose) by 8x8 blocks: 128 blocks of (8 tokens x
+        // 8 dk), four per ldmatrix/stmatrix pair, eight pairs per warp.  The
+        // previous state update has read the last K^T: this group passed its
+        // output stage, which follows it.
+        ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
+        if (!ok) record_error(&abort_flag);
+        if (named_sync_or(2, kAuxThreads, !ok)) break;
         const int r = lane & 7, m = lane >> 3;
 #pragma unroll
         for (int it = 0; it < 8; ++it) {
@@ -982,17 +1035,12 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           ldmatrix_x4_trans(smem_u32(sm + OFF_KQ + sw128_chunk(128, tb * 8 + r, cidx >> 3, cidx & 7)), f);
           stmatrix_x4(smem_u32(sm + OFF_KT + sw128_chunk(128, cidx * 8 + r, 0, tb)), f);
         }
+        fence_async_smem();
+        named_sync(2, kAuxThreads);
+        if (leader) mbar_arrive(&bars[B_KT_READY]);
       }
-      fence_async_smem();
-      named_sync(2, kAuxThreads);
-      if (leader) {
-        mbar_arrive(&bars[B_KT_READY]);
-        mbar_arrive(&bars[B_KQ_EMPTY]);
-      }
-
-      // y = exp(G) Y for all 64 tokens of row dv, read out of TMEM as soon as
-      // the X/Y MMA is done so that the next chunk's can start early.
-      ok = mbar_wait(&bars[B_X_DONE], par, kWaitNs);
+      // Y (the gates, read below, came with K and Q).
+      ok = mbar_wait(&bars[B_X_DONE], par, kWaitNs) && mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(2, kAuxThreads, !ok)) break;
       tc_fence_after();
@@ -1000,9 +1048,6 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       tmem_ld32(tq + TM_Y, *reinterpret_cast<float(*)[32]>(y));
       tmem_ld32(tq + TM_Y + 32, *reinterpret_cast<float(*)[32]>(y + 32));
       tmem_wait_ld();
-      tc_fence_before();
-      named_sync(2, kAuxThreads);
-      if (leader) mbar_arrive(&bars[B_Y_FREE]);
 #pragma unroll
       for (int i = 0; i < 64; i += 4) {
         const float4 g4 = *reinterpret_cast<const float4*>(gates + GATE_EG + i);
@@ -1010,6 +1055,12 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         y[i + 1] *= g4.y;
         y[i + 2] *= g4.z;
         y[i + 3] *= g4.w;
+      }
+      tc_fence_before();
+      named_sync(2, kAuxThreads);
+      if (leader) {
+        mbar_arrive(&bars[B_Y_FREE]);
+        mbar_arrive(&bars[B_KQ_EMPTY]);  // this chunk's gates are no longer needed here
       }
 
       // Output: y_t += O_t (both accumulator parts), then store.
@@ -1039,44 +1090,69 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           // 16 lanes of a token (8 dv each) reduce its row, gate it with z
           // and overwrite it in place: out = silu(z) * rms_norm(y, w, eps).
           __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
+          unsigned short* st16 = reinterpret_cast<unsigned short*>(st);
 #pragma unroll
-          for (int i = 0; i < 64; ++i) st[i * DH + dv] = __float2bfloat16_rn(y[i]);
-          ok = mbar_wait(&bars[B_Z_FULL], par, kWaitNs);
+          for (int i = 0; i < 64; i += 2) {
+            const uint32_t w2 = cvt_bf16x2(y[i], y[i + 1]);
+            st16[i * DH + dv] = (unsigned short)(w2 & 0xFFFFu);
+            st16[(i + 1) * DH + dv] = (unsigned short)(w2 >> 16);
+          }
+          ok = mbar_wait(&bars[B_Z_FULL0 + (c & 1)], (uint32_t)((c >> 1) & 1), kWaitNs);
           if (!ok) record_error(&abort_flag);
           if (named_sync_or(2, kAuxThreads, !ok)) break;  // every row is staged, z has landed
           const int g8 = (e & 15) * 8;
-          const __nv_bfloat16* zt = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_Z);
-#pragma unroll 2
-          for (int it = 0; it < 8; ++it) {
-            const int tt = (e >> 4) + 8 * it;
-            const uint4 yu = *reinterpret_cast<const uint4*>(st + tt * DH + g8);
-            const uint4 zu = *reinterpret_cast<const uint4*>(zt + tt * DH + g8);
-            const uint32_t yw[4] = {yu.x, yu.y, yu.z, yu.w}, zw[4] = {zu.x, zu.y, zu.z, zu.w};
-            float yv[8], zv[8], ss = 0.f;
+          const __nv_bfloat16* zt = reinterpret_cast<const __nv_bfloat16*>(sm + zoff[c & 1]);
+          // The 8 items (tokens (e >> 4) + 8 it) four at a time, phase by phase,
+          // so that the shuffle and special-function latencies overlap.
+#pragma unroll 1
+          for (int i0 = 0; i0 < 8; i0 += 4) {
+            uint4 yu[4], zu[4];
+            float ss[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              yv[2 * j] = bf16_lo_f(yw[j]);
-              yv[2 * j + 1] = bf16_hi_f(yw[j]);
-              zv[2 * j] = bf16_lo_f(zw[j]);
-              zv[2 * j + 1] = bf16_hi_f(zw[j]);
+            for (int k = 0; k < 4; ++k) {
+              const int tt = (e >> 4) + 8 * (i0 + k);
+              yu[k] = *reinterpret_cast<const uint4*>(st + tt * DH + g8);
+              zu[k] = *reinterpret_cast<const uint4*>(zt + tt * DH + g8);
             }
 #pragma unroll
-            for (int j = 0; j < 8; ++j) ss = fmaf(yv[j], yv[j], ss);
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t yw[4] = {yu[k].x, yu[k].y, yu[k].z, yu[k].w};
+              float acc = 0.f;
 #pragma unroll
-            for (int off = 8; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-            const float inv = rsqrtf(ss * (1.f / DH) + p.norm_eps);
-            uint32_t ow[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const float n0 = __bfloat162float(__float2bfloat16_rn(yv[2 * j] * inv * nw[2 * j]));
-              const float n1 = __bfloat162float(__float2bfloat16_rn(yv[2 * j + 1] * inv * nw[2 * j + 1]));
-              ow[j] = pack_bf16(silu_fast(zv[2 * j]) * n0, silu_fast(zv[2 * j + 1]) * n1);
+              for (int j = 0; j < 4; ++j) {
+                const float y0 = bf16_lo_f(yw[j]), y1 = bf16_hi_f(yw[j]);
+                acc = fmaf(y0, y0, acc);
+                acc = fmaf(y1, y1, acc);
+              }
+              ss[k] = acc;
             }
-            *reinterpret_cast<uint4*>(st + tt * DH + g8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+#pragma unroll
+            for (int off = 8; off >= 1; off >>= 1)
+#pragma unroll
+              for (int k = 0; k < 4; ++k) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], off);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int tt = (e >> 4) + 8 * (i0 + k);
+              const float inv = rsqrtf(ss[k] * (1.f / DH) + p.norm_eps);
+              const uint32_t yw[4] = {yu[k].x, yu[k].y, yu[k].z, yu[k].w};
+              const uint32_t zw[4] = {zu[k].x, zu[k].y, zu[k].z, zu[k].w};
+              uint32_t ow[4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                float n0 = bf16_lo_f(yw[j]) * inv * nw[2 * j], n1 = bf16_hi_f(yw[j]) * inv * nw[2 * j + 1];
+                round2_bf16(n0, n1);
+                ow[j] = pack_bf16(silu_fast(bf16_lo_f(zw[j])) * n0, silu_fast(bf16_hi_f(zw[j])) * n1);
+              }
+              *reinterpret_cast<uint4*>(st + tt * DH + g8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+            }
           }
           fence_async_smem();
           named_sync(2, kAuxThreads);
-          if (leader) mbar_arrive(&bars[B_Z_EMPTY]);
+          if (leader && c + 2 < nch) {  // z of chunk c + 2 into the tile just read
+            mbar_arrive_expect_tx(&bars[B_Z_FULL0 + (c & 1)], 64 * DH * 2);
+            tma_load_3d(base + zoff[c & 1], &zmap, &bars[B_Z_FULL0 + (c & 1)], 0, h, (int)(t0 + 2 * CH));
+            n_z = c + 3;
+          }
           if (n == CH) {
             if (leader) {
               tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
@@ -1094,9 +1170,13 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         } else if (n == CH) {
           // Whole chunk: stage [t][dv] in shared memory, one TMA tensor store.
           if (p.out_dtype == GDN_BF16) {
-            __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
+            unsigned short* st16 = reinterpret_cast<unsigned short*>(sm + OFF_OSTAGE);
 #pragma unroll
-            for (int i = 0; i < 64; ++i) st[i * DH + dv] = __float2bfloat16_rn(y[i]);
+            for (int i = 0; i < 64; i += 2) {
+              const uint32_t w2 = cvt_bf16x2(y[i], y[i + 1]);
+              st16[i * DH + dv] = (unsigned short)(w2 & 0xFFFFu);
+              st16[(i + 1) * DH + dv] = (unsigned short)(w2 >> 16);
+            }
           } else {
             float* st = reinterpret_cast<float*>(sm + OFF_OSTAGE);
 #pragma unroll
@@ -1127,6 +1207,12 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       }
     }
     if (leader) bulk_wait_group0();  // every output tile has reached global memory
+    // After an abort, let the z loads still in flight land (bounded) before
+    // the CTA releases its shared memory (tile i completes phase i >> 1 of
+    // barrier i & 1; waiting for a completed phase returns at once).
+    if (leader)
+      for (int64_t i = n_z - 2 < 0 ? 0 : n_z - 2; i < n_z; ++i)
+        mbar_wait(&bars[B_Z_FULL0 + (i & 1)], (uint32_t)((i >> 1) & 1), kWaitNs);
   }
 
   tc_fence_before();

@@ -30,6 +30,33 @@ __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_
 template <typename T>
 __device__ __forceinline__ float round_to(float x) { return to_f(from_f<T>(x)); }
 
+// Two floats to bf16 (round to nearest even) in one packed conversion: on
+// sm_100 it has about four times the per-value throughput of the scalar
+// conversion, which shares the special-function pipe with exp2 / rcp.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %2, %1;" : "=r"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void round2_bf16(float& a, float& b) {
+  const uint32_t w = cvt_bf16x2(a, b);
+  a = __uint_as_float(w << 16);
+  b = __uint_as_float(w & 0xFFFF0000u);
+}
+// Round 8 floats to the precision of T (pairwise for bf16).
+template <typename T>
+__device__ __forceinline__ void round8(float (&x)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = round_to<T>(x[i]);
+}
+template <>
+__device__ __forceinline__ void round8<float>(float (&)[8]) {}
+template <>
+__device__ __forceinline__ void round8<__nv_bfloat16>(float (&x)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) round2_bf16(x[i], x[i + 1]);
+}
+
 __device__ __forceinline__ float4 operator*(float4 a, float s) { return make_float4(a.x * s, a.y * s, a.z * s, a.w * s); }
 __device__ __forceinline__ float dot4(float4 a, float4 b) { return a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w; }
 
