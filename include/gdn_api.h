@@ -218,6 +218,39 @@ gdn_status gdn_fused_block(const gdn_block_args *args, gdn_stream_t stream);
  *    is read within a call. */
 gdn_status gdn_fused_block_noalloc(const gdn_block_args *args, gdn_stream_t stream);
 
+/* A linear projection with affine-quantized weights (the layer's in_proj_* /
+ * out_proj): out[m, n] = sum_k x[m, k] * W[n, k] with
+ * W[n, k] = scales[n, k / group_size] * q[n, k] + biases[n, k / group_size]
+ * (biases optional: 0), the unsigned `bits`-bit values q packed into uint32
+ * words along k, value j of a word in bits [j * bits, (j + 1) * bits).
+ *   x:      [m, k], row stride x_stride_m (elements, multiple of 8), bf16
+ *   w:      [n, k * bits / 32] uint32, rows contiguous
+ *   scales: [n, k / group_size], biases the same (or NULL), bf16
+ *   out:    [m, n], row stride out_stride_m (elements, multiple of 8), bf16
+ * bits 4 or 8; group_size 32, 64 or 128; k a multiple of 64 and of
+ * group_size.  Accumulation in float32; each dequantized weight is rounded
+ * to bf16 before the product.  Replaces quantized_linear / mx.quantized_matmul
+ * (model/moe_block.py:23-50) for the affine mode. */
+typedef struct {
+  int64_t m, n, k;
+  const void *x;
+  int64_t x_stride_m;
+  const uint32_t *w;
+  const void *scales;
+  const void *biases;
+  int32_t bits, group_size;
+  void *out;
+  int64_t out_stride_m;
+} gdn_qlinear_args;
+
+gdn_status gdn_quantized_linear(const gdn_qlinear_args *args, gdn_stream_t stream);
+
+/* W (as above) dequantized into a dense [n, k] matrix of out_dtype (float32
+ * or bf16) with row stride k: the same weights as gdn_quantized_linear uses,
+ * for callers whose activations are not bf16. */
+gdn_status gdn_dequantize(const gdn_qlinear_args *args, gdn_dtype out_dtype, void *dense,
+                          gdn_stream_t stream);
+
 /* Synchronises `stream`, then reports and clears any error a bounded
  * device-side wait recorded since the last call (GDN_ETIMEOUT), or a CUDA
  * error (GDN_ECUDA). */

@@ -372,6 +372,11 @@ gdn_status gdn_check_device_errors(gdn_stream_t stream) {
   if (e != cudaSuccess) return cuda_status(e, "stream synchronize");
   unsigned code = 0;
   e = gdn::read_and_clear_device_error(&code);
+  if (e == cudaSuccess) {
+    unsigned code2 = 0;
+    e = gdn::read_and_clear_qlinear_error(&code2);
+    code |= code2;
+  }
   if (e != cudaSuccess) return cuda_status(e, "reading the device error word");
   if (code) return fail(GDN_ETIMEOUT, "a bounded device wait gave up (code 0x%x)", code);
   return GDN_OK;

@@ -157,5 +157,6 @@ size_t chunked_workspace_bytes(const ScanParams& p);
 cudaError_t launch_chunked_scan(const ScanParams& p, cudaStream_t s);
 // Reads and clears the device error word of the chunked kernels (0 = none).
 cudaError_t read_and_clear_device_error(unsigned* code);
+cudaError_t read_and_clear_qlinear_error(unsigned* code);
 
 }  // namespace gdn

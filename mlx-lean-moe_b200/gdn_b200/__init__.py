@@ -15,18 +15,23 @@ from .gated_delta import (
     gated_delta_step,
 )
 from .linear_attention import LinearAttentionShape, Qwen3_5LinearAttention, gated_delta_block
+from .quantized import LinearWeights, QuantScheme, dequantize, quantized_linear
 from .recurrent_cache import BatchedRecurrentCache, RecurrentCache
 
 __all__ = [
     "BatchedRecurrentCache",
     "LinearAttentionShape",
+    "LinearWeights",
+    "QuantScheme",
     "Qwen3_5LinearAttention",
     "RecurrentCache",
     "check_device_errors",
+    "dequantize",
     "forget_gate",
     "gated_delta_block",
     "gated_delta_decode",
     "gated_delta_scan",
     "gated_delta_scan_varlen",
     "gated_delta_step",
+    "quantized_linear",
 ]

@@ -62,6 +62,18 @@ class BlockArgs(ctypes.Structure):
     ]
 
 
+class QLinearArgs(ctypes.Structure):
+    """``gdn_qlinear_args``."""
+
+    _fields_ = [
+        ("m", _i64), ("n", _i64), ("k", _i64),
+        ("x", _p), ("x_stride_m", _i64),
+        ("w", _p), ("scales", _p), ("biases", _p),
+        ("bits", _i32), ("group_size", _i32),
+        ("out", _p), ("out_stride_m", _i64),
+    ]
+
+
 EXPORTS = {
     "gdn_version": (ctypes.c_int, []),
     "gdn_last_error": (ctypes.c_char_p, []),
@@ -72,6 +84,8 @@ EXPORTS = {
     "gdn_block_workspace_size": (_enum, [ctypes.POINTER(BlockArgs), ctypes.POINTER(ctypes.c_size_t)]),
     "gdn_fused_block": (_enum, [ctypes.POINTER(BlockArgs), _p]),
     "gdn_fused_block_noalloc": (_enum, [ctypes.POINTER(BlockArgs), _p]),
+    "gdn_quantized_linear": (_enum, [ctypes.POINTER(QLinearArgs), _p]),
+    "gdn_dequantize": (_enum, [ctypes.POINTER(QLinearArgs), _enum, _p, _p]),
     "gdn_check_device_errors": (_enum, [_p]),
 }
 

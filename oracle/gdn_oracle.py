@@ -429,3 +429,82 @@ def rel_l2(actual, expected):
     den = math.sqrt(float(np.sum(e * e)))
     num = math.sqrt(float(np.sum((a - e) ** 2)))
     return num / den if den > 0 else num
+
+
+# ---------------------------------------------------------------------------
+# Affine-quantized linear projections (model/moe_block.py:23-50).
+#
+# The reference calls mx.quantized_matmul (mlx 0.32.2, uv.lock:268-269), a
+# third-party kernel absent from the reference tree.  Its published affine
+# format: the unsigned `bits`-bit values of a row are packed into uint32
+# words along the input dimension, value j of a word in bits
+# [j * bits, (j + 1) * bits); one scale and one bias per `group_size`
+# consecutive inputs; W = scale * q + bias.  Parity for this part is unpinned
+# against mlx itself (not installable here): the checks are the format's
+# known-answer packings and this restatement.
+
+
+def pack_affine(q, bits):
+    """Pack unsigned values q[n, k] (< 2**bits) into uint32 words [n, k * bits / 32]."""
+
+    q = np.asarray(q, np.uint64)
+    n, k = q.shape
+    per = 32 // bits
+    if 32 % bits or k % per:
+        raise ValueError("k must fill whole words")
+    if np.any(q >> np.uint64(bits)):
+        raise ValueError("value out of range for the bit width")
+    q = q.reshape(n, k // per, per)
+    shifts = (np.arange(per, dtype=np.uint64) * np.uint64(bits))[None, None, :]
+    return np.bitwise_or.reduce(q << shifts, axis=2).astype(np.uint32)
+
+
+def unpack_affine(w, bits):
+    """The inverse of pack_affine: uint32 words [n, kw] -> values [n, kw * 32 / bits]."""
+
+    w = np.asarray(w, np.uint32).astype(np.uint64)
+    n, kw = w.shape
+    per = 32 // bits
+    shifts = (np.arange(per, dtype=np.uint64) * np.uint64(bits))[None, None, :]
+    vals = (w[:, :, None] >> shifts) & np.uint64((1 << bits) - 1)
+    return vals.reshape(n, kw * per).astype(np.int64)
+
+
+def quantize_affine(dense, bits, group_size):
+    """Test weights: per-group min/max affine quantization of dense[n, k] with
+    bf16 scales and biases (bias = the group minimum, scale = range / levels).
+    Returns (words, scales, biases) with scales and biases as float32 holding
+    bf16 values."""
+
+    dense = np.asarray(dense, np.float32)
+    n, k = dense.shape
+    g = dense.reshape(n, k // group_size, group_size)
+    lo, hi = g.min(axis=2), g.max(axis=2)
+    levels = (1 << bits) - 1
+    scales = bf16_round(np.maximum(hi - lo, 1e-8) / levels)
+    biases = bf16_round(lo)
+    q = np.rint((g - biases[:, :, None]) / scales[:, :, None])
+    q = np.clip(q, 0, levels).astype(np.int64).reshape(n, k)
+    return pack_affine(q, bits), scales, biases
+
+
+def dequant_affine(words, scales, biases, bits, group_size):
+    """W[n, k] = scale * q + bias, each element rounded once to bf16 (the
+    operand the tensor-core GEMM multiplies).  scale * q is exact in float32
+    (an 8-bit mantissa times an integer below 256), so the float32 sum is one
+    fused multiply-add.  biases=None means zero."""
+
+    q = unpack_affine(words, bits).astype(np.float32)
+    n, k = q.shape
+    s = np.repeat(np.asarray(scales, np.float32), group_size, axis=1)
+    b = np.zeros_like(s) if biases is None else np.repeat(np.asarray(biases, np.float32), group_size, axis=1)
+    if s.shape != (n, k):
+        raise ValueError("scales do not match the packed weights")
+    return bf16_round(s * q + b)
+
+
+def quantized_linear_ref(x, words, scales, biases, bits, group_size):
+    """x[m, k] @ W^T in float64 with W from dequant_affine; returns float64 [m, n]."""
+
+    w = dequant_affine(words, scales, biases, bits, group_size).astype(np.float64)
+    return np.asarray(x, np.float64) @ w.T
