@@ -40,24 +40,27 @@ namespace {
 
 using namespace sm100;
 
-constexpr int QBM = 128, QBN = 256, QBK = 64;
+constexpr int QBM = 256, QBN = 256, QBK = 64;  // CTA tile: two 128-row accumulators share each B tile
 constexpr int kAStages = 3, kBStages = 2;
-constexpr uint32_t kATile = QBM * QBK * 2;            // 16 KB
+constexpr uint32_t kATile = QBM * QBK * 2;            // 32 KB
 constexpr uint32_t kWTile = QBN * QBK;                // up to 8-bit: 16 KB
 constexpr uint32_t kBTile = QBN * QBK * 2;            // 32 KB
-constexpr uint32_t QOFF_A = 0;
+constexpr uint32_t kOutSub = 128 * 64 * 2;            // one 128 x 64 bf16 output sub-tile
+constexpr uint32_t QOFF_A = 0;                        // A and W rings, then the output staging (8 sub-tiles)
 constexpr uint32_t QOFF_W = QOFF_A + kAStages * kATile;
-constexpr uint32_t QOFF_B = QOFF_W + kAStages * kWTile;  // also the output staging (4 x 16 KB)
+constexpr uint32_t QOFF_B = QOFF_W + kAStages * kWTile;
 constexpr uint32_t QSMEM_USED = QOFF_B + kBStages * kBTile;
+static_assert(8 * kOutSub <= QOFF_B, "output staging overlaps the B ring");
 constexpr size_t kQSmem = 1024 + QSMEM_USED;
-constexpr int kDqThreads = 256;  // warps 2-9
+constexpr int kDqThreads = 512;  // warps 2-17: two threads per weight row (one per 32-value half of a K-block)
+constexpr int kQThreads = 64 + kDqThreads;
 constexpr uint64_t kQWaitNs = 2000000000ull;
 
 struct QParams {
   int64_t m, n, k;
   const __nv_bfloat16* scales;
   const __nv_bfloat16* biases;
-  int bits, gs;
+  int bits, gs, gshift;  // gs == 1 << gshift
 };
 
 enum QBar { Q_FULL0, Q_EMPTY0 = Q_FULL0 + kAStages, Q_BFULL0 = Q_EMPTY0 + kAStages, Q_BEMPTY0 = Q_BFULL0 + kBStages,
@@ -72,37 +75,42 @@ __device__ __forceinline__ void q_record(volatile int* abort_flag) {
 __device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t u) { return *reinterpret_cast<__nv_bfloat162*>(&u); }
 __device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
 
-// Eight 4-bit values of one word -> four bf16x2 words s * q + b.
+// Eight 4-bit values of one word -> four bf16x2 words s * q + b, in value
+// order.  One AND-OR per pair puts nibbles j and j + 4 into the mantissas of
+// (128.0, 128.0); a byte permute pairs them up as (2i, 2i + 1).
 __device__ __forceinline__ uint4 dequant_word4(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
-  const __nv_bfloat162 k128 = as_bf2(0x43004300u);  // (128.0, 128.0)
+  const uint32_t m = 0x000F000Fu, mag = 0x43004300u;
+  const uint32_t p0 = (w & m) | mag, p1 = ((w >> 4) & m) | mag;  // (v0, v4), (v1, v5)
+  const uint32_t p2 = ((w >> 8) & m) | mag, p3 = ((w >> 12) & m) | mag;  // (v2, v6), (v3, v7)
+  const uint32_t q[4] = {__byte_perm(p0, p1, 0x5410), __byte_perm(p2, p3, 0x5410), __byte_perm(p0, p1, 0x7632),
+                         __byte_perm(p2, p3, 0x7632)};
+  const __nv_bfloat162 k128 = as_bf2(mag);
   uint32_t o[4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t t = w >> (8 * i);
-    const uint32_t p = (t & 0xFu) | ((t << 12) & 0xF0000u) | 0x43004300u;  // (128 + q_2i, 128 + q_2i+1)
-    o[i] = as_u32(__hfma2(__hsub2(as_bf2(p), k128), s2, b2));
-  }
+  for (int i = 0; i < 4; ++i) o[i] = as_u32(__hfma2(__hsub2(as_bf2(q[i]), k128), s2, b2));
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Four 8-bit values of each of two words -> four bf16x2 words s * q + b.
+// Eight 8-bit values of two words -> four bf16x2 words s * q + b.  A byte
+// permute places each value in the mantissa of 2^23; s * q is exact in
+// float32, so the FMA rounds once before the pairwise bf16 rounding.
 __device__ __forceinline__ uint4 dequant_words8(uint32_t w0, uint32_t w1, float s, float b) {
   uint32_t o[4];
-  const uint32_t ws[2] = {w0, w1};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint32_t w = ws[i >> 1];
-    const int sh = 16 * (i & 1);
-    const float q0 = __uint_as_float(0x4B000000u | ((w >> sh) & 0xFFu)) - 8388608.f;
-    const float q1 = __uint_as_float(0x4B000000u | ((w >> (sh + 8)) & 0xFFu)) - 8388608.f;
+    const uint32_t w = i < 2 ? w0 : w1;
+    const int j = 2 * (i & 1);
+    const float q0 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540 + j)) - 8388608.f;
+    const float q1 = __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7541 + j)) - 8388608.f;
     o[i] = cvt_bf16x2(fmaf(s, q0, b), fmaf(s, q1, b));
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-__global__ void __launch_bounds__(320, 1) qlinear_kernel(const __grid_constant__ CUtensorMap amap,
-                                                         const __grid_constant__ CUtensorMap wmap,
-                                                         const __grid_constant__ CUtensorMap omap, const QParams p) {
+__global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_constant__ CUtensorMap amap,
+                                                               const __grid_constant__ CUtensorMap wmap,
+                                                               const __grid_constant__ CUtensorMap omap,
+                                                               const QParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t bars[Q_NBARS];
@@ -123,7 +131,7 @@ __global__ void __launch_bounds__(320, 1) qlinear_kernel(const __grid_constant__
     }
     fence_mbar_init();
   }
-  if (warp == 0) tmem_alloc(&tmem_base, QBN);
+  if (warp == 0) tmem_alloc(&tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -154,7 +162,7 @@ __global__ void __launch_bounds__(320, 1) qlinear_kernel(const __grid_constant__
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16_f32(QBM, QBN);
+      const uint32_t idesc = idesc_bf16_f32(128, QBN);
       int kb = 0;
       for (; kb < nk; ++kb) {
         const int s = kb % kAStages, sb = kb % kBStages;
@@ -167,109 +175,110 @@ __global__ void __launch_bounds__(320, 1) qlinear_kernel(const __grid_constant__
         tc_fence_after();
         const uint32_t a = smem_u32(base + QOFF_A + s * kATile), b = smem_u32(base + QOFF_B + sb * kBTile);
 #pragma unroll
-        for (int ks = 0; ks < QBK / 16; ++ks)
-          mma_bf16(tmem, sdesc_sw128(a + ks * 32), sdesc_sw128(b + ks * 32), idesc, kb > 0 || ks > 0);
+        for (int ks = 0; ks < QBK / 16; ++ks) {
+          const uint64_t bd = sdesc_sw128(b + ks * 32);
+          mma_bf16(tmem, sdesc_sw128(a + ks * 32), bd, idesc, kb > 0 || ks > 0);                   // rows 0-127
+          mma_bf16(tmem + QBN, sdesc_sw128(a + 128 * 128 + ks * 32), bd, idesc, kb > 0 || ks > 0);  // rows 128-255
+        }
         mma_commit(&bars[Q_EMPTY0 + s]);
         mma_commit(&bars[Q_BEMPTY0 + sb]);
       }
-      // The accumulator is complete (or, after an abort, every MMA issued
+      // The accumulators are complete (or, after an abort, every MMA issued
       // has finished) when this commit's barrier completes.
       mma_commit(&bars[Q_ACC]);
       if (kb < nk) mbar_wait(&bars[Q_ACC], 0, kQWaitNs);
     }
   } else {
     // ------------------------------------------- dequantization, then epilogue
-    const int r = tid - 64;  // weight row of the tile (0..255)
+    const int t = tid - 64;
+    const int r = t & (QBN - 1), h = t >> 8;  // weight row of the tile, 32-value half of each K-block
     const int64_t row = n0 + r;
     const bool live = row < p.n;
-    const int64_t groups = p.k / p.gs;
+    const int groups = (int)(p.k >> p.gshift);
     const __nv_bfloat16* srow = p.scales + (live ? row : 0) * groups;
     const __nv_bfloat16* brow = p.biases ? p.biases + (live ? row : 0) * groups : nullptr;
-    const __nv_bfloat16 bzero = __float2bfloat16_rn(0.f);
-    // (scale, bias) of this row's first and second half of a K-block, one block ahead.
-    auto gate_of = [&](int kb, int hlf) -> int64_t { return ((int64_t)kb * QBK + hlf * 32) / p.gs; };
-    __nv_bfloat16 s_nx[2], b_nx[2];
+    // (scale, bias) of this thread's half of K-block kb; rows past n get
+    // zeros, so their (zero-filled) weights dequantize to 0.
+    auto load_sb = [&](int kb, __nv_bfloat16& sv, __nv_bfloat16& bv) {
+      const int g = (kb * QBK + h * 32) >> p.gshift;
+      sv = live ? srow[g] : __float2bfloat16_rn(0.f);
+      bv = (live && brow) ? brow[g] : __float2bfloat16_rn(0.f);
+    };
+    // Byte offsets of this thread's four 16-byte chunks (values 32h + 8j ..)
+    // in a 128-byte-swizzled K-major B tile.
+    uint32_t boff[4];
 #pragma unroll
-    for (int hlf = 0; hlf < 2; ++hlf) {
-      s_nx[hlf] = live ? srow[gate_of(0, hlf)] : bzero;
-      b_nx[hlf] = (live && brow) ? brow[gate_of(0, hlf)] : bzero;
-    }
+    for (int j = 0; j < 4; ++j) boff[j] = sw128_chunk(QBN, r, 0, 4 * h + j);
+    __nv_bfloat16 s_nx, b_nx;
+    load_sb(0, s_nx, b_nx);
     bool ok = true;
     for (int kb = 0; kb < nk; ++kb) {
       const int s = kb % kAStages, sb = kb % kBStages;
-      const __nv_bfloat16 s_cur[2] = {s_nx[0], s_nx[1]}, b_cur[2] = {b_nx[0], b_nx[1]};
-      if (kb + 1 < nk) {
-#pragma unroll
-        for (int hlf = 0; hlf < 2; ++hlf) {
-          s_nx[hlf] = live ? srow[gate_of(kb + 1, hlf)] : bzero;
-          b_nx[hlf] = (live && brow) ? brow[gate_of(kb + 1, hlf)] : bzero;
-        }
-      }
+      const __nv_bfloat16 s_cur = s_nx, b_cur = b_nx;
+      if (kb + 1 < nk) load_sb(kb + 1, s_nx, b_nx);
       ok = mbar_wait(&bars[Q_FULL0 + s], (uint32_t)((kb / kAStages) & 1), kQWaitNs) &&
            (kb < kBStages || mbar_wait(&bars[Q_BEMPTY0 + sb], (uint32_t)((kb / kBStages - 1) & 1), kQWaitNs));
       if (!ok) q_record(&abort_flag);
       if (named_sync_or(1, kDqThreads, !ok)) break;
-      const unsigned char* wsrc = base + QOFF_W + s * kWTile + (size_t)r * wbytes;
+      const unsigned char* wsrc = base + QOFF_W + s * kWTile + (size_t)r * wbytes + h * (wbytes / 2);
       unsigned char* bdst = base + QOFF_B + sb * kBTile;
       if (p.bits == 4) {
-        const uint4 w0 = reinterpret_cast<const uint4*>(wsrc)[0], w1 = reinterpret_cast<const uint4*>(wsrc)[1];
-        const uint32_t wd[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint4 w = *reinterpret_cast<const uint4*>(wsrc);
+        const __nv_bfloat162 s2 = __bfloat162bfloat162(s_cur), b2 = __bfloat162bfloat162(b_cur);
+        const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const __nv_bfloat162 s2 = __bfloat162bfloat162(s_cur[c >> 2]), b2 = __bfloat162bfloat162(b_cur[c >> 2]);
-          const uint4 v = live ? dequant_word4(wd[c], s2, b2) : make_uint4(0u, 0u, 0u, 0u);
-          *reinterpret_cast<uint4*>(bdst + sw128_chunk(QBN, r, 0, c)) = v;
-        }
+        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(bdst + boff[j]) = dequant_word4(wd[j], s2, b2);
       } else {
-        const uint4* w4 = reinterpret_cast<const uint4*>(wsrc);
-#pragma unroll
-        for (int c2 = 0; c2 < 4; ++c2) {
-          const uint4 w = w4[c2];
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int c = 2 * c2 + hh;
-            const float sv = __bfloat162float(s_cur[c >> 2]), bv = __bfloat162float(b_cur[c >> 2]);
-            const uint4 v = live ? dequant_words8(hh ? w.z : w.x, hh ? w.w : w.y, sv, bv) : make_uint4(0u, 0u, 0u, 0u);
-            *reinterpret_cast<uint4*>(bdst + sw128_chunk(QBN, r, 0, c)) = v;
-          }
-        }
+        const uint4 w01 = reinterpret_cast<const uint4*>(wsrc)[0], w23 = reinterpret_cast<const uint4*>(wsrc)[1];
+        const float sv = __bfloat162float(s_cur), bv = __bfloat162float(b_cur);
+        *reinterpret_cast<uint4*>(bdst + boff[0]) = dequant_words8(w01.x, w01.y, sv, bv);
+        *reinterpret_cast<uint4*>(bdst + boff[1]) = dequant_words8(w01.z, w01.w, sv, bv);
+        *reinterpret_cast<uint4*>(bdst + boff[2]) = dequant_words8(w23.x, w23.y, sv, bv);
+        *reinterpret_cast<uint4*>(bdst + boff[3]) = dequant_words8(w23.z, w23.w, sv, bv);
       }
       fence_async_smem();
       named_sync(1, kDqThreads);
-      if (r == 0) {
+      if (t == 0) {
         mbar_arrive(&bars[Q_BFULL0 + sb]);  // the operand is ready
         mbar_arrive(&bars[Q_EMPTY0 + s]);   // the packed weights are read
       }
     }
 
     // ------------------------------------------------------------ epilogue
+    // Warp w reads TMEM lanes 32 (w % 4) .. and columns 128 cb .. 128 cb + 127
+    // (cb = (w - 2) / 4): accumulator cb / 2 (tile rows 128 (cb / 2) ..),
+    // output columns 128 (cb % 2) ..; the staging (over the A and W rings,
+    // idle once the accumulators are complete) holds eight 128 x 64
+    // sub-tiles, accumulator-major.
     ok = !abort_flag && mbar_wait(&bars[Q_ACC], 0, kQWaitNs);
     if (!ok) q_record(&abort_flag);
     if (!named_sync_or(1, kDqThreads, !ok)) {
       tc_fence_after();
-      const int q = warp & 3, half = (warp - 2) >> 2;  // TMEM lane quarter; columns 128 * half ..
-      const int orow = q * 32 + lane;                  // output row of the tile
-      const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+      const int q = warp & 3, cb = (warp - 2) >> 2;
+      const int orow = q * 32 + lane;
+      const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + cb * 128;
 #pragma unroll 1
       for (int jj = 0; jj < 2; ++jj) {
-        const int j = half * 2 + jj;  // 64-column sub-tile
         float v[64];
-        tmem_ld32(tq + j * 64, *reinterpret_cast<float(*)[32]>(v));
-        tmem_ld32(tq + j * 64 + 32, *reinterpret_cast<float(*)[32]>(v + 32));
+        tmem_ld32(tq + jj * 64, *reinterpret_cast<float(*)[32]>(v));
+        tmem_ld32(tq + jj * 64 + 32, *reinterpret_cast<float(*)[32]>(v + 32));
         tmem_wait_ld();
-        unsigned char* st = base + QOFF_B + j * (QBM * 128);
+        unsigned char* st = base + QOFF_A + (uint32_t)(cb * 2 + jj) * kOutSub;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint4 o = make_uint4(cvt_bf16x2(v[8 * c], v[8 * c + 1]), cvt_bf16x2(v[8 * c + 2], v[8 * c + 3]),
                                      cvt_bf16x2(v[8 * c + 4], v[8 * c + 5]), cvt_bf16x2(v[8 * c + 6], v[8 * c + 7]));
-          *reinterpret_cast<uint4*>(st + sw128_chunk(QBM, orow, 0, c)) = o;
+          *reinterpret_cast<uint4*>(st + sw128_chunk(128, orow, 0, c)) = o;
         }
       }
       fence_async_smem();
       named_sync(1, kDqThreads);
-      if (r == 0) {
-        for (int j = 0; j < 4; ++j)
-          if (n0 + 64 * j < p.n) tma_store_2d(&omap, base + QOFF_B + j * (QBM * 128), (int)(n0 + 64 * j), (int)m0);
+      if (t == 0) {
+        for (int sub = 0; sub < 8; ++sub) {
+          const int64_t orow0 = m0 + 128 * (sub >> 2), ocol0 = n0 + 64 * (sub & 3);
+          if (orow0 < p.m && ocol0 < p.n)
+            tma_store_2d(&omap, base + QOFF_A + sub * kOutSub, (int)ocol0, (int)orow0);
+        }
         bulk_commit_group();
         bulk_wait_group_read0();
       }
@@ -277,7 +286,177 @@ __global__ void __launch_bounds__(320, 1) qlinear_kernel(const __grid_constant__
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, QBN);
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ---------------------------------------------------------------------------
+// Decode: m <= 8 tokens.  The weights stream from HBM once; each warp owns 16
+// weight rows and a strided share of K, dequantizes straight into the A
+// fragments of mma.sync m16n8k16 (A = 16 weight rows x 16 K, B = 16 K x 8
+// tokens) and accumulates in float32; the CTA's warps then add their K shares.
+//
+// Inside each run of 8 consecutive K the fragment takes the values in the
+// order (0, 4, 1, 5, 2, 6, 3, 7): one AND-OR of a 4-bit word yields exactly
+// the pairs (j, j + 4).  A dot product does not depend on the order of K, so
+// x is staged in shared memory in that same order and the products match.
+// ---------------------------------------------------------------------------
+constexpr int kGvMaxWarps = 16;
+constexpr int kGvMaxTokens = 8;
+constexpr int64_t kGvMaxK = 8192;  // staged x: 8 tokens x 8192 x 2 bytes = 128 KB
+
+struct GvParams {
+  int64_t m, n, k;
+  const __nv_bfloat16* x;
+  int64_t x_stride;
+  const uint32_t* w;
+  const __nv_bfloat16* scales;
+  const __nv_bfloat16* biases;
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  int gshift, row_groups;  // row_groups of 16 rows per CTA; the warps split K (warps / row_groups) ways
+};
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Values (j, j + 4) of a 4-bit word, j = 0..3, as bf16x2 s * q + b.
+__device__ __forceinline__ void gv_pairs4(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2, uint32_t (&o)[4]) {
+  const uint32_t m = 0x000F000Fu, mag = 0x43004300u;
+  const __nv_bfloat162 k128 = as_bf2(mag);
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    o[j] = as_u32(__hfma2(__hsub2(as_bf2(((w >> (4 * j)) & m) | mag), k128), s2, b2));
+}
+
+// Values (j, j + 4) of the 8-bit words w0 (values 0-3) and w1 (4-7).
+__device__ __forceinline__ void gv_pairs8(uint32_t w0, uint32_t w1, float s, float b, uint32_t (&o)[4]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float q0 = __uint_as_float(__byte_perm(w0, 0x4B000000u, 0x7540 + j)) - 8388608.f;
+    const float q1 = __uint_as_float(__byte_perm(w1, 0x4B000000u, 0x7540 + j)) - 8388608.f;
+    o[j] = cvt_bf16x2(fmaf(s, q0, b), fmaf(s, q1, b));
+  }
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(kGvMaxWarps * 32) qgemv_kernel(const GvParams p) {
+  extern __shared__ uint4 xs[];  // [m][k / 8] runs of 8, each in the order (0, 4, 1, 5, 2, 6, 3, 7)
+  __shared__ float red[kGvMaxWarps][4][32];
+  constexpr int U = BITS == 4 ? 4 : 2;       // chunks whose loads are in flight together
+  constexpr int NW = BITS / 4;               // uint4 per row and chunk: the thread's 32 values
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int64_t runs = p.k / 8;
+
+  for (int64_t i = tid; i < p.m * runs; i += blockDim.x) {
+    const int64_t tok = i / runs, r = i % runs;
+    const uint4 v = *reinterpret_cast<const uint4*>(p.x + tok * p.x_stride + 8 * r);
+    xs[i] = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
+                       __byte_perm(v.y, v.w, 0x7632));
+  }
+  __syncthreads();
+
+  const int ksplit = nwarps / p.row_groups;
+  const int rg = warp / ksplit, ks = warp % ksplit;
+  const int64_t rowA = ((int64_t)blockIdx.x * p.row_groups + rg) * 16 + g, rowB = rowA + 8;
+  const bool liveA = rowA < p.n, liveB = rowB < p.n;
+  const int64_t kw = p.k * BITS / 32, groups = p.k >> p.gshift;
+  const uint4* wA = reinterpret_cast<const uint4*>(p.w + (liveA ? rowA : 0) * kw);
+  const uint4* wB = reinterpret_cast<const uint4*>(p.w + (liveB ? rowB : 0) * kw);
+  const __nv_bfloat16* sA = p.scales + (liveA ? rowA : 0) * groups;
+  const __nv_bfloat16* sB = p.scales + (liveB ? rowB : 0) * groups;
+  const __nv_bfloat16* bA = p.biases ? p.biases + (liveA ? rowA : 0) * groups : nullptr;
+  const __nv_bfloat16* bB = p.biases ? p.biases + (liveB ? rowB : 0) * groups : nullptr;
+  const bool tok_live = g < p.m;
+  const uint4* xrow = xs + (tok_live ? g : 0) * runs;
+  const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
+
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int64_t nchunks = (p.k + 127) / 128;  // 128 K per warp step: 32 per thread
+  for (int64_t c0 = ks; c0 < nchunks; c0 += (int64_t)ksplit * U) {
+    uint4 va[U][NW], vb[U][NW];
+    __nv_bfloat16 sa[U], sb[U], ba[U], bb[U];
+    bool on[U];  // this lane's 32 values exist (lanes t4 >= 2 of a ragged last chunk, k % 128 == 64, have none)
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t kk = (c0 + (int64_t)u * ksplit) * 128 + 32 * t4;
+      on[u] = c0 + (int64_t)u * ksplit < nchunks && kk < p.k;
+      const int64_t grp = on[u] ? kk >> p.gshift : 0;
+      const int64_t wi = on[u] ? kk * BITS / 128 : 0;  // uint4 index of the thread's 32 values
+#pragma unroll
+      for (int e = 0; e < NW; ++e) {
+        va[u][e] = (on[u] && liveA) ? wA[wi + e] : make_uint4(0u, 0u, 0u, 0u);
+        vb[u][e] = (on[u] && liveB) ? wB[wi + e] : make_uint4(0u, 0u, 0u, 0u);
+      }
+      sa[u] = (on[u] && liveA) ? sA[grp] : zero;
+      sb[u] = (on[u] && liveB) ? sB[grp] : zero;
+      ba[u] = (on[u] && bA && liveA) ? bA[grp] : zero;
+      bb[u] = (on[u] && bB && liveB) ? bB[grp] : zero;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      // mma.sync is warp-wide: skip only whole chunks past the end (uniform
+      // across the warp); lanes without values feed zeros (zero words with
+      // zero scale and bias dequantize to 0, and their x is 0).
+      if (c0 + (int64_t)u * ksplit >= nchunks) continue;
+      const bool xon = on[u] && tok_live;
+      const int64_t run0 = on[u] ? ((c0 + (int64_t)u * ksplit) * 128 + 32 * t4) / 8 : 0;
+      if (BITS == 4) {
+        const __nv_bfloat162 sa2 = __bfloat162bfloat162(sa[u]), ba2 = __bfloat162bfloat162(ba[u]);
+        const __nv_bfloat162 sb2 = __bfloat162bfloat162(sb[u]), bb2 = __bfloat162bfloat162(bb[u]);
+        const uint32_t wa[4] = {va[u][0].x, va[u][0].y, va[u][0].z, va[u][0].w};
+        const uint32_t wb[4] = {vb[u][0].x, vb[u][0].y, vb[u][0].z, vb[u][0].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t pa[4], pb[4];
+          gv_pairs4(wa[j], sa2, ba2, pa);
+          gv_pairs4(wb[j], sb2, bb2, pb);
+          const uint4 xv = xon ? xrow[run0 + j] : make_uint4(0u, 0u, 0u, 0u);
+          mma_16816(acc, pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
+          mma_16816(acc, pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+        }
+      } else {
+        const float fsa = __bfloat162float(sa[u]), fba = __bfloat162float(ba[u]);
+        const float fsb = __bfloat162float(sb[u]), fbb = __bfloat162float(bb[u]);
+        const uint32_t wa[8] = {va[u][0].x, va[u][0].y, va[u][0].z, va[u][0].w,
+                                va[u][NW - 1].x, va[u][NW - 1].y, va[u][NW - 1].z, va[u][NW - 1].w};
+        const uint32_t wb[8] = {vb[u][0].x, vb[u][0].y, vb[u][0].z, vb[u][0].w,
+                                vb[u][NW - 1].x, vb[u][NW - 1].y, vb[u][NW - 1].z, vb[u][NW - 1].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t pa[4], pb[4];
+          gv_pairs8(wa[2 * j], wa[2 * j + 1], fsa, fba, pa);
+          gv_pairs8(wb[2 * j], wb[2 * j + 1], fsb, fbb, pb);
+          const uint4 xv = xon ? xrow[run0 + j] : make_uint4(0u, 0u, 0u, 0u);
+          mma_16816(acc, pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
+          mma_16816(acc, pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+        }
+      }
+    }
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) red[warp][i][lane] = acc[i];
+  __syncthreads();
+  if (ks == 0) {
+    float sum[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w = warp; w < warp + ksplit; ++w)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sum[i] += red[w][i][lane];
+    // sum[0], sum[1]: row g, tokens 2 t4, 2 t4 + 1; sum[2], sum[3]: row g + 8
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t tok = 2 * t4 + (i & 1), row = i < 2 ? rowA : rowB;
+      if (tok < p.m && row < p.n) p.out[tok * p.out_stride + row] = __float2bfloat16_rn(sum[i]);
+    }
+  }
 }
 
 // Dense copy of the dequantized weights: thread per (row, word).
@@ -359,6 +538,7 @@ gdn_status q_check(const gdn_qlinear_args* a, QParams* p) {
   p->biases = static_cast<const __nv_bfloat16*>(a->biases);
   p->bits = a->bits;
   p->gs = a->group_size;
+  p->gshift = a->group_size == 32 ? 5 : a->group_size == 64 ? 6 : 7;
   return GDN_OK;
 }
 
@@ -385,9 +565,48 @@ extern "C" gdn_status gdn_quantized_linear(const gdn_qlinear_args* a, gdn_stream
   gdn::QParams p;
   gdn_status st = gdn::q_check(a, &p);
   if (st != GDN_OK || a->m == 0) return st;
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  if (a->m <= gdn::kGvMaxTokens && a->k <= gdn::kGvMaxK) {
+    // decode: the weights stream once through the register-fed GEMV
+    gdn::GvParams g;
+    g.m = a->m;
+    g.n = a->n;
+    g.k = a->k;
+    g.x = static_cast<const __nv_bfloat16*>(a->x);
+    g.x_stride = a->x_stride_m;
+    g.w = a->w;
+    g.scales = p.scales;
+    g.biases = p.biases;
+    g.out = static_cast<__nv_bfloat16*>(a->out);
+    g.out_stride = a->out_stride_m;
+    g.gshift = p.gshift;
+    const int64_t rows16 = (a->n + 15) / 16;
+    int warps = 8;
+    g.row_groups = 1;
+    if (rows16 >= 4 * 148) g.row_groups = 2;
+    else if (a->k >= 16 * 128) warps = 16;
+    static bool gv_attr = false;
+    if (!gv_attr) {
+      const int mx = (int)(gdn::kGvMaxTokens * gdn::kGvMaxK * 2);
+      st = gdn::q_cuda(cudaFuncSetAttribute(gdn::qgemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx),
+                       "quantized_linear attribute");
+      if (st == GDN_OK)
+        st = gdn::q_cuda(cudaFuncSetAttribute(gdn::qgemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx),
+                         "quantized_linear attribute");
+      if (st != GDN_OK) return st;
+      gv_attr = true;
+    }
+    const unsigned grid = (unsigned)((rows16 + g.row_groups - 1) / g.row_groups);
+    const size_t smem = (size_t)(a->m * a->k * 2);
+    if (a->bits == 4)
+      gdn::qgemv_kernel<4><<<grid, warps * 32, smem, cs>>>(g);
+    else
+      gdn::qgemv_kernel<8><<<grid, warps * 32, smem, cs>>>(g);
+    return gdn::q_cuda(cudaGetLastError(), "quantized_linear launch");
+  }
   CUtensorMap amap, wmap, omap;
   const int64_t kw = a->k * a->bits / 32;  // words per weight row
-  if (!gdn::q_map(&amap, a->x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->k, a->m, a->x_stride_m * 2, 64, 128, true) ||
+  if (!gdn::q_map(&amap, a->x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->k, a->m, a->x_stride_m * 2, 64, gdn::QBM, true) ||
       !gdn::q_map(&wmap, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT32, kw, a->n, kw * 4, 64 * a->bits / 32, 256, false) ||
       !gdn::q_map(&omap, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->n, a->m, a->out_stride_m * 2, 64, 128, true))
     return gdn::set_error(GDN_ECUDA, "quantized_linear: tensor map encoding failed");
@@ -401,7 +620,7 @@ extern "C" gdn_status gdn_quantized_linear(const gdn_qlinear_args* a, gdn_stream
   }
   const dim3 grid((unsigned)((a->n + gdn::QBN - 1) / gdn::QBN), (unsigned)((a->m + gdn::QBM - 1) / gdn::QBM));
   if (grid.y > 65535) return gdn::set_error(GDN_EUNSUPPORTED, "m too large for one call (%lld)", (long long)a->m);
-  gdn::qlinear_kernel<<<grid, 320, gdn::kQSmem, static_cast<cudaStream_t>(stream)>>>(amap, wmap, omap, p);
+  gdn::qlinear_kernel<<<grid, gdn::kQThreads, gdn::kQSmem, cs>>>(amap, wmap, omap, p);
   return gdn::q_cuda(cudaGetLastError(), "quantized_linear launch");
 }
 

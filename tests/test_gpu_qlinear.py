@@ -54,7 +54,12 @@ def _check(out, ref):
 @pytest.mark.parametrize(
     "m,nn,k,bits,gs,biases",
     [
-        (1, 32, 2048, 4, 64, True),        # one decode token, in_proj_a/b width
+        (1, 32, 2048, 4, 64, True),        # one decode token, in_proj_a/b width (the GEMV)
+        (1, 12352, 2048, 4, 64, True),     # one token through the fused in-projection width
+        (3, 2048, 4096, 4, 64, True),      # out_proj, three tokens
+        (8, 1000, 1088, 4, 32, False),     # eight tokens, k % 128 == 64
+        (5, 777, 2048, 8, 64, True),       # 8-bit GEMV, ragged n
+        (2, 64, 192, 8, 64, True),        # 8-bit, k % 128 == 64
         (4, 4, 128, 4, 64, True),          # the reference test's in_proj_a shape
         (64, 256, 128, 4, 64, True),       # the reference test's in_proj_qkv shape
         (300, 999, 2048, 4, 64, True),     # ragged m and n (partial tiles, n % 8 != 0)
