@@ -8,9 +8,11 @@ causal depthwise conv + SiLU, q/k rms-norm, forget gate and beta, the scan,
 and ``silu(z) * rms_norm(y)``. The conv and ssm states are advanced in
 place.
 
-``Qwen3_5LinearAttention`` wraps it with the layer's dense projections
-(``in_proj_qkv/z/b/a`` and ``out_proj`` run as torch matmuls) so the layer
-is a drop-in for the reference's class with a ``RecurrentCache``.
+``Qwen3_5LinearAttention`` wraps it with the layer's projections
+(``in_proj_qkv/z/b/a`` and ``out_proj``), dense or affine-quantized as the
+reference's ``quantized_linear`` takes them (``model/moe_block.py:23-50``),
+so the layer is a drop-in for the reference's class with a
+``RecurrentCache``.
 """
 
 from __future__ import annotations
@@ -22,6 +24,7 @@ import torch
 
 from . import _lib
 from .gated_delta import _DTYPES, _require_cuda, _stream
+from .quantized import LinearWeights, QuantScheme, as_linear, concat_rows, quantized_linear
 from .recurrent_cache import RecurrentCache
 
 
@@ -135,34 +138,50 @@ def gated_delta_block(
 
 
 class Qwen3_5LinearAttention:
-    """``qw/linear_attention.py:35-127`` with dense projection weights
-    ``(out, in)``: projections as torch matmuls, everything between them in
-    one fused call. ``__call__(x, cache)`` takes ``(hidden,)`` for one decode
-    step or ``(L, hidden)`` and returns the same rank, advancing ``cache``."""
+    """``qw/linear_attention.py:35-127``.  Each projection is a dense
+    ``(out, in)`` tensor, a ``LinearWeights``, or a ``{weight, scales,
+    biases}`` dict stored with ``quant`` (the reference's
+    ``config.other_quant``).  The four input projections run as one GEMM
+    producing the mixed row q|k|v|z|b|a when they share a storage scheme;
+    everything between the projections is one fused call.
+    ``__call__(x, cache)`` takes ``(hidden,)`` for one decode step or
+    ``(L, hidden)`` and returns the same rank, advancing ``cache``."""
 
     def __init__(
         self,
         shape: LinearAttentionShape,
         rms_norm_eps: float,
-        in_proj_qkv: torch.Tensor,
-        in_proj_z: torch.Tensor,
-        in_proj_a: torch.Tensor,
-        in_proj_b: torch.Tensor,
+        in_proj_qkv,
+        in_proj_z,
+        in_proj_a,
+        in_proj_b,
         conv1d_weight: torch.Tensor,
         A_log: torch.Tensor,
         dt_bias: torch.Tensor,
         norm_weight: torch.Tensor,
-        out_proj: torch.Tensor,
+        out_proj,
         algo: str = "auto",
+        quant: QuantScheme | None = None,
     ) -> None:
         self.shape = shape
         self.eps = rms_norm_eps
-        # One matmul produces the mixed row q|k|v|z|b|a.
-        self.in_proj = torch.cat([in_proj_qkv, in_proj_z, in_proj_b, in_proj_a], dim=0)
+        parts = [as_linear(w, quant) for w in (in_proj_qkv, in_proj_z, in_proj_b, in_proj_a)]
+        # One GEMM produces the mixed row q|k|v|z|b|a when the storage agrees.
+        self.in_proj: LinearWeights | None = None
+        self.in_parts = parts
+        if len({p.quant for p in parts}) == 1:
+            self.in_proj = concat_rows(parts)
         self.conv_w = conv1d_weight.reshape(shape.conv_dim, shape.conv_kernel_dim)
         self.A_log, self.dt_bias, self.norm_weight = A_log, dt_bias, norm_weight
-        self.out_proj = out_proj
+        self.out_proj = as_linear(out_proj, quant)
         self.algo = algo
+
+    def _mixed(self, rows: torch.Tensor) -> torch.Tensor:
+        if self.in_proj is not None:
+            mixed = quantized_linear(rows, self.in_proj)
+        else:
+            mixed = torch.cat([quantized_linear(rows, p) for p in self.in_parts], dim=-1)
+        return mixed if mixed.stride(-1) == 1 and mixed.stride(0) % 8 == 0 else mixed.contiguous()
 
     def __call__(self, x: torch.Tensor, cache: RecurrentCache) -> torch.Tensor:
         if x.ndim not in (1, 2):
@@ -170,7 +189,7 @@ class Qwen3_5LinearAttention:
         squeeze = x.ndim == 1
         rows = x[None, :] if squeeze else x
         seq_len = rows.shape[0]
-        mixed = (rows @ self.in_proj.T).contiguous()
+        mixed = self._mixed(rows)
         conv_state, ssm_state = cache.state()
         new_conv = conv_state.clone()
         new_ssm = ssm_state.clone()
@@ -180,5 +199,5 @@ class Qwen3_5LinearAttention:
             algo=self.algo,
         )
         cache.update(new_conv, new_ssm, advance=seq_len)
-        result = out.reshape(seq_len, -1) @ self.out_proj.T
+        result = quantized_linear(out.reshape(seq_len, -1), self.out_proj)
         return result[0] if squeeze else result

@@ -153,3 +153,43 @@ def quantized_linear(x: torch.Tensor, tensors, quant: QuantScheme | None = None)
                                             ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)),
                    "quantized_linear")
     return out[:, :n].reshape(*lead, n)
+
+
+def as_linear(tensors, quant: QuantScheme | None = None) -> LinearWeights:
+    """A projection as ``LinearWeights``: a dense tensor stays dense whatever
+    ``quant`` says (the reference's rule, moe_block.py:33-36); a
+    ``{weight, scales[, biases]}`` dict takes ``quant``."""
+
+    if isinstance(tensors, LinearWeights):
+        return tensors
+    if isinstance(tensors, torch.Tensor):
+        return LinearWeights(tensors, None)
+    if isinstance(tensors, dict):
+        if quant is None:
+            raise ValueError("quantized linear weights require a quantization scheme")
+        return LinearWeights(tensors, quant)
+    raise TypeError(f"unsupported projection weights: {type(tensors).__name__}")
+
+
+def concat_rows(parts: list[LinearWeights]) -> LinearWeights:
+    """Stack projections that share a storage scheme along their output rows,
+    so one GEMM computes all of them (the block's mixed row q|k|v|z|b|a).
+    A part without biases contributes zero biases."""
+
+    quants = {p.quant for p in parts}
+    if len(quants) != 1:
+        raise ValueError("concat_rows needs projections with one storage scheme")
+    quant = quants.pop()
+    if quant is None:
+        return LinearWeights(torch.cat([p.tensors for p in parts], dim=0), None)
+    ws = [p.tensors["weight"] for p in parts]
+    if len({w.shape[1] for w in ws}) != 1:
+        raise ValueError("concat_rows needs projections with the same input width")
+    weight = torch.cat([w.view(torch.int32) for w in ws], dim=0)
+    scales = torch.cat([p.tensors["scales"] for p in parts], dim=0)
+    out = {"weight": weight, "scales": scales}
+    if any(p.tensors.get("biases") is not None for p in parts):
+        out["biases"] = torch.cat(
+            [p.tensors["biases"] if p.tensors.get("biases") is not None else torch.zeros_like(p.tensors["scales"])
+             for p in parts], dim=0)
+    return LinearWeights(out, quant)
