@@ -55,6 +55,7 @@ constexpr size_t kQSmem = 1024 + QSMEM_USED;
 constexpr int kDqThreads = 512;  // warps 2-17: two threads per weight row (one per 32-value half of a K-block)
 constexpr int kQThreads = 64 + kDqThreads;
 constexpr uint64_t kQWaitNs = 2000000000ull;
+constexpr int kScaleAhead = 8;  // K-blocks of scales and biases in flight per dequantizing thread
 
 struct QParams {
   int64_t m, n, k;
@@ -209,17 +210,30 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
     uint32_t boff[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) boff[j] = sw128_chunk(QBN, r, 0, 4 * h + j);
-    __nv_bfloat16 s_nx, b_nx;
-    load_sb(0, s_nx, b_nx);
-    bool ok = true;
-    for (int kb = 0; kb < nk; ++kb) {
+    // Scales and biases ride kScaleAhead K-blocks ahead in a register ring
+    // (the loop is unrolled by the ring's depth, so no slot is copied while
+    // its load is in flight): one block ahead, each block waited for a
+    // global-memory round trip.
+    __nv_bfloat16 sr[kScaleAhead], br[kScaleAhead];
+#pragma unroll
+    for (int j = 0; j < kScaleAhead; ++j)
+      if (j < nk) load_sb(j, sr[j], br[j]);
+    bool ok = true, stop = false;
+    for (int kbase = 0; kbase < nk && !stop; kbase += kScaleAhead)
+#pragma unroll
+    for (int j = 0; j < kScaleAhead; ++j) {
+      const int kb = kbase + j;
+      if (kb >= nk) break;
       const int s = kb % kAStages, sb = kb % kBStages;
-      const __nv_bfloat16 s_cur = s_nx, b_cur = b_nx;
-      if (kb + 1 < nk) load_sb(kb + 1, s_nx, b_nx);
+      const __nv_bfloat16 s_cur = sr[j], b_cur = br[j];
+      if (kb + kScaleAhead < nk) load_sb(kb + kScaleAhead, sr[j], br[j]);
       ok = mbar_wait(&bars[Q_FULL0 + s], (uint32_t)((kb / kAStages) & 1), kQWaitNs) &&
            (kb < kBStages || mbar_wait(&bars[Q_BEMPTY0 + sb], (uint32_t)((kb / kBStages - 1) & 1), kQWaitNs));
       if (!ok) q_record(&abort_flag);
-      if (named_sync_or(1, kDqThreads, !ok)) break;
+      if (named_sync_or(1, kDqThreads, !ok)) {
+        stop = true;
+        break;
+      }
       const unsigned char* wsrc = base + QOFF_W + s * kWTile + (size_t)r * wbytes + h * (wbytes / 2);
       unsigned char* bdst = base + QOFF_B + sb * kBTile;
       if (p.bits == 4) {
@@ -290,19 +304,22 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------
-// Decode: m <= 8 tokens.  The weights stream from HBM once; each warp owns 16
-// weight rows and a strided share of K, dequantizes straight into the A
-// fragments of mma.sync m16n8k16 (A = 16 weight rows x 16 K, B = 16 K x 8
-// tokens) and accumulates in float32; the CTA's warps then add their K shares.
+// Decode and small batches: up to 16 tokens.  The weights stream from HBM
+// once; each warp owns 16 weight rows and a strided share of K, dequantizes
+// straight into the A fragments of mma.sync m16n8k16 (A = 16 weight rows x 16
+// K, B = 16 K x 8 tokens; one or two token blocks) and accumulates in
+// float32; the CTA's warps then add their K shares in shared memory.  The
+// register-fed form needs no shared-memory round trip of the weights, which
+// a tcgen05 operand would; on this part each further token block costs about
+// as much as the first, so beyond two the tiled GEMM takes over.
 //
 // Inside each run of 8 consecutive K the fragment takes the values in the
 // order (0, 4, 1, 5, 2, 6, 3, 7): one AND-OR of a 4-bit word yields exactly
 // the pairs (j, j + 4).  A dot product does not depend on the order of K, so
 // x is staged in shared memory in that same order and the products match.
 // ---------------------------------------------------------------------------
-constexpr int kGvMaxWarps = 16;
-constexpr int kGvMaxTokens = 8;
-constexpr int64_t kGvMaxK = 8192;  // staged x: 8 tokens x 8192 x 2 bytes = 128 KB
+constexpr int kGvMaxTokens = 16;  // beyond two token blocks the tiled GEMM is faster
+constexpr size_t kGvMaxSmem = 220 * 1024;  // staged x: (m + 1) x k bf16
 
 struct GvParams {
   int64_t m, n, k;
@@ -344,70 +361,87 @@ __device__ __forceinline__ void gv_pairs8(uint32_t w0, uint32_t w1, float s, flo
   }
 }
 
-template <int BITS>
-__global__ void __launch_bounds__(kGvMaxWarps * 32) qgemv_kernel(const GvParams p) {
-  extern __shared__ uint4 xs[];  // [m][k / 8] runs of 8, each in the order (0, 4, 1, 5, 2, 6, 3, 7)
-  __shared__ float red[kGvMaxWarps][4][32];
-  constexpr int U = BITS == 4 ? 4 : 2;       // chunks whose loads are in flight together
-  constexpr int NW = BITS / 4;               // uint4 per row and chunk: the thread's 32 values
+template <int BITS, int WARPS, int NT>
+__global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? (NT == 1 ? 3 : 2) : 1) qgemv_kernel(const GvParams p) {
+  // [m + 1][k / 8] runs of 8, each in the order (0, 4, 1, 5, 2, 6, 3, 7); row m is zeros.
+  // After the main loop the same memory holds the warps' partial sums.
+  extern __shared__ uint4 xs[];
+  float(*red)[NT * 4][32] = reinterpret_cast<float(*)[NT * 4][32]>(xs);
+  constexpr int U = BITS == 4 ? 4 : 2;  // chunks whose loads are in flight together
+  constexpr int NW = BITS / 4;          // uint4 per row and chunk: the thread's 32 values
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nwarps = blockDim.x >> 5;
   const int g = lane >> 2, t4 = lane & 3;
-  const int64_t runs = p.k / 8;
+  const int m = (int)p.m, k = (int)p.k, runs = k / 8;
 
-  for (int64_t i = tid; i < p.m * runs; i += blockDim.x) {
-    const int64_t tok = i / runs, r = i % runs;
-    const uint4 v = *reinterpret_cast<const uint4*>(p.x + tok * p.x_stride + 8 * r);
-    xs[i] = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632), __byte_perm(v.y, v.w, 0x5410),
-                       __byte_perm(v.y, v.w, 0x7632));
-  }
-  __syncthreads();
-
-  const int ksplit = nwarps / p.row_groups;
+  const int ksplit = WARPS / p.row_groups;
   const int rg = warp / ksplit, ks = warp % ksplit;
   const int64_t rowA = ((int64_t)blockIdx.x * p.row_groups + rg) * 16 + g, rowB = rowA + 8;
   const bool liveA = rowA < p.n, liveB = rowB < p.n;
-  const int64_t kw = p.k * BITS / 32, groups = p.k >> p.gshift;
-  const uint4* wA = reinterpret_cast<const uint4*>(p.w + (liveA ? rowA : 0) * kw);
-  const uint4* wB = reinterpret_cast<const uint4*>(p.w + (liveB ? rowB : 0) * kw);
-  const __nv_bfloat16* sA = p.scales + (liveA ? rowA : 0) * groups;
-  const __nv_bfloat16* sB = p.scales + (liveB ? rowB : 0) * groups;
-  const __nv_bfloat16* bA = p.biases ? p.biases + (liveA ? rowA : 0) * groups : nullptr;
-  const __nv_bfloat16* bB = p.biases ? p.biases + (liveB ? rowB : 0) * groups : nullptr;
-  const bool tok_live = g < p.m;
-  const uint4* xrow = xs + (tok_live ? g : 0) * runs;
+  const int groups = k >> p.gshift;
+  // Rows past n read row 0 with a zero scale and bias: their products are 0.
+  const int64_t ra = liveA ? rowA : 0, rb = liveB ? rowB : 0;
+  const uint4* wA = reinterpret_cast<const uint4*>(p.w) + ra * (k * BITS / 128);
+  const uint4* wB = reinterpret_cast<const uint4*>(p.w) + rb * (k * BITS / 128);
+  const __nv_bfloat16* sA = p.scales + ra * groups;
+  const __nv_bfloat16* sB = p.scales + rb * groups;
+  const __nv_bfloat16* bA = p.biases ? p.biases + ra * groups : nullptr;
+  const __nv_bfloat16* bB = p.biases ? p.biases + rb * groups : nullptr;
   const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
+  const int nchunks = (k + 127) / 128;  // 128 K per warp step: 32 per thread
 
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  const int64_t nchunks = (p.k + 127) / 128;  // 128 K per warp step: 32 per thread
-  for (int64_t c0 = ks; c0 < nchunks; c0 += (int64_t)ksplit * U) {
-    uint4 va[U][NW], vb[U][NW];
-    __nv_bfloat16 sa[U], sb[U], ba[U], bb[U];
-    bool on[U];  // this lane's 32 values exist (lanes t4 >= 2 of a ragged last chunk, k % 128 == 64, have none)
+  uint4 va[U][NW], vb[U][NW];
+  __nv_bfloat16 sa[U], sb[U], ba[U], bb[U];
+  bool on[U];  // this lane's 32 values exist (lanes t4 >= 2 of a ragged last chunk, k % 128 == 64, have none)
+  auto load_batch = [&](int c0) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t kk = (c0 + (int64_t)u * ksplit) * 128 + 32 * t4;
-      on[u] = c0 + (int64_t)u * ksplit < nchunks && kk < p.k;
-      const int64_t grp = on[u] ? kk >> p.gshift : 0;
-      const int64_t wi = on[u] ? kk * BITS / 128 : 0;  // uint4 index of the thread's 32 values
+      const int c = c0 + u * ksplit;
+      if (c >= nchunks) continue;  // uniform across the warp
+      const int kk = c * 128 + 32 * t4;
+      on[u] = kk < k;
+      const int off = on[u] ? kk * BITS / 128 : 0;  // uint4 offset of the lane's 32 values in the row
+      const int grp = on[u] ? kk >> p.gshift : 0;
 #pragma unroll
       for (int e = 0; e < NW; ++e) {
-        va[u][e] = (on[u] && liveA) ? wA[wi + e] : make_uint4(0u, 0u, 0u, 0u);
-        vb[u][e] = (on[u] && liveB) ? wB[wi + e] : make_uint4(0u, 0u, 0u, 0u);
+        va[u][e] = wA[off + e];
+        vb[u][e] = wB[off + e];
       }
       sa[u] = (on[u] && liveA) ? sA[grp] : zero;
       sb[u] = (on[u] && liveB) ? sB[grp] : zero;
-      ba[u] = (on[u] && bA && liveA) ? bA[grp] : zero;
-      bb[u] = (on[u] && bB && liveB) ? bB[grp] : zero;
+      ba[u] = (on[u] && liveA && bA) ? bA[grp] : zero;
+      bb[u] = (on[u] && liveB && bB) ? bB[grp] : zero;
     }
+  };
+
+  // The first batch of weights does not need x: its loads go out before x
+  // is staged.
+  int c0 = ks;
+  load_batch(c0);
+  for (int tok = 0; tok < m; ++tok)
+    for (int r = tid; r < runs; r += WARPS * 32) {
+      const uint4 v = *reinterpret_cast<const uint4*>(p.x + tok * p.x_stride + 8 * r);
+      xs[tok * runs + r] = make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632),
+                                      __byte_perm(v.y, v.w, 0x5410), __byte_perm(v.y, v.w, 0x7632));
+    }
+  for (int r = tid; r < runs; r += WARPS * 32) xs[m * runs + r] = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
+  // token block t: tokens 8 t + g; tokens past m read the zero row
+  const uint4* xrow[NT];
+#pragma unroll
+  for (int t = 0; t < NT; ++t) xrow[t] = xs + (8 * t + g < m ? 8 * t + g : m) * runs + t4 * 4;
+  const uint4* xzero = xs + m * runs;
+
+  float acc[NT][4] = {};
+  for (; c0 < nchunks; c0 += ksplit * U) {
+    if (c0 != ks) load_batch(c0);
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       // mma.sync is warp-wide: skip only whole chunks past the end (uniform
-      // across the warp); lanes without values feed zeros (zero words with
-      // zero scale and bias dequantize to 0, and their x is 0).
-      if (c0 + (int64_t)u * ksplit >= nchunks) continue;
-      const bool xon = on[u] && tok_live;
-      const int64_t run0 = on[u] ? ((c0 + (int64_t)u * ksplit) * 128 + 32 * t4) / 8 : 0;
+      // across the warp); lanes without values have zero scales and biases
+      // and read the zero x row.
+      const int c = c0 + u * ksplit;
+      if (c >= nchunks) continue;
+      const int xoff = on[u] ? c * 16 : 0;
       if (BITS == 4) {
         const __nv_bfloat162 sa2 = __bfloat162bfloat162(sa[u]), ba2 = __bfloat162bfloat162(ba[u]);
         const __nv_bfloat162 sb2 = __bfloat162bfloat162(sb[u]), bb2 = __bfloat162bfloat162(bb[u]);
@@ -418,9 +452,12 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32) qgemv_kernel(const GvParams 
           uint32_t pa[4], pb[4];
           gv_pairs4(wa[j], sa2, ba2, pa);
           gv_pairs4(wb[j], sb2, bb2, pb);
-          const uint4 xv = xon ? xrow[run0 + j] : make_uint4(0u, 0u, 0u, 0u);
-          mma_16816(acc, pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
-          mma_16816(acc, pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const uint4 xv = on[u] ? xrow[t][xoff + j] : xzero[j];
+            mma_16816(acc[t], pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
+            mma_16816(acc[t], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+          }
         }
       } else {
         const float fsa = __bfloat162float(sa[u]), fba = __bfloat162float(ba[u]);
@@ -434,27 +471,37 @@ __global__ void __launch_bounds__(kGvMaxWarps * 32) qgemv_kernel(const GvParams 
           uint32_t pa[4], pb[4];
           gv_pairs8(wa[2 * j], wa[2 * j + 1], fsa, fba, pa);
           gv_pairs8(wb[2 * j], wb[2 * j + 1], fsb, fbb, pb);
-          const uint4 xv = xon ? xrow[run0 + j] : make_uint4(0u, 0u, 0u, 0u);
-          mma_16816(acc, pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
-          mma_16816(acc, pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const uint4 xv = on[u] ? xrow[t][xoff + j] : xzero[j];
+            mma_16816(acc[t], pa[0], pb[0], pa[1], pb[1], xv.x, xv.y);
+            mma_16816(acc[t], pa[2], pb[2], pa[3], pb[3], xv.z, xv.w);
+          }
         }
       }
     }
   }
 
+  __syncthreads();  // x is dead: its memory takes the partial sums
 #pragma unroll
-  for (int i = 0; i < 4; ++i) red[warp][i][lane] = acc[i];
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) red[warp][4 * t + i][lane] = acc[t][i];
   __syncthreads();
   if (ks == 0) {
-    float sum[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int w = warp; w < warp + ksplit; ++w)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) sum[i] += red[w][i][lane];
-    // sum[0], sum[1]: row g, tokens 2 t4, 2 t4 + 1; sum[2], sum[3]: row g + 8
+    for (int t = 0; t < NT; ++t) {
+      float sum[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int w = warp; w < warp + ksplit; ++w)
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t tok = 2 * t4 + (i & 1), row = i < 2 ? rowA : rowB;
-      if (tok < p.m && row < p.n) p.out[tok * p.out_stride + row] = __float2bfloat16_rn(sum[i]);
+        for (int i = 0; i < 4; ++i) sum[i] += red[w][4 * t + i][lane];
+      // sum[0], sum[1]: row g, tokens 8 t + 2 t4, + 1; sum[2], sum[3]: row g + 8
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tok = 8 * t + 2 * t4 + (i & 1);
+        const int64_t row = i < 2 ? rowA : rowB;
+        if (tok < m && row < p.n) p.out[tok * p.out_stride + row] = __float2bfloat16_rn(sum[i]);
+      }
     }
   }
 }
@@ -549,6 +596,26 @@ gdn_status q_cuda(cudaError_t e, const char* what) {
 
 }  // namespace
 
+template <int BITS, int WARPS, int NT>
+gdn_status gv_launch_one(const GvParams& g, unsigned grid, size_t smem, cudaStream_t cs) {
+  static bool attr = false;  // set once per instance (a repeat from a racing thread is harmless)
+  if (!attr) {
+    const gdn_status st = q_cuda(cudaFuncSetAttribute(qgemv_kernel<BITS, WARPS, NT>,
+                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGvMaxSmem),
+                                 "quantized_linear attribute");
+    if (st != GDN_OK) return st;
+    attr = true;
+  }
+  qgemv_kernel<BITS, WARPS, NT><<<grid, WARPS * 32, smem, cs>>>(g);
+  return q_cuda(cudaGetLastError(), "quantized_linear launch");
+}
+
+template <int BITS, int WARPS>
+gdn_status gv_launch(int nt, const GvParams& g, unsigned grid, size_t smem, cudaStream_t cs) {
+  if (nt == 1) return gv_launch_one<BITS, WARPS, 1>(g, grid, smem, cs);
+  return gv_launch_one<BITS, WARPS, 2>(g, grid, smem, cs);
+}
+
 cudaError_t read_and_clear_qlinear_error(unsigned* code) {
   cudaError_t e = cudaMemcpyFromSymbol(code, g_qlinear_error, sizeof(unsigned));
   if (e != cudaSuccess) return e;
@@ -566,8 +633,9 @@ extern "C" gdn_status gdn_quantized_linear(const gdn_qlinear_args* a, gdn_stream
   gdn_status st = gdn::q_check(a, &p);
   if (st != GDN_OK || a->m == 0) return st;
   cudaStream_t cs = static_cast<cudaStream_t>(stream);
-  if (a->m <= gdn::kGvMaxTokens && a->k <= gdn::kGvMaxK) {
-    // decode: the weights stream once through the register-fed GEMV
+  const size_t gv_x = (size_t)(a->m + 1) * (size_t)a->k * 2;
+  if (a->m <= gdn::kGvMaxTokens && gv_x <= gdn::kGvMaxSmem) {
+    // up to 16 tokens: the weights stream once through the register-fed GEMV
     gdn::GvParams g;
     g.m = a->m;
     g.n = a->n;
@@ -585,24 +653,13 @@ extern "C" gdn_status gdn_quantized_linear(const gdn_qlinear_args* a, gdn_stream
     g.row_groups = 1;
     if (rows16 >= 4 * 148) g.row_groups = 2;
     else if (a->k >= 16 * 128) warps = 16;
-    static bool gv_attr = false;
-    if (!gv_attr) {
-      const int mx = (int)(gdn::kGvMaxTokens * gdn::kGvMaxK * 2);
-      st = gdn::q_cuda(cudaFuncSetAttribute(gdn::qgemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx),
-                       "quantized_linear attribute");
-      if (st == GDN_OK)
-        st = gdn::q_cuda(cudaFuncSetAttribute(gdn::qgemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx),
-                         "quantized_linear attribute");
-      if (st != GDN_OK) return st;
-      gv_attr = true;
-    }
+    const int nt = a->m <= 8 ? 1 : 2;
     const unsigned grid = (unsigned)((rows16 + g.row_groups - 1) / g.row_groups);
-    const size_t smem = (size_t)(a->m * a->k * 2);
+    const size_t red = (size_t)warps * nt * 4 * 32 * sizeof(float);
+    const size_t smem = gv_x > red ? gv_x : red;
     if (a->bits == 4)
-      gdn::qgemv_kernel<4><<<grid, warps * 32, smem, cs>>>(g);
-    else
-      gdn::qgemv_kernel<8><<<grid, warps * 32, smem, cs>>>(g);
-    return gdn::q_cuda(cudaGetLastError(), "quantized_linear launch");
+      return warps == 8 ? gdn::gv_launch<4, 8>(nt, g, grid, smem, cs) : gdn::gv_launch<4, 16>(nt, g, grid, smem, cs);
+    return warps == 8 ? gdn::gv_launch<8, 8>(nt, g, grid, smem, cs) : gdn::gv_launch<8, 16>(nt, g, grid, smem, cs);
   }
   CUtensorMap amap, wmap, omap;
   const int64_t kw = a->k * a->bits / 32;  // words per weight row

@@ -20,9 +20,13 @@ pytestmark = pytest.mark.gpu
 
 # bf16 output: one rounding of an fp32 accumulation (rel-L2 about 1.1e-3
 # against the exact product); against the bf16-rounded exact product the
-# only differences are accumulation order and rare ties.
+# differences are the elements whose accumulation error crosses a rounding
+# tie, a share that grows with k (tensor-core accumulation over K).
 TOL_EXACT = 2e-3
-TOL_ROUNDED = 3e-4
+
+
+def _tol_rounded(k):
+    return 3e-4 * max(1.0, k / 2048) ** 0.5
 
 
 def _weights(rng, nrows, k, bits, gs, biases=True, signed_scales=True):
@@ -43,12 +47,12 @@ def _torch_weights(words, s, b):
     return out
 
 
-def _check(out, ref):
+def _check(out, ref, k):
     got = n(out).astype(np.float64)
     assert np.isfinite(got).all()
     e1 = O.rel_l2(got, ref)
     e2 = O.rel_l2(got, O.bf16_round(ref.astype(np.float32)))
-    assert e1 <= TOL_EXACT and e2 <= TOL_ROUNDED, (e1, e2)
+    assert e1 <= TOL_EXACT and e2 <= _tol_rounded(k), (e1, e2)
 
 
 @pytest.mark.parametrize(
@@ -60,6 +64,16 @@ def _check(out, ref):
         (8, 1000, 1088, 4, 32, False),     # eight tokens, k % 128 == 64
         (5, 777, 2048, 8, 64, True),       # 8-bit GEMV, ragged n
         (2, 64, 192, 8, 64, True),        # 8-bit, k % 128 == 64
+        (3, 40, 64, 4, 64, True),          # k = 64: half the lanes of the only chunk are empty
+        (1, 24, 64, 8, 32, False),
+        (12, 520, 2048, 4, 64, True),      # two token blocks
+        (16, 999, 1024, 8, 32, False),
+        (16, 40, 6400, 4, 64, True),       # x staged near its size limit: 17 x 6400 x 2 bytes
+        (16, 40, 8192, 4, 64, True),       # x too large to stage: the tiled GEMM
+        (17, 300, 2048, 4, 128, True),     # from 17 tokens on: the tiled GEMM
+        (32, 2048, 2048, 4, 64, True),
+        (200, 700, 2048, 4, 64, True),
+        (250, 300, 1024, 8, 64, True),
         (4, 4, 128, 4, 64, True),          # the reference test's in_proj_a shape
         (64, 256, 128, 4, 64, True),       # the reference test's in_proj_qkv shape
         (300, 999, 2048, 4, 64, True),     # ragged m and n (partial tiles, n % 8 != 0)
@@ -78,7 +92,7 @@ def test_quantized_linear_bf16_matches_oracle(m, nn, k, bits, gs, biases):
     out = quantized_linear(t(x, torch.bfloat16), _torch_weights(words, s, b), QuantScheme(bits=bits, group_size=gs))
     torch.cuda.synchronize()
     assert out.shape == (m, nn) and out.dtype == torch.bfloat16
-    _check(out, O.quantized_linear_ref(x, words, s, b, bits, gs))
+    _check(out, O.quantized_linear_ref(x, words, s, b, bits, gs), k)
     gdn_b200.check_device_errors()
 
 
@@ -113,7 +127,7 @@ def test_leading_dims_strided_rows_and_linear_weights():
     out = quantized_linear(xt, lw)
     assert out.shape == (2, 3, 80, 520)
     ref = O.quantized_linear_ref(x[..., 32:32 + 2048].reshape(-1, 2048), words, s, b, 4, 64)
-    _check(out.reshape(-1, 520), ref)
+    _check(out.reshape(-1, 520), ref, 2048)
 
 
 def test_quantize_then_matmul_close_to_dense():
@@ -125,7 +139,7 @@ def test_quantize_then_matmul_close_to_dense():
     x = O.bf16_round(rng.standard_normal((4, 128)).astype(np.float32))
     out = quantized_linear(t(x, torch.bfloat16), _torch_weights(words, s, b), QuantScheme(bits=4, group_size=64))
     eff = O.dequant_affine(words, s, b, 4, 64)
-    _check(out, x.astype(np.float64) @ eff.astype(np.float64).T)
+    _check(out, x.astype(np.float64) @ eff.astype(np.float64).T, 128)
 
 
 def test_empty_batch():
