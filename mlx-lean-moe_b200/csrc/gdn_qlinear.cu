@@ -49,7 +49,9 @@ constexpr uint32_t kOutSub = 128 * 64 * 2;            // one 128 x 64 bf16 outpu
 constexpr uint32_t QOFF_A = 0;                        // A and W rings, then the output staging (8 sub-tiles)
 constexpr uint32_t QOFF_W = QOFF_A + kAStages * kATile;
 constexpr uint32_t QOFF_B = QOFF_W + kAStages * kWTile;
-constexpr uint32_t QSMEM_USED = QOFF_B + kBStages * kBTile;
+constexpr uint32_t kScTile = 8 * QBN * 2;                 // 8 groups x 256 rows of bf16 scales (or biases): 4 KB
+constexpr uint32_t QOFF_SC = QOFF_B + kBStages * kBTile;  // 2 stages x (scales, biases)
+constexpr uint32_t QSMEM_USED = QOFF_SC + 2 * 2 * kScTile;
 static_assert(8 * kOutSub <= QOFF_B, "output staging overlaps the B ring");
 constexpr size_t kQSmem = 1024 + QSMEM_USED;
 constexpr int kDqThreads = 512;  // warps 2-17: two threads per weight row (one per 32-value half of a K-block)
@@ -62,10 +64,12 @@ struct QParams {
   const __nv_bfloat16* scales;
   const __nv_bfloat16* biases;
   int bits, gs, gshift;  // gs == 1 << gshift
+  int scale_tma;         // scales (and biases) arrive as TMA tiles of 8 groups x 256 rows
+  int sshift;            // K-blocks per scale tile: 8 * gs / 64 == 1 << sshift
 };
 
 enum QBar { Q_FULL0, Q_EMPTY0 = Q_FULL0 + kAStages, Q_BFULL0 = Q_EMPTY0 + kAStages, Q_BEMPTY0 = Q_BFULL0 + kBStages,
-            Q_ACC = Q_BEMPTY0 + kBStages, Q_NBARS };
+            Q_ACC = Q_BEMPTY0 + kBStages, Q_SCFULL0, Q_SCEMPTY0 = Q_SCFULL0 + 2, Q_NBARS = Q_SCEMPTY0 + 2 };
 
 __device__ __forceinline__ void q_record(volatile int* abort_flag) {
   *abort_flag = 1;
@@ -111,6 +115,8 @@ __device__ __forceinline__ uint4 dequant_words8(uint32_t w0, uint32_t w1, float 
 __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_constant__ CUtensorMap amap,
                                                                const __grid_constant__ CUtensorMap wmap,
                                                                const __grid_constant__ CUtensorMap omap,
+                                                               const __grid_constant__ CUtensorMap smap,
+                                                               const __grid_constant__ CUtensorMap bmap,
                                                                const QParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -143,9 +149,25 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
     if (lane == 0) {
       prefetch_tensormap(&amap);
       prefetch_tensormap(&wmap);
-      int issued = 0;
+      if (p.scale_tma) {
+        prefetch_tensormap(&smap);
+        if (p.biases) prefetch_tensormap(&bmap);
+      }
+      int issued = 0, sc_issued = 0;
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % kAStages;
+        if (p.scale_tma && (kb & ((1 << p.sshift) - 1)) == 0) {
+          // the next tile of scales and biases (8 groups), double-buffered
+          const int tile = kb >> p.sshift, st = tile & 1;
+          if (tile >= 2 && !mbar_wait(&bars[Q_SCEMPTY0 + st], (uint32_t)((tile / 2 - 1) & 1), kQWaitNs))
+            q_record(&abort_flag);
+          if (abort_flag) break;
+          mbar_arrive_expect_tx(&bars[Q_SCFULL0 + st], p.biases ? 2 * kScTile : kScTile);
+          tma_load_2d(base + QOFF_SC + st * 2 * kScTile, &smap, &bars[Q_SCFULL0 + st], tile * 8, (int)n0);
+          if (p.biases)
+            tma_load_2d(base + QOFF_SC + st * 2 * kScTile + kScTile, &bmap, &bars[Q_SCFULL0 + st], tile * 8, (int)n0);
+          ++sc_issued;
+        }
         if (kb >= kAStages && !mbar_wait(&bars[Q_EMPTY0 + s], (uint32_t)((kb / kAStages - 1) & 1), kQWaitNs))
           q_record(&abort_flag);
         if (abort_flag) break;
@@ -156,9 +178,12 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
       }
       // After an abort, let this thread's copies land (bounded) before the
       // CTA releases its shared memory.
-      if (abort_flag)
+      if (abort_flag) {
         for (int kb = issued - kAStages < 0 ? 0 : issued - kAStages; kb < issued; ++kb)
           mbar_wait(&bars[Q_FULL0 + kb % kAStages], (uint32_t)((kb / kAStages) & 1), kQWaitNs);
+        for (int tile = sc_issued - 2 < 0 ? 0 : sc_issued - 2; tile < sc_issued; ++tile)
+          mbar_wait(&bars[Q_SCFULL0 + (tile & 1)], (uint32_t)((tile / 2) & 1), kQWaitNs);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -217,7 +242,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
     __nv_bfloat16 sr[kScaleAhead], br[kScaleAhead];
 #pragma unroll
     for (int j = 0; j < kScaleAhead; ++j)
-      if (j < nk) load_sb(j, sr[j], br[j]);
+      if (j < nk && !p.scale_tma) load_sb(j, sr[j], br[j]);
     bool ok = true, stop = false;
     for (int kbase = 0; kbase < nk && !stop; kbase += kScaleAhead)
 #pragma unroll
@@ -225,9 +250,23 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
       const int kb = kbase + j;
       if (kb >= nk) break;
       const int s = kb % kAStages, sb = kb % kBStages;
-      const __nv_bfloat16 s_cur = sr[j], b_cur = br[j];
-      if (kb + kScaleAhead < nk) load_sb(kb + kScaleAhead, sr[j], br[j]);
-      ok = mbar_wait(&bars[Q_FULL0 + s], (uint32_t)((kb / kAStages) & 1), kQWaitNs) &&
+      __nv_bfloat16 s_cur, b_cur;
+      const int tile = kb >> p.sshift;
+      const int in_tile = kb & ((1 << p.sshift) - 1);
+      if (p.scale_tma) {
+        // this row's group within the tile: rows past n were zero-filled
+        const unsigned char* sc = base + QOFF_SC + (tile & 1) * 2 * kScTile + r * 16 +
+                                  2 * (((kb * QBK + h * 32) >> p.gshift) - 8 * tile);
+        ok = in_tile != 0 || mbar_wait(&bars[Q_SCFULL0 + (tile & 1)], (uint32_t)((tile >> 1) & 1), kQWaitNs);
+        s_cur = *reinterpret_cast<const __nv_bfloat16*>(sc);
+        b_cur = p.biases ? *reinterpret_cast<const __nv_bfloat16*>(sc + kScTile) : __float2bfloat16_rn(0.f);
+      } else {
+        ok = true;
+        s_cur = sr[j];
+        b_cur = br[j];
+        if (kb + kScaleAhead < nk) load_sb(kb + kScaleAhead, sr[j], br[j]);
+      }
+      ok = ok && mbar_wait(&bars[Q_FULL0 + s], (uint32_t)((kb / kAStages) & 1), kQWaitNs) &&
            (kb < kBStages || mbar_wait(&bars[Q_BEMPTY0 + sb], (uint32_t)((kb / kBStages - 1) & 1), kQWaitNs));
       if (!ok) q_record(&abort_flag);
       if (named_sync_or(1, kDqThreads, !ok)) {
@@ -255,6 +294,8 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
       if (t == 0) {
         mbar_arrive(&bars[Q_BFULL0 + sb]);  // the operand is ready
         mbar_arrive(&bars[Q_EMPTY0 + s]);   // the packed weights are read
+        if (p.scale_tma && (in_tile == (1 << p.sshift) - 1 || kb == nk - 1))
+          mbar_arrive(&bars[Q_SCEMPTY0 + (tile & 1)]);  // the tile's scales are read
       }
     }
 
@@ -586,6 +627,9 @@ gdn_status q_check(const gdn_qlinear_args* a, QParams* p) {
   p->bits = a->bits;
   p->gs = a->group_size;
   p->gshift = a->group_size == 32 ? 5 : a->group_size == 64 ? 6 : 7;
+  p->sshift = p->gshift - 3;
+  // scale tiles by TMA when a row of scales is a whole number of 16-byte units
+  p->scale_tma = (a->k / a->group_size) % 8 == 0 && a16(a->scales) && (!a->biases || a16(a->biases));
   return GDN_OK;
 }
 
@@ -675,9 +719,18 @@ extern "C" gdn_status gdn_quantized_linear(const gdn_qlinear_args* a, gdn_stream
     if (st != GDN_OK) return st;
     attr = true;
   }
+  CUtensorMap smap, bmap;
+  std::memset(&smap, 0, sizeof(smap));
+  std::memset(&bmap, 0, sizeof(bmap));
+  const int64_t groups = a->k / a->group_size;
+  if (p.scale_tma &&
+      (!gdn::q_map(&smap, a->scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, groups, a->n, groups * 2, 8, gdn::QBN, false) ||
+       (a->biases &&
+        !gdn::q_map(&bmap, a->biases, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, groups, a->n, groups * 2, 8, gdn::QBN, false))))
+    return gdn::set_error(GDN_ECUDA, "quantized_linear: tensor map encoding failed");
   const dim3 grid((unsigned)((a->n + gdn::QBN - 1) / gdn::QBN), (unsigned)((a->m + gdn::QBM - 1) / gdn::QBM));
   if (grid.y > 65535) return gdn::set_error(GDN_EUNSUPPORTED, "m too large for one call (%lld)", (long long)a->m);
-  gdn::qlinear_kernel<<<grid, gdn::kQThreads, gdn::kQSmem, cs>>>(amap, wmap, omap, p);
+  gdn::qlinear_kernel<<<grid, gdn::kQThreads, gdn::kQSmem, cs>>>(amap, wmap, omap, smap, bmap, p);
   return gdn::q_cuda(cudaGetLastError(), "quantized_linear launch");
 }
 
