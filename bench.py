@@ -8,7 +8,7 @@ one decode launch over the batch; ``value`` is the state HBM traffic
 prefill number of config 3 (T=8192) under ``"prefill"``.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|varlen]
+                    [--workload decode|varlen|qproj] [--tokens M]
 
 ``--workload varlen`` is config 5 instead: 64 packed sequences (lengths
 ``default_rng(1).integers(256, 16384, 64, endpoint=True)``, 516,496 tokens)
@@ -16,6 +16,11 @@ split across the ranks by longest-processing-time bin packing, one prefill
 over each rank's sequences followed by 256 decode steps; ``value`` is the
 prefill rate in tokens/s over all ranks (strong scaling: the total is fixed),
 and the decode phase is reported beside it.
+
+``--workload qproj`` times only the 4-bit quantized in-projection (12,352 x
+2,048) at ``--tokens`` rows, for profiling the projection kernels.  The
+default line also carries ``"layer"``: config 4 from hidden states in to
+hidden states out, with 4-bit affine projections around the fused block.
 
 ``--impl reference`` times the reference's CPU path (its ops-path recurrence,
 restated on torch's CPU backend with every host thread; MLX is not
@@ -292,6 +297,105 @@ def measure_block(device, iters=3):
     return statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(iters)), Bb * T
 
 
+HIDDEN = 2048
+
+
+def quantized_weights(device, rows, cols, gen, bits=4, group=64):
+    """Random affine-quantized weights in the reference's storage (uint32 words
+    as int32, bf16 scales and biases); values of a trained layer's scale."""
+    words = torch.randint(-2**31, 2**31 - 1, (rows, cols * bits // 32), dtype=torch.int32, device=device,
+                          generator=gen)
+    scales = (torch.rand(rows, cols // group, device=device, generator=gen) * 2e-3 + 1e-3).bfloat16()
+    biases = (-(2 ** (bits - 1)) * scales.float()).bfloat16()
+    return {"weight": words, "scales": scales, "biases": biases}
+
+
+def measure_layer(device, iters=3):
+    """Config 4 as a whole layer: hidden states in (B=8 x T=4096, 2048 wide,
+    bf16), the four input projections as one 4-bit quantized GEMM into the
+    mixed row, the fused block, the 4-bit out_proj, hidden states out."""
+    import gdn_b200
+    from gdn_b200 import LinearWeights, QuantScheme, concat_rows, quantized_linear
+    from gdn_b200.linear_attention import LinearAttentionShape
+
+    shape = LinearAttentionShape(HK, HV, D, D, 4)
+    Bb, T = 8, 4096
+    q4 = QuantScheme(bits=4, group_size=64)
+    gen = torch.Generator(device).manual_seed(5)
+    in_proj = concat_rows([LinearWeights(quantized_weights(device, r, HIDDEN, gen), q4)
+                           for r in (shape.conv_dim, shape.value_dim, HV, HV)])
+    out_proj = LinearWeights(quantized_weights(device, HIDDEN, shape.value_dim, gen), q4)
+    x = torch.randn(Bb * T, HIDDEN, device=device, generator=gen).bfloat16()
+    conv_w = torch.randn(shape.conv_dim, 4, device=device, generator=gen) * 0.1
+    A_log = torch.rand(HV, device=device, generator=gen) * 1.5
+    dt_bias = torch.randn(HV, device=device, generator=gen) * 0.1
+    norm_w = torch.ones(D, device=device)
+    conv_state = torch.zeros(Bb, 3, shape.conv_dim, device=device)
+    ssm = torch.zeros(Bb, HV, D, D, device=device)
+    core = torch.empty(Bb * T, HV, D, device=device, dtype=torch.bfloat16)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    def run(record):
+        conv_state.zero_()
+        ssm.zero_()
+        if record:
+            ev[0].record()
+        mixed = quantized_linear(x, in_proj)
+        if record:
+            ev[1].record()
+        gdn_b200.gated_delta_block(mixed, shape, conv_w, A_log, dt_bias, norm_w, 1e-6, conv_state, ssm,
+                                   n_seqs=Bb, out=core)
+        if record:
+            ev[2].record()
+        out = quantized_linear(core.view(Bb * T, -1), out_proj)
+        if record:
+            ev[3].record()
+        return out
+
+    for _ in range(2):
+        run(False)
+    torch.cuda.synchronize()
+    parts = []
+    for _ in range(iters):
+        run(True)
+        torch.cuda.synchronize()
+        parts.append([ev[i].elapsed_time(ev[i + 1]) for i in range(3)])
+    med = [statistics.median(p[i] for p in parts) for i in range(3)]
+    n_tok = Bb * T
+    gemm_flop = 2 * n_tok * HIDDEN * (shape.mixed_width + shape.value_dim)
+    return {"tokens": n_tok, "in_proj_ms": med[0], "block_ms": med[1], "out_proj_ms": med[2],
+            "ms": sum(med), "gemm_flop": gemm_flop}
+
+
+def run_qproj(args):
+    """Only the quantized in-projection (12,352 x 2,048, 4-bit, group 64) at
+    ``--tokens`` rows: the GEMV up to 16 tokens, the tiled GEMM beyond; for
+    profiling the projection kernels on their own."""
+    from gdn_b200 import QuantScheme, quantized_linear
+
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device).manual_seed(6)
+    n = 2 * HK * D + 2 * HV * D + 2 * HV  # q|k|v|z|b|a: 12,352
+    w = quantized_weights(device, n, HIDDEN, gen)
+    q4 = QuantScheme(bits=4, group_size=64)
+    x = torch.randn(args.tokens, HIDDEN, device=device, generator=gen).bfloat16()
+    for _ in range(args.warmup):
+        quantized_linear(x, w, q4)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        quantized_linear(x, w, q4)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    flop = 2 * args.tokens * n * HIDDEN
+    print(json.dumps({"metric": "quantized in-projection TFLOP/s", "value": flop / (ms / 1e3) / 1e12,
+                      "unit": "TFLOP/s", "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                      "config": {"workload": f"in_proj {args.tokens} x {n} x {HIDDEN}, 4-bit affine, group 64"},
+                      "dtype": "bf16", "data": "synthetic"}), flush=True)
+
+
 def cpu_prefill_sample(n_tokens=512):
     """The reference's CPU path on the first ``n_tokens`` tokens of config 5's
     first sequence (all host threads); returns tokens/s."""
@@ -415,9 +519,16 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="decode only: no e2e, prefill or CPU legs (for profiler runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiler runs)")
-    ap.add_argument("--workload", choices=["decode", "varlen"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "varlen", "qproj"], default="decode")
+    ap.add_argument("--tokens", type=int, default=4096, help="rows of x for --workload qproj")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.workload == "qproj":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's quantized matmul is MLX's "
+                              "(mx.quantized_matmul), not installable on this box"}), flush=True)
+            return
+        return run_qproj(args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)
@@ -564,6 +675,14 @@ def main():
                                    "projection, conv+norms+gates+scan+gated RMSNorm (two state resets included)",
                          "achieved_tflops": blk_flop / (blk_ms / 1e3) / 1e12,
                          "frac_of_bf16_peak": blk_flop / (blk_ms / 1e3) / 1e12 / tc_peak}
+        lay = measure_layer(device)
+        line["layer"] = {
+            "value": lay["tokens"] / (lay["ms"] / 1e3), "unit": "tok/s", "ms": lay["ms"],
+            "in_proj_ms": lay["in_proj_ms"], "block_ms": lay["block_ms"], "out_proj_ms": lay["out_proj_ms"],
+            "projection_tflops": lay["gemm_flop"] / ((lay["in_proj_ms"] + lay["out_proj_ms"]) / 1e3) / 1e12,
+            "config": "config 4 as a whole layer: hidden states B=8 x T=4096 x 2048 bf16 in and out; in_proj "
+                      "(q|k|v|z|b|a, 12,352 x 2,048) and out_proj (2,048 x 4,096) 4-bit affine, group 64 "
+                      "(tcgen05 GEMM with on-the-fly dequantization); the fused block between them"}
 
         # --- CPU baseline (rank 0, N=1 only) --------------------------------
         if rank == 0 and world == 1 and not args.no_cpu_baseline:

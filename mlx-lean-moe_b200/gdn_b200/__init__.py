@@ -15,7 +15,7 @@ from .gated_delta import (
     gated_delta_step,
 )
 from .linear_attention import LinearAttentionShape, Qwen3_5LinearAttention, gated_delta_block
-from .quantized import LinearWeights, QuantScheme, dequantize, quantized_linear
+from .quantized import LinearWeights, QuantScheme, as_linear, concat_rows, dequantize, quantized_linear
 from .recurrent_cache import BatchedRecurrentCache, RecurrentCache
 
 __all__ = [
@@ -25,7 +25,9 @@ __all__ = [
     "QuantScheme",
     "Qwen3_5LinearAttention",
     "RecurrentCache",
+    "as_linear",
     "check_device_errors",
+    "concat_rows",
     "dequantize",
     "forget_gate",
     "gated_delta_block",
