@@ -55,6 +55,7 @@ constexpr uint32_t QSMEM_USED = QOFF_SC + 2 * 2 * kScTile;
 static_assert(8 * kOutSub <= QOFF_B, "output staging overlaps the B ring");
 constexpr size_t kQSmem = 1024 + QSMEM_USED;
 constexpr int kDqThreads = 512;  // warps 2-17: two threads per weight row (one per 32-value half of a K-block)
+constexpr int kDqWarps = kDqThreads / 32;
 constexpr int kQThreads = 64 + kDqThreads;
 constexpr uint64_t kQWaitNs = 2000000000ull;
 constexpr int kScaleAhead = 8;  // K-blocks of scales and biases in flight per dequantizing thread
@@ -132,9 +133,12 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
 
   if (tid == 0) {
     abort_flag = 0;
+    // The dequantizing warps arrive one by one (no CTA-wide barrier per K-block).
     for (int i = 0; i < Q_NBARS; ++i) {
-      const bool empty = i >= Q_EMPTY0 && i < Q_EMPTY0 + kAStages;  // MMA commit + dequantizers
-      mbar_init(&bars[i], empty ? 2 : 1);
+      uint32_t count = 1;
+      if (i >= Q_EMPTY0 && i < Q_EMPTY0 + kAStages) count = 1 + kDqWarps;  // MMA commit + every dequantizing warp
+      if ((i >= Q_BFULL0 && i < Q_BFULL0 + kBStages) || i >= Q_SCEMPTY0) count = kDqWarps;
+      mbar_init(&bars[i], count);
     }
     fence_mbar_init();
   }
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
       ok = ok && mbar_wait(&bars[Q_FULL0 + s], (uint32_t)((kb / kAStages) & 1), kQWaitNs) &&
            (kb < kBStages || mbar_wait(&bars[Q_BEMPTY0 + sb], (uint32_t)((kb / kBStages - 1) & 1), kQWaitNs));
       if (!ok) q_record(&abort_flag);
-      if (named_sync_or(1, kDqThreads, !ok)) {
+      if (!__all_sync(0xffffffffu, ok)) {  // the warp's lanes leave together
         stop = true;
         break;
       }
@@ -289,13 +293,14 @@ __global__ void __launch_bounds__(kQThreads, 1) qlinear_kernel(const __grid_cons
         *reinterpret_cast<uint4*>(bdst + boff[2]) = dequant_words8(w23.x, w23.y, sv, bv);
         *reinterpret_cast<uint4*>(bdst + boff[3]) = dequant_words8(w23.z, w23.w, sv, bv);
       }
+      // each lane's writes reach the async proxy; the warp's lane 0 arrives for it
       fence_async_smem();
-      named_sync(1, kDqThreads);
-      if (t == 0) {
-        mbar_arrive(&bars[Q_BFULL0 + sb]);  // the operand is ready
-        mbar_arrive(&bars[Q_EMPTY0 + s]);   // the packed weights are read
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars[Q_BFULL0 + sb]);  // this warp's rows of the operand are ready
+        mbar_arrive(&bars[Q_EMPTY0 + s]);   // and its packed weights are read
         if (p.scale_tma && (in_tile == (1 << p.sshift) - 1 || kb == nk - 1))
-          mbar_arrive(&bars[Q_SCEMPTY0 + (tile & 1)]);  // the tile's scales are read
+          mbar_arrive(&bars[Q_SCEMPTY0 + (tile & 1)]);  // and the tile's scales
       }
     }
 
