@@ -3,23 +3,30 @@
 // (the reference's quantized_linear, model/moe_block.py:23-50, which calls
 // mx.quantized_matmul in its affine mode).
 //
-// One CTA per 128 x 256 output tile (tokens x output features), looping over
-// K in blocks of 64:
-//   warp 0     TMA: the x tile (128 x 64 bf16, 128-byte swizzle) and the
-//              packed weight rows (256 x 64 values) into a 3-stage ring;
-//   warps 2-9  dequantization: thread r expands row r of the weight block
-//              into bf16, in the 128-byte-swizzled K-major operand layout
-//              (2-stage ring), then, after the last block, the epilogue;
-//   warp 1     one tcgen05.mma (M = 128, N = 256, K = 16) per 16 of K into a
-//              128 x 256 fp32 accumulator in TMEM.
+// From 17 tokens on (qlinear_kernel): one CTA per 256 x 256 output tile
+// (tokens x output features), looping over K in blocks of 64:
+//   warp 0      TMA: the x tile (256 x 64 bf16, 128-byte swizzle) and the
+//               packed weight rows (256 x 64 values) into a 3-stage ring,
+//               and every 8 groups a tile of scales and biases (8 x 256 bf16)
+//               into a 2-stage ring;
+//   warps 2-17  dequantization: two threads per weight row (one per 32-value
+//               half of the block) expand it into bf16 in the 128-byte-
+//               swizzled K-major operand layout (2-stage ring); each warp
+//               arrives for itself once its rows are written; after the
+//               last block, the epilogue;
+//   warp 1      two tcgen05.mma (M = 128, N = 256, K = 16) per 16 of K, one
+//               per 128-row half of the tile, into two 128 x 256 fp32
+//               accumulators in TMEM (all 512 columns).
 // 4-bit values become bf16 pairs with the magic-number method (OR the nibble
 // into the mantissa of 128.0, subtract 128: Kim et al., "Who Says Elephants
 // Can't Run", 2022), then one bf16x2 FMA with the group's scale and bias: a
 // single rounding of s * q + b to bf16.  8-bit values go through float32
-// (OR into the mantissa of 2^23) and one FMA, then a pairwise bf16 rounding.
-// The epilogue stages the tile as four 128 x 64 bf16 sub-tiles (128-byte
-// swizzle) and writes them with TMA stores; the TMA loads zero-fill, and the
-// stores clip, the parts of edge tiles outside x and out.
+// (a byte permute into the mantissa of 2^23) and one FMA, then a pairwise
+// bf16 rounding.  The epilogue stages the tile as eight 128 x 64 bf16
+// sub-tiles (128-byte swizzle) over the idle A and W rings and writes them
+// with TMA stores; the TMA loads zero-fill, and the stores clip, the parts of
+// edge tiles outside x, the weights and out.  Up to 16 tokens run the
+// register-fed GEMV further down instead.
 //
 // Every wait is bounded (2 s); on a timeout the kernel records an error for
 // gdn_check_device_errors, lets its own copies and MMAs land (bounded), frees
