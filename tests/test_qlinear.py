@@ -128,3 +128,36 @@ def test_dequantize_rejects_bad_arguments():
     assert st in (_lib.GDN_EINVAL, _lib.GDN_EUNSUPPORTED)
     assert lib.gdn_dequantize(ctypes.byref(_args()), _lib.GDN_F32, None, None) == _lib.GDN_EINVAL
     assert lib.gdn_dequantize(ctypes.byref(_args(bits=5)), _lib.GDN_F32, 0x5000, None) == _lib.GDN_EUNSUPPORTED
+
+
+def test_as_linear_and_concat_rows_on_host():
+    from gdn_b200 import LinearWeights, as_linear, concat_rows
+
+    q4 = QuantScheme(bits=4, group_size=64)
+    dense = torch.randn(3, 128)
+    assert as_linear(dense, q4).quant is None  # a dense tensor stays dense
+    with pytest.raises(ValueError, match="quantization scheme"):
+        as_linear({"weight": torch.zeros(2, 16, dtype=torch.int32)})
+    with pytest.raises(TypeError):
+        as_linear([1, 2, 3])
+
+    def part(rows, seed, biases=True):
+        g = torch.Generator().manual_seed(seed)
+        t = {"weight": torch.randint(0, 2**31 - 1, (rows, 16), dtype=torch.int32, generator=g),
+             "scales": torch.rand(rows, 2, generator=g).bfloat16()}
+        if biases:
+            t["biases"] = torch.rand(rows, 2, generator=g).bfloat16()
+        return LinearWeights(t, q4)
+
+    a, b, c = part(5, 1), part(3, 2, biases=False), part(4, 3)
+    cat = concat_rows([a, b, c])
+    assert cat.quant == q4
+    torch.testing.assert_close(cat.tensors["weight"], torch.cat([a.tensors["weight"], b.tensors["weight"],
+                                                                  c.tensors["weight"]]))
+    # the part without biases contributes zeros
+    assert torch.all(cat.tensors["biases"][5:8] == 0)
+    torch.testing.assert_close(cat.tensors["biases"][:5], a.tensors["biases"])
+    d = concat_rows([LinearWeights(dense, None), LinearWeights(torch.randn(2, 128), None)])
+    assert d.quant is None and d.tensors.shape == (5, 128)
+    with pytest.raises(ValueError):
+        concat_rows([a, LinearWeights(dense, None)])
