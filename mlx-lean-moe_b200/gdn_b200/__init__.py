@@ -7,6 +7,7 @@ conferencebeefwood46/mlx-lean-moe's ``qwen3_5.gated_delta`` module and its
 """
 
 from .gated_delta import (
+    DecodePlan,
     check_device_errors,
     forget_gate,
     gated_delta_decode,
@@ -20,6 +21,7 @@ from .recurrent_cache import BatchedRecurrentCache, RecurrentCache
 
 __all__ = [
     "BatchedRecurrentCache",
+    "DecodePlan",
     "LinearAttentionShape",
     "LinearWeights",
     "QuantScheme",

@@ -301,6 +301,73 @@ def gated_delta_decode(
     return out, state_out
 
 
+class DecodePlan:
+    """``gated_delta_decode`` prepared once for fixed buffers.
+
+    A server's decode loop writes each step's q, k, v, g, beta into the same
+    tensors and advances the same state; ``DecodePlan`` validates them and
+    builds the argument block once, and ``run()`` only launches (on the
+    current stream), the state advancing in place as with
+    ``gated_delta_decode(..., inplace=True)``.  The buffers must be usable as
+    given (q/k/v of one supported dtype and g/beta float32 or bfloat16 alike,
+    feature dimensions contiguous): a plan never copies, so later writes to
+    the caller's tensors are what ``run()`` reads."""
+
+    def __init__(
+        self,
+        q: torch.Tensor,
+        k: torch.Tensor,
+        v: torch.Tensor,
+        g: torch.Tensor,
+        beta: torch.Tensor,
+        state: torch.Tensor,
+        *,
+        g_is_log: bool = False,
+        state_slots: torch.Tensor | None = None,
+        out_dtype: torch.dtype = torch.float32,
+        out: torch.Tensor | None = None,
+    ) -> None:
+        device = _require_cuda(q, k, v, g, beta, state, state_slots, out)
+        if q.ndim != 3 or k.shape != q.shape or v.ndim != 3 or v.shape[0] != q.shape[0]:
+            raise ValueError("q/k must be (B, Hk, Dk) and v (B, Hv, Dv)")
+        bsz, hv, dv = q.shape[0], v.shape[1], v.shape[2]
+        if tuple(g.shape) != (bsz, hv) or beta.shape != g.shape:
+            raise ValueError("g and beta must have shape (B, value_heads)")
+        n_rows = state.shape[0]
+        if tuple(state.shape[1:]) != (hv, dv, q.shape[2]) or state.dtype != torch.float32 or not state.is_contiguous():
+            raise ValueError("state must be a contiguous float32 (B or slots, Hv, Dv, Dk) tensor")
+        if state_slots is None and n_rows != bsz:
+            raise ValueError("state must have one row per sequence when state_slots is None")
+        if state_slots is not None and (state_slots.dtype != torch.int32 or state_slots.shape != (bsz,)):
+            raise ValueError("state_slots must be an int32 (B,) tensor")
+        if _qkv_common(q, k, v)[0] is not q or any(t.stride(-1) != 1 for t in (q, k, v)):
+            raise ValueError("DecodePlan needs q, k, v of one supported dtype with contiguous feature dimensions")
+        g2, beta2 = _prepare_gates(g, beta)
+        if g2 is not g or beta2 is not beta:
+            raise ValueError("DecodePlan needs g and beta of one dtype (float32 or bfloat16), last dim contiguous")
+        if out is None:
+            out = torch.empty((bsz, hv, dv), dtype=out_dtype, device=device)
+        elif tuple(out.shape) != (bsz, hv, dv) or not out.is_contiguous():
+            raise ValueError("out must be a contiguous (B, Hv, Dv) tensor")
+        d = _lib.DecodeArgs()
+        d.base = _scan_args(q, k, v, g, beta, state, state, out, bsz, None, g_is_log, "auto")
+        d.state_slots = state_slots.data_ptr() if state_slots is not None else None
+        d.n_slots = n_rows if state_slots is not None else 0
+        self._args = d
+        self._argp = ctypes.byref(d)
+        self._lib = _lib.load()
+        self._keep = (q, k, v, g, beta, state, state_slots)
+        self.device = device
+        self.out = out
+        self.state = state
+
+    def run(self) -> torch.Tensor:
+        """One decode step on the current stream; returns ``out``."""
+        _lib.check(self._lib.gdn_decode(self._argp, torch.cuda.current_stream(self.device).cuda_stream),
+                   "gated_delta_decode")
+        return self.out
+
+
 def check_device_errors(device: torch.device | None = None) -> None:
     """Synchronise the current stream and raise if a bounded device wait of
     the library gave up since the last check."""

@@ -79,3 +79,27 @@ def test_decode_multiplier_gate_and_bf16_output():
     ey, est = oracle_c.scan_varlen(q, k, v, g, beta, np.arange(5), s)
     assert O.rel_l2(n(y), ey) < 4e-3  # bf16 rounding of the output
     assert O.rel_l2(n(st), est) < TOL
+
+
+def test_decode_plan_matches_the_call_over_steps_and_slots():
+    # a fixed-buffer decode loop: new contents every step, one prepared call
+    bsz, hk, hv, d = 6, 2, 4, 64
+    q0, k0, v0, g0, b0, s0 = O.decode_inputs(21, bsz, hk, hv, d, d)
+    q, k, v = (t(x, torch.bfloat16) for x in (q0, k0, v0))
+    g, beta = t(g0), t(b0)
+    pool = t(np.concatenate([s0, s0 * 0.5]))  # 12 slots, this batch uses 6 of them
+    slots = torch.tensor([7, 0, 3, 11, 5, 9], dtype=torch.int32, device=q.device)
+    ref_pool = pool.clone()
+    plan = gdn_b200.DecodePlan(q, k, v, g, beta, pool, g_is_log=True, state_slots=slots)
+    for step in range(4):
+        qs, ks, vs, gs, bs, _ = O.decode_inputs(100 + step, bsz, hk, hv, d, d)
+        for dst, src in ((q, qs), (k, ks), (v, vs), (g, gs), (beta, bs)):
+            dst.copy_(t(src, dst.dtype))
+        y_ref, _ = gdn_b200.gated_delta_decode(q, k, v, g, beta, ref_pool, g_is_log=True, state_slots=slots)
+        y = plan.run()
+        torch.testing.assert_close(y, y_ref, rtol=0, atol=0)
+    torch.testing.assert_close(pool, ref_pool, rtol=0, atol=0)
+    with pytest.raises(ValueError, match="never copies|one supported dtype"):
+        gdn_b200.DecodePlan(q.double(), k.double(), v.double(), g, beta, pool, state_slots=slots)
+    with pytest.raises(ValueError, match="g and beta"):
+        gdn_b200.DecodePlan(q, k, v, g.double(), beta, pool, state_slots=slots)

@@ -57,3 +57,11 @@ def test_recurrent_cache_layout_and_update():
 def test_linear_attention_shape():
     s = LinearAttentionShape(16, 32, 128, 128, 4)
     assert s.conv_dim == 8192 and s.mixed_width == 12352
+
+
+def test_decode_plan_rejects_cpu_tensors():
+    import gdn_b200
+
+    x = torch.zeros(2, 1, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        gdn_b200.DecodePlan(x, x, x, torch.zeros(2, 1), torch.zeros(2, 1), torch.zeros(2, 1, 8, 8))
