@@ -228,9 +228,11 @@ gdn_status gdn_fused_block_noalloc(const gdn_block_args *args, gdn_stream_t stre
  *   scales: [n, k / group_size], biases the same (or NULL), bf16
  *   out:    [m, n], row stride out_stride_m (elements, multiple of 8), bf16
  * bits 4 or 8; group_size 32, 64 or 128; k a multiple of 64 and of
- * group_size.  Accumulation in float32; each dequantized weight is rounded
- * to bf16 before the product.  Replaces quantized_linear / mx.quantized_matmul
- * (model/moe_block.py:23-50) for the affine mode. */
+ * group_size; x, w and out 16-byte aligned.  Accumulation in float32; each
+ * dequantized weight is rounded to bf16 before the product.  Up to 16 rows of
+ * x (decode) stream the weights once through a register-fed kernel; more
+ * rows run the tiled tensor-core GEMM.  Replaces quantized_linear /
+ * mx.quantized_matmul (model/moe_block.py:23-50) for the affine mode. */
 typedef struct {
   int64_t m, n, k;
   const void *x;
