@@ -508,3 +508,77 @@ def quantized_linear_ref(x, words, scales, biases, bits, group_size):
 
     w = dequant_affine(words, scales, biases, bits, group_size).astype(np.float64)
     return np.asarray(x, np.float64) @ w.T
+
+
+# ---------------------------------------------------------------------------
+# Softmax attention layer (qw/attention.py:40-99) with its growing KV cache
+# (cache/kv_cache.py:28-102): grouped-query heads, the output gate carried in
+# q_proj's second half, q/k RMS norms with weights, rotary embedding of the
+# leading rotary_dim features (model/rope.py: feature i pairs with
+# i + rotary_dim / 2), the causal mask aligned to the newest query.
+# ---------------------------------------------------------------------------
+
+
+def rope_leading(x, rotary_dim, base, offset):
+    """x (L, H, D): rotate features [0, rotary_dim) of the token at position
+    offset + l by angle (offset + l) * base ** (-2 i / rotary_dim)."""
+
+    x = np.asarray(x, np.float64)
+    out = x.copy()
+    half = rotary_dim // 2
+    inv = base ** (-np.arange(half, dtype=np.float64) * 2.0 / rotary_dim)
+    ang = (offset + np.arange(x.shape[0], dtype=np.float64))[:, None] * inv[None, :]
+    cos, sin = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+    a, b = x[..., :half], x[..., half:rotary_dim]
+    out[..., :half] = a * cos - b * sin
+    out[..., half:rotary_dim] = b * cos + a * sin
+    return out
+
+
+def attention_core(q, keys, values, scale):
+    """q (L, H, D) for the newest L of T cached positions; keys/values
+    (Hkv, T, D). Query l of head h sees key positions <= T - L + l of head
+    h // (H / Hkv). Returns (L, H, D) in float64."""
+
+    q = np.asarray(q, np.float64)
+    keys = np.asarray(keys, np.float64)
+    values = np.asarray(values, np.float64)
+    length, heads, _ = q.shape
+    hkv, t, _ = keys.shape
+    rep = heads // hkv
+    out = np.empty_like(q)
+    allowed = np.arange(t)[None, :] <= (t - length + np.arange(length))[:, None]
+    for h in range(heads):
+        s = q[:, h, :] @ keys[h // rep].T * scale
+        s = np.where(allowed, s, -np.inf)
+        s = s - s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        out[:, h, :] = (p / p.sum(axis=1, keepdims=True)) @ values[h // rep]
+    return out
+
+
+def attention_layer(x, w, keys, values, heads, kv_heads, head_dim, rotary_dim, theta, eps, rnd=_ident):
+    """One call of ``Qwen3_5Attention.__call__`` (qw/attention.py:40-99):
+    x (L, hidden) float; dense projections w[q_proj|k_proj|v_proj|o_proj]
+    (out, in) and the norm weights; keys/values the cache (Hkv, T0, D) before
+    the call. ``rnd`` rounds where the reference materializes activations in
+    a narrower dtype. Returns (out (L, hidden), keys, values) with the cache
+    grown by L."""
+
+    x = np.asarray(x, np.float64)
+    length = x.shape[0]
+    qg = rnd(x @ np.asarray(w["q_proj"], np.float64).T).reshape(length, heads, 2 * head_dim)  # :56-59
+    q, gate = qg[..., :head_dim], qg[..., head_dim:]
+    q = rnd(rms_norm(q, w["q_norm"], eps))  # :60
+    k = rnd(rms_norm(rnd(x @ np.asarray(w["k_proj"], np.float64).T).reshape(length, kv_heads, head_dim),
+                     w["k_norm"], eps))  # :62-65
+    v = rnd(x @ np.asarray(w["v_proj"], np.float64).T).reshape(length, kv_heads, head_dim)  # :66-68
+    offset = keys.shape[1]  # :74
+    q = rnd(rope_leading(q, rotary_dim, theta, offset))  # :78-80
+    k = rnd(rope_leading(k, rotary_dim, theta, offset))  # :81-83
+    keys = np.concatenate([keys, k.transpose(1, 0, 2)], axis=1)  # :85
+    values = np.concatenate([values, v.transpose(1, 0, 2)], axis=1)
+    o = rnd(attention_core(q, keys, values, head_dim ** -0.5)).reshape(length, heads * head_dim)  # :87-94
+    o = rnd(o * sigmoid(gate.reshape(length, heads * head_dim)))  # :96
+    out = rnd(o @ np.asarray(w["o_proj"], np.float64).T)  # :97
+    return out, keys, values

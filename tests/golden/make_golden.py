@@ -14,7 +14,8 @@ prove they are the same bytes). What it runs:
   from the test file with ``ast`` and executed as written (their only MLX
   use, ``mx.array``, becomes ``np.asarray``);
 * the reference's own modules ``qw/gated_delta.py``,
-  ``qw/linear_attention.py`` and ``cache/recurrent_cache.py``, imported
+  ``qw/linear_attention.py``, ``cache/recurrent_cache.py``, ``qw/attention.py``,
+  ``model/rope.py`` and ``cache/kv_cache.py``, imported
   unchanged on the numpy MLX stand-in of ``mlx_numpy_shim.py`` (no Metal, so
   ``gated_delta_scan`` takes its ops path ``qw/gated_delta.py:93-109``).
 
@@ -42,6 +43,8 @@ METAL_SHAPES = [(1, 32, 5, 3, 6), (7, 64, 32, 2, 2), (17, 128, 128, 16, 32), (12
 LONG_LENGTH = 2048
 # Layer test shapes of tests/test_qwen3_5_linear_attention.py:20-29.
 LAYER = dict(hidden=128, hk=2, hv=4, dk=32, dv=32, kernel=4, eps=1e-6)
+# Attention test shapes of tests/test_qwen3_5_attention.py:20-27.
+ATTN = dict(hidden=128, heads=4, kv_heads=2, head_dim=32, rotary=8, theta=10000000.0, eps=1e-6)
 # (seed, seq_len) cases of tests/test_qwen3_5_gated_delta.py.
 GDN_CASES = [(0, 1), (0, 5), (1, 5), (2, 1), (3, 4)]
 
@@ -84,6 +87,25 @@ def layer_case(seed: int, x_seed: int, seq_len: int):
     w["norm_weight"] = (rng.standard_normal(dv).astype(np.float32) * 0.1 + 1.0).astype(np.float32)
     x = np.random.default_rng(x_seed).standard_normal((seq_len, hidden)).astype(np.float32)
     return w, x
+
+
+def attn_case(seed: int):
+    """Dense weights of one attention case, drawn in the order of
+    ``_build_pair`` (``tests/test_qwen3_5_attention.py:74-86``): q_proj (queries
+    and gate, 2 x heads x head_dim rows), k_proj, v_proj, o_proj ~ 0.05 N(0,1);
+    q_norm, k_norm ~ 1 + 0.1 N(0,1)."""
+
+    h, hkv, hd, hidden = ATTN["heads"], ATTN["kv_heads"], ATTN["head_dim"], ATTN["hidden"]
+    rng = np.random.default_rng(seed)
+
+    def dense(out_dim, in_dim):
+        return (rng.standard_normal((out_dim, in_dim)).astype(np.float32) * 0.05).astype(np.float32)
+
+    w = {"q_proj": dense(h * hd * 2, hidden), "k_proj": dense(hkv * hd, hidden), "v_proj": dense(hkv * hd, hidden),
+         "o_proj": dense(hidden, h * hd)}
+    w["q_norm"] = (rng.standard_normal(hd).astype(np.float32) * 0.1 + 1.0).astype(np.float32)
+    w["k_norm"] = (rng.standard_normal(hd).astype(np.float32) * 0.1 + 1.0).astype(np.float32)
+    return w
 
 
 def _extract_functions(path: str, names: list[str], namespace: dict) -> dict:
@@ -230,6 +252,57 @@ def main() -> None:
     arrays["layer_chunks/conv_state"] = cache.state()[0]
     arrays["layer_chunks/ssm_state"] = cache.state()[1]
     arrays["layer_chunks/size"] = np.array(cache.size)
+
+    # 5. The softmax-attention layer, through the reference's Qwen3_5Attention
+    #    and GrowingKVCache (float32, dense projections).
+    at = refmods["attention"]
+    kvc = refmods["kv_cache"]
+    attn_config = qc.Qwen3_5Config(
+        num_layers=1, hidden_size=ATTN["hidden"], vocab_size=64, rms_norm_eps=ATTN["eps"],
+        num_attention_heads=ATTN["heads"], num_key_value_heads=ATTN["kv_heads"], head_dim=ATTN["head_dim"],
+        rope_theta=ATTN["theta"], rotary_dim=ATTN["rotary"], is_linear_per_layer=(False,), linear=lin,
+        num_experts=4, experts_per_token=2, moe_intermediate_size=32, shared_expert_intermediate_size=64,
+        norm_topk_prob=True, expert_quant=quant, router_quant=quant, shared_gate_quant=quant, other_quant=quant,
+    )
+
+    def attn_layer(w):
+        return at.Qwen3_5Attention(attn_config, **w)
+
+    def kv_cache(max_context=16):
+        return kvc.GrowingKVCache(max_context=max_context, num_kv_heads=ATTN["kv_heads"],
+                                  head_dim=ATTN["head_dim"], dtype=np.float32)
+
+    manifest["source"]["attention"] = "qw/attention.py Qwen3_5Attention + cache/kv_cache.py GrowingKVCache"
+    # 5a. One call of 1 and of 6 tokens from a fresh cache (seed 0, x seed 200).
+    for seq_len in (1, 6):
+        w = attn_case(0)
+        x = np.random.default_rng(200).standard_normal((seq_len, ATTN["hidden"])).astype(np.float32)
+        key = f"attn_fresh_{seq_len}"
+        manifest["inputs"][key] = {k: sha(v) for k, v in {**w, "x": x}.items()}
+        cache = kv_cache()
+        arrays[f"{key}/out"] = attn_layer(w)(x, cache)
+        keys, values = cache.state()
+        arrays[f"{key}/keys"], arrays[f"{key}/values"] = keys, values
+    # 5b. Five decode steps against one batched call (seed 1, x seed 201).
+    w = attn_case(1)
+    x = np.random.default_rng(201).standard_normal((5, ATTN["hidden"])).astype(np.float32)
+    manifest["inputs"]["attn_steps"] = {k: sha(v) for k, v in {**w, "x": x}.items()}
+    layer = attn_layer(w)
+    batched = layer(x, kv_cache())
+    cache = kv_cache()
+    stepwise = np.stack([layer(x[t], cache) for t in range(5)])
+    np.testing.assert_allclose(batched, stepwise, rtol=1e-3, atol=1e-4)
+    arrays["attn_steps/out"] = stepwise
+    arrays["attn_steps/batched"] = batched
+    # 5c. Three calls of 4 tokens into one cache: the causal mask of a call
+    #     that starts at an offset (seed 3, x seed 203).
+    w = attn_case(3)
+    xs = np.random.default_rng(203).standard_normal((3, 4, ATTN["hidden"])).astype(np.float32)
+    manifest["inputs"]["attn_chunks"] = {k: sha(v) for k, v in {**w, "x": xs}.items()}
+    layer = attn_layer(w)
+    cache = kv_cache()
+    arrays["attn_chunks/out"] = np.concatenate([layer(xc, cache) for xc in xs])
+    arrays["attn_chunks/keys"], arrays["attn_chunks/values"] = cache.state()
 
     np.savez_compressed(os.path.join(HERE, "golden.npz"), **arrays)
     with open(os.path.join(HERE, "golden_manifest.json"), "w") as f:

@@ -10,7 +10,14 @@ Only the operations that the reference's hot-path modules call are provided:
 * ``mlx_lean_moe/model/qwen3_5/linear_attention.py``: ``mx.concatenate``,
   ``mx.conv1d`` (depthwise, cross-correlation, no padding), ``mx.split``,
   ``mx.fast.rms_norm``, ``mx.sigmoid``, ``nn.silu``;
-* ``mlx_lean_moe/cache/recurrent_cache.py``: ``mx.zeros``.
+* ``mlx_lean_moe/cache/recurrent_cache.py``: ``mx.zeros``;
+* ``mlx_lean_moe/model/rope.py``: ``mx.fast.rope`` (non-traditional: feature
+  i pairs with i + dims / 2; position = offset + index along the sequence);
+* ``mlx_lean_moe/model/qwen3_5/attention.py``:
+  ``mx.fast.scaled_dot_product_attention`` (grouped-query heads, the causal
+  mask aligned to the last query: query i of L sees keys j <= T - L + i),
+  ``mx.sigmoid``;
+* ``mlx_lean_moe/cache/kv_cache.py``: ``mx.zeros``, ``mx.concatenate``.
 
 Each follows MLX's documented semantics for float32 inputs; no other dtype is
 exercised by the golden generator.
@@ -71,6 +78,45 @@ def _softplus(x):
     return np.logaddexp(np.zeros((), dtype=x.dtype), x).astype(x.dtype)
 
 
+def _rope(x, dims, traditional=False, base=10000.0, scale=1.0, offset=0):
+    """(B, H, L, D): rotate features [0, dims) pairwise (i, i + dims / 2) by
+    angle (offset + l) * scale * base ** (-2 i / dims); the rest pass."""
+
+    assert not traditional
+    x = np.asarray(x)
+    out = x.astype(np.float64).copy()
+    half = dims // 2
+    inv = base ** (-np.arange(half, dtype=np.float64) * 2.0 / dims)
+    pos = (offset + np.arange(x.shape[-2], dtype=np.float64)) * scale
+    ang = pos[:, None] * inv[None, :]
+    cos, sin = np.cos(ang), np.sin(ang)
+    a, b = out[..., :half].copy(), out[..., half:dims].copy()
+    out[..., :half] = a * cos - b * sin
+    out[..., half:dims] = b * cos + a * sin
+    return out.astype(x.dtype)
+
+
+def _sdpa(q, k, v, scale, mask=None):
+    """q (B, H, L, D), k/v (B, Hkv, T, D): softmax(scale q k^T [+ causal]) v,
+    query head h reading key/value head h // (H / Hkv)."""
+
+    q, k, v = (np.asarray(a) for a in (q, k, v))
+    bsz, h, length, _ = q.shape
+    hkv, t = k.shape[1], k.shape[2]
+    rep = h // hkv
+    kk = np.repeat(k.astype(np.float64), rep, axis=1)
+    vv = np.repeat(v.astype(np.float64), rep, axis=1)
+    s = np.einsum("bhld,bhtd->bhlt", q.astype(np.float64), kk) * scale
+    if mask is not None:
+        assert mask == "causal"
+        allowed = np.arange(t)[None, :] <= (t - length + np.arange(length))[:, None]
+        s = np.where(allowed[None, None], s, -np.inf)
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p /= p.sum(axis=-1, keepdims=True)
+    return np.einsum("bhlt,bhtd->bhld", p, vv).astype(q.dtype)
+
+
 def build_modules() -> dict[str, types.ModuleType]:
     core = types.ModuleType("mlx.core")
     core.array = np.ndarray
@@ -91,7 +137,7 @@ def build_modules() -> dict[str, types.ModuleType]:
     core.gpu = "gpu"
     core.default_device = lambda: "cpu"
     core.metal = types.SimpleNamespace(is_available=lambda: False)
-    core.fast = types.SimpleNamespace(rms_norm=_rms_norm)
+    core.fast = types.SimpleNamespace(rms_norm=_rms_norm, rope=_rope, scaled_dot_product_attention=_sdpa)
 
     nn = types.ModuleType("mlx.nn")
     nn.silu = _silu
@@ -149,5 +195,10 @@ def load_reference_modules(src_root: str) -> dict[str, types.ModuleType]:
     modules["linear_attention"] = load(
         "mlx_lean_moe.model.qwen3_5.linear_attention",
         "mlx_lean_moe/model/qwen3_5/linear_attention.py",
+    )
+    modules["kv_cache"] = load("mlx_lean_moe.cache.kv_cache", "mlx_lean_moe/cache/kv_cache.py")
+    modules["rope"] = load("mlx_lean_moe.model.rope", "mlx_lean_moe/model/rope.py")
+    modules["attention"] = load(
+        "mlx_lean_moe.model.qwen3_5.attention", "mlx_lean_moe/model/qwen3_5/attention.py"
     )
     return modules

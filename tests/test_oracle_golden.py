@@ -6,7 +6,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from make_golden import GDN_CASES, LAYER, METAL_SHAPES, LONG_LENGTH, layer_case, metal_key, sha
+from make_golden import ATTN, GDN_CASES, LAYER, METAL_SHAPES, LONG_LENGTH, attn_case, layer_case, metal_key, sha
 from oracle import gdn_oracle as O
 from oracle import oracle_c
 
@@ -151,3 +151,57 @@ def test_bf16_round_is_round_to_nearest_even():
     x = np.random.default_rng(0).standard_normal(10000).astype(np.float32) * 10
     want = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
     np.testing.assert_array_equal(O.bf16_round(x), want)
+
+
+def _attn(x, w, keys, values):
+    return O.attention_layer(x, w, keys, values, ATTN["heads"], ATTN["kv_heads"], ATTN["head_dim"],
+                             ATTN["rotary"], ATTN["theta"], ATTN["eps"])
+
+
+def _empty_cache():
+    return np.zeros((ATTN["kv_heads"], 0, ATTN["head_dim"])), np.zeros((ATTN["kv_heads"], 0, ATTN["head_dim"]))
+
+
+@pytest.mark.parametrize("seq_len", [1, 6])
+def test_attention_oracle_matches_reference_layer(seq_len, golden, manifest):
+    w = attn_case(0)
+    x = np.random.default_rng(200).standard_normal((seq_len, ATTN["hidden"])).astype(np.float32)
+    assert manifest["inputs"][f"attn_fresh_{seq_len}"]["x"] == sha(x)
+    assert manifest["inputs"][f"attn_fresh_{seq_len}"]["q_proj"] == sha(w["q_proj"])
+    out, keys, values = _attn(x, w, *_empty_cache())
+    np.testing.assert_allclose(out, golden[f"attn_fresh_{seq_len}/out"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(keys, golden[f"attn_fresh_{seq_len}/keys"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(values, golden[f"attn_fresh_{seq_len}/values"], rtol=1e-5, atol=1e-6)
+
+
+def test_attention_oracle_decode_steps_and_offset_chunks(golden):
+    w = attn_case(1)
+    x = np.random.default_rng(201).standard_normal((5, ATTN["hidden"])).astype(np.float32)
+    keys, values = _empty_cache()
+    outs = []
+    for t in range(5):
+        o, keys, values = _attn(x[t:t + 1], w, keys, values)
+        outs.append(o[0])
+    np.testing.assert_allclose(np.stack(outs), golden["attn_steps/out"], rtol=1e-4, atol=1e-5)
+    batched, _, _ = _attn(x, w, *_empty_cache())
+    np.testing.assert_allclose(batched, golden["attn_steps/batched"], rtol=1e-4, atol=1e-5)
+
+    w = attn_case(3)
+    xs = np.random.default_rng(203).standard_normal((3, 4, ATTN["hidden"])).astype(np.float32)
+    keys, values = _empty_cache()
+    outs = []
+    for xc in xs:
+        o, keys, values = _attn(xc, w, keys, values)
+        outs.append(o)
+    np.testing.assert_allclose(np.concatenate(outs), golden["attn_chunks/out"], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(keys, golden["attn_chunks/keys"], rtol=1e-5, atol=1e-6)
+
+
+def test_rope_leaves_the_tail_and_rotates_pairs():
+    # the reference's rope test: features past rotary_dim pass unchanged
+    x = np.random.default_rng(1).standard_normal((3, 2, 16))
+    out = O.rope_leading(x, 4, 10000.0, 7)
+    np.testing.assert_array_equal(out[..., 4:], x[..., 4:])
+    # position 0 is the identity; a pair keeps its norm
+    np.testing.assert_allclose(O.rope_leading(x, 4, 10000.0, 0)[0], x[0])
+    np.testing.assert_allclose(np.hypot(out[..., 0], out[..., 2]), np.hypot(x[..., 0], x[..., 2]))
