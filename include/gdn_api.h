@@ -253,6 +253,51 @@ gdn_status gdn_quantized_linear(const gdn_qlinear_args *args, gdn_stream_t strea
 gdn_status gdn_dequantize(const gdn_qlinear_args *args, gdn_dtype out_dtype, void *dense,
                           gdn_stream_t stream);
 
+/* The softmax-attention layer between its projections (the reference's
+ * Qwen3_5Attention.__call__, qw/attention.py:56-96, with GrowingKVCache,
+ * cache/kv_cache.py:28-102), for one sequence:
+ *   q, gate = qg split per head; q = rope(rms_norm(q, q_norm, eps));
+ *   k = rope(rms_norm(k_new, k_norm, eps)); the cache rows
+ *   [cache_len - n_tokens, cache_len) receive k and v_new; then
+ *   out = sdpa(q, keys, values, scale, causal) * sigmoid(gate),
+ * with grouped-query heads (query head h reads key/value head
+ * h / (heads / kv_heads)), the causal mask aligned to the newest query, and
+ * rope rotating features [0, rotary_dim) pairwise (i, i + rotary_dim / 2) by
+ * position * rope_base^(-2i / rotary_dim).  Activations and caches share
+ * act_dtype (F32 or BF16); the norms and the softmax run in float32.
+ *   qg:     [n_tokens, heads * 2 * head_dim]  (per head: queries | gate)
+ *   k_new, v_new: [n_tokens, kv_heads * head_dim]
+ *   q_norm, k_norm: [head_dim] float32
+ *   k_cache, v_cache: [kv_heads, capacity, head_dim], 16-byte aligned
+ *   out:    [n_tokens, heads * head_dim]
+ * head_dim 32, 64, 128 or 256.  The workspace holds the rotated queries and,
+ * for calls with few rows (decode), the partial rows of the key splits. */
+typedef struct {
+  int64_t n_tokens;          /* new tokens of this call                    */
+  int64_t cache_len;         /* cached positions after this call           */
+  int64_t capacity;          /* rows allocated per head in the caches      */
+  int32_t heads, kv_heads, head_dim, rotary_dim;
+  float rope_base, eps, scale;
+  const void *qg;
+  int64_t qg_stride_t;
+  const void *k_new;
+  int64_t k_stride_t;
+  const void *v_new;
+  int64_t v_stride_t;
+  const float *q_norm;
+  const float *k_norm;
+  void *k_cache;
+  void *v_cache;
+  gdn_dtype act_dtype;
+  void *out;
+  int64_t out_stride_t;
+  void *workspace;
+  size_t workspace_bytes;
+} gdn_attn_args;
+
+gdn_status gdn_attention_workspace_size(const gdn_attn_args *args, size_t *bytes);
+gdn_status gdn_attention(const gdn_attn_args *args, gdn_stream_t stream);
+
 /* Synchronises `stream`, then reports and clears any error a bounded
  * device-side wait recorded since the last call (GDN_ETIMEOUT), or a CUDA
  * error (GDN_ECUDA). */

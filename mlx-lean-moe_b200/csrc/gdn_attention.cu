@@ -1,0 +1,486 @@
+// The softmax-attention layer's core (the reference's Qwen3_5Attention
+// between its projections, qw/attention.py:56-96, with the GrowingKVCache of
+// cache/kv_cache.py): q/k RMS norms with weights, rotary embedding of the
+// leading rotary_dim features (model/rope.py: feature i pairs with
+// i + rotary_dim / 2, angle = position * base^(-2i / rotary_dim)), the append
+// of this call's keys and values to a head-major cache, grouped-query
+// attention with the causal mask aligned to the newest query, and the
+// output gate sigmoid(gate) carried in q_proj's second half.
+//
+// attn_prep_kernel     one CTA per (token, row of q / k / v heads): the
+//                      norms and the rotation in float32, rounded to the
+//                      activation dtype where the reference materializes
+//                      arrays; q to the workspace, k and v into the cache.
+//                      Rotation angles are reduced modulo 2 pi in double
+//                      precision before sincosf, so long positions keep
+//                      their accuracy.
+// attn_fwd_kernel      flash-style attention on the CUDA cores in float32:
+//                      one CTA per (kRows query rows of one key/value head,
+//                      key split); its four warps take interleaved tiles of
+//                      32 keys (lane = key for the scores, lane = feature for
+//                      the output) with their own running max and sum, merged
+//                      at the end; K tiles pass through shared memory, V rows
+//                      are read by the whole warp.  One split finishes the
+//                      rows (normalization, gate, output); several write
+//                      partial (max, sum, output) rows that
+// attn_combine_kernel  adds up, then gates and writes.
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <cstring>
+
+#include "gdn_api.h"
+#include "gdn_common.cuh"
+
+namespace gdn {
+namespace {
+
+constexpr int kRows = 8;        // query rows (token x head) per CTA
+constexpr int kWarps = 4;
+constexpr int kKeyTile = 32;    // keys per warp step
+constexpr int kMaxHeadDim = 256;
+
+struct AttnParams {
+  int64_t n_tokens, cache_len, offset;  // offset = cache_len - n_tokens: position of the first new token
+  int heads, kv_heads, head_dim, rotary_dim, group;  // group = heads / kv_heads
+  float eps, scale;
+  double log_base;                      // ln(rope base)
+  const void* qg;
+  int64_t qg_st;
+  const void* k_new;
+  int64_t k_st;
+  const void* v_new;
+  int64_t v_st;
+  const float* q_norm;
+  const float* k_norm;
+  void* k_cache;
+  void* v_cache;
+  int64_t cache_sh;                     // elements between heads of the caches (capacity * head_dim)
+  void* q_ws;                           // [n_tokens, heads, head_dim] in the activation dtype
+  float* part;                          // [splits, n_tokens * heads, head_dim + 2] partial rows
+  int splits;
+  void* out;
+  int64_t out_st;
+};
+
+// ------------------------------------------------------------------ prep
+template <typename T>
+__global__ void __launch_bounds__(kMaxHeadDim) attn_prep_kernel(const AttnParams p) {
+  __shared__ float xs[kMaxHeadDim];
+  __shared__ float red[kMaxHeadDim / 32];
+  const int64_t t = blockIdx.x;
+  const int row = blockIdx.y;  // [0, heads): q; [heads, heads + kv): k; then v
+  const int d = threadIdx.x, hd = p.head_dim;
+  const bool is_q = row < p.heads, is_k = !is_q && row < p.heads + p.kv_heads;
+  const int h = is_q ? row : is_k ? row - p.heads : row - p.heads - p.kv_heads;
+  const int64_t pos = p.offset + t;
+  if (!is_q && !is_k) {  // v: a copy into the cache
+    const T* src = static_cast<const T*>(p.v_new) + t * p.v_st + (int64_t)h * hd;
+    static_cast<T*>(p.v_cache)[h * p.cache_sh + pos * hd + d] = src[d];
+    return;
+  }
+  const T* src = is_q ? static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * hd
+                      : static_cast<const T*>(p.k_new) + t * p.k_st + (int64_t)h * hd;
+  const float x = to_f(src[d]);
+  // mean of squares over the head's features
+  float ss = x * x;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((d & 31) == 0) red[d >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < hd / 32; ++i) tot += red[i];
+  const float w = is_q ? p.q_norm[d] : p.k_norm[d];
+  const float xn = round_to<T>(x / sqrtf(tot / (float)hd + p.eps) * w);
+  xs[d] = xn;
+  __syncthreads();
+  float y = xn;
+  const int half = p.rotary_dim / 2;
+  if (d < p.rotary_dim) {
+    const int i = d < half ? d : d - half;
+    // angle = pos * base^(-2i / rotary_dim), reduced modulo 2 pi in double
+    const double ang = remainder((double)pos * exp(-2.0 * i / p.rotary_dim * p.log_base), 6.283185307179586);
+    float sn, cs;
+    sincosf((float)ang, &sn, &cs);
+    y = d < half ? xn * cs - xs[d + half] * sn : xn * cs + xs[d - half] * sn;
+  }
+  const T yo = from_f<T>(y);
+  if (is_q)
+    static_cast<T*>(p.q_ws)[(t * p.heads + h) * hd + d] = yo;
+  else
+    static_cast<T*>(p.k_cache)[h * p.cache_sh + pos * hd + d] = yo;
+}
+
+// ------------------------------------------------------------ attention
+// Shared memory: q rows (float32), then per warp a K tile of 32 keys in the
+// activation dtype with each row padded by 16 bytes (odd 16-byte stride: the
+// lanes' 16-byte reads of their own key rows are free of bank conflicts) and
+// the tile's probabilities; the warps' final rows reuse the K tiles.
+template <typename T, int HD>
+struct AttnSmem {
+  static constexpr int kVec = 16 / (int)sizeof(T);                 // elements per 16-byte vector
+  static constexpr int kKRow = HD + kVec;                          // padded K row (elements)
+  static constexpr size_t kQ = (size_t)kRows * HD * 4;
+  static constexpr size_t kK = (size_t)kWarps * kKeyTile * kKRow * sizeof(T);
+  static constexpr size_t kP = (size_t)kWarps * kRows * kKeyTile * 4;
+  static constexpr size_t kMerge = (size_t)kWarps * kRows * (HD + 2) * 4;
+  static constexpr size_t kBytes = kQ + (kK > kMerge ? kK : kMerge) + kP;
+};
+
+template <typename T>
+__device__ __forceinline__ void load_vec(const T* src, float* dst, int n) {
+  // n consecutive elements (n * sizeof(T) a multiple of 16, src 16-byte aligned)
+  for (int i = 0; i < n; i += 16 / (int)sizeof(T)) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src + i);
+    if constexpr (sizeof(T) == 4) {
+      dst[i] = __uint_as_float(u.x);
+      dst[i + 1] = __uint_as_float(u.y);
+      dst[i + 2] = __uint_as_float(u.z);
+      dst[i + 3] = __uint_as_float(u.w);
+    } else {
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        dst[i + 2 * j] = __uint_as_float(w[j] << 16);
+        dst[i + 2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+      }
+    }
+  }
+}
+
+template <typename T, int HD>
+__global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams p) {
+  using SM = AttnSmem<T, HD>;
+  constexpr int DPL = HD / 32;  // output features per lane (consecutive)
+  extern __shared__ __align__(16) unsigned char smem[];
+  float* qs = reinterpret_cast<float*>(smem);
+  T* kt_all = reinterpret_cast<T*>(smem + SM::kQ);
+  float* mrg = reinterpret_cast<float*>(smem + SM::kQ);  // after the key loop
+  float* ps_all = reinterpret_cast<float*>(smem + SM::kQ + (SM::kK > SM::kMerge ? SM::kK : SM::kMerge));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hk = blockIdx.y, split = blockIdx.z;
+  const int64_t rows_all = p.n_tokens * p.group;
+  const int64_t r0 = (int64_t)blockIdx.x * kRows;
+
+  // this CTA's rows: (token, head) pairs of kv head hk; their causal limits
+  int64_t lim[kRows];  // keys [0, lim) are visible to the row (0: inactive row)
+  int64_t kmax = 0;
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    const int64_t R = r0 + r;
+    lim[r] = R < rows_all ? p.offset + R / p.group + 1 : 0;
+    kmax = lim[r] > kmax ? lim[r] : kmax;
+  }
+  // q rows into shared memory (float32)
+  for (int i = tid; i < kRows * HD; i += kWarps * 32) {
+    const int r = i / HD, d = i % HD;
+    const int64_t R = r0 + r;
+    float v = 0.f;
+    if (R < rows_all) {
+      const int64_t t = R / p.group;
+      const int h = hk * p.group + (int)(R % p.group);
+      v = to_f(static_cast<const T*>(p.q_ws)[(t * p.heads + h) * HD + d]);
+    }
+    qs[i] = v;
+  }
+  __syncthreads();
+
+  // this split's keys
+  const int64_t per = (((p.cache_len + p.splits - 1) / p.splits) + kKeyTile - 1) / kKeyTile * kKeyTile;
+  const int64_t kbeg = (int64_t)split * per;
+  const int64_t kend = min(kbeg + per, kmax);
+
+  float m[kRows], lsum[kRows], o[kRows][DPL];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    m[r] = -INFINITY;
+    lsum[r] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) o[r][i] = 0.f;
+  }
+  T* kt = kt_all + (size_t)warp * kKeyTile * SM::kKRow;
+  float* ps = ps_all + (size_t)warp * kRows * kKeyTile;
+  const T* kc = static_cast<const T*>(p.k_cache) + hk * p.cache_sh;
+  const T* vc = static_cast<const T*>(p.v_cache) + hk * p.cache_sh;
+
+  for (int64_t k0 = kbeg + (int64_t)warp * kKeyTile; k0 < kend; k0 += (int64_t)kWarps * kKeyTile) {
+    const int nvalid = (int)min((int64_t)kKeyTile, kend - k0);  // warp-uniform
+    // stage the K tile (16-byte vectors, whole warp)
+    constexpr int VPR = HD / SM::kVec;  // vectors per row
+    for (int i = lane; i < nvalid * VPR; i += 32) {
+      const int row = i / VPR, col = (i % VPR) * SM::kVec;
+      *reinterpret_cast<uint4*>(kt + row * SM::kKRow + col) =
+          *reinterpret_cast<const uint4*>(kc + (k0 + row) * HD + col);
+    }
+    __syncwarp();
+    // scores: lane = key
+    float s[kRows];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) s[r] = 0.f;
+    if (lane < nvalid) {
+      const T* krow = kt + lane * SM::kKRow;
+#pragma unroll 2
+      for (int d = 0; d < HD; d += SM::kVec) {
+        float kv[SM::kVec];
+        load_vec<T>(krow + d, kv, SM::kVec);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          const float4* q4 = reinterpret_cast<const float4*>(qs + r * HD + d);
+#pragma unroll
+          for (int e = 0; e < SM::kVec; e += 4) {
+            const float4 qv = q4[e / 4];
+            s[r] = fmaf(qv.x, kv[e], fmaf(qv.y, kv[e + 1], fmaf(qv.z, kv[e + 2], fmaf(qv.w, kv[e + 3], s[r]))));
+          }
+        }
+      }
+    }
+    // online softmax per row
+    const int64_t kpos = k0 + lane;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r) {
+      const bool ok = lane < nvalid && kpos < lim[r];
+      const float sv = ok ? s[r] * p.scale : -INFINITY;
+      float tm = sv;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
+      const float mn = fmaxf(m[r], tm);
+      const float alpha = mn == -INFINITY ? 1.f : __expf(m[r] - mn);
+      const float pj = ok ? __expf(sv - mn) : 0.f;
+      lsum[r] = lsum[r] * alpha + pj;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) o[r][i] *= alpha;
+      m[r] = mn;
+      ps[r * kKeyTile + lane] = pj;
+    }
+    __syncwarp();
+    // output: lane = features [lane * DPL, +DPL)
+    for (int j = 0; j < nvalid; ++j) {
+      float vv[DPL];
+      if constexpr (DPL * sizeof(T) >= 16) {
+        load_vec<T>(vc + (k0 + j) * HD + lane * DPL, vv, DPL);
+      } else {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) vv[i] = to_f(vc[(k0 + j) * HD + lane * DPL + i]);
+      }
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) {
+        const float pr = ps[r * kKeyTile + j];
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) o[r][i] = fmaf(pr, vv[i], o[r][i]);
+      }
+    }
+    __syncwarp();
+  }
+
+  // merge the warps: row sums over lanes, then (max, sum, output) per warp
+#pragma unroll
+  for (int r = 0; r < kRows; ++r)
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], off);
+  __syncthreads();  // every warp is done with its K tile
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    float* mr = mrg + ((size_t)warp * kRows + r) * (HD + 2);
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) mr[lane * DPL + i] = o[r][i];
+    if (lane == 0) {
+      mr[HD] = m[r];
+      mr[HD + 1] = lsum[r];
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < kRows * HD; i += kWarps * 32) {
+    const int r = i / HD, d = i % HD;
+    const int64_t R = r0 + r;
+    if (R >= rows_all) continue;
+    float mm = -INFINITY;
+    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, mrg[((size_t)w * kRows + r) * (HD + 2) + HD]);
+    float acc = 0.f, l = 0.f;
+    if (mm != -INFINITY)
+      for (int w = 0; w < kWarps; ++w) {
+        const float* mr = mrg + ((size_t)w * kRows + r) * (HD + 2);
+        const float sc = __expf(mr[HD] - mm);
+        acc += sc * mr[d];
+        l += sc * mr[HD + 1];
+      }
+    const int64_t t = R / p.group;
+    const int h = hk * p.group + (int)(R % p.group);
+    const int64_t row = t * p.heads + h;
+    if (p.splits == 1) {
+      const T* gate = static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * HD + HD;
+      const float att = round_to<T>(acc / l);
+      const float gt = round_to<T>(sigmoid_f(to_f(gate[d])));
+      static_cast<T*>(p.out)[t * p.out_st + (int64_t)h * HD + d] = from_f<T>(att * gt);
+    } else {
+      float* pr = p.part + ((size_t)split * p.n_tokens * p.heads + row) * (HD + 2);
+      pr[d] = acc;
+      if (d == 0) {
+        pr[HD] = mm;
+        pr[HD + 1] = l;
+      }
+    }
+  }
+}
+
+// Adds the splits' partial rows: out = sum_s e^(m_s - m) o_s / sum_s e^(m_s - m) l_s.
+template <typename T>
+__global__ void attn_combine_kernel(const AttnParams p) {
+  const int hd = p.head_dim;
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t rows = p.n_tokens * p.heads;
+  if (i >= rows * hd) return;
+  const int64_t row = i / hd;
+  const int d = (int)(i % hd);
+  const size_t stride = (size_t)rows * (hd + 2);
+  float mm = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) mm = fmaxf(mm, p.part[s * stride + row * (hd + 2) + hd]);
+  float acc = 0.f, l = 0.f;
+  for (int s = 0; s < p.splits; ++s) {
+    const float* pr = p.part + s * stride + row * (hd + 2);
+    const float sc = pr[hd] == -INFINITY ? 0.f : __expf(pr[hd] - mm);
+    acc += sc * pr[d];
+    l += sc * pr[hd + 1];
+  }
+  const int64_t t = row / p.heads;
+  const int h = (int)(row % p.heads);
+  const T* gate = static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * hd + hd;
+  const float att = round_to<T>(acc / l);
+  const float gt = round_to<T>(sigmoid_f(to_f(gate[d])));
+  static_cast<T*>(p.out)[t * p.out_st + (int64_t)h * hd + d] = from_f<T>(att * gt);
+}
+
+template <typename T, int HD>
+gdn_status launch_fwd(const AttnParams& p, dim3 grid, cudaStream_t s) {
+  static bool attr = false;  // set once per instance (a repeat from a racing thread is harmless)
+  constexpr size_t smem = AttnSmem<T, HD>::kBytes;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_fwd_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return set_error(GDN_ECUDA, "attention: shared-memory attribute");
+    attr = true;
+  }
+  attn_fwd_kernel<T, HD><<<grid, kWarps * 32, smem, s>>>(p);
+  return GDN_OK;
+}
+
+template <typename T>
+gdn_status launch_fwd_hd(const AttnParams& p, dim3 grid, cudaStream_t s) {
+  switch (p.head_dim) {
+    case 32: return launch_fwd<T, 32>(p, grid, s);
+    case 64: return launch_fwd<T, 64>(p, grid, s);
+    case 128: return launch_fwd<T, 128>(p, grid, s);
+    default: return launch_fwd<T, 256>(p, grid, s);
+  }
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Checks the arguments and fills everything but the workspace pointers.
+gdn_status attn_setup(const gdn_attn_args* a, AttnParams* p, size_t* ws_bytes) {
+  if (!a) return set_error(GDN_EINVAL, "args is NULL");
+  if (a->n_tokens < 0 || a->cache_len < a->n_tokens || a->capacity < a->cache_len)
+    return set_error(GDN_EINVAL, "attention needs 0 <= n_tokens <= cache_len <= capacity");
+  if (a->heads <= 0 || a->kv_heads <= 0 || a->heads % a->kv_heads)
+    return set_error(GDN_EINVAL, "heads must be a positive multiple of kv_heads");
+  if (a->head_dim != 32 && a->head_dim != 64 && a->head_dim != 128 && a->head_dim != 256)
+    return set_error(GDN_EUNSUPPORTED, "head_dim must be 32, 64, 128 or 256 (got %d)", a->head_dim);
+  if (a->rotary_dim < 0 || a->rotary_dim > a->head_dim || a->rotary_dim % 2)
+    return set_error(GDN_EINVAL, "rotary_dim must be even and at most head_dim");
+  if (a->act_dtype != GDN_F32 && a->act_dtype != GDN_BF16)
+    return set_error(GDN_EUNSUPPORTED, "attention runs float32 or bf16 activations");
+  if (a->n_tokens > 0 && (!a->qg || !a->k_new || !a->v_new || !a->q_norm || !a->k_norm || !a->k_cache ||
+                          !a->v_cache || !a->out))
+    return set_error(GDN_EINVAL, "tensor pointers must be non-NULL");
+  const size_t es = a->act_dtype == GDN_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(a->k_cache) | reinterpret_cast<uintptr_t>(a->v_cache)) & 15u)
+    return set_error(GDN_EINVAL, "the caches must be 16-byte aligned");
+  if (a->n_tokens > 0x7fffffffLL || a->cache_len > 0x7fffffffLL)
+    return set_error(GDN_EUNSUPPORTED, "n_tokens and cache_len must be < 2^31");
+  p->n_tokens = a->n_tokens;
+  p->cache_len = a->cache_len;
+  p->offset = a->cache_len - a->n_tokens;
+  p->heads = a->heads;
+  p->kv_heads = a->kv_heads;
+  p->head_dim = a->head_dim;
+  p->rotary_dim = a->rotary_dim;
+  p->group = a->heads / a->kv_heads;
+  p->eps = a->eps;
+  p->scale = a->scale;
+  p->log_base = std::log((double)a->rope_base);
+  p->qg = a->qg;
+  p->qg_st = a->qg_stride_t;
+  p->k_new = a->k_new;
+  p->k_st = a->k_stride_t;
+  p->v_new = a->v_new;
+  p->v_st = a->v_stride_t;
+  p->q_norm = a->q_norm;
+  p->k_norm = a->k_norm;
+  p->k_cache = a->k_cache;
+  p->v_cache = a->v_cache;
+  p->cache_sh = a->capacity * a->head_dim;
+  p->out = a->out;
+  p->out_st = a->out_stride_t;
+  // key splits: enough CTAs for the machine when the rows are few (decode)
+  const int64_t row_ctas = (a->n_tokens * p->group + kRows - 1) / kRows * a->kv_heads;
+  int64_t splits = 1;
+  if (row_ctas > 0 && row_ctas < 2 * 148) {
+    splits = (2 * 148 + row_ctas - 1) / row_ctas;
+    const int64_t max_by_keys = (a->cache_len + kWarps * kKeyTile - 1) / (kWarps * kKeyTile);
+    if (splits > max_by_keys) splits = max_by_keys;
+    if (splits > 64) splits = 64;
+    if (splits < 1) splits = 1;
+  }
+  p->splits = (int)splits;
+  const size_t q_bytes = align256((size_t)a->n_tokens * a->heads * a->head_dim * es);
+  const size_t part_bytes =
+      splits > 1 ? align256((size_t)splits * a->n_tokens * a->heads * (a->head_dim + 2) * 4) : 0;
+  *ws_bytes = q_bytes + part_bytes;
+  return GDN_OK;
+}
+
+}  // namespace
+}  // namespace gdn
+
+extern "C" gdn_status gdn_attention_workspace_size(const gdn_attn_args* a, size_t* bytes) {
+  gdn::AttnParams p;
+  if (!bytes) return gdn::set_error(GDN_EINVAL, "bytes is NULL");
+  return gdn::attn_setup(a, &p, bytes);
+}
+
+extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream) {
+  gdn::AttnParams p;
+  size_t need = 0;
+  gdn_status st = gdn::attn_setup(a, &p, &need);
+  if (st != GDN_OK) return st;
+  if (a->n_tokens == 0) return GDN_OK;
+  if (!a->workspace || a->workspace_bytes < need)
+    return gdn::set_error(GDN_EINVAL, "workspace too small: %zu bytes needed", need);
+  const size_t es = a->act_dtype == GDN_F32 ? 4 : 2;
+  unsigned char* ws = static_cast<unsigned char*>(a->workspace);
+  p.q_ws = ws;
+  p.part = reinterpret_cast<float*>(ws + gdn::align256((size_t)a->n_tokens * a->heads * a->head_dim * es));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const dim3 pgrid((unsigned)a->n_tokens, (unsigned)(a->heads + 2 * a->kv_heads));
+  const int64_t row_blocks = (a->n_tokens * p.group + gdn::kRows - 1) / gdn::kRows;
+  if (row_blocks > 0x7fffffffLL) return gdn::set_error(GDN_EUNSUPPORTED, "too many rows for one call");
+  const dim3 fgrid((unsigned)row_blocks, (unsigned)a->kv_heads, (unsigned)p.splits);
+  if (a->act_dtype == GDN_F32) {
+    gdn::attn_prep_kernel<float><<<pgrid, a->head_dim, 0, s>>>(p);
+    st = gdn::launch_fwd_hd<float>(p, fgrid, s);
+    if (st == GDN_OK && p.splits > 1) {
+      const int64_t n = a->n_tokens * a->heads * a->head_dim;
+      gdn::attn_combine_kernel<float><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p);
+    }
+  } else {
+    gdn::attn_prep_kernel<__nv_bfloat16><<<pgrid, a->head_dim, 0, s>>>(p);
+    st = gdn::launch_fwd_hd<__nv_bfloat16>(p, fgrid, s);
+    if (st == GDN_OK && p.splits > 1) {
+      const int64_t n = a->n_tokens * a->heads * a->head_dim;
+      gdn::attn_combine_kernel<__nv_bfloat16><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p);
+    }
+  }
+  if (st != GDN_OK) return st;
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return gdn::set_error(GDN_ECUDA, "attention launch: %s", cudaGetErrorString(e));
+  return GDN_OK;
+}

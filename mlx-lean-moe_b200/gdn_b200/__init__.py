@@ -15,12 +15,17 @@ from .gated_delta import (
     gated_delta_scan_varlen,
     gated_delta_step,
 )
+from .attention import AttentionShape, GrowingKVCache, Qwen3_5Attention, attention_core
 from .linear_attention import LinearAttentionShape, Qwen3_5LinearAttention, gated_delta_block
 from .quantized import LinearWeights, QuantScheme, as_linear, concat_rows, dequantize, quantized_linear
 from .recurrent_cache import BatchedRecurrentCache, RecurrentCache
 
 __all__ = [
+    "AttentionShape",
     "BatchedRecurrentCache",
+    "GrowingKVCache",
+    "Qwen3_5Attention",
+    "attention_core",
     "DecodePlan",
     "LinearAttentionShape",
     "LinearWeights",

@@ -74,6 +74,24 @@ class QLinearArgs(ctypes.Structure):
     ]
 
 
+class AttnArgs(ctypes.Structure):
+    """``gdn_attn_args``."""
+
+    _fields_ = [
+        ("n_tokens", _i64), ("cache_len", _i64), ("capacity", _i64),
+        ("heads", _i32), ("kv_heads", _i32), ("head_dim", _i32), ("rotary_dim", _i32),
+        ("rope_base", ctypes.c_float), ("eps", ctypes.c_float), ("scale", ctypes.c_float),
+        ("qg", _p), ("qg_stride_t", _i64),
+        ("k_new", _p), ("k_stride_t", _i64),
+        ("v_new", _p), ("v_stride_t", _i64),
+        ("q_norm", _p), ("k_norm", _p),
+        ("k_cache", _p), ("v_cache", _p),
+        ("act_dtype", _enum),
+        ("out", _p), ("out_stride_t", _i64),
+        ("workspace", _p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 EXPORTS = {
     "gdn_version": (ctypes.c_int, []),
     "gdn_last_error": (ctypes.c_char_p, []),
@@ -86,6 +104,8 @@ EXPORTS = {
     "gdn_fused_block_noalloc": (_enum, [ctypes.POINTER(BlockArgs), _p]),
     "gdn_quantized_linear": (_enum, [ctypes.POINTER(QLinearArgs), _p]),
     "gdn_dequantize": (_enum, [ctypes.POINTER(QLinearArgs), _enum, _p, _p]),
+    "gdn_attention_workspace_size": (_enum, [ctypes.POINTER(AttnArgs), ctypes.POINTER(ctypes.c_size_t)]),
+    "gdn_attention": (_enum, [ctypes.POINTER(AttnArgs), _p]),
     "gdn_check_device_errors": (_enum, [_p]),
 }
 

@@ -579,6 +579,6 @@ def attention_layer(x, w, keys, values, heads, kv_heads, head_dim, rotary_dim, t
     keys = np.concatenate([keys, k.transpose(1, 0, 2)], axis=1)  # :85
     values = np.concatenate([values, v.transpose(1, 0, 2)], axis=1)
     o = rnd(attention_core(q, keys, values, head_dim ** -0.5)).reshape(length, heads * head_dim)  # :87-94
-    o = rnd(o * sigmoid(gate.reshape(length, heads * head_dim)))  # :96
+    o = rnd(o * rnd(sigmoid(gate.reshape(length, heads * head_dim))))  # :96
     out = rnd(o @ np.asarray(w["o_proj"], np.float64).T)  # :97
     return out, keys, values

@@ -53,7 +53,8 @@ def _c_layout(tmp_path, struct: str, fields: list[str]) -> list[int]:
 
 
 @pytest.mark.parametrize("py,c", [(_lib.ScanArgs, "gdn_scan_args"), (_lib.DecodeArgs, "gdn_decode_args"),
-                                  (_lib.BlockArgs, "gdn_block_args"), (_lib.QLinearArgs, "gdn_qlinear_args")])
+                                  (_lib.BlockArgs, "gdn_block_args"), (_lib.QLinearArgs, "gdn_qlinear_args"),
+                                  (_lib.AttnArgs, "gdn_attn_args")])
 def test_ctypes_structs_match_c_layout(tmp_path, py, c):
     fields = [f[0] for f in py._fields_]
     got = [ctypes.sizeof(py)] + [getattr(py, f).offset for f in fields]

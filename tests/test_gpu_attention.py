@@ -1,0 +1,123 @@
+"""The softmax-attention layer (gdn_attention) against the reference's own
+Qwen3_5Attention + GrowingKVCache (golden vectors, float32) and against the
+oracle's restatement with bf16 rounding at the model's head shape."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import gdn_b200
+from gdn_b200 import AttentionShape, GrowingKVCache, Qwen3_5Attention
+from gpu_helpers import dev, n, t
+from make_golden import ATTN, attn_case
+from oracle import gdn_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SMALL = AttentionShape(ATTN["heads"], ATTN["kv_heads"], ATTN["head_dim"], ATTN["rotary"], ATTN["theta"])
+
+
+def _layer(w, shape=SMALL, eps=ATTN["eps"], dtype=torch.float32):
+    return Qwen3_5Attention(shape, eps, t(w["q_proj"], dtype), t(w["q_norm"]), t(w["k_proj"], dtype),
+                            t(w["k_norm"]), t(w["v_proj"], dtype), t(w["o_proj"], dtype))
+
+
+def _cache(shape=SMALL, max_context=16, dtype=torch.float32):
+    return GrowingKVCache(max_context, shape.num_key_value_heads, shape.head_dim, dtype=dtype, device=dev())
+
+
+@pytest.mark.parametrize("seq_len", [1, 6])
+def test_attention_matches_reference_layer(seq_len, golden):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    w = attn_case(0)
+    x = np.random.default_rng(200).standard_normal((seq_len, ATTN["hidden"])).astype(np.float32)
+    cache = _cache()
+    out = _layer(w)(t(x), cache)
+    np.testing.assert_allclose(n(out), golden[f"attn_fresh_{seq_len}/out"], rtol=1e-4, atol=1e-5)
+    keys, values = cache.state()
+    np.testing.assert_allclose(n(keys), golden[f"attn_fresh_{seq_len}/keys"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(n(values), golden[f"attn_fresh_{seq_len}/values"], rtol=1e-5, atol=1e-6)
+    assert cache.size == seq_len
+
+
+def test_attention_decode_steps_and_offset_chunks(golden):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    w = attn_case(1)
+    x = np.random.default_rng(201).standard_normal((5, ATTN["hidden"])).astype(np.float32)
+    layer, cache = _layer(w), _cache()
+    stepwise = torch.stack([layer(t(x[i]), cache) for i in range(5)])
+    np.testing.assert_allclose(n(stepwise), golden["attn_steps/out"], rtol=1e-4, atol=1e-5)
+    batched = layer(t(x), _cache())
+    np.testing.assert_allclose(n(batched), golden["attn_steps/batched"], rtol=1e-4, atol=1e-5)
+
+    w = attn_case(3)
+    xs = np.random.default_rng(203).standard_normal((3, 4, ATTN["hidden"])).astype(np.float32)
+    layer, cache = _layer(w), _cache()
+    outs = torch.cat([layer(t(xc), cache) for xc in xs])
+    np.testing.assert_allclose(n(outs), golden["attn_chunks/out"], rtol=1e-4, atol=1e-5)
+    keys, values = cache.state()
+    np.testing.assert_allclose(n(keys), golden["attn_chunks/keys"], rtol=1e-5, atol=1e-6)
+    assert cache.size == 12
+
+
+def _random_weights(rng, shape, hidden, scale):
+    h, hkv, hd = shape.num_attention_heads, shape.num_key_value_heads, shape.head_dim
+    dense = lambda o, i: (rng.standard_normal((o, i)) * scale).astype(np.float32)
+    w = {"q_proj": dense(h * hd * 2, hidden), "k_proj": dense(hkv * hd, hidden), "v_proj": dense(hkv * hd, hidden),
+         "o_proj": dense(hidden, h * hd)}
+    w["q_norm"] = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    w["k_norm"] = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    return w
+
+
+def _bf16_weights(w):
+    return {k: (O.bf16_round(v) if k.endswith("proj") else v) for k, v in w.items()}
+
+
+def test_attention_bf16_at_model_shape_prefill_growth_and_decode():
+    # the model's attention heads: 16 queries over 2 key/value heads of 256, rotary 64
+    shape = AttentionShape(16, 2, 256, 64, 10000000.0)
+    hidden, eps = 2048, 1e-6
+    rng = np.random.default_rng(11)
+    w = _bf16_weights(_random_weights(rng, shape, hidden, 0.02))
+    layer = _layer(w, shape, eps, torch.bfloat16)
+    cache = _cache(shape, max_context=1024, dtype=torch.bfloat16)
+    keys = np.zeros((2, 0, 256))
+    values = np.zeros((2, 0, 256))
+    for L in (250, 10, 1, 1, 3):  # crosses the 256-token growth block; decode rows take the key splits
+        x = O.bf16_round(rng.standard_normal((L, hidden)).astype(np.float32))
+        got = layer(t(x, torch.bfloat16), cache)
+        want, keys, values = O.attention_layer(x, w, keys, values, 16, 2, 256, 64, 10000000.0, eps,
+                                               rnd=O.bf16_round)
+        assert O.rel_l2(n(got), want) < 1e-2, (L, O.rel_l2(n(got), want))
+    assert cache.size == 265 and cache.allocated_size == 512
+    gk, gv = cache.state()
+    assert O.rel_l2(n(gk), keys) < 1e-2 and O.rel_l2(n(gv), values) < 1e-2
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim,rotary", [(8, 8, 64, 64), (6, 2, 128, 32), (4, 1, 256, 0)])
+def test_attention_float32_other_head_shapes(heads, kv_heads, head_dim, rotary):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    shape = AttentionShape(heads, kv_heads, head_dim, rotary, 10000.0)
+    rng = np.random.default_rng(heads + head_dim)
+    w = _random_weights(rng, shape, 96, 0.1)
+    layer, cache = _layer(w, shape, 1e-6), _cache(shape, max_context=300)
+    keys, values = np.zeros((kv_heads, 0, head_dim)), np.zeros((kv_heads, 0, head_dim))
+    for L in (37, 1, 140):
+        x = rng.standard_normal((L, 96)).astype(np.float32)
+        got = layer(t(x), cache)
+        want, keys, values = O.attention_layer(x, w, keys, values, heads, kv_heads, head_dim, rotary, 10000.0, 1e-6)
+        np.testing.assert_allclose(n(got), want, rtol=2e-4, atol=2e-5)
+
+
+def test_cache_capacity_is_a_hard_limit():
+    cache = _cache(max_context=4)
+    w = attn_case(0)
+    layer = _layer(w)
+    layer(t(np.zeros((3, ATTN["hidden"]), np.float32)), cache)
+    with pytest.raises(IndexError):
+        layer(t(np.zeros((2, ATTN["hidden"]), np.float32)), cache)
+    assert cache.size == 3
+    gdn_b200.check_device_errors()
