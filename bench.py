@@ -367,6 +367,69 @@ def measure_layer(device, iters=3):
             "ms": sum(med), "gemm_flop": gemm_flop}
 
 
+def measure_attention(device, iters=3):
+    """The softmax-attention core at the model's attention shape (16 query
+    heads over 2 key/value heads of 256, rotary 64, bf16): a 4,096-token
+    prefill from an empty cache, and one decode token against 4,096 cached
+    positions."""
+    import gdn_b200
+    from gdn_b200 import AttentionShape, GrowingKVCache
+
+    shape = AttentionShape(16, 2, 256, 64, 10000000.0)
+    L = 4096
+    gen = torch.Generator(device).manual_seed(7)
+    qg = torch.randn(L, 16 * 512, device=device, generator=gen).bfloat16()
+    k = torch.randn(L, 2 * 256, device=device, generator=gen).bfloat16()
+    v = torch.randn(L, 2 * 256, device=device, generator=gen).bfloat16()
+    qn = torch.ones(256, device=device)
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ms = []
+        for _ in range(iters):
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            ms.append(e0.elapsed_time(e1))
+        return statistics.median(ms)
+
+    def prefill():
+        cache = GrowingKVCache(L + 1, 2, 256, dtype=torch.bfloat16, device=device)
+        cache.reserve(L)
+        gdn_b200.attention_core(qg, k, v, qn, qn, shape, 1e-6, cache)
+
+    pre_ms = timed(prefill)
+    cache = GrowingKVCache(L + 64, 2, 256, dtype=torch.bfloat16, device=device)
+    gdn_b200.attention_core(qg, k, v, qn, qn, shape, 1e-6, cache)
+
+    # decode as a CUDA-graph replay (device time; the Python call alone costs
+    # more than the three launches): the same position every time, 4,096
+    # cached keys and values
+    cache.commit(L)
+    gdn_b200.attention_core(qg[:1], k[:1], v[:1], qn, qn, shape, 1e-6, cache)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        cache.commit(L)
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(20):
+                gdn_b200.attention_core(qg[:1], k[:1], v[:1], qn, qn, shape, 1e-6, cache)
+                cache.commit(L)
+    torch.cuda.synchronize()
+    dec_ms = timed(graph.replay) / 20
+    del graph
+    flop = 4 * 256 * 16 * L * (L + 1) / 2
+    kv_bytes = 2 * 2 * (L + 1) * 256 * 2
+    return {"prefill_ms": pre_ms, "prefill_tflops": flop / (pre_ms / 1e3) / 1e12,
+            "decode_us": dec_ms * 1e3, "decode_kv_gbs": kv_bytes / (dec_ms / 1e3) / 1e9}
+
+
 def run_qproj(args):
     """Only the quantized in-projection (12,352 x 2,048, 4-bit, group 64) at
     ``--tokens`` rows: the GEMV up to 16 tokens, the tiled GEMM beyond; for
@@ -693,6 +756,13 @@ def main():
                                    "projection, conv+norms+gates+scan+gated RMSNorm (two state resets included)",
                          "achieved_tflops": blk_flop / (blk_ms / 1e3) / 1e12,
                          "frac_of_bf16_peak": blk_flop / (blk_ms / 1e3) / 1e12 / tc_peak}
+        att = measure_attention(device)
+        line["attention"] = {
+            "prefill_ms": att["prefill_ms"], "prefill_tflops": att["prefill_tflops"],
+            "decode_us": att["decode_us"], "decode_kv_gbs": att["decode_kv_gbs"],
+            "config": "softmax-attention core (norms, rotary, cache append, grouped-query causal attention, "
+                      "gate) at 16/2 heads of 256, rotary 64, bf16: 4,096-token prefill; one decode token "
+                      "against 4,096 cached positions (CUDA-core flash-style kernel)"}
         lay = measure_layer(device)
         line["layer"] = {
             "value": lay["tokens"] / (lay["ms"] / 1e3), "unit": "tok/s", "ms": lay["ms"],
