@@ -24,6 +24,8 @@
 //                      rows (normalization, gate, output); several write
 //                      partial (max, sum, output) rows that
 // attn_combine_kernel  adds up, then gates and writes.
+// attn_mma_kernel      bf16 prefill (calls with enough rows for one key
+//                      split) on the tensor cores: see its comment below.
 #include <cuda_bf16.h>
 
 #include <cmath>
@@ -349,6 +351,232 @@ __global__ void attn_combine_kernel(const AttnParams p) {
   static_cast<T*>(p.out)[t * p.out_st + (int64_t)h * hd + d] = from_f<T>(att * gt);
 }
 
+// ------------------------------------------------- prefill, tensor cores
+// bf16 prefill on mma.sync m16n8k16 (bf16 x bf16 -> float32), FA2-style: one
+// CTA per (64 queries, query head), four warps of 16 query rows.  K and V
+// tiles of 64 keys (the key/value head of the group) pass through shared
+// memory by cp.async, double-buffered; each 16-byte chunk of a row sits at
+// chunk ^ (row & 7) so that ldmatrix reads are free of bank conflicts.
+// S = Q K^T: A fragments of Q by ldmatrix, B fragments of K by ldmatrix (K
+// rows are the B operand's columns); the online softmax runs on the S
+// fragments; P goes from the S accumulators straight into A fragments;
+// O += P V: B fragments of V by ldmatrix.trans.  The causal mask applies on
+// the tiles that cross the diagonal.
+constexpr int kMQ = 64;   // queries per CTA
+constexpr int kMK = 64;   // keys per tile
+
+template <int HD>
+struct MmaSmem {
+  static constexpr size_t kTile = (size_t)kMK * HD * 2;  // one K or V tile, bf16
+  static constexpr size_t kQ = (size_t)kMQ * HD * 2;
+  static constexpr size_t kBytes = kQ + 4 * kTile;      // Q, K[2], V[2]
+};
+
+__device__ __forceinline__ uint32_t swz(int row, int col, int hd) {
+  // byte offset of element (row, col) in a [rows][hd] bf16 tile, 16-byte chunks XOR-swizzled
+  return (uint32_t)(row * hd * 2 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
+  using SM = MmaSmem<HD>;
+  constexpr int NT = HD / 8;      // output n-tiles of 8 features
+  constexpr int KC = HD / 8;      // 16-byte chunks per row
+  extern __shared__ __align__(16) unsigned char smem_mma[];
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem_mma);
+  const uint32_t sQ = sbase, sK0 = sbase + SM::kQ, sV0 = sK0 + 2 * SM::kTile;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int h = blockIdx.y, hk = h / p.group;
+  const int64_t q0 = (int64_t)blockIdx.x * kMQ;  // first query (token index of this call)
+  const __nv_bfloat16* qw = static_cast<const __nv_bfloat16*>(p.q_ws);
+  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(p.k_cache) + hk * p.cache_sh;
+  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(p.v_cache) + hk * p.cache_sh;
+  // keys this CTA needs: up to the newest of its queries
+  const int64_t q_last = min(q0 + kMQ, p.n_tokens) - 1;
+  const int64_t kneed = p.offset + q_last + 1;
+  const int ntiles = (int)((kneed + kMK - 1) / kMK);
+
+  // Q tile (rows past n_tokens zero-filled)
+  for (int i = tid; i < kMQ * KC; i += 128) {
+    const int r = i / KC, c = (i % KC) * 8;
+    const int64_t t = q0 + r;
+    const bool ok = t < p.n_tokens;
+    cp_async16(sQ + swz(r, c, HD), qw + ((ok ? t : 0) * p.heads + h) * HD + c, ok);
+  }
+  auto load_kv = [&](int tile, int buf) {
+    const int64_t k0 = (int64_t)tile * kMK;
+    for (int i = tid; i < kMK * KC; i += 128) {
+      const int r = i / KC, c = (i % KC) * 8;
+      const int64_t kp = k0 + r;
+      const bool ok = kp < kneed;
+      const int64_t src = (ok ? kp : 0) * HD + c;
+      cp_async16(sK0 + buf * SM::kTile + swz(r, c, HD), kc + src, ok);
+      cp_async16(sV0 + buf * SM::kTile + swz(r, c, HD), vc + src, ok);
+    }
+  };
+  load_kv(0, 0);
+  cp_async_commit();
+
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g and g + 8 of this warp
+  const float sl2 = p.scale * 1.4426950408889634f;           // scores in log2 units
+  const int64_t qpos0 = p.offset + q0 + warp * 16 + g, qpos1 = qpos0 + 8;
+
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int buf = tile & 1;
+    if (tile + 1 < ntiles) load_kv(tile + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();  // this tile (and Q) have landed
+    __syncthreads();
+    const uint32_t sK = sK0 + buf * SM::kTile, sV = sV0 + buf * SM::kTile;
+
+    // S = Q K^T for this warp's 16 rows x 64 keys
+    float s[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(sQ + swz(warp * 16 + (lane & 15), ks * 16 + (lane >> 4) * 8, HD), a);
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {  // pairs of key n-tiles
+        uint32_t b[4];
+        const int krow = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int kcol = ks * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(sK + swz(krow, kcol, HD), b);
+        mma16816(s[2 * np], a, b[0], b[1]);
+        mma16816(s[2 * np + 1], a, b[2], b[3]);
+      }
+    }
+    // mask and online softmax (rows g: s[n][0..1], g + 8: s[n][2..3])
+    const int64_t k0 = (int64_t)tile * kMK;
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int64_t kp = k0 + n * 8 + 2 * t4 + e;
+        s[n][e] = kp <= qpos0 ? s[n][e] * sl2 : -INFINITY;
+        s[n][2 + e] = kp <= qpos1 ? s[n][2 + e] * sl2 : -INFINITY;
+        mx0 = fmaxf(mx0, s[n][e]);
+        mx1 = fmaxf(mx1, s[n][2 + e]);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float al0 = mx0 == -INFINITY ? 1.f : exp2f(m0 - mx0), al1 = mx1 == -INFINITY ? 1.f : exp2f(m1 - mx1);
+    m0 = mx0;
+    m1 = mx1;
+    l0 *= al0;
+    l1 *= al1;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      o[n][0] *= al0;
+      o[n][1] *= al0;
+      o[n][2] *= al1;
+      o[n][3] *= al1;
+    }
+    uint32_t pa[4][4];  // P as A fragments: 4 k-steps of 16 keys
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      const float p00 = m0 == -INFINITY ? 0.f : exp2f(s[n][0] - m0), p01 = m0 == -INFINITY ? 0.f : exp2f(s[n][1] - m0);
+      const float p10 = m1 == -INFINITY ? 0.f : exp2f(s[n][2] - m1), p11 = m1 == -INFINITY ? 0.f : exp2f(s[n][3] - m1);
+      l0 += p00 + p01;
+      l1 += p10 + p11;
+      pa[n >> 1][(n & 1) * 2] = cvt_bf16x2(p00, p01);
+      pa[n >> 1][(n & 1) * 2 + 1] = cvt_bf16x2(p10, p11);
+    }
+    // O += P V
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {  // pairs of feature n-tiles
+        uint32_t b[4];
+        const int vrow = ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int vcol = np * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(sV + swz(vrow, vcol, HD), b);
+        mma16816(o[2 * np], pa[ks], b[0], b[1]);
+        mma16816(o[2 * np + 1], pa[ks], b[2], b[3]);
+      }
+    }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
+  }
+  cp_async_wait<0>();
+
+  // rows g and g + 8: normalize, gate, store
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const __nv_bfloat16* qg = static_cast<const __nv_bfloat16*>(p.qg);
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int64_t t = q0 + warp * 16 + g + half * 8;
+    if (t >= p.n_tokens) continue;
+    const float inv = 1.f / (half ? l1 : l0);
+    const __nv_bfloat16* gate = qg + t * p.qg_st + (int64_t)h * 2 * HD + HD;
+    __nv_bfloat16* dst = out + t * p.out_st + (int64_t)h * HD;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int d = n * 8 + 2 * t4;
+      const float a0 = round_to<__nv_bfloat16>(o[n][half * 2] * inv);
+      const float a1 = round_to<__nv_bfloat16>(o[n][half * 2 + 1] * inv);
+      const float g0 = round_to<__nv_bfloat16>(sigmoid_f(__bfloat162float(gate[d])));
+      const float g1 = round_to<__nv_bfloat16>(sigmoid_f(__bfloat162float(gate[d + 1])));
+      *reinterpret_cast<uint32_t*>(dst + d) = cvt_bf16x2(a0 * g0, a1 * g1);
+    }
+  }
+}
+
+template <int HD>
+gdn_status launch_mma(const AttnParams& p, cudaStream_t s) {
+  static bool attr = false;
+  constexpr size_t smem = MmaSmem<HD>::kBytes;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return set_error(GDN_ECUDA, "attention: shared-memory attribute");
+    attr = true;
+  }
+  const dim3 grid((unsigned)((p.n_tokens + kMQ - 1) / kMQ), (unsigned)p.heads);
+  attn_mma_kernel<HD><<<grid, 128, smem, s>>>(p);
+  return GDN_OK;
+}
+
 template <typename T, int HD>
 gdn_status launch_fwd(const AttnParams& p, dim3 grid, cudaStream_t s) {
   static bool attr = false;  // set once per instance (a repeat from a racing thread is harmless)
@@ -430,6 +658,8 @@ gdn_status attn_setup(const gdn_attn_args* a, AttnParams* p, size_t* ws_bytes) {
     if (splits > 64) splits = 64;
     if (splits < 1) splits = 1;
   }
+  // bf16 prefill with head_dim >= 64 runs the tensor-core kernel, one key split
+  if (a->act_dtype == GDN_BF16 && a->head_dim >= 64 && (a->n_tokens >= kMQ || splits == 1)) splits = 1;
   p->splits = (int)splits;
   const size_t q_bytes = align256((size_t)a->n_tokens * a->heads * a->head_dim * es);
   const size_t part_bytes =
@@ -473,7 +703,15 @@ extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream)
     }
   } else {
     gdn::attn_prep_kernel<__nv_bfloat16><<<pgrid, a->head_dim, 0, s>>>(p);
-    st = gdn::launch_fwd_hd<__nv_bfloat16>(p, fgrid, s);
+    if (p.splits == 1 && a->head_dim >= 64) {  // prefill: the tensor-core kernel
+      switch (a->head_dim) {
+        case 64: st = gdn::launch_mma<64>(p, s); break;
+        case 128: st = gdn::launch_mma<128>(p, s); break;
+        default: st = gdn::launch_mma<256>(p, s); break;
+      }
+    } else {
+      st = gdn::launch_fwd_hd<__nv_bfloat16>(p, fgrid, s);
+    }
     if (st == GDN_OK && p.splits > 1) {
       const int64_t n = a->n_tokens * a->heads * a->head_dim;
       gdn::attn_combine_kernel<__nv_bfloat16><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p);

@@ -121,3 +121,22 @@ def test_cache_capacity_is_a_hard_limit():
         layer(t(np.zeros((2, ATTN["hidden"]), np.float32)), cache)
     assert cache.size == 3
     gdn_b200.check_device_errors()
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim,rotary", [(8, 2, 64, 16), (4, 4, 128, 128), (16, 4, 256, 64)])
+def test_attention_bf16_tensor_core_prefill(heads, kv_heads, head_dim, rotary):
+    # enough rows for one key split: the mma.sync prefill, then a second
+    # chunk whose queries start at an offset (the causal mask off the diagonal)
+    shape = AttentionShape(heads, kv_heads, head_dim, rotary, 1000000.0)
+    hidden = 256
+    rng = np.random.default_rng(head_dim + heads)
+    w = _bf16_weights(_random_weights(rng, shape, hidden, 0.05))
+    layer = _layer(w, shape, 1e-6, torch.bfloat16)
+    cache = _cache(shape, max_context=1024, dtype=torch.bfloat16)
+    keys, values = np.zeros((kv_heads, 0, head_dim)), np.zeros((kv_heads, 0, head_dim))
+    for L in (130, 300):
+        x = O.bf16_round(rng.standard_normal((L, hidden)).astype(np.float32))
+        got = layer(t(x, torch.bfloat16), cache)
+        want, keys, values = O.attention_layer(x, w, keys, values, heads, kv_heads, head_dim, rotary, 1000000.0,
+                                               1e-6, rnd=O.bf16_round)
+        assert O.rel_l2(n(got), want) < 1e-2, (L, O.rel_l2(n(got), want))
