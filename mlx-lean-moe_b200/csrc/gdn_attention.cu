@@ -19,8 +19,9 @@
 //                      key split); its four warps take interleaved tiles of
 //                      32 keys (lane = key for the scores, lane = feature for
 //                      the output) with their own running max and sum, merged
-//                      at the end; K tiles pass through shared memory, V rows
-//                      are read by the whole warp.  One split finishes the
+//                      at the end; K and V tiles pass through shared memory
+//                      by cp.async (V from global memory only for float32 at
+//                      head_dim 256, where the tiles do not fit).  One split finishes the
 //                      rows (normalization, gate, output); several write
 //                      partial (max, sum, output) rows that
 // attn_combine_kernel  adds up, then gates and writes.
@@ -64,6 +65,14 @@ struct AttnParams {
   void* out;
   int64_t out_st;
 };
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ------------------------------------------------------------------ prep
 template <typename T>
@@ -123,7 +132,11 @@ struct AttnSmem {
   static constexpr int kVec = 16 / (int)sizeof(T);                 // elements per 16-byte vector
   static constexpr int kKRow = HD + kVec;                          // padded K row (elements)
   static constexpr size_t kQ = (size_t)kRows * HD * 4;
-  static constexpr size_t kK = (size_t)kWarps * kKeyTile * kKRow * sizeof(T);
+  static constexpr size_t kKT = (size_t)kKeyTile * kKRow * sizeof(T);  // one warp's K tile
+  static constexpr size_t kVT = (size_t)kKeyTile * HD * sizeof(T);     // one warp's V tile
+  // V tiles through shared memory too, where they fit (not float32 at head_dim 256)
+  static constexpr bool kStageV = (size_t)kWarps * (kKT + kVT) <= 160 * 1024;
+  static constexpr size_t kK = (size_t)kWarps * (kKT + (kStageV ? kVT : 0));
   static constexpr size_t kP = (size_t)kWarps * kRows * kKeyTile * 4;
   static constexpr size_t kMerge = (size_t)kWarps * kRows * (HD + 2) * 4;
   static constexpr size_t kBytes = kQ + (kK > kMerge ? kK : kMerge) + kP;
@@ -200,20 +213,25 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
 #pragma unroll
     for (int i = 0; i < DPL; ++i) o[r][i] = 0.f;
   }
-  T* kt = kt_all + (size_t)warp * kKeyTile * SM::kKRow;
+  T* kt = reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(kt_all) +
+                               (size_t)warp * (SM::kKT + (SM::kStageV ? SM::kVT : 0)));
+  T* vt = reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(kt) + SM::kKT);  // used when kStageV
   float* ps = ps_all + (size_t)warp * kRows * kKeyTile;
   const T* kc = static_cast<const T*>(p.k_cache) + hk * p.cache_sh;
   const T* vc = static_cast<const T*>(p.v_cache) + hk * p.cache_sh;
 
   for (int64_t k0 = kbeg + (int64_t)warp * kKeyTile; k0 < kend; k0 += (int64_t)kWarps * kKeyTile) {
     const int nvalid = (int)min((int64_t)kKeyTile, kend - k0);  // warp-uniform
-    // stage the K tile (16-byte vectors, whole warp)
+    // stage the K (and V) tile by cp.async: every copy in flight at once
     constexpr int VPR = HD / SM::kVec;  // vectors per row
     for (int i = lane; i < nvalid * VPR; i += 32) {
       const int row = i / VPR, col = (i % VPR) * SM::kVec;
-      *reinterpret_cast<uint4*>(kt + row * SM::kKRow + col) =
-          *reinterpret_cast<const uint4*>(kc + (k0 + row) * HD + col);
+      cp_async16((uint32_t)__cvta_generic_to_shared(kt + row * SM::kKRow + col), kc + (k0 + row) * HD + col, true);
+      if constexpr (SM::kStageV)
+        cp_async16((uint32_t)__cvta_generic_to_shared(vt + row * HD + col), vc + (k0 + row) * HD + col, true);
     }
+    cp_async_commit();
+    cp_async_wait<0>();
     __syncwarp();
     // scores: lane = key
     float s[kRows];
@@ -258,7 +276,12 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
     // output: lane = features [lane * DPL, +DPL)
     for (int j = 0; j < nvalid; ++j) {
       float vv[DPL];
-      if constexpr (DPL * sizeof(T) >= 16) {
+      if constexpr (SM::kStageV && DPL * sizeof(T) >= 16) {
+        load_vec<T>(vt + j * HD + lane * DPL, vv, DPL);
+      } else if constexpr (SM::kStageV) {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) vv[i] = to_f(vt[j * HD + lane * DPL + i]);
+      } else if constexpr (DPL * sizeof(T) >= 16) {
         load_vec<T>(vc + (k0 + j) * HD + lane * DPL, vv, DPL);
       } else {
 #pragma unroll
@@ -376,14 +399,6 @@ __device__ __forceinline__ uint32_t swz(int row, int col, int hd) {
   // byte offset of element (row, col) in a [rows][hd] bf16 tile, 16-byte chunks XOR-swizzled
   return (uint32_t)(row * hd * 2 + ((((col >> 3) ^ (row & 7))) << 4) + (col & 7) * 2);
 }
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
