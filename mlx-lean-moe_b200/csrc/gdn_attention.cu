@@ -7,7 +7,7 @@
 // attention with the causal mask aligned to the newest query, and the
 // output gate sigmoid(gate) carried in q_proj's second half.
 //
-// attn_prep_kernel     one CTA per (token, row of q / k / v heads): the
+// attn_prep_kernel     one warp per (token, row of q / k / v heads): the
 //                      norms and the rotation in float32, rounded to the
 //                      activation dtype where the reference materializes
 //                      arrays; q to the workspace, k and v into the cache.
@@ -16,12 +16,10 @@
 //                      their accuracy.
 // attn_fwd_kernel      flash-style attention on the CUDA cores in float32:
 //                      one CTA per (kRows query rows of one key/value head,
-//                      key split); its four warps take interleaved tiles of
-//                      32 keys (lane = key for the scores, lane = feature for
-//                      the output) with their own running max and sum, merged
-//                      at the end; K and V tiles pass through shared memory
-//                      by cp.async (V from global memory only for float32 at
-//                      head_dim 256, where the tiles do not fit).  One split finishes the
+//                      key split); its four warps share each 32-key K/V tile
+//                      (cp.async, double-buffered) and own two rows each, with
+//                      their own running max and sum (lane = key for the
+//                      scores, lane = features for the output).  One split finishes the
 //                      rows (normalization, gate, output); several write
 //                      partial (max, sum, output) rows that
 // attn_combine_kernel  adds up, then gates and writes.
@@ -47,7 +45,7 @@ struct AttnParams {
   int64_t n_tokens, cache_len, offset;  // offset = cache_len - n_tokens: position of the first new token
   int heads, kv_heads, head_dim, rotary_dim, group;  // group = heads / kv_heads
   float eps, scale;
-  double log_base;                      // ln(rope base)
+  double inv_freq[kMaxHeadDim / 2];     // rope_base^(-2i / rotary_dim), from the host in double
   const void* qg;
   int64_t qg_st;
   const void* k_new;
@@ -60,7 +58,7 @@ struct AttnParams {
   void* v_cache;
   int64_t cache_sh;                     // elements between heads of the caches (capacity * head_dim)
   void* q_ws;                           // [n_tokens, heads, head_dim] in the activation dtype
-  float* part;                          // [splits, n_tokens * heads, head_dim + 2] partial rows
+  float* part;                          // [splits, n_tokens * heads, head_dim + 4]: output, max, sum, pad
   int splits;
   void* out;
   int64_t out_st;
@@ -75,71 +73,84 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ------------------------------------------------------------------ prep
+// One warp per (token, head row): rows [0, heads) are queries, then the
+// kv_heads keys, then the kv_heads values; each lane holds head_dim / 32
+// consecutive features.  The norm reduces by shuffles; the rotation reads its
+// partner features from the warp's row in shared memory.
+constexpr int kPrepWarps = 8;
+
 template <typename T>
-__global__ void __launch_bounds__(kMaxHeadDim) attn_prep_kernel(const AttnParams p) {
-  __shared__ float xs[kMaxHeadDim];
-  __shared__ float red[kMaxHeadDim / 32];
-  const int64_t t = blockIdx.x;
-  const int row = blockIdx.y;  // [0, heads): q; [heads, heads + kv): k; then v
-  const int d = threadIdx.x, hd = p.head_dim;
+__device__ __forceinline__ void load_feat(const T* src, float (&x)[8], int dpl) {
+  for (int e = 0; e < dpl; ++e) x[e] = to_f(src[e]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPrepWarps * 32) attn_prep_kernel(const AttnParams p) {
+  __shared__ float xs[kPrepWarps][kMaxHeadDim];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows = p.heads + 2 * p.kv_heads;
+  const int64_t item = (int64_t)blockIdx.x * kPrepWarps + warp;
+  if (item >= p.n_tokens * rows) return;  // the whole warp
+  const int64_t t = item / rows;
+  const int row = (int)(item % rows);
+  const int hd = p.head_dim, dpl = hd / 32, d0 = lane * dpl;
   const bool is_q = row < p.heads, is_k = !is_q && row < p.heads + p.kv_heads;
   const int h = is_q ? row : is_k ? row - p.heads : row - p.heads - p.kv_heads;
   const int64_t pos = p.offset + t;
   if (!is_q && !is_k) {  // v: a copy into the cache
-    const T* src = static_cast<const T*>(p.v_new) + t * p.v_st + (int64_t)h * hd;
-    static_cast<T*>(p.v_cache)[h * p.cache_sh + pos * hd + d] = src[d];
+    const T* src = static_cast<const T*>(p.v_new) + t * p.v_st + (int64_t)h * hd + d0;
+    T* dst = static_cast<T*>(p.v_cache) + h * p.cache_sh + pos * hd + d0;
+    for (int e = 0; e < dpl; ++e) dst[e] = src[e];
     return;
   }
   const T* src = is_q ? static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * hd
                       : static_cast<const T*>(p.k_new) + t * p.k_st + (int64_t)h * hd;
-  const float x = to_f(src[d]);
-  // mean of squares over the head's features
-  float ss = x * x;
+  float x[8];
+  load_feat<T>(src + d0, x, dpl);
+  float ss = 0.f;
+  for (int e = 0; e < dpl; ++e) ss += x[e] * x[e];
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  if ((d & 31) == 0) red[d >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-  for (int i = 0; i < hd / 32; ++i) tot += red[i];
-  const float w = is_q ? p.q_norm[d] : p.k_norm[d];
-  const float xn = round_to<T>(x / sqrtf(tot / (float)hd + p.eps) * w);
-  xs[d] = xn;
-  __syncthreads();
-  float y = xn;
-  const int half = p.rotary_dim / 2;
-  if (d < p.rotary_dim) {
-    const int i = d < half ? d : d - half;
-    // angle = pos * base^(-2i / rotary_dim), reduced modulo 2 pi in double
-    const double ang = remainder((double)pos * exp(-2.0 * i / p.rotary_dim * p.log_base), 6.283185307179586);
-    float sn, cs;
-    sincosf((float)ang, &sn, &cs);
-    y = d < half ? xn * cs - xs[d + half] * sn : xn * cs + xs[d - half] * sn;
+  const float inv = 1.f / sqrtf(ss / (float)hd + p.eps);
+  const float* wn = is_q ? p.q_norm : p.k_norm;
+  float* xr = xs[warp];
+  for (int e = 0; e < dpl; ++e) {
+    x[e] = round_to<T>(x[e] * inv * wn[d0 + e]);
+    xr[d0 + e] = x[e];
   }
-  const T yo = from_f<T>(y);
-  if (is_q)
-    static_cast<T*>(p.q_ws)[(t * p.heads + h) * hd + d] = yo;
-  else
-    static_cast<T*>(p.k_cache)[h * p.cache_sh + pos * hd + d] = yo;
+  __syncwarp();
+  const int half = p.rotary_dim / 2;
+  T* dst = is_q ? static_cast<T*>(p.q_ws) + (t * p.heads + h) * hd + d0
+                : static_cast<T*>(p.k_cache) + h * p.cache_sh + pos * hd + d0;
+  for (int e = 0; e < dpl; ++e) {
+    const int d = d0 + e;
+    float y = x[e];
+    if (d < p.rotary_dim) {
+      const int i = d < half ? d : d - half;
+      // angle = pos * base^(-2i / rotary_dim), reduced modulo 2 pi in double
+      const double ang = remainder((double)pos * p.inv_freq[i], 6.283185307179586);
+      float sn, cs;
+      sincosf((float)ang, &sn, &cs);
+      y = d < half ? x[e] * cs - xr[d + half] * sn : x[e] * cs + xr[d - half] * sn;
+    }
+    dst[e] = from_f<T>(y);
+  }
 }
 
 // ------------------------------------------------------------ attention
-// Shared memory: q rows (float32), then per warp a K tile of 32 keys in the
-// activation dtype with each row padded by 16 bytes (odd 16-byte stride: the
-// lanes' 16-byte reads of their own key rows are free of bank conflicts) and
-// the tile's probabilities; the warps' final rows reuse the K tiles.
+// Shared memory: the CTA's q rows (float32), then two buffers of a 32-key K
+// tile (activation dtype, each row padded by 16 bytes: an odd 16-byte stride
+// keeps the lanes' reads of their own key rows free of bank conflicts) and
+// of the V tile, then each warp's probabilities.
 template <typename T, int HD>
 struct AttnSmem {
   static constexpr int kVec = 16 / (int)sizeof(T);                 // elements per 16-byte vector
   static constexpr int kKRow = HD + kVec;                          // padded K row (elements)
   static constexpr size_t kQ = (size_t)kRows * HD * 4;
-  static constexpr size_t kKT = (size_t)kKeyTile * kKRow * sizeof(T);  // one warp's K tile
-  static constexpr size_t kVT = (size_t)kKeyTile * HD * sizeof(T);     // one warp's V tile
-  // V tiles through shared memory too, where they fit (not float32 at head_dim 256)
-  static constexpr bool kStageV = (size_t)kWarps * (kKT + kVT) <= 160 * 1024;
-  static constexpr size_t kK = (size_t)kWarps * (kKT + (kStageV ? kVT : 0));
-  static constexpr size_t kP = (size_t)kWarps * kRows * kKeyTile * 4;
-  static constexpr size_t kMerge = (size_t)kWarps * kRows * (HD + 2) * 4;
-  static constexpr size_t kBytes = kQ + (kK > kMerge ? kK : kMerge) + kP;
+  static constexpr size_t kKT = (size_t)kKeyTile * kKRow * sizeof(T);  // one K tile
+  static constexpr size_t kVT = (size_t)kKeyTile * HD * sizeof(T);     // one V tile
+  static constexpr size_t kP = (size_t)kRows * kKeyTile * 4;
+  static constexpr size_t kBytes = kQ + 2 * (kKT + kVT) + kP;
 };
 
 template <typename T>
@@ -163,30 +174,36 @@ __device__ __forceinline__ void load_vec(const T* src, float* dst, int n) {
   }
 }
 
+// One CTA: kRows query rows of one key/value head and one key split; the
+// four warps share each K/V tile (cp.async, double-buffered) and each owns
+// kRows / kWarps rows with its own running max and sum.
 template <typename T, int HD>
 __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams p) {
   using SM = AttnSmem<T, HD>;
-  constexpr int DPL = HD / 32;  // output features per lane (consecutive)
+  constexpr int DPL = HD / 32;            // output features per lane (consecutive)
+  constexpr int RPW = kRows / kWarps;     // query rows per warp
+  constexpr int VPR = HD / SM::kVec;      // 16-byte vectors per row
   extern __shared__ __align__(16) unsigned char smem[];
   float* qs = reinterpret_cast<float*>(smem);
-  T* kt_all = reinterpret_cast<T*>(smem + SM::kQ);
-  float* mrg = reinterpret_cast<float*>(smem + SM::kQ);  // after the key loop
-  float* ps_all = reinterpret_cast<float*>(smem + SM::kQ + (SM::kK > SM::kMerge ? SM::kK : SM::kMerge));
+  unsigned char* tiles = smem + SM::kQ;  // K[0], V[0], K[1], V[1]
+  float* ps_all = reinterpret_cast<float*>(smem + SM::kQ + 2 * (SM::kKT + SM::kVT));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hk = blockIdx.y, split = blockIdx.z;
   const int64_t rows_all = p.n_tokens * p.group;
   const int64_t r0 = (int64_t)blockIdx.x * kRows;
 
-  // this CTA's rows: (token, head) pairs of kv head hk; their causal limits
-  int64_t lim[kRows];  // keys [0, lim) are visible to the row (0: inactive row)
+  // the CTA's rows: (token, head) pairs of kv head hk, and their causal limits
   int64_t kmax = 0;
-#pragma unroll
   for (int r = 0; r < kRows; ++r) {
     const int64_t R = r0 + r;
-    lim[r] = R < rows_all ? p.offset + R / p.group + 1 : 0;
-    kmax = lim[r] > kmax ? lim[r] : kmax;
+    if (R < rows_all) kmax = max(kmax, p.offset + R / p.group + 1);
   }
-  // q rows into shared memory (float32)
+  int64_t lim[RPW];  // keys [0, lim) are visible to this warp's row i (0: inactive row)
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    const int64_t R = r0 + warp * RPW + i;
+    lim[i] = R < rows_all ? p.offset + R / p.group + 1 : 0;
+  }
   for (int i = tid; i < kRows * HD; i += kWarps * 32) {
     const int r = i / HD, d = i % HD;
     const int64_t R = r0 + r;
@@ -198,58 +215,64 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
     }
     qs[i] = v;
   }
-  __syncthreads();
 
   // this split's keys
   const int64_t per = (((p.cache_len + p.splits - 1) / p.splits) + kKeyTile - 1) / kKeyTile * kKeyTile;
   const int64_t kbeg = (int64_t)split * per;
   const int64_t kend = min(kbeg + per, kmax);
-
-  float m[kRows], lsum[kRows], o[kRows][DPL];
-#pragma unroll
-  for (int r = 0; r < kRows; ++r) {
-    m[r] = -INFINITY;
-    lsum[r] = 0.f;
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) o[r][i] = 0.f;
-  }
-  T* kt = reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(kt_all) +
-                               (size_t)warp * (SM::kKT + (SM::kStageV ? SM::kVT : 0)));
-  T* vt = reinterpret_cast<T*>(reinterpret_cast<unsigned char*>(kt) + SM::kKT);  // used when kStageV
-  float* ps = ps_all + (size_t)warp * kRows * kKeyTile;
+  const int ntiles = kend > kbeg ? (int)((kend - kbeg + kKeyTile - 1) / kKeyTile) : 0;
   const T* kc = static_cast<const T*>(p.k_cache) + hk * p.cache_sh;
   const T* vc = static_cast<const T*>(p.v_cache) + hk * p.cache_sh;
-
-  for (int64_t k0 = kbeg + (int64_t)warp * kKeyTile; k0 < kend; k0 += (int64_t)kWarps * kKeyTile) {
-    const int nvalid = (int)min((int64_t)kKeyTile, kend - k0);  // warp-uniform
-    // stage the K (and V) tile by cp.async: every copy in flight at once
-    constexpr int VPR = HD / SM::kVec;  // vectors per row
-    for (int i = lane; i < nvalid * VPR; i += 32) {
+  auto issue = [&](int tile) {
+    const int64_t k0 = kbeg + (int64_t)tile * kKeyTile;
+    const int nv = (int)min((int64_t)kKeyTile, kend - k0);
+    T* kt = reinterpret_cast<T*>(tiles + (tile & 1) * (SM::kKT + SM::kVT));
+    T* vt = reinterpret_cast<T*>(tiles + (tile & 1) * (SM::kKT + SM::kVT) + SM::kKT);
+    for (int i = tid; i < nv * VPR; i += kWarps * 32) {
       const int row = i / VPR, col = (i % VPR) * SM::kVec;
       cp_async16((uint32_t)__cvta_generic_to_shared(kt + row * SM::kKRow + col), kc + (k0 + row) * HD + col, true);
-      if constexpr (SM::kStageV)
-        cp_async16((uint32_t)__cvta_generic_to_shared(vt + row * HD + col), vc + (k0 + row) * HD + col, true);
+      cp_async16((uint32_t)__cvta_generic_to_shared(vt + row * HD + col), vc + (k0 + row) * HD + col, true);
     }
-    cp_async_commit();
-    cp_async_wait<0>();
-    __syncwarp();
-    // scores: lane = key
-    float s[kRows];
+  };
+  if (ntiles > 0) issue(0);
+  cp_async_commit();
+
+  float m[RPW], lsum[RPW], o[RPW][DPL];
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) s[r] = 0.f;
+  for (int i = 0; i < RPW; ++i) {
+    m[i] = -INFINITY;
+    lsum[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) o[i][e] = 0.f;
+  }
+  float* ps = ps_all + warp * RPW * kKeyTile;
+
+  for (int tile = 0; tile < ntiles; ++tile) {
+    if (tile + 1 < ntiles) issue(tile + 1);
+    cp_async_commit();
+    cp_async_wait<1>();  // this tile's copies (and the q rows' stores, by the barrier) are done
+    __syncthreads();
+    const int64_t k0 = kbeg + (int64_t)tile * kKeyTile;
+    const int nvalid = (int)min((int64_t)kKeyTile, kend - k0);  // uniform
+    const T* kt = reinterpret_cast<const T*>(tiles + (tile & 1) * (SM::kKT + SM::kVT));
+    const T* vt = reinterpret_cast<const T*>(tiles + (tile & 1) * (SM::kKT + SM::kVT) + SM::kKT);
+    // scores: lane = key
+    float s[RPW];
+#pragma unroll
+    for (int i = 0; i < RPW; ++i) s[i] = 0.f;
     if (lane < nvalid) {
       const T* krow = kt + lane * SM::kKRow;
-#pragma unroll 2
+#pragma unroll 4
       for (int d = 0; d < HD; d += SM::kVec) {
         float kv[SM::kVec];
         load_vec<T>(krow + d, kv, SM::kVec);
 #pragma unroll
-        for (int r = 0; r < kRows; ++r) {
-          const float4* q4 = reinterpret_cast<const float4*>(qs + r * HD + d);
+        for (int i = 0; i < RPW; ++i) {
+          const float4* q4 = reinterpret_cast<const float4*>(qs + (warp * RPW + i) * HD + d);
 #pragma unroll
           for (int e = 0; e < SM::kVec; e += 4) {
             const float4 qv = q4[e / 4];
-            s[r] = fmaf(qv.x, kv[e], fmaf(qv.y, kv[e + 1], fmaf(qv.z, kv[e + 2], fmaf(qv.w, kv[e + 3], s[r]))));
+            s[i] = fmaf(qv.x, kv[e], fmaf(qv.y, kv[e + 1], fmaf(qv.z, kv[e + 2], fmaf(qv.w, kv[e + 3], s[i]))));
           }
         }
       }
@@ -257,121 +280,143 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
     // online softmax per row
     const int64_t kpos = k0 + lane;
 #pragma unroll
-    for (int r = 0; r < kRows; ++r) {
-      const bool ok = lane < nvalid && kpos < lim[r];
-      const float sv = ok ? s[r] * p.scale : -INFINITY;
+    for (int i = 0; i < RPW; ++i) {
+      const bool ok = lane < nvalid && kpos < lim[i];
+      const float sv = ok ? s[i] * p.scale : -INFINITY;
       float tm = sv;
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
-      const float mn = fmaxf(m[r], tm);
-      const float alpha = mn == -INFINITY ? 1.f : __expf(m[r] - mn);
+      const float mn = fmaxf(m[i], tm);
+      const float alpha = mn == -INFINITY ? 1.f : __expf(m[i] - mn);
       const float pj = ok ? __expf(sv - mn) : 0.f;
-      lsum[r] = lsum[r] * alpha + pj;
+      lsum[i] = lsum[i] * alpha + pj;
 #pragma unroll
-      for (int i = 0; i < DPL; ++i) o[r][i] *= alpha;
-      m[r] = mn;
-      ps[r * kKeyTile + lane] = pj;
+      for (int e = 0; e < DPL; ++e) o[i][e] *= alpha;
+      m[i] = mn;
+      ps[i * kKeyTile + lane] = pj;
     }
     __syncwarp();
     // output: lane = features [lane * DPL, +DPL)
     for (int j = 0; j < nvalid; ++j) {
       float vv[DPL];
-      if constexpr (SM::kStageV && DPL * sizeof(T) >= 16) {
+      if constexpr (DPL * sizeof(T) >= 16) {
         load_vec<T>(vt + j * HD + lane * DPL, vv, DPL);
-      } else if constexpr (SM::kStageV) {
-#pragma unroll
-        for (int i = 0; i < DPL; ++i) vv[i] = to_f(vt[j * HD + lane * DPL + i]);
-      } else if constexpr (DPL * sizeof(T) >= 16) {
-        load_vec<T>(vc + (k0 + j) * HD + lane * DPL, vv, DPL);
       } else {
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) vv[i] = to_f(vc[(k0 + j) * HD + lane * DPL + i]);
+        for (int e = 0; e < DPL; ++e) vv[e] = to_f(vt[j * HD + lane * DPL + e]);
       }
 #pragma unroll
-      for (int r = 0; r < kRows; ++r) {
-        const float pr = ps[r * kKeyTile + j];
+      for (int i = 0; i < RPW; ++i) {
+        const float pr = ps[i * kKeyTile + j];
 #pragma unroll
-        for (int i = 0; i < DPL; ++i) o[r][i] = fmaf(pr, vv[i], o[r][i]);
+        for (int e = 0; e < DPL; ++e) o[i][e] = fmaf(pr, vv[e], o[i][e]);
       }
     }
-    __syncwarp();
+    __syncthreads();  // every warp is done with this buffer before it is refilled
   }
+  cp_async_wait<0>();
 
-  // merge the warps: row sums over lanes, then (max, sum, output) per warp
+  // this warp's rows: the sum over lanes, then the output or the partial row
 #pragma unroll
-  for (int r = 0; r < kRows; ++r)
+  for (int i = 0; i < RPW; ++i) {
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) lsum[r] += __shfl_xor_sync(0xffffffffu, lsum[r], off);
-  __syncthreads();  // every warp is done with its K tile
-#pragma unroll
-  for (int r = 0; r < kRows; ++r) {
-    float* mr = mrg + ((size_t)warp * kRows + r) * (HD + 2);
-#pragma unroll
-    for (int i = 0; i < DPL; ++i) mr[lane * DPL + i] = o[r][i];
-    if (lane == 0) {
-      mr[HD] = m[r];
-      mr[HD + 1] = lsum[r];
-    }
-  }
-  __syncthreads();
-  for (int i = tid; i < kRows * HD; i += kWarps * 32) {
-    const int r = i / HD, d = i % HD;
-    const int64_t R = r0 + r;
+    for (int off = 16; off >= 1; off >>= 1) lsum[i] += __shfl_xor_sync(0xffffffffu, lsum[i], off);
+    const int64_t R = r0 + warp * RPW + i;
     if (R >= rows_all) continue;
-    float mm = -INFINITY;
-    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, mrg[((size_t)w * kRows + r) * (HD + 2) + HD]);
-    float acc = 0.f, l = 0.f;
-    if (mm != -INFINITY)
-      for (int w = 0; w < kWarps; ++w) {
-        const float* mr = mrg + ((size_t)w * kRows + r) * (HD + 2);
-        const float sc = __expf(mr[HD] - mm);
-        acc += sc * mr[d];
-        l += sc * mr[HD + 1];
-      }
     const int64_t t = R / p.group;
     const int h = hk * p.group + (int)(R % p.group);
     const int64_t row = t * p.heads + h;
     if (p.splits == 1) {
       const T* gate = static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * HD + HD;
-      const float att = round_to<T>(acc / l);
-      const float gt = round_to<T>(sigmoid_f(to_f(gate[d])));
-      static_cast<T*>(p.out)[t * p.out_st + (int64_t)h * HD + d] = from_f<T>(att * gt);
+      T* dst = static_cast<T*>(p.out) + t * p.out_st + (int64_t)h * HD;
+      const float inv = 1.f / lsum[i];
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) {
+        const int d = lane * DPL + e;
+        const float att = round_to<T>(o[i][e] * inv);
+        const float gt = round_to<T>(sigmoid_f(to_f(gate[d])));
+        dst[d] = from_f<T>(att * gt);
+      }
     } else {
-      float* pr = p.part + ((size_t)split * p.n_tokens * p.heads + row) * (HD + 2);
-      pr[d] = acc;
-      if (d == 0) {
-        pr[HD] = mm;
-        pr[HD + 1] = l;
+      float* pr = p.part + ((size_t)split * p.n_tokens * p.heads + row) * (HD + 4);
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) pr[lane * DPL + e] = o[i][e];
+      if (lane == 0) {
+        pr[HD] = m[i];
+        pr[HD + 1] = lsum[i];
       }
     }
   }
 }
 
 // Adds the splits' partial rows: out = sum_s e^(m_s - m) o_s / sum_s e^(m_s - m) l_s.
+// One CTA per output row (token, head): warp 0 turns the splits' maxima and
+// sums into weights in shared memory; the four warps then take every fourth
+// split, each lane a run of head_dim / 32 features (16-byte loads, all of a
+// warp's loads in flight), and their sums meet in shared memory.
+constexpr int kMaxSplits = 160;
+
 template <typename T>
-__global__ void attn_combine_kernel(const AttnParams p) {
-  const int hd = p.head_dim;
-  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  const int64_t rows = p.n_tokens * p.heads;
-  if (i >= rows * hd) return;
-  const int64_t row = i / hd;
-  const int d = (int)(i % hd);
-  const size_t stride = (size_t)rows * (hd + 2);
-  float mm = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) mm = fmaxf(mm, p.part[s * stride + row * (hd + 2) + hd]);
-  float acc = 0.f, l = 0.f;
-  for (int s = 0; s < p.splits; ++s) {
-    const float* pr = p.part + s * stride + row * (hd + 2);
-    const float sc = pr[hd] == -INFINITY ? 0.f : __expf(pr[hd] - mm);
-    acc += sc * pr[d];
-    l += sc * pr[hd + 1];
+__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
+  __shared__ float wsplit[kMaxSplits];
+  __shared__ float inv_l;
+  __shared__ __align__(16) float red[4][kMaxHeadDim];
+  const int hd = p.head_dim, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t row = blockIdx.x;  // t * heads + h
+  const size_t stride = (size_t)p.n_tokens * p.heads * (hd + 4);
+  const float* base = p.part + row * (hd + 4);
+  if (warp == 0) {
+    float mm = -INFINITY;
+    for (int s = lane; s < p.splits; s += 32) mm = fmaxf(mm, base[s * stride + hd]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
+    float l = 0.f;
+    for (int s = lane; s < p.splits; s += 32) {
+      const float ms = base[s * stride + hd];
+      const float w = ms == -INFINITY ? 0.f : __expf(ms - mm);
+      wsplit[s] = w;
+      l += w * base[s * stride + hd + 1];
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    if (lane == 0) inv_l = 1.f / l;
   }
+  __syncthreads();
+  const int dpl = hd / 32;  // 1, 2, 4 or 8 features per lane
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int s = warp; s < p.splits; s += 4) {
+    const float w = wsplit[s];
+    const float* src = base + s * stride + lane * dpl;
+    if (dpl >= 4) {
+      const float4 a = reinterpret_cast<const float4*>(src)[0];
+      acc[0] = fmaf(w, a.x, acc[0]);
+      acc[1] = fmaf(w, a.y, acc[1]);
+      acc[2] = fmaf(w, a.z, acc[2]);
+      acc[3] = fmaf(w, a.w, acc[3]);
+      if (dpl == 8) {
+        const float4 b = reinterpret_cast<const float4*>(src)[1];
+        acc[4] = fmaf(w, b.x, acc[4]);
+        acc[5] = fmaf(w, b.y, acc[5]);
+        acc[6] = fmaf(w, b.z, acc[6]);
+        acc[7] = fmaf(w, b.w, acc[7]);
+      }
+    } else {
+      for (int e = 0; e < dpl; ++e) acc[e] = fmaf(w, src[e], acc[e]);
+    }
+  }
+  for (int e = 0; e < dpl; ++e) red[warp][lane * dpl + e] = acc[e];
+  __syncthreads();
   const int64_t t = row / p.heads;
   const int h = (int)(row % p.heads);
   const T* gate = static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * hd + hd;
-  const float att = round_to<T>(acc / l);
-  const float gt = round_to<T>(sigmoid_f(to_f(gate[d])));
-  static_cast<T*>(p.out)[t * p.out_st + (int64_t)h * hd + d] = from_f<T>(att * gt);
+  T* dst = static_cast<T*>(p.out) + t * p.out_st + (int64_t)h * hd;
+  for (int d = tid; d < hd; d += 128) {
+    const float sum = red[0][d] + red[1][d] + red[2][d] + red[3][d];
+    const float att = round_to<T>(sum * inv_l);
+    const float gt = round_to<T>(sigmoid_f(to_f(gate[d])));
+    dst[d] = from_f<T>(att * gt);
+  }
 }
 
 // ------------------------------------------------- prefill, tensor cores
@@ -649,7 +694,8 @@ gdn_status attn_setup(const gdn_attn_args* a, AttnParams* p, size_t* ws_bytes) {
   p->group = a->heads / a->kv_heads;
   p->eps = a->eps;
   p->scale = a->scale;
-  p->log_base = std::log((double)a->rope_base);
+  for (int i = 0; i < a->rotary_dim / 2; ++i)
+    p->inv_freq[i] = std::exp(-2.0 * i / a->rotary_dim * std::log((double)a->rope_base));
   p->qg = a->qg;
   p->qg_st = a->qg_stride_t;
   p->k_new = a->k_new;
@@ -668,9 +714,9 @@ gdn_status attn_setup(const gdn_attn_args* a, AttnParams* p, size_t* ws_bytes) {
   int64_t splits = 1;
   if (row_ctas > 0 && row_ctas < 2 * 148) {
     splits = (2 * 148 + row_ctas - 1) / row_ctas;
-    const int64_t max_by_keys = (a->cache_len + kWarps * kKeyTile - 1) / (kWarps * kKeyTile);
+    const int64_t max_by_keys = (a->cache_len + 2 * kKeyTile - 1) / (2 * kKeyTile);  // two tiles a split at least
     if (splits > max_by_keys) splits = max_by_keys;
-    if (splits > 64) splits = 64;
+    if (splits > kMaxSplits) splits = kMaxSplits;
     if (splits < 1) splits = 1;
   }
   // bf16 prefill with head_dim >= 64 runs the tensor-core kernel, one key split
@@ -678,7 +724,7 @@ gdn_status attn_setup(const gdn_attn_args* a, AttnParams* p, size_t* ws_bytes) {
   p->splits = (int)splits;
   const size_t q_bytes = align256((size_t)a->n_tokens * a->heads * a->head_dim * es);
   const size_t part_bytes =
-      splits > 1 ? align256((size_t)splits * a->n_tokens * a->heads * (a->head_dim + 2) * 4) : 0;
+      splits > 1 ? align256((size_t)splits * a->n_tokens * a->heads * (a->head_dim + 4) * 4) : 0;
   *ws_bytes = q_bytes + part_bytes;
   return GDN_OK;
 }
@@ -705,19 +751,19 @@ extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream)
   p.q_ws = ws;
   p.part = reinterpret_cast<float*>(ws + gdn::align256((size_t)a->n_tokens * a->heads * a->head_dim * es));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const dim3 pgrid((unsigned)a->n_tokens, (unsigned)(a->heads + 2 * a->kv_heads));
+  const int64_t prep_items = a->n_tokens * (a->heads + 2 * a->kv_heads);
+  const dim3 pgrid((unsigned)((prep_items + gdn::kPrepWarps - 1) / gdn::kPrepWarps));
   const int64_t row_blocks = (a->n_tokens * p.group + gdn::kRows - 1) / gdn::kRows;
   if (row_blocks > 0x7fffffffLL) return gdn::set_error(GDN_EUNSUPPORTED, "too many rows for one call");
   const dim3 fgrid((unsigned)row_blocks, (unsigned)a->kv_heads, (unsigned)p.splits);
   if (a->act_dtype == GDN_F32) {
-    gdn::attn_prep_kernel<float><<<pgrid, a->head_dim, 0, s>>>(p);
+    gdn::attn_prep_kernel<float><<<pgrid, gdn::kPrepWarps * 32, 0, s>>>(p);
     st = gdn::launch_fwd_hd<float>(p, fgrid, s);
     if (st == GDN_OK && p.splits > 1) {
-      const int64_t n = a->n_tokens * a->heads * a->head_dim;
-      gdn::attn_combine_kernel<float><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p);
+      gdn::attn_combine_kernel<float><<<(unsigned)(a->n_tokens * a->heads), 128, 0, s>>>(p);
     }
   } else {
-    gdn::attn_prep_kernel<__nv_bfloat16><<<pgrid, a->head_dim, 0, s>>>(p);
+    gdn::attn_prep_kernel<__nv_bfloat16><<<pgrid, gdn::kPrepWarps * 32, 0, s>>>(p);
     if (p.splits == 1 && a->head_dim >= 64) {  // prefill: the tensor-core kernel
       switch (a->head_dim) {
         case 64: st = gdn::launch_mma<64>(p, s); break;
@@ -728,8 +774,7 @@ extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream)
       st = gdn::launch_fwd_hd<__nv_bfloat16>(p, fgrid, s);
     }
     if (st == GDN_OK && p.splits > 1) {
-      const int64_t n = a->n_tokens * a->heads * a->head_dim;
-      gdn::attn_combine_kernel<__nv_bfloat16><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p);
+      gdn::attn_combine_kernel<__nv_bfloat16><<<(unsigned)(a->n_tokens * a->heads), 128, 0, s>>>(p);
     }
   }
   if (st != GDN_OK) return st;
