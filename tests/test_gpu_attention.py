@@ -140,3 +140,51 @@ def test_attention_bf16_tensor_core_prefill(heads, kv_heads, head_dim, rotary):
         want, keys, values = O.attention_layer(x, w, keys, values, heads, kv_heads, head_dim, rotary, 1000000.0,
                                                1e-6, rnd=O.bf16_round)
         assert O.rel_l2(n(got), want) < 1e-2, (L, O.rel_l2(n(got), want))
+
+
+def _quantized(w):
+    """The reference test's construction (tests/test_qwen3_5_attention.py:64-71):
+    4-bit, group 64 projections and the dequantized dense copy."""
+    from gdn_b200 import QuantScheme
+
+    q, d = {}, {}
+    for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
+        words, s, b = O.quantize_affine(w[name], 4, 64)
+        q[name] = {"weight": torch.from_numpy(words.view(np.int32)).to(dev()), "scales": t(s, torch.bfloat16),
+                   "biases": t(b, torch.bfloat16)}
+        d[name] = O.dequant_affine(words, s, b, 4, 64)
+    return q, d, QuantScheme(bits=4, group_size=64)
+
+
+def test_quantized_attention_equals_dense_on_dequantized_weights():
+    torch.backends.cuda.matmul.allow_tf32 = False
+    w = attn_case(0)
+    q, d, quant = _quantized(w)
+    qlayer = Qwen3_5Attention(SMALL, ATTN["eps"], q["q_proj"], t(w["q_norm"]), q["k_proj"], t(w["k_norm"]),
+                              q["v_proj"], q["o_proj"], quant=quant)
+    dlayer = _layer({**w, **d})
+    cq, cd = _cache(), _cache()
+    rng = np.random.default_rng(5)
+    for L in (6, 1, 3):
+        x = t(rng.standard_normal((L, ATTN["hidden"])).astype(np.float32))
+        torch.testing.assert_close(qlayer(x if L > 1 else x[0], cq), dlayer(x if L > 1 else x[0], cd),
+                                   rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(cq.state()[0], cd.state()[0], rtol=1e-5, atol=1e-6)
+
+
+def test_quantized_attention_bf16_model_shape():
+    shape = AttentionShape(16, 2, 256, 64, 10000000.0)
+    rng = np.random.default_rng(17)
+    w = _random_weights(rng, shape, 2048, 0.02)
+    q, d, quant = _quantized(w)
+    layer = Qwen3_5Attention(shape, 1e-6, q["q_proj"], t(w["q_norm"]), q["k_proj"], t(w["k_norm"]), q["v_proj"],
+                             q["o_proj"], quant=quant)
+    cache = _cache(shape, max_context=512, dtype=torch.bfloat16)
+    keys, values = np.zeros((2, 0, 256)), np.zeros((2, 0, 256))
+    dw = {**w, **d}
+    for L in (200, 1):  # the GEMM and tensor-core prefill, then the GEMV and split-key decode
+        x = O.bf16_round(rng.standard_normal((L, 2048)).astype(np.float32))
+        got = layer(t(x, torch.bfloat16), cache)
+        want, keys, values = O.attention_layer(x, dw, keys, values, 16, 2, 256, 64, 10000000.0, 1e-6,
+                                               rnd=O.bf16_round)
+        assert O.rel_l2(n(got), want) < 1e-2, (L, O.rel_l2(n(got), want))
