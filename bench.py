@@ -8,7 +8,7 @@ one decode launch over the batch; ``value`` is the state HBM traffic
 prefill number of config 3 (T=8192) under ``"prefill"``.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|varlen|qproj] [--tokens M]
+                    [--workload decode|varlen|qproj|attn] [--tokens M]
 
 ``--workload varlen`` is config 5 instead: 64 packed sequences (lengths
 ``default_rng(1).integers(256, 16384, 64, endpoint=True)``, 516,496 tokens)
@@ -18,7 +18,9 @@ prefill rate in tokens/s over all ranks (strong scaling: the total is fixed),
 and the decode phase is reported beside it.
 
 ``--workload qproj`` times only the 4-bit quantized in-projection (12,352 x
-2,048) at ``--tokens`` rows, for profiling the projection kernels.  The
+2,048) at ``--tokens`` rows, ``--workload attn`` only the attention core
+(prefill of ``--tokens`` tokens, or one decode token against 4,096 cached
+positions with ``--tokens 1``), for profiling those kernels.  The
 default line also carries ``"layer"``: config 4 from hidden states in to
 hidden states out, with 4-bit affine projections around the fused block.
 
@@ -430,6 +432,50 @@ def measure_attention(device, iters=3):
             "decode_us": dec_ms * 1e3, "decode_kv_gbs": kv_bytes / (dec_ms / 1e3) / 1e9}
 
 
+def run_attn(args):
+    """Only the softmax-attention core at the model's attention shape (16
+    query heads over 2 key/value heads of 256, rotary 64, bf16): with
+    ``--tokens`` L > 1 a prefill of L tokens from an empty cache per step,
+    with L = 1 one decode token against 4,096 cached positions per step; for
+    profiling the attention kernels on their own."""
+    import gdn_b200
+    from gdn_b200 import AttentionShape, GrowingKVCache
+
+    device = torch.device("cuda", 0)
+    shape = AttentionShape(16, 2, 256, 64, 10000000.0)
+    L = max(args.tokens, 4096)
+    gen = torch.Generator(device).manual_seed(7)
+    qg = torch.randn(L, 16 * 512, device=device, generator=gen).bfloat16()
+    k = torch.randn(L, 2 * 256, device=device, generator=gen).bfloat16()
+    v = torch.randn(L, 2 * 256, device=device, generator=gen).bfloat16()
+    qn = torch.ones(256, device=device)
+    cache = GrowingKVCache(L + 64, 2, 256, dtype=torch.bfloat16, device=device)
+    n = args.tokens
+    if n == 1:
+        gdn_b200.attention_core(qg[:4096], k[:4096], v[:4096], qn, qn, shape, 1e-6, cache)
+
+    def step():
+        cache.commit(4096 if n == 1 else 0)
+        gdn_b200.attention_core(qg[:n], k[:n], v[:n], qn, qn, shape, 1e-6, cache)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    flop = 4 * 256 * 16 * (n * 4096 if n == 1 else n * (n + 1) / 2)
+    print(json.dumps({"metric": "attention core TFLOP/s", "value": flop / (ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                      "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                      "config": {"workload": (f"prefill {n} tokens" if n > 1 else "decode, 4,096 cached") +
+                                 ", 16/2 heads of 256, rotary 64, bf16"},
+                      "dtype": "bf16", "data": "synthetic"}), flush=True)
+
+
 def run_qproj(args):
     """Only the quantized in-projection (12,352 x 2,048, 4-bit, group 64) at
     ``--tokens`` rows: the GEMV up to 16 tokens, the tiled GEMM beyond; for
@@ -582,16 +628,17 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="decode only: no e2e, prefill or CPU legs (for profiler runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiler runs)")
-    ap.add_argument("--workload", choices=["decode", "varlen", "qproj"], default="decode")
-    ap.add_argument("--tokens", type=int, default=4096, help="rows of x for --workload qproj")
+    ap.add_argument("--workload", choices=["decode", "varlen", "qproj", "attn"], default="decode")
+    ap.add_argument("--tokens", type=int, default=4096, help="rows of x for --workload qproj / attn")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.workload == "qproj":
+    if args.workload in ("qproj", "attn"):
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the reference's quantized matmul is MLX's "
-                              "(mx.quantized_matmul), not installable on this box"}), flush=True)
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's quantized matmul and attention "
+                              "are MLX's (mx.quantized_matmul, mx.fast.scaled_dot_product_attention), not "
+                              "installable on this box"}), flush=True)
             return
-        return run_qproj(args)
+        return run_qproj(args) if args.workload == "qproj" else run_attn(args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)

@@ -421,7 +421,8 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
 
 // ------------------------------------------------- prefill, tensor cores
 // bf16 prefill on mma.sync m16n8k16 (bf16 x bf16 -> float32), FA2-style: one
-// CTA per (64 queries, query head), four warps of 16 query rows.  K and V
+// CTA per (128 queries, query head), eight warps of 16 query rows sharing
+// each K/V tile.  K and V
 // tiles of 64 keys (the key/value head of the group) pass through shared
 // memory by cp.async, double-buffered; each 16-byte chunk of a row sits at
 // chunk ^ (row & 7) so that ldmatrix reads are free of bank conflicts.
@@ -430,7 +431,8 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
 // fragments; P goes from the S accumulators straight into A fragments;
 // O += P V: B fragments of V by ldmatrix.trans.  The causal mask applies on
 // the tiles that cross the diagonal.
-constexpr int kMQ = 64;   // queries per CTA
+constexpr int kMQ = 128;  // queries per CTA: eight warps of 16 rows
+constexpr int kMmaThreads = 256;
 constexpr int kMK = 64;   // keys per tile
 
 template <int HD>
@@ -464,7 +466,7 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
 }
 
 template <int HD>
-__global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(kMmaThreads, 1) attn_mma_kernel(const AttnParams p) {
   using SM = MmaSmem<HD>;
   constexpr int NT = HD / 8;      // output n-tiles of 8 features
   constexpr int KC = HD / 8;      // 16-byte chunks per row
@@ -484,7 +486,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
   const int ntiles = (int)((kneed + kMK - 1) / kMK);
 
   // Q tile (rows past n_tokens zero-filled)
-  for (int i = tid; i < kMQ * KC; i += 128) {
+  for (int i = tid; i < kMQ * KC; i += kMmaThreads) {
     const int r = i / KC, c = (i % KC) * 8;
     const int64_t t = q0 + r;
     const bool ok = t < p.n_tokens;
@@ -492,7 +494,7 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const AttnParams p) {
   }
   auto load_kv = [&](int tile, int buf) {
     const int64_t k0 = (int64_t)tile * kMK;
-    for (int i = tid; i < kMK * KC; i += 128) {
+    for (int i = tid; i < kMK * KC; i += kMmaThreads) {
       const int r = i / KC, c = (i % KC) * 8;
       const int64_t kp = k0 + r;
       const bool ok = kp < kneed;
@@ -633,7 +635,7 @@ gdn_status launch_mma(const AttnParams& p, cudaStream_t s) {
     attr = true;
   }
   const dim3 grid((unsigned)((p.n_tokens + kMQ - 1) / kMQ), (unsigned)p.heads);
-  attn_mma_kernel<HD><<<grid, 128, smem, s>>>(p);
+  attn_mma_kernel<HD><<<grid, kMmaThreads, smem, s>>>(p);
   return GDN_OK;
 }
 
