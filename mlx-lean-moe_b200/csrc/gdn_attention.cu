@@ -16,8 +16,8 @@
 //                      their accuracy.
 // attn_fwd_kernel      flash-style attention on the CUDA cores in float32:
 //                      one CTA per (kRows query rows of one key/value head,
-//                      key split); its four warps share each 32-key K/V tile
-//                      (cp.async, double-buffered) and own two rows each, with
+//                      key split); its eight warps share each 32-key K/V tile
+//                      (cp.async, double-buffered) and own one row each, with
 //                      their own running max and sum (lane = key for the
 //                      scores, lane = features for the output).  One split finishes the
 //                      rows (normalization, gate, output); several write
@@ -37,7 +37,7 @@ namespace gdn {
 namespace {
 
 constexpr int kRows = 8;        // query rows (token x head) per CTA
-constexpr int kWarps = 4;
+constexpr int kWarps = 8;      // one query row each
 constexpr int kKeyTile = 32;    // keys per warp step
 constexpr int kMaxHeadDim = 256;
 
