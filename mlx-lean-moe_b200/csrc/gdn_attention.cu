@@ -7,7 +7,7 @@
 // attention with the causal mask aligned to the newest query, and the
 // output gate sigmoid(gate) carried in q_proj's second half.
 //
-// attn_prep_kernel     one warp per (token, row of q / k / v heads): the
+// attn_prep_kernel     one CTA per token, a warp per row of q / k / v heads: the
 //                      norms and the rotation in float32, rounded to the
 //                      activation dtype where the reference materializes
 //                      arrays; q to the workspace, k and v into the cache.
@@ -25,10 +25,16 @@
 // attn_combine_kernel  adds up, then gates and writes.
 // attn_mma_kernel      bf16 prefill (calls with enough rows for one key
 //                      split) on the tensor cores: see its comment below.
+//
+// The attention and combine kernels are launched as programmatic dependents
+// of the kernel before them: they start while it finishes, and the
+// attention kernel fetches keys cached by earlier calls before it waits for
+// the prep kernel's output.
 #include <cuda_bf16.h>
 
 #include <cmath>
 #include <cstring>
+#include <type_traits>
 
 #include "gdn_api.h"
 #include "gdn_common.cuh"
@@ -72,68 +78,168 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// ------------------------------------------------------------------ prep
-// One warp per (token, head row): rows [0, heads) are queries, then the
-// kv_heads keys, then the kv_heads values; each lane holds head_dim / 32
-// consecutive features.  The norm reduces by shuffles; the rotation reads its
-// partner features from the warp's row in shared memory.
-constexpr int kPrepWarps = 8;
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while the kernel before it on the
+// stream is still running; griddep_wait() then blocks until that kernel has
+// completed and its memory writes are visible.  Without the attribute (or
+// with nothing before it) the wait returns at once.  griddep_launch_dependents()
+// lets the next such kernel start launching before this one ends.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-template <typename T>
-__device__ __forceinline__ void load_feat(const T* src, float (&x)[8], int dpl) {
-  for (int e = 0; e < dpl; ++e) x[e] = to_f(src[e]);
+// ------------------------------------------------------------------ prep
+// One CTA per token.  Its threads first compute the token's (cos, sin) per
+// rotary frequency into shared memory (once for all of its heads); then each
+// warp takes head rows of the token: rows [0, heads) are queries, then the
+// kv_heads keys, then the kv_heads values, each lane holding head_dim / 32
+// consecutive features.  The norm reduces by shuffles; the rotation reads its
+// partner features from the warp's row in shared memory.  A warp's first
+// row is loaded before the angles are computed.  VEC: every row start is
+// aligned to its lane's run of features (up to 16 bytes), so each lane moves
+// its run in vector accesses.
+constexpr int kPrepMaxWarps = 32;
+
+template <int B>
+struct VecOf;
+template <>
+struct VecOf<16> { using type = uint4; };
+template <>
+struct VecOf<8> { using type = uint2; };
+template <>
+struct VecOf<4> { using type = uint32_t; };
+template <>
+struct VecOf<2> { using type = uint16_t; };
+
+// N consecutive elements of T (vector accesses of up to 16 bytes when VEC).
+template <typename T, int N, bool VEC>
+__device__ __forceinline__ void ld_run(const T* src, float (&x)[N]) {
+  alignas(16) T v[N];
+  if constexpr (VEC) {
+    constexpr int B = N * (int)sizeof(T), W = B >= 16 ? 16 : B;
+    using V = typename VecOf<W>::type;
+#pragma unroll
+    for (int i = 0; i < B / W; ++i) reinterpret_cast<V*>(v)[i] = reinterpret_cast<const V*>(src)[i];
+  } else {
+#pragma unroll
+    for (int e = 0; e < N; ++e) v[e] = src[e];
+  }
+#pragma unroll
+  for (int e = 0; e < N; ++e) x[e] = to_f(v[e]);
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kPrepWarps * 32) attn_prep_kernel(const AttnParams p) {
-  __shared__ float xs[kPrepWarps][kMaxHeadDim];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows = p.heads + 2 * p.kv_heads;
-  const int64_t item = (int64_t)blockIdx.x * kPrepWarps + warp;
-  if (item >= p.n_tokens * rows) return;  // the whole warp
-  const int64_t t = item / rows;
-  const int row = (int)(item % rows);
-  const int hd = p.head_dim, dpl = hd / 32, d0 = lane * dpl;
-  const bool is_q = row < p.heads, is_k = !is_q && row < p.heads + p.kv_heads;
-  const int h = is_q ? row : is_k ? row - p.heads : row - p.heads - p.kv_heads;
-  const int64_t pos = p.offset + t;
-  if (!is_q && !is_k) {  // v: a copy into the cache
-    const T* src = static_cast<const T*>(p.v_new) + t * p.v_st + (int64_t)h * hd + d0;
-    T* dst = static_cast<T*>(p.v_cache) + h * p.cache_sh + pos * hd + d0;
-    for (int e = 0; e < dpl; ++e) dst[e] = src[e];
-    return;
-  }
-  const T* src = is_q ? static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * hd
-                      : static_cast<const T*>(p.k_new) + t * p.k_st + (int64_t)h * hd;
-  float x[8];
-  load_feat<T>(src + d0, x, dpl);
-  float ss = 0.f;
-  for (int e = 0; e < dpl; ++e) ss += x[e] * x[e];
+template <typename T, int N, bool VEC>
+__device__ __forceinline__ void st_run(T* dst, const float (&x)[N]) {
+  alignas(16) T v[N];
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && N % 2 == 0) {
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = 1.f / sqrtf(ss / (float)hd + p.eps);
-  const float* wn = is_q ? p.q_norm : p.k_norm;
-  float* xr = xs[warp];
-  for (int e = 0; e < dpl; ++e) {
-    x[e] = round_to<T>(x[e] * inv * wn[d0 + e]);
-    xr[d0 + e] = x[e];
+    for (int e = 0; e < N; e += 2) *reinterpret_cast<uint32_t*>(&v[e]) = cvt_bf16x2(x[e], x[e + 1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < N; ++e) v[e] = from_f<T>(x[e]);
   }
-  __syncwarp();
-  const int half = p.rotary_dim / 2;
-  T* dst = is_q ? static_cast<T*>(p.q_ws) + (t * p.heads + h) * hd + d0
-                : static_cast<T*>(p.k_cache) + h * p.cache_sh + pos * hd + d0;
-  for (int e = 0; e < dpl; ++e) {
-    const int d = d0 + e;
-    float y = x[e];
-    if (d < p.rotary_dim) {
-      const int i = d < half ? d : d - half;
-      // angle = pos * base^(-2i / rotary_dim), reduced modulo 2 pi in double
-      const double ang = remainder((double)pos * p.inv_freq[i], 6.283185307179586);
-      float sn, cs;
-      sincosf((float)ang, &sn, &cs);
-      y = d < half ? x[e] * cs - xr[d + half] * sn : x[e] * cs + xr[d - half] * sn;
+  if constexpr (VEC) {
+    constexpr int B = N * (int)sizeof(T), W = B >= 16 ? 16 : B;
+    using V = typename VecOf<W>::type;
+#pragma unroll
+    for (int i = 0; i < B / W; ++i) reinterpret_cast<V*>(dst)[i] = reinterpret_cast<const V*>(v)[i];
+  } else {
+#pragma unroll
+    for (int e = 0; e < N; ++e) dst[e] = v[e];
+  }
+}
+
+// Rounds N floats to the precision of T (in pairs for bf16).
+template <typename T, int N>
+__device__ __forceinline__ void round_run(float (&x)[N]) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && N % 2 == 0) {
+#pragma unroll
+    for (int e = 0; e < N; e += 2) round2_bf16(x[e], x[e + 1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < N; ++e) x[e] = round_to<T>(x[e]);
+  }
+}
+
+// The rotation angle pos * f reduced to about [-pi, pi] in double: k = the
+// integer nearest ang / (2 pi), then ang - k * 2 pi with 2 pi split in two
+// doubles (C1 = 2 pi rounded to double, C2 = 2 pi - C1), each product taken
+// inside one fused multiply-add (Cody and Waite's additive range reduction).
+__device__ __forceinline__ float rope_angle(int64_t pos, double f) {
+  const double ang = (double)pos * f;
+  const double k = rint(ang * 0.15915494309189535);
+  double r = fma(-k, 6.283185307179586, ang);
+  r = fma(-k, 2.4492935982947064e-16, r);
+  return (float)r;
+}
+
+template <typename T, int HD, bool VEC>
+__global__ void __launch_bounds__(kPrepMaxWarps * 32) attn_prep_kernel(const AttnParams p) {
+  constexpr int DPL = HD / 32;
+  __shared__ float xs[kPrepMaxWarps][HD];
+  __shared__ float2 rot[HD / 2];  // (cos, sin) of this token's angle per frequency
+  griddep_launch_dependents();    // the attention kernel waits for this grid before it reads q or the new keys
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int64_t t = blockIdx.x;
+  const int64_t pos = p.offset + t;
+  const int rows = p.heads + 2 * p.kv_heads, half = p.rotary_dim / 2, d0 = lane * DPL;
+  // row r of this token: its source and the norm weights (queries, keys) or nothing (values)
+  auto load = [&](int r, float (&x)[DPL], float (&w)[DPL]) {
+    if (r < p.heads) {
+      ld_run<T, DPL, VEC>(static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)r * 2 * HD + d0, x);
+      ld_run<float, DPL, VEC>(p.q_norm + d0, w);
+    } else if (r < p.heads + p.kv_heads) {
+      ld_run<T, DPL, VEC>(static_cast<const T*>(p.k_new) + t * p.k_st + (int64_t)(r - p.heads) * HD + d0, x);
+      ld_run<float, DPL, VEC>(p.k_norm + d0, w);
+    } else {
+      ld_run<T, DPL, VEC>(
+          static_cast<const T*>(p.v_new) + t * p.v_st + (int64_t)(r - p.heads - p.kv_heads) * HD + d0, x);
     }
-    dst[e] = from_f<T>(y);
+  };
+  float x[DPL], w[DPL];
+  int row = warp;
+  if (row < rows) load(row, x, w);  // in flight while the angles are computed
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    float sn, cs;
+    sincosf(rope_angle(pos, p.inv_freq[i]), &sn, &cs);
+    rot[i] = make_float2(cs, sn);
+  }
+  __syncthreads();
+  float* xr = xs[warp];
+  while (row < rows) {
+    if (row >= p.heads + p.kv_heads) {  // v: a copy into the cache
+      st_run<T, DPL, VEC>(
+          static_cast<T*>(p.v_cache) + (row - p.heads - p.kv_heads) * p.cache_sh + pos * HD + d0, x);
+    } else {
+      const bool is_q = row < p.heads;
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) ss += x[e] * x[e];
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = 1.f / sqrtf(ss / (float)HD + p.eps);
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) x[e] = x[e] * inv * w[e];
+      round_run<T, DPL>(x);
+      __syncwarp();  // the previous row's partner reads are done
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) xr[d0 + e] = x[e];
+      __syncwarp();
+      float y[DPL];
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) {
+        const int d = d0 + e;
+        y[e] = x[e];
+        if (d < p.rotary_dim) {
+          const float2 cs = rot[d < half ? d : d - half];
+          y[e] = d < half ? x[e] * cs.x - xr[d + half] * cs.y : x[e] * cs.x + xr[d - half] * cs.y;
+        }
+      }
+      T* dst = is_q ? static_cast<T*>(p.q_ws) + (t * p.heads + row) * HD + d0
+                    : static_cast<T*>(p.k_cache) + (row - p.heads) * p.cache_sh + pos * HD + d0;
+      st_run<T, DPL, VEC>(dst, y);
+    }
+    row += nwarps;
+    if (row < rows) load(row, x, w);
   }
 }
 
@@ -175,8 +281,11 @@ __device__ __forceinline__ void load_vec(const T* src, float* dst, int n) {
 }
 
 // One CTA: kRows query rows of one key/value head and one key split; the
-// four warps share each K/V tile (cp.async, double-buffered) and each owns
-// kRows / kWarps rows with its own running max and sum.
+// eight warps share each K/V tile (cp.async, double-buffered, rows past the
+// split's end zero-filled) and each owns kRows / kWarps rows with its own
+// running max and sum.  Launched as a programmatic dependent of the prep
+// kernel: the first tile, when it holds only keys cached by earlier calls, is
+// requested before the wait for the prep kernel's q rows and new keys.
 template <typename T, int HD>
 __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams p) {
   using SM = AttnSmem<T, HD>;
@@ -187,33 +296,25 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
   float* qs = reinterpret_cast<float*>(smem);
   unsigned char* tiles = smem + SM::kQ;  // K[0], V[0], K[1], V[1]
   float* ps_all = reinterpret_cast<float*>(smem + SM::kQ + 2 * (SM::kKT + SM::kVT));
+  griddep_launch_dependents();  // the combine kernel waits for this grid before it reads the partial rows
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int hk = blockIdx.y, split = blockIdx.z;
   const int64_t rows_all = p.n_tokens * p.group;
   const int64_t r0 = (int64_t)blockIdx.x * kRows;
-
-  // the CTA's rows: (token, head) pairs of kv head hk, and their causal limits
-  int64_t kmax = 0;
-  for (int r = 0; r < kRows; ++r) {
-    const int64_t R = r0 + r;
-    if (R < rows_all) kmax = max(kmax, p.offset + R / p.group + 1);
-  }
-  int64_t lim[RPW];  // keys [0, lim) are visible to this warp's row i (0: inactive row)
+  // rows run in token order, so the CTA's last row has the furthest causal limit
+  const int64_t kmax = p.offset + (min(r0 + kRows, rows_all) - 1) / p.group + 1;
+  int64_t lim[RPW];   // keys [0, lim) are visible to this warp's row i (0: inactive row)
+  int64_t qrow[RPW];  // the row's element offset in q_ws (-1: inactive)
 #pragma unroll
   for (int i = 0; i < RPW; ++i) {
     const int64_t R = r0 + warp * RPW + i;
-    lim[i] = R < rows_all ? p.offset + R / p.group + 1 : 0;
-  }
-  for (int i = tid; i < kRows * HD; i += kWarps * 32) {
-    const int r = i / HD, d = i % HD;
-    const int64_t R = r0 + r;
-    float v = 0.f;
+    lim[i] = 0;
+    qrow[i] = -1;
     if (R < rows_all) {
       const int64_t t = R / p.group;
-      const int h = hk * p.group + (int)(R % p.group);
-      v = to_f(static_cast<const T*>(p.q_ws)[(t * p.heads + h) * HD + d]);
+      lim[i] = p.offset + t + 1;
+      qrow[i] = (t * p.heads + hk * p.group + (R - t * p.group)) * HD;
     }
-    qs[i] = v;
   }
 
   // this split's keys
@@ -228,13 +329,29 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
     const int nv = (int)min((int64_t)kKeyTile, kend - k0);
     T* kt = reinterpret_cast<T*>(tiles + (tile & 1) * (SM::kKT + SM::kVT));
     T* vt = reinterpret_cast<T*>(tiles + (tile & 1) * (SM::kKT + SM::kVT) + SM::kKT);
-    for (int i = tid; i < nv * VPR; i += kWarps * 32) {
+    for (int i = tid; i < kKeyTile * VPR; i += kWarps * 32) {
       const int row = i / VPR, col = (i % VPR) * SM::kVec;
-      cp_async16((uint32_t)__cvta_generic_to_shared(kt + row * SM::kKRow + col), kc + (k0 + row) * HD + col, true);
-      cp_async16((uint32_t)__cvta_generic_to_shared(vt + row * HD + col), vc + (k0 + row) * HD + col, true);
+      const bool ok = row < nv;  // rows past the split's end are zero-filled
+      const int64_t src = (k0 + (ok ? row : 0)) * HD + col;
+      cp_async16((uint32_t)__cvta_generic_to_shared(kt + row * SM::kKRow + col), kc + src, ok);
+      cp_async16((uint32_t)__cvta_generic_to_shared(vt + row * HD + col), vc + src, ok);
     }
   };
-  if (ntiles > 0) issue(0);
+  const bool early = ntiles > 0 && kbeg + kKeyTile <= p.offset;  // tile 0 holds earlier calls' keys only
+  if (early) issue(0);
+  griddep_wait();
+#pragma unroll
+  for (int i = 0; i < RPW; ++i) {
+    float qv[DPL];
+    if (qrow[i] >= 0) {
+      ld_run<T, DPL, true>(static_cast<const T*>(p.q_ws) + qrow[i] + lane * DPL, qv);
+    } else {
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) qv[e] = 0.f;
+    }
+    st_run<float, DPL, true>(qs + (warp * RPW + i) * HD + lane * DPL, qv);
+  }
+  if (ntiles > 0 && !early) issue(0);
   cp_async_commit();
 
   float m[RPW], lsum[RPW], o[RPW][DPL];
@@ -256,24 +373,25 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
     const int nvalid = (int)min((int64_t)kKeyTile, kend - k0);  // uniform
     const T* kt = reinterpret_cast<const T*>(tiles + (tile & 1) * (SM::kKT + SM::kVT));
     const T* vt = reinterpret_cast<const T*>(tiles + (tile & 1) * (SM::kKT + SM::kVT) + SM::kKT);
-    // scores: lane = key
-    float s[RPW];
+    // scores: lane = key, four partial sums per row
+    float acc[RPW][4];
 #pragma unroll
-    for (int i = 0; i < RPW; ++i) s[i] = 0.f;
-    if (lane < nvalid) {
-      const T* krow = kt + lane * SM::kKRow;
+    for (int i = 0; i < RPW; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    const T* krow = kt + lane * SM::kKRow;
 #pragma unroll 4
-      for (int d = 0; d < HD; d += SM::kVec) {
-        float kv[SM::kVec];
-        load_vec<T>(krow + d, kv, SM::kVec);
+    for (int d = 0; d < HD; d += SM::kVec) {
+      float kv[SM::kVec];
+      load_vec<T>(krow + d, kv, SM::kVec);
 #pragma unroll
-        for (int i = 0; i < RPW; ++i) {
-          const float4* q4 = reinterpret_cast<const float4*>(qs + (warp * RPW + i) * HD + d);
+      for (int i = 0; i < RPW; ++i) {
+        const float4* q4 = reinterpret_cast<const float4*>(qs + (warp * RPW + i) * HD + d);
 #pragma unroll
-          for (int e = 0; e < SM::kVec; e += 4) {
-            const float4 qv = q4[e / 4];
-            s[i] = fmaf(qv.x, kv[e], fmaf(qv.y, kv[e + 1], fmaf(qv.z, kv[e + 2], fmaf(qv.w, kv[e + 3], s[i]))));
-          }
+        for (int e = 0; e < SM::kVec; e += 4) {
+          const float4 qv = q4[e / 4];
+          acc[i][0] = fmaf(qv.x, kv[e], acc[i][0]);
+          acc[i][1] = fmaf(qv.y, kv[e + 1], acc[i][1]);
+          acc[i][2] = fmaf(qv.z, kv[e + 2], acc[i][2]);
+          acc[i][3] = fmaf(qv.w, kv[e + 3], acc[i][3]);
         }
       }
     }
@@ -282,7 +400,7 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
 #pragma unroll
     for (int i = 0; i < RPW; ++i) {
       const bool ok = lane < nvalid && kpos < lim[i];
-      const float sv = ok ? s[i] * p.scale : -INFINITY;
+      const float sv = ok ? ((acc[i][0] + acc[i][1]) + (acc[i][2] + acc[i][3])) * p.scale : -INFINITY;
       float tm = sv;
 #pragma unroll
       for (int off = 16; off >= 1; off >>= 1) tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, off));
@@ -296,8 +414,9 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
       ps[i * kKeyTile + lane] = pj;
     }
     __syncwarp();
-    // output: lane = features [lane * DPL, +DPL)
-    for (int j = 0; j < nvalid; ++j) {
+    // output: lane = features [lane * DPL, +DPL); keys past nvalid have p = 0 and zero rows
+#pragma unroll 8
+    for (int j = 0; j < kKeyTile; ++j) {
       float vv[DPL];
       if constexpr (DPL * sizeof(T) >= 16) {
         load_vec<T>(vt + j * HD + lane * DPL, vv, DPL);
@@ -321,11 +440,10 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
   for (int i = 0; i < RPW; ++i) {
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) lsum[i] += __shfl_xor_sync(0xffffffffu, lsum[i], off);
-    const int64_t R = r0 + warp * RPW + i;
-    if (R >= rows_all) continue;
-    const int64_t t = R / p.group;
-    const int h = hk * p.group + (int)(R % p.group);
-    const int64_t row = t * p.heads + h;
+    if (qrow[i] < 0) continue;
+    const int64_t row = qrow[i] / HD;  // t * heads + h
+    const int64_t t = row / p.heads;
+    const int h = (int)(row - t * p.heads);
     if (p.splits == 1) {
       const T* gate = static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * HD + HD;
       T* dst = static_cast<T*>(p.out) + t * p.out_st + (int64_t)h * HD;
@@ -339,8 +457,7 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
       }
     } else {
       float* pr = p.part + ((size_t)split * p.n_tokens * p.heads + row) * (HD + 4);
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) pr[lane * DPL + e] = o[i][e];
+      st_run<float, DPL, true>(pr + lane * DPL, o[i]);
       if (lane == 0) {
         pr[HD] = m[i];
         pr[HD + 1] = lsum[i];
@@ -350,73 +467,79 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_kernel(const AttnParams 
 }
 
 // Adds the splits' partial rows: out = sum_s e^(m_s - m) o_s / sum_s e^(m_s - m) l_s.
-// One CTA per output row (token, head): warp 0 turns the splits' maxima and
-// sums into weights in shared memory; the four warps then take every fourth
-// split, each lane a run of head_dim / 32 features (16-byte loads, all of a
-// warp's loads in flight), and their sums meet in shared memory.
+// One CTA per (output row, 64 features), launched as a programmatic dependent
+// of the attention kernel: warp w takes splits w, w + 8, ... with all of its
+// loads issued at once (two features per lane), weights them by its own
+// largest max, and the eight warps' sums meet in shared memory.
 constexpr int kMaxSplits = 160;
+constexpr int kCombWarps = 8;
+constexpr int kCombFeat = 64;
 
 template <typename T>
-__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
-  __shared__ float wsplit[kMaxSplits];
-  __shared__ float inv_l;
-  __shared__ __align__(16) float red[4][kMaxHeadDim];
-  const int hd = p.head_dim, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+__global__ void __launch_bounds__(kCombWarps * 32) attn_combine_kernel(const AttnParams p) {
+  constexpr int kPer = kMaxSplits / kCombWarps;
+  __shared__ float wm[kCombWarps], wl[kCombWarps];
+  __shared__ float2 wacc[kCombWarps][32];
+  griddep_wait();
+  const int hd = p.head_dim, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = blockIdx.x;  // t * heads + h
+  const int f = blockIdx.y * kCombFeat + 2 * lane;
+  const bool fok = f < hd;
   const size_t stride = (size_t)p.n_tokens * p.heads * (hd + 4);
   const float* base = p.part + row * (hd + 4);
-  if (warp == 0) {
-    float mm = -INFINITY;
-    for (int s = lane; s < p.splits; s += 32) mm = fmaxf(mm, base[s * stride + hd]);
+  float ms[kPer], ls[kPer];
+  float2 os[kPer];
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
-    float l = 0.f;
-    for (int s = lane; s < p.splits; s += 32) {
-      const float ms = base[s * stride + hd];
-      const float w = ms == -INFINITY ? 0.f : __expf(ms - mm);
-      wsplit[s] = w;
-      l += w * base[s * stride + hd + 1];
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-    if (lane == 0) inv_l = 1.f / l;
-  }
-  __syncthreads();
-  const int dpl = hd / 32;  // 1, 2, 4 or 8 features per lane
-  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-  for (int s = warp; s < p.splits; s += 4) {
-    const float w = wsplit[s];
-    const float* src = base + s * stride + lane * dpl;
-    if (dpl >= 4) {
-      const float4 a = reinterpret_cast<const float4*>(src)[0];
-      acc[0] = fmaf(w, a.x, acc[0]);
-      acc[1] = fmaf(w, a.y, acc[1]);
-      acc[2] = fmaf(w, a.z, acc[2]);
-      acc[3] = fmaf(w, a.w, acc[3]);
-      if (dpl == 8) {
-        const float4 b = reinterpret_cast<const float4*>(src)[1];
-        acc[4] = fmaf(w, b.x, acc[4]);
-        acc[5] = fmaf(w, b.y, acc[5]);
-        acc[6] = fmaf(w, b.z, acc[6]);
-        acc[7] = fmaf(w, b.w, acc[7]);
-      }
-    } else {
-      for (int e = 0; e < dpl; ++e) acc[e] = fmaf(w, src[e], acc[e]);
+  for (int j = 0; j < kPer; ++j) {
+    const int s = warp + j * kCombWarps;
+    ms[j] = -INFINITY;
+    ls[j] = 0.f;
+    os[j] = make_float2(0.f, 0.f);
+    if (s < p.splits) {
+      const float* src = base + s * stride;
+      ms[j] = src[hd];
+      ls[j] = src[hd + 1];
+      if (fok) os[j] = *reinterpret_cast<const float2*>(src + f);
     }
   }
-  for (int e = 0; e < dpl; ++e) red[warp][lane * dpl + e] = acc[e];
+  float mw = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) mw = fmaxf(mw, ms[j]);
+  float lw = 0.f, ax = 0.f, ay = 0.f;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const float w = ms[j] == -INFINITY ? 0.f : __expf(ms[j] - mw);
+    lw = fmaf(w, ls[j], lw);
+    ax = fmaf(w, os[j].x, ax);
+    ay = fmaf(w, os[j].y, ay);
+  }
+  if (lane == 0) {
+    wm[warp] = mw;
+    wl[warp] = lw;
+  }
+  wacc[warp][lane] = make_float2(ax, ay);
   __syncthreads();
+  if (warp != 0 || !fok) return;
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kCombWarps; ++w) M = fmaxf(M, wm[w]);
+  float L = 0.f, X = 0.f, Y = 0.f;
+#pragma unroll
+  for (int w = 0; w < kCombWarps; ++w) {
+    const float c = wm[w] == -INFINITY ? 0.f : __expf(wm[w] - M);
+    L = fmaf(c, wl[w], L);
+    X = fmaf(c, wacc[w][lane].x, X);
+    Y = fmaf(c, wacc[w][lane].y, Y);
+  }
+  const float inv = 1.f / L;
   const int64_t t = row / p.heads;
-  const int h = (int)(row % p.heads);
+  const int h = (int)(row - t * p.heads);
   const T* gate = static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)h * 2 * hd + hd;
   T* dst = static_cast<T*>(p.out) + t * p.out_st + (int64_t)h * hd;
-  for (int d = tid; d < hd; d += 128) {
-    const float sum = red[0][d] + red[1][d] + red[2][d] + red[3][d];
-    const float att = round_to<T>(sum * inv_l);
-    const float gt = round_to<T>(sigmoid_f(to_f(gate[d])));
-    dst[d] = from_f<T>(att * gt);
-  }
+  const float a0 = round_to<T>(X * inv), a1 = round_to<T>(Y * inv);
+  const float g0 = round_to<T>(sigmoid_f(to_f(gate[f]))), g1 = round_to<T>(sigmoid_f(to_f(gate[f + 1])));
+  dst[f] = from_f<T>(a0 * g0);
+  dst[f + 1] = from_f<T>(a1 * g1);
 }
 
 // ------------------------------------------------- prefill, tensor cores
@@ -475,8 +598,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_mma_kernel(const AttnPara
   const uint32_t sQ = sbase, sK0 = sbase + SM::kQ, sV0 = sK0 + 2 * SM::kTile;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  const int h = blockIdx.y, hk = h / p.group;
-  const int64_t q0 = (int64_t)blockIdx.x * kMQ;  // first query (token index of this call)
+  // query tiles in reverse order: the tiles with the most keys (the last
+  // queries) start first and the short ones fill the tail of the grid
+  const int h = blockIdx.x, hk = h / p.group;
+  const int64_t q0 = (int64_t)(gridDim.y - 1 - blockIdx.y) * kMQ;  // first query (token index of this call)
   const __nv_bfloat16* qw = static_cast<const __nv_bfloat16*>(p.q_ws);
   const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(p.k_cache) + hk * p.cache_sh;
   const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(p.v_cache) + hk * p.cache_sh;
@@ -634,8 +759,56 @@ gdn_status launch_mma(const AttnParams& p, cudaStream_t s) {
       return set_error(GDN_ECUDA, "attention: shared-memory attribute");
     attr = true;
   }
-  const dim3 grid((unsigned)((p.n_tokens + kMQ - 1) / kMQ), (unsigned)p.heads);
+  const int64_t qtiles = (p.n_tokens + kMQ - 1) / kMQ;
+  if (qtiles > 65535) return set_error(GDN_EUNSUPPORTED, "attention: at most %d tokens per call", 65535 * kMQ);
+  const dim3 grid((unsigned)p.heads, (unsigned)qtiles);
   attn_mma_kernel<HD><<<grid, kMmaThreads, smem, s>>>(p);
+  return GDN_OK;
+}
+
+// Launches kernel as a programmatic dependent of the kernel before it on the
+// stream (it may start while that one runs and calls griddep_wait() before
+// reading its results).
+cudaError_t launch_dependent(void (*kernel)(AttnParams), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             const AttnParams& p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+template <typename T, int HD>
+void launch_prep(const AttnParams& p, bool vec, dim3 grid, cudaStream_t s) {
+  const int rows = p.heads + 2 * p.kv_heads;
+  const int threads = 32 * (rows < kPrepMaxWarps ? rows : kPrepMaxWarps);
+  if (vec)
+    attn_prep_kernel<T, HD, true><<<grid, threads, 0, s>>>(p);
+  else
+    attn_prep_kernel<T, HD, false><<<grid, threads, 0, s>>>(p);
+}
+
+template <typename T>
+void launch_prep_hd(const AttnParams& p, bool vec, dim3 grid, cudaStream_t s) {
+  switch (p.head_dim) {
+    case 32: return launch_prep<T, 32>(p, vec, grid, s);
+    case 64: return launch_prep<T, 64>(p, vec, grid, s);
+    case 128: return launch_prep<T, 128>(p, vec, grid, s);
+    default: return launch_prep<T, 256>(p, vec, grid, s);
+  }
+}
+
+template <typename T>
+gdn_status launch_combine(const AttnParams& p, cudaStream_t s) {
+  const dim3 grid((unsigned)(p.n_tokens * p.heads), (unsigned)((p.head_dim + kCombFeat - 1) / kCombFeat));
+  const cudaError_t e = launch_dependent(attn_combine_kernel<T>, grid, dim3(kCombWarps * 32), 0, s, p);
+  if (e != cudaSuccess) return set_error(GDN_ECUDA, "attention combine launch: %s", cudaGetErrorString(e));
   return GDN_OK;
 }
 
@@ -649,7 +822,8 @@ gdn_status launch_fwd(const AttnParams& p, dim3 grid, cudaStream_t s) {
       return set_error(GDN_ECUDA, "attention: shared-memory attribute");
     attr = true;
   }
-  attn_fwd_kernel<T, HD><<<grid, kWarps * 32, smem, s>>>(p);
+  const cudaError_t e = launch_dependent(attn_fwd_kernel<T, HD>, grid, dim3(kWarps * 32), smem, s, p);
+  if (e != cudaSuccess) return set_error(GDN_ECUDA, "attention launch: %s", cudaGetErrorString(e));
   return GDN_OK;
 }
 
@@ -716,7 +890,7 @@ gdn_status attn_setup(const gdn_attn_args* a, AttnParams* p, size_t* ws_bytes) {
   int64_t splits = 1;
   if (row_ctas > 0 && row_ctas < 2 * 148) {
     splits = (2 * 148 + row_ctas - 1) / row_ctas;
-    const int64_t max_by_keys = (a->cache_len + 2 * kKeyTile - 1) / (2 * kKeyTile);  // two tiles a split at least
+    const int64_t max_by_keys = (a->cache_len + kKeyTile - 1) / kKeyTile;  // one tile a split at least
     if (splits > max_by_keys) splits = max_by_keys;
     if (splits > kMaxSplits) splits = kMaxSplits;
     if (splits < 1) splits = 1;
@@ -748,24 +922,30 @@ extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream)
   if (a->n_tokens == 0) return GDN_OK;
   if (!a->workspace || a->workspace_bytes < need)
     return gdn::set_error(GDN_EINVAL, "workspace too small: %zu bytes needed", need);
+  if (reinterpret_cast<uintptr_t>(a->workspace) & 15u) return gdn::set_error(GDN_EINVAL, "the workspace must be 16-byte aligned");
   const size_t es = a->act_dtype == GDN_F32 ? 4 : 2;
   unsigned char* ws = static_cast<unsigned char*>(a->workspace);
   p.q_ws = ws;
   p.part = reinterpret_cast<float*>(ws + gdn::align256((size_t)a->n_tokens * a->heads * a->head_dim * es));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int64_t prep_items = a->n_tokens * (a->heads + 2 * a->kv_heads);
-  const dim3 pgrid((unsigned)((prep_items + gdn::kPrepWarps - 1) / gdn::kPrepWarps));
+  // vector accesses in the prep kernel when every row start is aligned to a lane's run of features
+  const size_t run = (size_t)(a->head_dim / 32) * es, run_t = run < 16 ? run : 16;
+  const size_t run_f = (size_t)(a->head_dim / 32) * 4 < 16 ? (size_t)(a->head_dim / 32) * 4 : 16;
+  auto al = [](const void* ptr, size_t n) { return reinterpret_cast<uintptr_t>(ptr) % n == 0; };
+  const bool vec = al(a->qg, run_t) && al(a->k_new, run_t) && al(a->v_new, run_t) &&
+                   (a->qg_stride_t * (int64_t)es) % (int64_t)run_t == 0 &&
+                   (a->k_stride_t * (int64_t)es) % (int64_t)run_t == 0 &&
+                   (a->v_stride_t * (int64_t)es) % (int64_t)run_t == 0 && al(a->q_norm, run_f) && al(a->k_norm, run_f);
+  const dim3 pgrid((unsigned)a->n_tokens);  // one CTA per token
   const int64_t row_blocks = (a->n_tokens * p.group + gdn::kRows - 1) / gdn::kRows;
   if (row_blocks > 0x7fffffffLL) return gdn::set_error(GDN_EUNSUPPORTED, "too many rows for one call");
   const dim3 fgrid((unsigned)row_blocks, (unsigned)a->kv_heads, (unsigned)p.splits);
   if (a->act_dtype == GDN_F32) {
-    gdn::attn_prep_kernel<float><<<pgrid, gdn::kPrepWarps * 32, 0, s>>>(p);
+    gdn::launch_prep_hd<float>(p, vec, pgrid, s);
     st = gdn::launch_fwd_hd<float>(p, fgrid, s);
-    if (st == GDN_OK && p.splits > 1) {
-      gdn::attn_combine_kernel<float><<<(unsigned)(a->n_tokens * a->heads), 128, 0, s>>>(p);
-    }
+    if (st == GDN_OK && p.splits > 1) st = gdn::launch_combine<float>(p, s);
   } else {
-    gdn::attn_prep_kernel<__nv_bfloat16><<<pgrid, gdn::kPrepWarps * 32, 0, s>>>(p);
+    gdn::launch_prep_hd<__nv_bfloat16>(p, vec, pgrid, s);
     if (p.splits == 1 && a->head_dim >= 64) {  // prefill: the tensor-core kernel
       switch (a->head_dim) {
         case 64: st = gdn::launch_mma<64>(p, s); break;
@@ -775,9 +955,7 @@ extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream)
     } else {
       st = gdn::launch_fwd_hd<__nv_bfloat16>(p, fgrid, s);
     }
-    if (st == GDN_OK && p.splits > 1) {
-      gdn::attn_combine_kernel<__nv_bfloat16><<<(unsigned)(a->n_tokens * a->heads), 128, 0, s>>>(p);
-    }
+    if (st == GDN_OK && p.splits > 1) st = gdn::launch_combine<__nv_bfloat16>(p, s);
   }
   if (st != GDN_OK) return st;
   const cudaError_t e = cudaGetLastError();
