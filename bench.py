@@ -426,10 +426,35 @@ def measure_attention(device, iters=3):
     torch.cuda.synchronize()
     dec_ms = timed(graph.replay) / 20
     del graph
+
+    # the whole layer at one decode token: the fused 4-bit q|gate|k|v GEMV,
+    # the core, the 4-bit o_proj GEMV (hidden 2,048, group 64)
+    from gdn_b200 import LinearWeights, QuantScheme, Qwen3_5Attention
+
+    q4 = QuantScheme(bits=4, group_size=64)
+    qw = lambda rows, cols: LinearWeights(quantized_weights(device, rows, cols, gen), q4)
+    layer = Qwen3_5Attention(shape, 1e-6, qw(16 * 512, HIDDEN), qn, qw(2 * 256, HIDDEN), qn, qw(2 * 256, HIDDEN),
+                             qw(HIDDEN, 16 * 256))
+    x1 = torch.randn(HIDDEN, device=device, generator=gen).bfloat16()
+    cache.commit(L)
+    layer(x1, cache)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        cache.commit(L)
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(20):
+                layer(x1, cache)
+                cache.commit(L)
+    torch.cuda.synchronize()
+    layer_ms = timed(graph.replay) / 20
+    del graph
     flop = 4 * 256 * 16 * L * (L + 1) / 2
     kv_bytes = 2 * 2 * (L + 1) * 256 * 2
     return {"prefill_ms": pre_ms, "prefill_tflops": flop / (pre_ms / 1e3) / 1e12,
-            "decode_us": dec_ms * 1e3, "decode_kv_gbs": kv_bytes / (dec_ms / 1e3) / 1e9}
+            "decode_us": dec_ms * 1e3, "decode_kv_gbs": kv_bytes / (dec_ms / 1e3) / 1e9,
+            "layer_decode_us": layer_ms * 1e3}
 
 
 def run_attn(args):
@@ -807,9 +832,12 @@ def main():
         line["attention"] = {
             "prefill_ms": att["prefill_ms"], "prefill_tflops": att["prefill_tflops"],
             "decode_us": att["decode_us"], "decode_kv_gbs": att["decode_kv_gbs"],
+            "layer_decode_us": att["layer_decode_us"],
             "config": "softmax-attention core (norms, rotary, cache append, grouped-query causal attention, "
                       "gate) at 16/2 heads of 256, rotary 64, bf16: 4,096-token prefill; one decode token "
-                      "against 4,096 cached positions (CUDA-core flash-style kernel)"}
+                      "against 4,096 cached positions (CUDA-core flash-style kernel), timed as a CUDA-graph "
+                      "replay with the cache resident in L2; layer_decode_us: the whole layer at that "
+                      "token (hidden 2,048: fused 4-bit q|gate|k|v GEMV, the core, 4-bit o_proj GEMV)"}
         lay = measure_layer(device)
         line["layer"] = {
             "value": lay["tokens"] / (lay["ms"] / 1e3), "unit": "tok/s", "ms": lay["ms"],

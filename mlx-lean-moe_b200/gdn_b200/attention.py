@@ -19,7 +19,7 @@ import torch
 
 from . import _lib
 from .gated_delta import _DTYPES, _require_cuda, _stream
-from .quantized import QuantScheme, as_linear, quantized_linear
+from .quantized import LinearWeights, QuantScheme, as_linear, concat_rows, quantized_linear
 
 
 class GrowingKVCache:
@@ -154,15 +154,25 @@ class Qwen3_5Attention:
         self.q_proj, self.k_proj = as_linear(q_proj, quant), as_linear(k_proj, quant)
         self.v_proj, self.o_proj = as_linear(v_proj, quant), as_linear(o_proj, quant)
         self.q_norm, self.k_norm = q_norm, k_norm
+        # One product gives q|gate, k and v when the three share a storage
+        # scheme (one GEMV per decode step instead of three).
+        parts = (self.q_proj, self.k_proj, self.v_proj)
+        self.qkv_proj: LinearWeights | None = concat_rows(list(parts)) if len({p.quant for p in parts}) == 1 else None
 
     def __call__(self, x: torch.Tensor, cache: GrowingKVCache) -> torch.Tensor:
         if x.ndim not in (1, 2):
             raise ValueError(f"Qwen3_5Attention expects 1-D or 2-D x, got shape {tuple(x.shape)}")
         squeeze = x.ndim == 1
         rows = x[None, :] if squeeze else x
-        qg = quantized_linear(rows, self.q_proj)
-        k = quantized_linear(rows, self.k_proj)
-        v = quantized_linear(rows, self.v_proj)
+        if self.qkv_proj is not None:
+            qkv = quantized_linear(rows, self.qkv_proj)
+            s = self.shape
+            nq, nkv = s.num_attention_heads * 2 * s.head_dim, s.num_key_value_heads * s.head_dim
+            qg, k, v = qkv[:, :nq], qkv[:, nq:nq + nkv], qkv[:, nq + nkv:]
+        else:
+            qg = quantized_linear(rows, self.q_proj)
+            k = quantized_linear(rows, self.k_proj)
+            v = quantized_linear(rows, self.v_proj)
         out = attention_core(qg, k, v, self.q_norm, self.k_norm, self.shape, self.eps, cache)
         out = quantized_linear(out, self.o_proj)
         return out[0] if squeeze else out

@@ -188,3 +188,40 @@ def test_quantized_attention_bf16_model_shape():
         want, keys, values = O.attention_layer(x, dw, keys, values, 16, 2, 256, 64, 10000000.0, 1e-6,
                                                rnd=O.bf16_round)
         assert O.rel_l2(n(got), want) < 1e-2, (L, O.rel_l2(n(got), want))
+
+
+def test_decode_captured_in_a_cuda_graph_equals_the_eager_call():
+    # the attention and combine kernels are launched as programmatic
+    # dependents of the kernel before them; a captured replay must give the
+    # eager call's bits
+    shape = AttentionShape(16, 2, 256, 64, 10000000.0)
+    rng = np.random.default_rng(23)
+    L = 300
+    bf = lambda *s: t(O.bf16_round(rng.standard_normal(s).astype(np.float32)), torch.bfloat16)
+    qg, k, v = bf(L, 16 * 512), bf(L, 512), bf(L, 512)
+    qn = t((1 + 0.1 * rng.standard_normal(256)).astype(np.float32))
+    kn = t((1 + 0.1 * rng.standard_normal(256)).astype(np.float32))
+
+    def filled():
+        cache = GrowingKVCache(L + 8, 2, 256, dtype=torch.bfloat16, device=dev())
+        gdn_b200.attention_core(qg[:L - 1], k[:L - 1], v[:L - 1], qn, kn, shape, 1e-6, cache)
+        return cache
+
+    want = gdn_b200.attention_core(qg[L - 1:], k[L - 1:], v[L - 1:], qn, kn, shape, 1e-6, filled())
+    cache = filled()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev())
+    side.wait_stream(torch.cuda.current_stream(dev()))
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            got = gdn_b200.attention_core(qg[L - 1:], k[L - 1:], v[L - 1:], qn, kn, shape, 1e-6, cache)
+    torch.cuda.current_stream(dev()).wait_stream(side)
+    for _ in range(2):  # the replay rewrites the same cache position
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(got, want)
+    keys, _ = cache.state()
+    assert cache.size == L and torch.isfinite(keys.float()).all()
+    del graph
+    gdn_b200.check_device_errors()

@@ -65,3 +65,19 @@ def test_decode_plan_rejects_cpu_tensors():
     x = torch.zeros(2, 1, 8)
     with pytest.raises(ValueError, match="CUDA"):
         gdn_b200.DecodePlan(x, x, x, torch.zeros(2, 1), torch.zeros(2, 1), torch.zeros(2, 1, 8, 8))
+
+
+def test_attention_layer_fuses_projections_sharing_a_storage_scheme():
+    from gdn_b200 import AttentionShape, QuantScheme, Qwen3_5Attention
+
+    shape = AttentionShape(4, 2, 32, 16, 10000.0)
+    dense = lambda o, i: torch.randn(o, i)
+    layer = Qwen3_5Attention(shape, 1e-6, dense(256, 64), torch.ones(32), dense(64, 64), torch.ones(32),
+                             dense(64, 64), dense(64, 128))
+    assert layer.qkv_proj is not None and layer.qkv_proj.tensors.shape == (384, 64)
+    torch.testing.assert_close(layer.qkv_proj.tensors[256:320], layer.k_proj.tensors)
+    q4 = QuantScheme(bits=4, group_size=64)
+    quantized_k = {"weight": torch.zeros(64, 8, dtype=torch.int32), "scales": torch.ones(64, 1).bfloat16()}
+    mixed = Qwen3_5Attention(shape, 1e-6, dense(256, 64), torch.ones(32), gdn_b200.LinearWeights(quantized_k, q4),
+                             torch.ones(32), dense(64, 64), dense(64, 128))
+    assert mixed.qkv_proj is None  # one projection stored differently: three products
