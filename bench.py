@@ -410,7 +410,8 @@ def measure_attention(device, iters=3):
 
     # decode as a CUDA-graph replay (device time; the Python call alone costs
     # more than the three launches): the same position every time, 4,096
-    # cached keys and values
+    # cached keys and values.  Thread-local capture: under torchrun the
+    # process-group watchdog thread queries events while this thread captures.
     cache.commit(L)
     gdn_b200.attention_core(qg[:1], k[:1], v[:1], qn, qn, shape, 1e-6, cache)
     torch.cuda.synchronize()
@@ -419,7 +420,7 @@ def measure_attention(device, iters=3):
     side.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(side):
         cache.commit(L)
-        with torch.cuda.graph(graph, stream=side):
+        with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
             for _ in range(20):
                 gdn_b200.attention_core(qg[:1], k[:1], v[:1], qn, qn, shape, 1e-6, cache)
                 cache.commit(L)
@@ -443,7 +444,7 @@ def measure_attention(device, iters=3):
     side.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(side):
         cache.commit(L)
-        with torch.cuda.graph(graph, stream=side):
+        with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
             for _ in range(20):
                 layer(x1, cache)
                 cache.commit(L)
