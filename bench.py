@@ -369,6 +369,51 @@ def measure_layer(device, iters=3):
             "ms": sum(med), "gemm_flop": gemm_flop}
 
 
+def measure_layer_decode(device, iters=3):
+    """The linear-attention layer (Qwen3_5LinearAttention, the model's shape:
+    16/32 heads of 128, hidden 2,048, 4-bit group-64 projections) at one
+    decode token with its RecurrentCache, as a CUDA-graph replay: the fused
+    in-projection GEMV, the fused block on one token, the out_proj GEMV."""
+    import gdn_b200
+    from gdn_b200 import LinearWeights, QuantScheme
+    from gdn_b200.linear_attention import LinearAttentionShape
+
+    shape = LinearAttentionShape(HK, HV, D, D, 4)
+    q4 = QuantScheme(bits=4, group_size=64)
+    gen = torch.Generator(device).manual_seed(8)
+    qw = lambda rows, cols: LinearWeights(quantized_weights(device, rows, cols, gen), q4)
+    layer = gdn_b200.Qwen3_5LinearAttention(
+        shape, 1e-6, qw(shape.conv_dim, HIDDEN), qw(shape.value_dim, HIDDEN), qw(HV, HIDDEN), qw(HV, HIDDEN),
+        torch.randn(shape.conv_dim, 4, 1, device=device, generator=gen) * 0.1,
+        torch.rand(HV, device=device, generator=gen) * 1.5, torch.randn(HV, device=device, generator=gen) * 0.1,
+        torch.ones(D, device=device), qw(HIDDEN, shape.value_dim))
+    cache = gdn_b200.RecurrentCache(4, shape.conv_dim, HV, D, D, device=device)
+    x1 = torch.randn(HIDDEN, device=device, generator=gen).bfloat16()
+    layer(x1, cache)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side, capture_error_mode="thread_local"):
+            for _ in range(20):
+                layer(x1, cache)
+    torch.cuda.synchronize()
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ms = []
+    for _ in range(iters):
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms.append(e0.elapsed_time(e1) / 20)
+    del graph
+    return statistics.median(ms) * 1e3
+
+
 def measure_attention(device, iters=3):
     """The softmax-attention core at the model's attention shape (16 query
     heads over 2 key/value heads of 256, rotary 64, bf16): a 4,096-token
@@ -844,9 +889,12 @@ def main():
             "value": lay["tokens"] / (lay["ms"] / 1e3), "unit": "tok/s", "ms": lay["ms"],
             "in_proj_ms": lay["in_proj_ms"], "block_ms": lay["block_ms"], "out_proj_ms": lay["out_proj_ms"],
             "projection_tflops": lay["gemm_flop"] / ((lay["in_proj_ms"] + lay["out_proj_ms"]) / 1e3) / 1e12,
+            "decode_us": measure_layer_decode(device),
             "config": "config 4 as a whole layer: hidden states B=8 x T=4096 x 2048 bf16 in and out; in_proj "
                       "(q|k|v|z|b|a, 12,352 x 2,048) and out_proj (2,048 x 4,096) 4-bit affine, group 64 "
-                      "(tcgen05 GEMM with on-the-fly dequantization); the fused block between them"}
+                      "(tcgen05 GEMM with on-the-fly dequantization); the fused block between them; "
+                      "decode_us: the same layer (Qwen3_5LinearAttention with a RecurrentCache) at one "
+                      "decode token, device time of a CUDA-graph replay"}
 
         # --- CPU baseline (rank 0, N=1 only) --------------------------------
         if rank == 0 and world == 1 and not args.no_cpu_baseline:

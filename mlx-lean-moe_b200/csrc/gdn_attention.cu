@@ -78,15 +78,6 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Programmatic dependent launch.  A kernel launched with the programmatic
-// stream-serialization attribute may start while the kernel before it on the
-// stream is still running; griddep_wait() then blocks until that kernel has
-// completed and its memory writes are visible.  Without the attribute (or
-// with nothing before it) the wait returns at once.  griddep_launch_dependents()
-// lets the next such kernel start launching before this one ends.
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
-
 // ------------------------------------------------------------------ prep
 // One CTA per token.  Its threads first compute the token's (cos, sin) per
 // rotary frequency into shared memory (once for all of its heads); then each
@@ -766,24 +757,6 @@ gdn_status launch_mma(const AttnParams& p, cudaStream_t s) {
   return GDN_OK;
 }
 
-// Launches kernel as a programmatic dependent of the kernel before it on the
-// stream (it may start while that one runs and calls griddep_wait() before
-// reading its results).
-cudaError_t launch_dependent(void (*kernel)(AttnParams), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                             const AttnParams& p) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, p);
-}
-
 template <typename T, int HD>
 void launch_prep(const AttnParams& p, bool vec, dim3 grid, cudaStream_t s) {
   const int rows = p.heads + 2 * p.kv_heads;
@@ -945,6 +918,9 @@ extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream)
     st = gdn::launch_fwd_hd<float>(p, fgrid, s);
     if (st == GDN_OK && p.splits > 1) st = gdn::launch_combine<float>(p, s);
   } else {
+    // a plain launch: the attention kernel, its dependent, reads keys cached
+    // by earlier calls before it waits, which is safe only when everything
+    // before the prep kernel has completed once it starts
     gdn::launch_prep_hd<__nv_bfloat16>(p, vec, pgrid, s);
     if (p.splits == 1 && a->head_dim >= 64) {  // prefill: the tensor-core kernel
       switch (a->head_dim) {

@@ -79,6 +79,8 @@ __device__ __forceinline__ float conv_src(const BlockParams& p, int64_t b, int64
 // A conv head is Dk channels of q or k, or Dv channels of v; one warp each.
 template <typename T, typename TS>
 __global__ void __launch_bounds__(128) block_prologue_kernel(const BlockParams p) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
   const int64_t t0 = blockIdx.x * (int64_t)TT;
   const int n_heads = 2 * p.hk + p.hv;
   const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
@@ -165,6 +167,8 @@ __global__ void __launch_bounds__(128) block_prologue_kernel(const BlockParams p
 // index is >= the written one, so the update is safe in place.
 template <typename T, typename TS>
 __global__ void block_conv_tail_kernel(const BlockParams p) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
   const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
   const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t b = blockIdx.y;
@@ -189,6 +193,8 @@ __global__ void block_conv_tail_kernel(const BlockParams p) {
 // out = silu(z) * rms_norm(y -> T, norm_w, eps); one warp per (token, head).
 template <typename T>
 __global__ void __launch_bounds__(256) block_epilogue_kernel(const BlockParams p) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
   const int64_t row = blockIdx.x * 8LL + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= p.n_tokens * p.hv) return;
@@ -320,6 +326,8 @@ __device__ __forceinline__ void conv_row(const BlockParams& p, int64_t conv_dim,
 // of Dk channels is Dk/8 consecutive lanes (Dk a power of two <= 256).
 template <typename T, typename TS, int K>
 __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockParams p) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
   const int64_t t0 = blockIdx.x * (int64_t)VT;
   const int64_t t_end = min(t0 + VT, p.n_tokens);
   const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
@@ -443,6 +451,8 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
 // row, 8 values per lane.
 template <typename T>
 __global__ void __launch_bounds__(256) block_epilogue_fast_kernel(const BlockParams p) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
   const int lanes = p.dv / 8;
   const int64_t gtid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t row = gtid / lanes;
@@ -483,8 +493,7 @@ bool fast_shapes(const BlockParams& p) {
 
 template <typename T, typename TS, int K>
 cudaError_t launch_prologue_fast(dim3 grid, const BlockParams& p, cudaStream_t s) {
-  block_prologue_fast_kernel<T, TS, K><<<grid, 256, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(block_prologue_fast_kernel<T, TS, K>, grid, dim3(256), 0, s, p);
 }
 
 template <typename T, typename TS>
@@ -505,8 +514,7 @@ cudaError_t prologue_t(const BlockParams& p, cudaStream_t s) {
   const int64_t gx = (p.n_tokens + TT - 1) / TT;
   if (gx == 0) return cudaSuccess;
   dim3 grid((unsigned)gx, (unsigned)((n_heads + 3) / 4 + 1));
-  block_prologue_kernel<T, TS><<<grid, 128, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(block_prologue_kernel<T, TS>, grid, dim3(128), 0, s, p);
 }
 
 template <typename T, typename TS>
@@ -514,8 +522,7 @@ cudaError_t tail_t(const BlockParams& p, cudaStream_t s) {
   const int64_t conv_dim = 2LL * p.hk * p.dk + (int64_t)p.hv * p.dv;
   if (p.kernel <= 1 || p.n_seqs == 0) return cudaSuccess;
   dim3 grid((unsigned)((conv_dim + 255) / 256), (unsigned)p.n_seqs);
-  block_conv_tail_kernel<T, TS><<<grid, 256, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(block_conv_tail_kernel<T, TS>, grid, dim3(256), 0, s, p);
 }
 
 }  // namespace
@@ -549,17 +556,13 @@ cudaError_t launch_block_epilogue(const BlockParams& p, cudaStream_t s) {
     const int64_t threads = rows * (p.dv / 8);
     const unsigned grid = (unsigned)((threads + 255) / 256);
     if (p.act_dtype == GDN_BF16)
-      block_epilogue_fast_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);
-    else
-      block_epilogue_fast_kernel<float><<<grid, 256, 0, s>>>(p);
-    return cudaGetLastError();
+      return launch_dependent(block_epilogue_fast_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, p);
+    return launch_dependent(block_epilogue_fast_kernel<float>, dim3(grid), dim3(256), 0, s, p);
   }
   const unsigned grid = (unsigned)((rows + 7) / 8);
   if (p.act_dtype == GDN_BF16)
-    block_epilogue_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p);
-  else
-    block_epilogue_kernel<float><<<grid, 256, 0, s>>>(p);
-  return cudaGetLastError();
+    return launch_dependent(block_epilogue_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, p);
+  return launch_dependent(block_epilogue_kernel<float>, dim3(grid), dim3(256), 0, s, p);
 }
 
 }  // namespace gdn

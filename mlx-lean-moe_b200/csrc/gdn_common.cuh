@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "gdn_api.h"
 
 namespace gdn {
@@ -87,6 +89,35 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + ex2_approx(x * -1.4426950408889634f)); }
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched by launch_dependent() may
+// start while the kernel before it on the stream is still running;
+// griddep_wait() blocks until that kernel has completed and its memory writes
+// are visible (at once when there is no such kernel or the launch was a
+// plain one).  Every kernel launched by launch_dependent() calls
+// griddep_wait() in every CTA before it reads or writes memory that earlier
+// work may touch, so completion stays ordered along the stream.
+// griddep_launch_dependents() lets the next dependent launch begin.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // Internal launch interface (one struct, filled by gdn_api.cu after checks)

@@ -416,6 +416,8 @@ __device__ __forceinline__ void gv_pairs8(uint32_t w0, uint32_t w1, float s, flo
 
 template <int BITS, int WARPS, int NT>
 __global__ void __launch_bounds__(WARPS * 32, WARPS == 8 ? (NT == 1 ? 3 : 2) : 1) qgemv_kernel(const GvParams p) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
   // [m + 1][k / 8] runs of 8, each in the order (0, 4, 1, 5, 2, 6, 3, 7); row m is zeros.
   // After the main loop the same memory holds the warps' partial sums.
   extern __shared__ uint4 xs[];
@@ -662,8 +664,8 @@ gdn_status gv_launch_one(const GvParams& g, unsigned grid, size_t smem, cudaStre
     if (st != GDN_OK) return st;
     attr = true;
   }
-  qgemv_kernel<BITS, WARPS, NT><<<grid, WARPS * 32, smem, cs>>>(g);
-  return q_cuda(cudaGetLastError(), "quantized_linear launch");
+  return q_cuda(launch_dependent(qgemv_kernel<BITS, WARPS, NT>, dim3(grid), dim3(WARPS * 32), smem, cs, g),
+                "quantized_linear launch");
 }
 
 template <int BITS, int WARPS>

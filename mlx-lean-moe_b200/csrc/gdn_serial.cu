@@ -146,6 +146,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const ScanParams p) {
 // is processed, so global-memory latency stays off the token loop.
 template <int DKP, typename T>
 __global__ void __launch_bounds__(128) serial_scan_kernel(const ScanParams p) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
   using L = Layout<DKP>;
   constexpr int TB = DKP >= 256 ? 16 : 32;
   constexpr int NK = TB * DKP / 128;                       // k (and q) values staged per thread
@@ -299,10 +301,8 @@ cudaError_t launch_one(const ScanParams& p, cudaStream_t s, bool decode) {
   if (gx <= 0) return cudaSuccess;
   if (gx > 0x7fffffffLL || p.hv > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid((unsigned)gx, (unsigned)p.hv);
-  if (decode)
-    decode_kernel<DKP, T><<<grid, 128, 0, s>>>(p);
-  else
-    serial_scan_kernel<DKP, T><<<grid, 128, 0, s>>>(p);
+  if (!decode) return launch_dependent(serial_scan_kernel<DKP, T>, grid, dim3(128), 0, s, p);
+  decode_kernel<DKP, T><<<grid, 128, 0, s>>>(p);
   return cudaGetLastError();
 }
 

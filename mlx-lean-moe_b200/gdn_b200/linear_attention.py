@@ -191,8 +191,11 @@ class Qwen3_5LinearAttention:
         seq_len = rows.shape[0]
         mixed = self._mixed(rows)
         conv_state, ssm_state = cache.state()
-        new_conv = conv_state.clone()
-        new_ssm = ssm_state.clone()
+        # the block writes every row of both new states when it has tokens, so
+        # fresh buffers need no copy of the old ones (which stay as they were,
+        # as with the reference's functional update)
+        new_conv = torch.empty_like(conv_state) if seq_len else conv_state.clone()
+        new_ssm = torch.empty_like(ssm_state) if seq_len else ssm_state.clone()
         out, _, _ = gated_delta_block(
             mixed, self.shape, self.conv_w, self.A_log, self.dt_bias, self.norm_weight, self.eps,
             conv_state[None], ssm_state[None], conv_state_out=new_conv[None], ssm_state_out=new_ssm[None],
