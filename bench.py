@@ -8,7 +8,7 @@ one decode launch over the batch; ``value`` is the state HBM traffic
 prefill number of config 3 (T=8192) under ``"prefill"``.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|varlen|qproj|attn] [--tokens M]
+                    [--workload decode|varlen|qproj|attn|layerdecode] [--tokens M]
 
 ``--workload varlen`` is config 5 instead: 64 packed sequences (lengths
 ``default_rng(1).integers(256, 16384, 64, endpoint=True)``, 516,496 tokens)
@@ -20,7 +20,9 @@ and the decode phase is reported beside it.
 ``--workload qproj`` times only the 4-bit quantized in-projection (12,352 x
 2,048) at ``--tokens`` rows, ``--workload attn`` only the attention core
 (prefill of ``--tokens`` tokens, or one decode token against 4,096 cached
-positions with ``--tokens 1``), for profiling those kernels.  The
+positions with ``--tokens 1``), ``--workload layerdecode`` the
+linear-attention layer at one decode token launched eagerly, for profiling
+those kernels.  The
 default line also carries ``"layer"``: config 4 from hidden states in to
 hidden states out, with 4-bit affine projections around the fused block.
 
@@ -369,11 +371,10 @@ def measure_layer(device, iters=3):
             "ms": sum(med), "gemm_flop": gemm_flop}
 
 
-def measure_layer_decode(device, iters=3):
-    """The linear-attention layer (Qwen3_5LinearAttention, the model's shape:
-    16/32 heads of 128, hidden 2,048, 4-bit group-64 projections) at one
-    decode token with its RecurrentCache, as a CUDA-graph replay: the fused
-    in-projection GEMV, the fused block on one token, the out_proj GEMV."""
+def linear_layer_at_decode(device):
+    """Qwen3_5LinearAttention at the model's shape (16/32 heads of 128,
+    hidden 2,048, 4-bit group-64 projections), its RecurrentCache and one
+    decode token of hidden state."""
     import gdn_b200
     from gdn_b200 import LinearWeights, QuantScheme
     from gdn_b200.linear_attention import LinearAttentionShape
@@ -389,6 +390,14 @@ def measure_layer_decode(device, iters=3):
         torch.ones(D, device=device), qw(HIDDEN, shape.value_dim))
     cache = gdn_b200.RecurrentCache(4, shape.conv_dim, HV, D, D, device=device)
     x1 = torch.randn(HIDDEN, device=device, generator=gen).bfloat16()
+    return layer, cache, x1
+
+
+def measure_layer_decode(device, iters=3):
+    """The linear-attention layer at one decode token, as a CUDA-graph
+    replay: the fused in-projection GEMV, the fused block on one token, the
+    out_proj GEMV."""
+    layer, cache, x1 = linear_layer_at_decode(device)
     layer(x1, cache)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
@@ -547,6 +556,29 @@ def run_attn(args):
                       "dtype": "bf16", "data": "synthetic"}), flush=True)
 
 
+def run_layerdecode(args):
+    """Only the linear-attention layer at one decode token, launched eagerly
+    (one kernel after another, as ncu lists them); for profiling the decode
+    chain's kernels."""
+    device = torch.device("cuda", 0)
+    layer, cache, x1 = linear_layer_at_decode(device)
+    for _ in range(args.warmup):
+        layer(x1, cache)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        layer(x1, cache)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / max(args.steps, 1)
+    print(json.dumps({"metric": "linear-attention layer decode step", "value": ms * 1e3, "unit": "us",
+                      "higher_is_better": False, "steps": args.steps, "warmup": args.warmup,
+                      "config": {"workload": "Qwen3_5LinearAttention at one decode token, 16/32 heads of 128, "
+                                             "hidden 2,048, 4-bit projections, launched eagerly"},
+                      "dtype": "bf16", "data": "synthetic"}), flush=True)
+
+
 def run_qproj(args):
     """Only the quantized in-projection (12,352 x 2,048, 4-bit, group 64) at
     ``--tokens`` rows: the GEMV up to 16 tokens, the tiled GEMM beyond; for
@@ -699,17 +731,17 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="decode only: no e2e, prefill or CPU legs (for profiler runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiler runs)")
-    ap.add_argument("--workload", choices=["decode", "varlen", "qproj", "attn"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "varlen", "qproj", "attn", "layerdecode"], default="decode")
     ap.add_argument("--tokens", type=int, default=4096, help="rows of x for --workload qproj / attn")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.workload in ("qproj", "attn"):
+    if args.workload in ("qproj", "attn", "layerdecode"):
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the reference's quantized matmul and attention "
                               "are MLX's (mx.quantized_matmul, mx.fast.scaled_dot_product_attention), not "
                               "installable on this box"}), flush=True)
             return
-        return run_qproj(args) if args.workload == "qproj" else run_attn(args)
+        return {"qproj": run_qproj, "attn": run_attn, "layerdecode": run_layerdecode}[args.workload](args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)

@@ -357,6 +357,8 @@ gdn_status gdn_fused_block(const gdn_block_args* args, gdn_stream_t stream) {
     return fail(GDN_EINVAL, "workspace too small: %zu bytes given, %zu needed", args->workspace_bytes, L.total);
   if (!aligned16(args->workspace)) return fail(GDN_EINVAL, "workspace must be 16-byte aligned");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!chunked && gdn::block_decode_supported(p, sp.state_in, sp.state_out))  // one token per sequence
+    return cuda_status(gdn::launch_block_decode(p, sp.state_in, sp.state_out, s), "block decode launch");
   st = cuda_status(gdn::launch_block_prologue(p, s), "block prologue launch");
   if (st != GDN_OK) return st;
   st = cuda_status(gdn::launch_block_conv_tail(p, s), "conv tail launch");

@@ -484,6 +484,165 @@ __global__ void __launch_bounds__(256) block_epilogue_fast_kernel(const BlockPar
   if (valid) store8<T>(static_cast<T*>(p.out) + rr * p.dv + d0, o);
 }
 
+// ------------------------------------------------------------------ decode
+// Every sequence one token (decode through the layer): the whole block for
+// one (sequence, value head) in one CTA of 384 threads, used when the new
+// conv tail goes to a buffer of its own.
+//  phase 1, a thread per channel of the head (warps 0-3 q, 4-7 k, 8-11 v):
+//    the causal conv over the conv state and the token, SiLU, the q/k RMS
+//    norms and scales, rounded where block_prologue_fast_kernel rounds; the
+//    new conv tail of those channels (q/k channels by the first value head of
+//    their group only); the gates (thread 0).
+//  phase 2, warps 0-7: the state update of decode_kernel, a state row over 8
+//    lanes, the state loads issued before phase 1.
+//  phase 3, warps 0-3: the gated RMS norm of block_epilogue_fast_kernel.
+constexpr int kDecDim = 128;  // Dk = Dv
+
+template <typename T, typename TS, int K>
+__global__ void __launch_bounds__(384) block_decode_kernel(const BlockParams p, const float* state_in,
+                                                           float* state_out) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
+  constexpr int LPR = 8, VEC = 4, RPG = 4, ITER = 4;  // 8 warps x 4 rows x 4 passes = 128 rows
+  __shared__ __align__(16) float qs[kDecDim];
+  __shared__ __align__(16) float ks[kDecDim];
+  __shared__ float vs[kDecDim], ys[kDecDim];
+  __shared__ float red[8];
+  __shared__ float gate[2];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x;
+  const int64_t b = blockIdx.y;  // sequence b is token b
+  const int group = p.hv / p.hk, kh = h / group;
+  const int64_t key_dim = (int64_t)p.hk * kDecDim;
+  const int64_t conv_dim = 2 * key_dim + (int64_t)p.hv * kDecDim;
+  const T* mrow = static_cast<const T*>(p.mixed) + b * p.mixed_st;
+  const int64_t head_off = (b * p.hv + h) * (int64_t)kDecDim * kDecDim;
+  const int grp = lane / LPR, l = lane % LPR;
+  const int row0 = warp * (RPG * ITER) + grp;
+
+  float4 s[ITER][VEC];
+  if (warp < 8) {
+#pragma unroll
+    for (int i = 0; i < ITER; ++i)
+#pragma unroll
+      for (int j = 0; j < VEC; ++j)
+        s[i][j] = state_in ? *reinterpret_cast<const float4*>(state_in + head_off +
+                                                               (int64_t)(row0 + i * RPG) * kDecDim + (j * LPR + l) * 4)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+
+  // phase 1
+  const int part = tid >> 7, i = tid & 127;  // 0: q, 1: k, 2: v
+  const int64_t c = part == 0 ? kh * kDecDim + i : part == 1 ? key_dim + kh * kDecDim + i
+                                                             : 2 * key_dim + (int64_t)h * kDecDim + i;
+  float win[K > 1 ? K - 1 : 1];
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j)
+    win[j] = p.conv_state_in
+                 ? round_to<T>(to_f(static_cast<const TS*>(p.conv_state_in)[(b * (K - 1) + j) * conv_dim + c]))
+                 : 0.f;
+  const float cur = to_f(mrow[c]);
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < K - 1; ++j) acc += round_to<T>(p.conv_w[c * K + j]) * win[j];
+  acc += round_to<T>(p.conv_w[c * K + K - 1]) * cur;
+  float x = round_to<T>(silu_fast(round_to<T>(acc)));
+  if constexpr (K > 1) {
+    if (part == 2 || h % group == 0) {
+      TS* tail = static_cast<TS*>(p.conv_state_out) + b * (K - 1) * conv_dim + c;
+#pragma unroll
+      for (int r = 0; r < K - 1; ++r) tail[r * conv_dim] = from_f<TS>(r < K - 2 ? win[r + 1] : cur);
+    }
+  }
+  if (tid == 0) {
+    const int64_t off_b = conv_dim + (int64_t)p.hv * kDecDim, off_a = off_b + p.hv;
+    const float av = to_f(mrow[off_a + h]), bv = to_f(mrow[off_b + h]);
+    gate[0] = expf(-expf(p.A_log[h]) * softplus_f(av + p.dt_bias[h]));
+    gate[1] = round_to<T>(sigmoid_f(bv));
+  }
+  float ss = part < 2 ? x * x : 0.f;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if (lane == 0 && warp < 8) red[warp] = ss;
+  __syncthreads();
+  if (part < 2) {
+    const float tot = red[part * 4] + red[part * 4 + 1] + red[part * 4 + 2] + red[part * 4 + 3];
+    const float inv = rsqrtf(tot / (float)kDecDim + 1e-6f);
+    x = round_to<T>(round_to<T>(x * inv) * (part == 0 ? 1.f / (float)kDecDim : rsqrtf((float)kDecDim)));
+    (part == 0 ? qs : ks)[i] = x;
+  } else {
+    vs[i] = x;
+  }
+  __syncthreads();
+
+  // phase 2
+  if (warp < 8) {
+    const float gv = gate[0], bv = gate[1];
+    float4 kq[VEC], qq[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      kq[j] = *reinterpret_cast<const float4*>(ks + (j * LPR + l) * 4);
+      qq[j] = *reinterpret_cast<const float4*>(qs + (j * LPR + l) * 4);
+    }
+    float* sout = state_out + head_off;
+#pragma unroll
+    for (int it = 0; it < ITER; ++it) {
+      const int row = row0 + it * RPG;
+      float r = 0.f;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        s[it][j] = s[it][j] * gv;
+        r += dot4(s[it][j], kq[j]);
+      }
+#pragma unroll
+      for (int off = LPR / 2; off >= 1; off >>= 1) r += __shfl_xor_sync(0xffffffffu, r, off);
+      const float d = (vs[row] - r) * bv;
+      float y = 0.f;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        s[it][j].x += kq[j].x * d;
+        s[it][j].y += kq[j].y * d;
+        s[it][j].z += kq[j].z * d;
+        s[it][j].w += kq[j].w * d;
+        y += dot4(s[it][j], qq[j]);
+        *reinterpret_cast<float4*>(sout + (int64_t)row * kDecDim + (j * LPR + l) * 4) = s[it][j];
+      }
+#pragma unroll
+      for (int off = LPR / 2; off >= 1; off >>= 1) y += __shfl_xor_sync(0xffffffffu, y, off);
+      if (l == 0) ys[row] = round_to<T>(y);
+    }
+  }
+  __syncthreads();
+
+  // phase 3
+  float y = 0.f;
+  if (warp < 4) {
+    y = ys[tid];
+    float sq = y * y;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+    if (lane == 0) red[warp] = sq;
+  }
+  __syncthreads();
+  if (warp < 4) {
+    const float inv = rsqrtf((red[0] + red[1] + red[2] + red[3]) / (float)kDecDim + p.eps);
+    const float o = round_to<T>(y * inv * p.norm_w[tid]);
+    const float z = to_f(mrow[conv_dim + (int64_t)h * kDecDim + tid]);
+    static_cast<T*>(p.out)[(b * p.hv + h) * (int64_t)kDecDim + tid] = from_f<T>(o * silu_fast(z));
+  }
+}
+
+template <typename T, typename TS>
+cudaError_t decode_t(const BlockParams& p, const float* state_in, float* state_out, cudaStream_t s) {
+  const dim3 grid((unsigned)p.hv, (unsigned)p.n_seqs);
+  switch (p.kernel) {
+    case 1: return launch_dependent(block_decode_kernel<T, TS, 1>, grid, dim3(384), 0, s, p, state_in, state_out);
+    case 2: return launch_dependent(block_decode_kernel<T, TS, 2>, grid, dim3(384), 0, s, p, state_in, state_out);
+    case 3: return launch_dependent(block_decode_kernel<T, TS, 3>, grid, dim3(384), 0, s, p, state_in, state_out);
+    default: return launch_dependent(block_decode_kernel<T, TS, 4>, grid, dim3(384), 0, s, p, state_in, state_out);
+  }
+}
+
 bool pow2_in(int x, int lo, int hi) { return x >= lo && x <= hi && (x & (x - 1)) == 0; }
 
 bool fast_shapes(const BlockParams& p) {
@@ -563,6 +722,27 @@ cudaError_t launch_block_epilogue(const BlockParams& p, cudaStream_t s) {
   if (p.act_dtype == GDN_BF16)
     return launch_dependent(block_epilogue_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s, p);
   return launch_dependent(block_epilogue_kernel<float>, dim3(grid), dim3(256), 0, s, p);
+}
+
+bool block_decode_supported(const BlockParams& p, const float* state_in, const float* state_out) {
+  if (p.n_tokens != p.n_seqs || p.n_seqs < 1 || p.cu_seqlens || p.dk != kDecDim || p.dv != kDecDim) return false;
+  if (p.kernel < 1 || p.kernel > 4 || p.hv % p.hk || p.n_seqs > 65535) return false;
+  if ((reinterpret_cast<uintptr_t>(state_in) | reinterpret_cast<uintptr_t>(state_out)) & 15u) return false;
+  if (p.kernel > 1 && p.conv_state_in) {  // the conv tail must not overwrite state that other CTAs still read
+    const size_t bytes = (size_t)p.n_seqs * (p.kernel - 1) * (2 * (size_t)p.hk * p.dk + (size_t)p.hv * p.dv) *
+                         (p.conv_state_dtype == GDN_BF16 ? 2 : 4);
+    const uintptr_t in = reinterpret_cast<uintptr_t>(p.conv_state_in), out = reinterpret_cast<uintptr_t>(p.conv_state_out);
+    if (in < out + bytes && out < in + bytes) return false;
+  }
+  return true;
+}
+
+cudaError_t launch_block_decode(const BlockParams& p, const float* state_in, float* state_out, cudaStream_t s) {
+  const bool st_bf = p.conv_state_dtype == GDN_BF16;
+  if (p.act_dtype == GDN_BF16)
+    return st_bf ? decode_t<__nv_bfloat16, __nv_bfloat16>(p, state_in, state_out, s)
+                 : decode_t<__nv_bfloat16, float>(p, state_in, state_out, s);
+  return st_bf ? decode_t<float, __nv_bfloat16>(p, state_in, state_out, s) : decode_t<float, float>(p, state_in, state_out, s);
 }
 
 }  // namespace gdn

@@ -181,6 +181,10 @@ cudaError_t launch_forget_gate(const void* a, gdn_dtype dt, int64_t a_st, int64_
 cudaError_t launch_block_prologue(const BlockParams& p, cudaStream_t s);
 cudaError_t launch_block_conv_tail(const BlockParams& p, cudaStream_t s);
 cudaError_t launch_block_epilogue(const BlockParams& p, cudaStream_t s);
+// Every sequence one token, Dk = Dv = 128, conv width <= 4, the conv tail
+// written apart from the conv state it reads: the whole block in one kernel.
+bool block_decode_supported(const BlockParams& p, const float* state_in, const float* state_out);
+cudaError_t launch_block_decode(const BlockParams& p, const float* state_in, float* state_out, cudaStream_t s);
 
 // Chunked (tensor-core) prefill.
 bool chunked_supported(const ScanParams& p);
