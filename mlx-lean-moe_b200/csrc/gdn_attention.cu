@@ -25,6 +25,9 @@
 // attn_combine_kernel  adds up, then gates and writes.
 // attn_mma_kernel      bf16 prefill (calls with enough rows for one key
 //                      split) on the tensor cores: see its comment below.
+// attn_dec_mma_kernel  bf16 decode (one token, a key/value head's query
+//                      heads within 16 rows) on the tensor cores, one warp
+//                      per key split, into the combine.
 //
 // The attention and combine kernels are launched as programmatic dependents
 // of the kernel before them: they start while it finishes, and the
@@ -785,6 +788,200 @@ gdn_status launch_combine(const AttnParams& p, cudaStream_t s) {
   return GDN_OK;
 }
 
+// ----------------------------------------------- decode, tensor cores
+// bf16 calls with one token whose query heads of a key/value head fit 16
+// rows (decode): the query rows (zero-padded to 16) times each key split on
+// mma.sync m16n8k16, one warp per 32-key split tile with the operand layouts
+// of attn_mma_kernel (Q by ldmatrix, K by ldmatrix, P from the score
+// accumulators, V by ldmatrix.trans), an online softmax over the split's
+// tiles, and the split's partial (max in natural-log units, sum, output)
+// rows for attn_combine_kernel.  Each warp owns a single-buffered K/V tile;
+// the first, when it holds keys cached by earlier calls only, is requested
+// before the wait for the prep kernel.
+constexpr int kDQ = 16;     // query rows of the MMA tile
+constexpr int kDK = 32;     // keys per tile
+constexpr int kDWarps = 4;  // warps (splits) per CTA
+
+template <int HD>
+struct DecSmem {
+  static constexpr size_t kQ = (size_t)kDQ * HD * 2;
+  static constexpr size_t kTile = (size_t)kDK * HD * 2;
+  static constexpr size_t kBytes = kQ + (size_t)kDWarps * 2 * kTile;  // Q, then K and V per warp
+};
+
+template <int HD>
+__global__ void __launch_bounds__(kDWarps * 32) attn_dec_mma_kernel(const AttnParams p) {
+  using SM = DecSmem<HD>;
+  constexpr int NT = HD / 8;  // output n-tiles of 8 features
+  constexpr int KC = HD / 8;  // 16-byte chunks per row
+  extern __shared__ __align__(16) unsigned char smem_dec[];
+  griddep_launch_dependents();  // the combine kernel waits for this grid before it reads the partial rows
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem_dec);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  const int hk = blockIdx.y;
+  const int split = blockIdx.x * kDWarps + warp;
+  const bool live = split < p.splits;  // warp-uniform
+  const uint32_t sQ = sbase, sK = sbase + (uint32_t)(SM::kQ + (size_t)warp * 2 * SM::kTile), sV = sK + SM::kTile;
+  const __nv_bfloat16* kc = static_cast<const __nv_bfloat16*>(p.k_cache) + hk * p.cache_sh;
+  const __nv_bfloat16* vc = static_cast<const __nv_bfloat16*>(p.v_cache) + hk * p.cache_sh;
+
+  // this split's keys (one token: all cached keys are visible)
+  const int64_t per = (((p.cache_len + p.splits - 1) / p.splits) + kKeyTile - 1) / kKeyTile * kKeyTile;
+  const int64_t kbeg = (int64_t)split * per;
+  const int64_t kend = live ? min(kbeg + per, p.cache_len) : kbeg;
+  const int ntiles = kend > kbeg ? (int)((kend - kbeg + kDK - 1) / kDK) : 0;
+  auto load_tile = [&](int tile) {  // by this warp only; rows past the split's end zero-filled
+    const int64_t k0 = kbeg + (int64_t)tile * kDK;
+    for (int i = lane; i < kDK * KC; i += 32) {
+      const int r = i / KC, c = (i % KC) * 8;
+      const int64_t kp = k0 + r;
+      const bool ok = kp < kend;
+      const int64_t src = (ok ? kp : k0) * HD + c;
+      cp_async16(sK + swz(r, c, HD), kc + src, ok);
+      cp_async16(sV + swz(r, c, HD), vc + src, ok);
+    }
+  };
+  const bool early = ntiles > 0 && kbeg + kDK <= p.offset;  // tile 0 holds earlier calls' keys only
+  if (early) load_tile(0);
+  griddep_wait();
+  // Q: rows r < group are the query heads hk * group + r of the token
+  const __nv_bfloat16* qw = static_cast<const __nv_bfloat16*>(p.q_ws);
+  for (int i = tid; i < kDQ * KC; i += kDWarps * 32) {
+    const int r = i / KC, c = (i % KC) * 8;
+    const bool ok = r < p.group;
+    cp_async16(sQ + swz(r, c, HD), qw + (int64_t)(hk * p.group + (ok ? r : 0)) * HD + c, ok);
+  }
+  if (ntiles > 0 && !early) load_tile(0);
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();  // Q from every thread; each warp's own tile
+
+  float o[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g and g + 8
+  const float sl2 = p.scale * 1.4426950408889634f;           // scores in log2 units
+  for (int tile = 0; tile < ntiles; ++tile) {
+    if (tile > 0) {  // single buffer: the previous tile is done (warp-synchronous ldmatrix reads)
+      __syncwarp();
+      load_tile(tile);
+      cp_async_commit();
+      cp_async_wait<0>();
+      __syncwarp();
+    }
+    // S = Q K^T: 16 rows x 32 keys
+    float s[4][4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t a[4];
+      ldsm_x4(sQ + swz(lane & 15, ks * 16 + (lane >> 4) * 8, HD), a);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t b[4];
+        const int krow = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int kcol = ks * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(sK + swz(krow, kcol, HD), b);
+        mma16816(s[2 * np], a, b[0], b[1]);
+        mma16816(s[2 * np + 1], a, b[2], b[3]);
+      }
+    }
+    const int64_t k0 = kbeg + (int64_t)tile * kDK;
+    float mx0 = m0, mx1 = m1;
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const bool ok = k0 + n * 8 + 2 * t4 + e < kend;
+        s[n][e] = ok ? s[n][e] * sl2 : -INFINITY;
+        s[n][2 + e] = ok ? s[n][2 + e] * sl2 : -INFINITY;
+        mx0 = fmaxf(mx0, s[n][e]);
+        mx1 = fmaxf(mx1, s[n][2 + e]);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+    }
+    const float al0 = mx0 == -INFINITY ? 1.f : exp2f(m0 - mx0), al1 = mx1 == -INFINITY ? 1.f : exp2f(m1 - mx1);
+    m0 = mx0;
+    m1 = mx1;
+    l0 *= al0;
+    l1 *= al1;
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      o[n][0] *= al0;
+      o[n][1] *= al0;
+      o[n][2] *= al1;
+      o[n][3] *= al1;
+    }
+    uint32_t pa[2][4];  // P as A fragments: 2 k-steps of 16 keys
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const float p00 = m0 == -INFINITY ? 0.f : exp2f(s[n][0] - m0), p01 = m0 == -INFINITY ? 0.f : exp2f(s[n][1] - m0);
+      const float p10 = m1 == -INFINITY ? 0.f : exp2f(s[n][2] - m1), p11 = m1 == -INFINITY ? 0.f : exp2f(s[n][3] - m1);
+      l0 += p00 + p01;
+      l1 += p10 + p11;
+      pa[n >> 1][(n & 1) * 2] = cvt_bf16x2(p00, p01);
+      pa[n >> 1][(n & 1) * 2 + 1] = cvt_bf16x2(p10, p11);
+    }
+    // O += P V
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        uint32_t b[4];
+        const int vrow = ks * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+        const int vcol = np * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(sV + swz(vrow, vcol, HD), b);
+        mma16816(o[2 * np], pa[ks], b[0], b[1]);
+        mma16816(o[2 * np + 1], pa[ks], b[2], b[3]);
+      }
+    }
+  }
+  if (!live) return;  // no barrier follows
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  // partial rows g and g + 8 (when they are query heads): output, max (natural log), sum
+  const float ln2 = 0.6931471805599453f;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int r = g + 8 * half;
+    if (r >= p.group) continue;
+    float* pr = p.part + ((size_t)split * p.n_tokens * p.heads + (size_t)(hk * p.group + r)) * (HD + 4);
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+      *reinterpret_cast<float2*>(pr + n * 8 + 2 * t4) = make_float2(o[n][2 * half], o[n][2 * half + 1]);
+    if (t4 == 0) {
+      const float mm = half ? m1 : m0;
+      pr[HD] = mm == -INFINITY ? -INFINITY : mm * ln2;
+      pr[HD + 1] = half ? l1 : l0;
+    }
+  }
+}
+
+template <int HD>
+gdn_status launch_dec_mma(const AttnParams& p, cudaStream_t s) {
+  static bool attr = false;
+  constexpr size_t smem = DecSmem<HD>::kBytes;
+  if (!attr) {
+    if (cudaFuncSetAttribute(attn_dec_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess)
+      return set_error(GDN_ECUDA, "attention: shared-memory attribute");
+    attr = true;
+  }
+  const dim3 grid((unsigned)((p.splits + kDWarps - 1) / kDWarps), (unsigned)p.kv_heads);
+  const cudaError_t e = launch_dependent(attn_dec_mma_kernel<HD>, grid, dim3(kDWarps * 32), smem, s, p);
+  if (e != cudaSuccess) return set_error(GDN_ECUDA, "attention launch: %s", cudaGetErrorString(e));
+  return GDN_OK;
+}
+
 template <typename T, int HD>
 gdn_status launch_fwd(const AttnParams& p, dim3 grid, cudaStream_t s) {
   static bool attr = false;  // set once per instance (a repeat from a racing thread is harmless)
@@ -927,6 +1124,12 @@ extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream)
         case 64: st = gdn::launch_mma<64>(p, s); break;
         case 128: st = gdn::launch_mma<128>(p, s); break;
         default: st = gdn::launch_mma<256>(p, s); break;
+      }
+    } else if (a->n_tokens == 1 && p.group <= gdn::kDQ && a->head_dim >= 64) {  // decode: tensor cores
+      switch (a->head_dim) {
+        case 64: st = gdn::launch_dec_mma<64>(p, s); break;
+        case 128: st = gdn::launch_dec_mma<128>(p, s); break;
+        default: st = gdn::launch_dec_mma<256>(p, s); break;
       }
     } else {
       st = gdn::launch_fwd_hd<__nv_bfloat16>(p, fgrid, s);

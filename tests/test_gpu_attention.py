@@ -225,3 +225,27 @@ def test_decode_captured_in_a_cuda_graph_equals_the_eager_call():
     assert cache.size == L and torch.isfinite(keys.float()).all()
     del graph
     gdn_b200.check_device_errors()
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim,rotary,cached",
+                         [(8, 8, 64, 16, 300), (6, 2, 128, 32, 700), (16, 1, 128, 64, 200), (4, 1, 64, 16, 5200)])
+def test_attention_bf16_decode_on_tensor_cores(heads, kv_heads, head_dim, rotary, cached):
+    # one token against a cache filled on the GPU: the tensor-core decode
+    # (query groups of 1, 3 and 16 rows; 5,200 cached positions give two
+    # tiles per key split and splits past the end), against the oracle given
+    # the same cached keys and values
+    shape = AttentionShape(heads, kv_heads, head_dim, rotary, 1000000.0)
+    hidden = 128
+    rng = np.random.default_rng(heads * 100 + head_dim)
+    w = _bf16_weights(_random_weights(rng, shape, hidden, 0.05))
+    layer = _layer(w, shape, 1e-6, torch.bfloat16)
+    cache = _cache(shape, max_context=cached + 4, dtype=torch.bfloat16)
+    layer(t(O.bf16_round(rng.standard_normal((cached, hidden)).astype(np.float32)), torch.bfloat16), cache)
+    for _ in range(2):
+        keys, values = (n(a).astype(np.float64) for a in cache.state())
+        x = O.bf16_round(rng.standard_normal((1, hidden)).astype(np.float32))
+        got = layer(t(x, torch.bfloat16), cache)
+        want, _, _ = O.attention_layer(x, w, keys, values, heads, kv_heads, head_dim, rotary, 1000000.0, 1e-6,
+                                       rnd=O.bf16_round)
+        assert O.rel_l2(n(got), want) < 1e-2, O.rel_l2(n(got), want)
+    gdn_b200.check_device_errors()
