@@ -800,7 +800,7 @@ gdn_status launch_combine(const AttnParams& p, cudaStream_t s) {
 // before the wait for the prep kernel.
 constexpr int kDQ = 16;     // query rows of the MMA tile
 constexpr int kDK = 32;     // keys per tile
-constexpr int kDWarps = 4;  // warps (splits) per CTA
+constexpr int kDWarps = 1;  // warps (splits) per CTA: the split tiles spread over every SM
 
 template <int HD>
 struct DecSmem {
