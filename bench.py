@@ -59,7 +59,7 @@ DECODE_BYTES = STATE_BYTES + 2 * B * HK * D * 2 + B * HV * D * 2 + 2 * B * HV * 
 # DRAM bytes of one decode_kernel launch at config 2, from one ncu capture (read + write).
 DECODE_NCU_TRAFFIC = 135_301_120 + 76_251_648
 PREFILL_T = 8192
-PREFILL_FLOP = 182_955 * PREFILL_T * HV  # chunked WY count per token-head, see DESIGN.md
+PREFILL_FLOP = 182_955 * PREFILL_T * HV  # chunked WY count per token-head: (10 C^2 d + 6 C d^2 + 2/3 C^3) / C, C = 64, d = 128
 
 
 def peaks():

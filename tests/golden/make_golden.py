@@ -1,9 +1,9 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
-Run in a container that has the reference tree (read-only) at
-``REFERENCE_ROOT`` (default ``/root/reference``)::
+Run where the reference project is checked out (read-only), with
+``REFERENCE_ROOT`` set to that checkout::
 
-    python tests/golden/make_golden.py
+    REFERENCE_ROOT=<reference checkout> python tests/golden/make_golden.py
 
 It writes ``golden.npz`` (outputs) and ``golden_manifest.json`` (sha256 of
 every input array, so tests can regenerate the inputs from their seeds and
@@ -36,7 +36,7 @@ import types
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", "/root/reference")
+REFERENCE_ROOT = os.environ.get("REFERENCE_ROOT", "")
 
 # Shapes of tests/test_gated_delta_metal.py:42-45, (L, Dk, Dv, Hk, Hv).
 METAL_SHAPES = [(1, 32, 5, 3, 6), (7, 64, 32, 2, 2), (17, 128, 128, 16, 32), (129, 256, 7, 2, 6)]
@@ -118,6 +118,8 @@ def _extract_functions(path: str, names: list[str], namespace: dict) -> dict:
 
 
 def main() -> None:
+    if not REFERENCE_ROOT:
+        raise SystemExit("set REFERENCE_ROOT to the reference project's checkout")
     sys.path.insert(0, HERE)
     import mlx_numpy_shim
 
