@@ -123,3 +123,66 @@ def test_block_workspace_size_is_host_only():
     assert lib.gdn_block_workspace_size(ctypes.byref(b), ctypes.byref(size)) == _lib.GDN_OK
     # q, k, v, y (bf16, the act dtype) + g, beta (fp32), each 256-byte aligned
     assert size.value >= 64 * (2 * 64 * 2 + 128 * 2 + 4 * 4 * 2 + 128 * 2)
+
+
+def _attn_args(n_tokens=1, cache_len=4097):
+    a = _lib.AttnArgs()
+    a.n_tokens, a.cache_len, a.capacity = n_tokens, cache_len, max(cache_len, 4352)
+    a.heads, a.kv_heads, a.head_dim, a.rotary_dim = 16, 2, 256, 64
+    a.rope_base, a.eps, a.scale = 1e7, 1e-6, 256 ** -0.5
+    a.qg, a.qg_stride_t = 0x10000, 16 * 512
+    a.k_new, a.k_stride_t, a.v_new, a.v_stride_t = 0x20000, 512, 0x30000, 512
+    a.q_norm = a.k_norm = 0x40000
+    a.k_cache, a.v_cache = 0x50000, 0x60000
+    a.act_dtype = _lib.GDN_BF16
+    a.out, a.out_stride_t = 0x70000, 16 * 256
+    return a
+
+
+def _align256(x):
+    return (x + 255) // 256 * 256
+
+
+def test_attention_workspace_follows_the_split_rule():
+    # one decode token: splits = min(2 x 148 CTAs over the row blocks, one
+    # 32-key tile each, 160); the q rows, then the splits' partial rows
+    # (head_dim + 4 floats each)
+    lib = _lib.load()
+    size = ctypes.c_size_t(0)
+    assert lib.gdn_attention_workspace_size(ctypes.byref(_attn_args()), ctypes.byref(size)) == _lib.GDN_OK
+    assert size.value == _align256(16 * 256 * 2) + _align256(129 * 16 * 260 * 4)  # 4,097 keys: 129 tiles
+    assert lib.gdn_attention_workspace_size(ctypes.byref(_attn_args(1, 8000)), ctypes.byref(size)) == _lib.GDN_OK
+    assert size.value == _align256(16 * 256 * 2) + _align256(148 * 16 * 260 * 4)  # 296 CTAs over 2 heads
+    one_kv = _attn_args(1, 8000)
+    one_kv.heads, one_kv.kv_heads = 8, 1
+    assert lib.gdn_attention_workspace_size(ctypes.byref(one_kv), ctypes.byref(size)) == _lib.GDN_OK
+    assert size.value == _align256(8 * 256 * 2) + _align256(160 * 8 * 260 * 4)  # capped at 160
+    # a prefill of 4,096 tokens: one split, no partial rows
+    assert lib.gdn_attention_workspace_size(ctypes.byref(_attn_args(4096, 4096)), ctypes.byref(size)) == _lib.GDN_OK
+    assert size.value == _align256(4096 * 16 * 256 * 2)
+
+
+@pytest.mark.parametrize(
+    "mutate,fragment",
+    [
+        (lambda a: setattr(a, "head_dim", 96), "head_dim"),
+        (lambda a: setattr(a, "rotary_dim", 63), "rotary_dim"),
+        (lambda a: setattr(a, "kv_heads", 3), "multiple of kv_heads"),
+        (lambda a: setattr(a, "cache_len", 0), "n_tokens <= cache_len"),
+        (lambda a: setattr(a, "k_cache", 0x50008), "16-byte aligned"),
+        (lambda a: setattr(a, "qg", None), "non-NULL"),
+        (lambda a: setattr(a, "act_dtype", _lib.GDN_F16), "float32 or bf16"),
+        (lambda a: setattr(a, "workspace_bytes", 64), "workspace too small"),
+        (lambda a: setattr(a, "workspace", 0x80008), "workspace must be 16-byte aligned"),
+    ],
+)
+def test_attention_rejects_bad_arguments_before_any_launch(mutate, fragment):
+    lib = _lib.load()
+    a = _attn_args()
+    size = ctypes.c_size_t(0)
+    assert lib.gdn_attention_workspace_size(ctypes.byref(a), ctypes.byref(size)) == _lib.GDN_OK
+    a.workspace, a.workspace_bytes = 0x80000, size.value
+    mutate(a)
+    st = lib.gdn_attention(ctypes.byref(a), None)
+    assert st in (_lib.GDN_EINVAL, _lib.GDN_EUNSUPPORTED)
+    assert fragment in lib.gdn_last_error().decode()
