@@ -8,7 +8,7 @@ one decode launch over the batch; ``value`` is the state HBM traffic
 prefill number of config 3 (T=8192) under ``"prefill"``.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|varlen|qproj|attn|layerdecode] [--tokens M]
+                    [--workload decode|varlen|prefill|qproj|attn|layerdecode] [--tokens M]
 
 ``--workload varlen`` is config 5 instead: 64 packed sequences (lengths
 ``default_rng(1).integers(256, 16384, 64, endpoint=True)``, 516,496 tokens)
@@ -32,7 +32,10 @@ installable here) on the same workload, rank 0 only.
 
 Multi-GPU (torchrun, one rank per GPU): each rank decodes its own batch of 64
 sequences (sequence sharding, no collective on the data path), timing is the
-max over ranks, ``scaling`` is weak.
+max over ranks, ``scaling`` is weak. The line's ``"sharded"`` object carries
+the strong-scaled configurations at every world size (N=1 included, as the
+base of the curve): config 5 LPT-sharded by sequence, and config 3 sharded by
+value head with the NCCL all-gather of its outputs timed apart.
 """
 
 from __future__ import annotations
@@ -56,10 +59,22 @@ METRIC = "GDN prefill tok/s & decode state HBM GB/s (% peak) at 1/2/4/8 B200 vs 
 B, HK, HV, D = 64, 16, 32, 128
 STATE_BYTES = 2 * B * HV * D * D * 4  # read + write of the fp32 state
 DECODE_BYTES = STATE_BYTES + 2 * B * HK * D * 2 + B * HV * D * 2 + 2 * B * HV * 4 + B * HV * D * 4
-# DRAM bytes of one decode_kernel launch at config 2, from one ncu capture (read + write).
+# DRAM bytes per decode_kernel launch at config 2 (read + write), from an ncu
+# capture of consecutive launches with the cache left alone between them
+# (see profiles/decode_config2.md).
 DECODE_NCU_TRAFFIC = 135_301_120 + 76_251_648
+DECODE_NCU_SOURCE = ("ncu capture of one launch at config 2 after an L2 flush (dram__bytes_read.sum 135,301,120 + "
+                     "dram__bytes_write.sum 76,251,648; the rest of the state write-back leaves L2 after the launch)")
 PREFILL_T = 8192
 PREFILL_FLOP = 182_955 * PREFILL_T * HV  # chunked WY count per token-head: (10 C^2 d + 6 C d^2 + 2/3 C^3) / C, C = 64, d = 128
+# Algorithmic bytes of one config-3 call: q, k (bf16) + v (bf16) + g, beta (fp32) + y (fp32) + final state (fp32).
+PREFILL_BYTES = 2 * PREFILL_T * HK * D * 2 + PREFILL_T * HV * D * 2 + 2 * PREFILL_T * HV * 4 + PREFILL_T * HV * D * 4 \
+    + HV * D * D * 4
+# Counters of the config-3 prefill kernels from one ncu capture of a call
+# (profiles/chunked_prefill_config3.md): the tensor pipe's share of the scan
+# kernels' active cycles, and the DRAM bytes of all the call's kernels.
+PREFILL_NCU = {"tensor_pipe_frac": None, "traffic": None,
+               "ncu_source": "not captured on this tree yet"}
 
 
 def peaks():
@@ -168,6 +183,18 @@ def cpu_decode_sample(budget_s=10.0):
     return steps, elapsed
 
 
+def mlx_probe():
+    """Whether the reference's own CPU path could run on this host: it needs
+    mlx (``import mlx.core``, mlx 0.32.2 in the reference's lock file) and
+    the reference's sources. Returns a one-line finding for the JSON line."""
+    try:
+        import mlx.core as mx  # noqa: F401
+    except Exception as e:  # ImportError on hosts without mlx
+        return f"import mlx.core failed ({type(e).__name__}: {e}); the torch-CPU restatement is timed instead"
+    return ("import mlx.core succeeded, but the reference's sources are not on this host; the torch-CPU "
+            "restatement is timed instead")
+
+
 def dist_setup(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -198,7 +225,7 @@ def run_reference(args, world, rank):
                        "global_batch": 1, "seq_len": 512, "parallelism": "cpu"},
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
                              "sample": "512 tokens of one config-5 sequence per step (torch-CPU restatement of the "
-                                       "reference's ops path; MLX unavailable on this box)"},
+                                       "reference's ops path); MLX probe: " + mlx_probe()},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
         print(json.dumps(line), flush=True)
@@ -232,14 +259,15 @@ def run_reference(args, world, rank):
                                    "state carried", "global_batch": B, "seq_len": 1, "parallelism": "cpu"},
             "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port",
                              "sample": f"{args.steps} full decode steps of 64 sequences (torch-CPU restatement "
-                                       "of the reference's ops path; MLX unavailable on this box)"},
+                                       "of the reference's ops path); MLX probe: " + mlx_probe()},
             "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
         print(json.dumps(line), flush=True)
 
 
-def measure_prefill(device, iters=3):
-    """Config 3: one sequence of 8192 tokens, bf16 q/k/v, fp32 state from 0."""
+def measure_prefill(device, iters=3, warmup=2):
+    """Config 3: one sequence of 8192 tokens, bf16 q/k/v, fp32 state from 0.
+    Median device time of one call (ms)."""
     import gdn_b200
 
     rng = np.random.default_rng(3)
@@ -253,7 +281,7 @@ def measure_prefill(device, iters=3):
     state = torch.zeros(1, HV, D, D, device=device)
     out = torch.empty(PREFILL_T, HV, D, device=device)
     st_out = torch.empty_like(state)
-    for _ in range(2):
+    for _ in range(warmup):
         gdn_b200.gated_delta_scan_varlen(q, k, v, g, beta, state, g_is_log=True, state_out=st_out, out=out)
     torch.cuda.synchronize()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * iters)]
@@ -556,6 +584,21 @@ def run_attn(args):
                       "dtype": "bf16", "data": "synthetic"}), flush=True)
 
 
+def run_prefill(args):
+    """Only config 3 (one sequence of 8,192 tokens, 16/32 heads of 128, bf16
+    q/k/v, fp32 state from 0), K calls back to back; for profiling the
+    prefill kernels on their own."""
+    device = torch.device("cuda", 0)
+    ms = measure_prefill(device, iters=max(args.steps, 1), warmup=args.warmup)
+    _, tc_peak, _ = peaks()
+    print(json.dumps({"metric": "config-3 prefill tok/s", "value": PREFILL_T / (ms / 1e3), "unit": "tok/s",
+                      "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                      "achieved_tflops": PREFILL_FLOP / (ms / 1e3) / 1e12,
+                      "frac_of_bf16_peak": PREFILL_FLOP / (ms / 1e3) / 1e12 / tc_peak,
+                      "config": {"workload": "config 3: B=1, T=8192, 16/32 heads, d=128, bf16 q/k/v, fp32 out"},
+                      "dtype": "bf16", "data": "synthetic"}), flush=True)
+
+
 def run_layerdecode(args):
     """Only the linear-attention layer at one decode token, launched eagerly
     (one kernel after another, as ncu lists them); for profiling the decode
@@ -626,15 +669,16 @@ def cpu_prefill_sample(n_tokens=512):
     return n_tokens / (time.perf_counter() - t0)
 
 
-def run_varlen(args, world, rank, local):
-    """Config 5 on this rank's share of the sequences (see module docstring)."""
+def varlen_setup(world, rank, device):
+    """Config 5 on this rank's share of the 64 sequences (LPT partition of
+    the lengths): the packed inputs, one prefill over them and 256 decode
+    steps with the carried states. Returns (prefill, decode, info)."""
     import gdn_b200
     from gdn_b200.sharding import lpt_partition
 
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
     lengths = np.random.default_rng(1).integers(256, 16384, size=64, endpoint=True)
-    mine = lpt_partition(lengths, world)[rank]
+    parts = lpt_partition(lengths, world)
+    mine = parts[rank]
     my_len = [int(lengths[i]) for i in mine]
     n_loc = len(my_len)
     n_tok = int(sum(my_len))
@@ -669,7 +713,16 @@ def run_varlen(args, world, rank, local):
                                             dg[i % 4, :n_loc], db[i % 4, :n_loc], state[:n_loc], g_is_log=True,
                                             out=dout[:n_loc])
 
-    for _ in range(args.warmup):
+    loads = [int(sum(int(lengths[i]) for i in p_)) for p_ in parts]
+    info = {"lengths": lengths, "n_decode": n_decode, "tokens": int(lengths.sum()),
+            "lpt_max_over_mean": max(loads) / (sum(loads) / len(loads))}
+    return prefill, decode, info
+
+
+def time_varlen(prefill, decode, steps, warmup, world, device, sampler=None):
+    """Device time (ms, summed over steps, max over ranks) of the config-5
+    prefill and of its decode phase."""
+    for _ in range(warmup):
         prefill()
         decode()
     torch.cuda.synchronize()
@@ -677,9 +730,10 @@ def run_varlen(args, world, rank, local):
         torch.distributed.barrier()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
     pf_ms, dec_ms = 0.0, 0.0
-    sampler = ClockSampler(local)
-    with sampler:
-        for _ in range(args.steps):
+    import contextlib
+
+    with sampler if sampler is not None else contextlib.nullcontext():
+        for _ in range(steps):
             ev[0].record()
             prefill()
             ev[1].record()
@@ -693,7 +747,18 @@ def run_varlen(args, world, rank, local):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         pf_ms, dec_ms = float(t[0]), float(t[1])
         torch.distributed.barrier()
-    total_tok = int(lengths.sum())
+    return pf_ms, dec_ms
+
+
+def run_varlen(args, world, rank, local):
+    """Config 5 on this rank's share of the sequences (see module docstring)."""
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    prefill, decode, info = varlen_setup(world, rank, device)
+    sampler = ClockSampler(local)
+    pf_ms, dec_ms = time_varlen(prefill, decode, args.steps, args.warmup, world, device, sampler)
+    total_tok = info["tokens"]
+    n_decode = info["n_decode"]
     dec_bytes = n_decode * (2 * 64 * HV * D * D * 4)  # state read + write of all 64 sequences per step
     hbm_peak, tc_peak, peak_kind = peaks()
     pf_s = pf_ms / 1e3 / args.steps
@@ -707,19 +772,96 @@ def run_varlen(args, world, rank, local):
                    "global_batch": 64, "seq_len": "256..16384 (packed)", "parallelism": f"sequence-sharded x{world}",
                    "l2": "inputs (4.2 GB of q/k/v) far larger than L2"},
         "prefill": {"ms": pf_ms / args.steps, "achieved_tflops": PREFILL_FLOP / PREFILL_T * total_tok / pf_s / 1e12,
-                    "frac_of_bf16_peak": PREFILL_FLOP / PREFILL_T * total_tok / pf_s / 1e12 / tc_peak},
+                    "frac_of_bf16_peak": PREFILL_FLOP / PREFILL_T * total_tok / pf_s / 1e12 / tc_peak,
+                    "lpt_max_over_mean": info["lpt_max_over_mean"]},
         "decode": {"value": dec_bytes / (dec_ms / 1e3 / args.steps) / 1e9, "unit": "GB/s", "steps": n_decode,
                    "ms": dec_ms / args.steps, "peak": hbm_peak, "peak_kind": peak_kind},
         "clocks": sampler.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = {"value": cpu_prefill_sample(), "unit": "tok/s", "cores": os.cpu_count() or 1,
-                                "kind": "port", "sample": "first 512 tokens of one config-5 sequence (torch-CPU "
-                                "restatement of the reference's ops path, all threads); MLX CPU unavailable"}
+                                "kind": "port", "sample": "first 512 tokens of one config-5-shaped sequence "
+                                "(torch-CPU restatement of the reference's ops path, all threads); MLX probe: "
+                                + mlx_probe()}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def measure_sharded(world, rank, device, steps=3):
+    """The sharded configurations at this world size (every rank takes part,
+    collectives in the same order on all ranks): config 5 LPT-sharded by
+    sequence (strong scaling, no collective), and config 3 sharded by value
+    head (whole GQA groups) with the NCCL all-gather of the outputs timed
+    apart. Device times are max over ranks."""
+    import gdn_b200
+    from gdn_b200.sharding import all_gather_heads, head_shard
+
+    hbm_peak, tc_peak, _ = peaks()
+    res = {}
+    prefill, decode, info = varlen_setup(world, rank, device)
+    pf_ms, dec_ms = time_varlen(prefill, decode, steps, 1, world, device)
+    del prefill, decode
+    pf_s = pf_ms / 1e3 / steps
+    tflops = PREFILL_FLOP / PREFILL_T * info["tokens"] / pf_s / 1e12
+    res["config5"] = {
+        "prefill_tok_s": info["tokens"] / pf_s, "prefill_ms": pf_ms / steps, "prefill_tflops": tflops,
+        "prefill_frac_of_bf16_peak": tflops / tc_peak, "lpt_max_over_mean": info["lpt_max_over_mean"],
+        "decode_gbs": info["n_decode"] * (2 * 64 * HV * D * D * 4) / (dec_ms / 1e3 / steps) / 1e9,
+        "decode_ms": dec_ms / steps, "scaling": "strong",
+        "note": "64 sequences (516,496 tokens) LPT-packed over the ranks, prefill then 256 decode steps per "
+                "sequence; no collective"}
+    torch.cuda.empty_cache()
+
+    # config 3 by value head: this rank's GQA groups, then the all-gather
+    ks, vs = head_shard(HK, HV, rank, world)
+    gen = torch.Generator(device).manual_seed(3)
+    q = torch.nn.functional.normalize(torch.randn(PREFILL_T, HK, D, device=device, generator=gen), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(PREFILL_T, HK, D, device=device, generator=gen), dim=-1)
+    v = torch.randn(PREFILL_T, HV, D, device=device, generator=gen)
+    beta = torch.sigmoid(torch.randn(PREFILL_T, HV, device=device, generator=gen))
+    g = -torch.nn.functional.softplus(torch.randn(PREFILL_T, HV, device=device, generator=gen))
+    ql, kl, vl = (x.bfloat16().contiguous() for x in (q[:, ks], k[:, ks], v[:, vs]))
+    gl, bl = g[:, vs].contiguous(), beta[:, vs].contiguous()
+    out = torch.empty(PREFILL_T, HV // world, D, device=device, dtype=torch.bfloat16)
+
+    def scan():
+        gdn_b200.gated_delta_scan_varlen(ql, kl, vl, gl, bl, None, g_is_log=True, out=out)
+
+    def gather():
+        return all_gather_heads(out, world) if world > 1 else out
+
+    for _ in range(2):
+        scan()
+        gather()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    scan_ms = ag_ms = 0.0
+    for _ in range(steps):
+        ev[0].record()
+        scan()
+        ev[1].record()
+        gather()
+        ev[2].record()
+        torch.cuda.synchronize()
+        scan_ms += ev[0].elapsed_time(ev[1])
+        ag_ms += ev[1].elapsed_time(ev[2])
+    if world > 1:
+        t = torch.tensor([scan_ms, ag_ms, scan_ms + ag_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        scan_ms, ag_ms, tot_ms = (float(x) for x in t)
+        torch.distributed.barrier()
+    else:
+        tot_ms = scan_ms + ag_ms
+    res["config3_head_sharded"] = {
+        "tok_s": PREFILL_T / (tot_ms / 1e3 / steps), "ms": tot_ms / steps, "scan_ms": scan_ms / steps,
+        "all_gather_ms": ag_ms / steps, "heads_per_rank": HV // world, "scaling": "strong",
+        "note": "T=8192, value heads split over the ranks with their key heads, bf16 outputs all-gathered "
+                "(NCCL all_gather_into_tensor) into [8192, 32, 128] on every rank"}
+    return res
 
 
 def main():
@@ -731,17 +873,21 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="decode only: no e2e, prefill or CPU legs (for profiler runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiler runs)")
-    ap.add_argument("--workload", choices=["decode", "varlen", "qproj", "attn", "layerdecode"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "varlen", "prefill", "qproj", "attn", "layerdecode"],
+                    default="decode")
     ap.add_argument("--tokens", type=int, default=4096, help="rows of x for --workload qproj / attn")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.workload in ("qproj", "attn", "layerdecode"):
+    if args.workload in ("qproj", "attn", "layerdecode", "prefill"):
         if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the reference's quantized matmul and attention "
-                              "are MLX's (mx.quantized_matmul, mx.fast.scaled_dot_product_attention), not "
-                              "installable on this box"}), flush=True)
+            why = ("a profiling workload of this build's own kernels; the reference arm times config 2 (default) "
+                   "and config 5 (--workload varlen)") if args.workload == "prefill" else (
+                   "the reference's quantized matmul and attention are MLX's (mx.quantized_matmul, "
+                   "mx.fast.scaled_dot_product_attention), not installable on this box")
+            print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
             return
-        return {"qproj": run_qproj, "attn": run_attn, "layerdecode": run_layerdecode}[args.workload](args)
+        return {"qproj": run_qproj, "attn": run_attn, "layerdecode": run_layerdecode,
+                "prefill": run_prefill}[args.workload](args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)
@@ -788,31 +934,45 @@ def main():
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # Timed region: K decode steps back to back with the state carried in
+    # place, as config 2 defines its workload (consecutive steps); the 128 MiB
+    # state is larger than L2, and each step also drains the write-back the
+    # step before it left in L2.
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     sampler = ClockSampler(local)
     with sampler:
+        e0.record()
         for i in range(args.steps):
-            flush_w.fill_(i & 0xFF)  # evict the state from L2 between timed steps
-            flush_r.sum()
-            starts[i].record()
             step(i)
-            ends[i].record()
+        e1.record()
         torch.cuda.synchronize()
     if world > 1:
         torch.distributed.barrier()
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    total_ms = sum(step_ms)
+    own_ms = e0.elapsed_time(e1)
+    total_ms = own_ms
     if world > 1:
         t = torch.tensor([total_ms], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         total_ms = float(t.item())
     value = world * DECODE_BYTES * args.steps / (total_ms / 1e3) / 1e9
     mean_ms = total_ms / args.steps
-    achieved = DECODE_BYTES / (statistics.mean(step_ms) / 1e3) / 1e9
+    achieved = DECODE_BYTES / (own_ms / args.steps / 1e3) / 1e9
+
+    # The same launches one at a time, L2 flushed before each (per-launch
+    # figure with no write-back of an earlier step inside the kernel's time).
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    for i in range(args.steps):
+        flush_w.fill_(i & 0xFF)
+        flush_r.sum()
+        starts[i].record()
+        step(i)
+        ends[i].record()
+    torch.cuda.synchronize()
+    flushed_ms = statistics.mean(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
 
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -820,19 +980,23 @@ def main():
         "vs_baseline": None, "dtype": "f32 state / bf16 q,k,v",
         "data": "synthetic (seeded; config 2 value distributions)",
         "config": {"workload": "decode, config 2: B=64 sequences x 1 token per rank, 16/32 heads, d=128, "
-                               "fp32 state [64,32,128,128] carried in place",
+                               "fp32 state [64,32,128,128] carried in place, steps back to back",
                    "global_batch": B * world, "seq_len": 1, "parallelism": f"sequence-sharded x{world}",
-                   "l2": "flushed before every timed step (256 MiB write, then 256 MiB read so no dirty "
-                         "flush lines remain)"},
+                   "l2": "not flushed: the 128 MiB state is larger than L2 and every step reads and rewrites "
+                         "all of it (the flushed per-launch figure is under roofline.flushed)"},
         "gpu_launches": args.steps,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": DECODE_NCU_TRAFFIC,
-                     "traffic_source": "one ncu capture of this kernel at config 2 (dram__bytes_read.sum "
-                                       "135,301,120 + dram__bytes_write.sum 76,251,648; the rest of the "
-                                       "state write-back leaves L2 after the launch)",
+                     "traffic_source": DECODE_NCU_SOURCE,
                      "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6.65 TB/s",
-                     "bytes_per_launch": DECODE_BYTES, "kernel": "decode_kernel<128, bf16>"},
+                     "bytes_per_launch": DECODE_BYTES, "kernel": "decode_kernel<128, bf16>",
+                     "timing": "back-to-back launches, one event pair around the timed region / K",
+                     "flushed": {"ms_per_launch": flushed_ms,
+                                 "achieved": DECODE_BYTES / (flushed_ms / 1e3) / 1e9,
+                                 "frac": DECODE_BYTES / (flushed_ms / 1e3) / 1e9 / hbm_peak,
+                                 "note": "L2 flushed before each launch (256 MiB write, then 256 MiB read); "
+                                         "part of each launch's state write-back leaves L2 after it ends"}},
         "clocks": sampler.summary(),
     }
 
@@ -892,11 +1056,15 @@ def main():
 
         # --- config 3 prefill (secondary metric) --------------------------
         pf_ms = measure_prefill(device)
+        pf_tflops = PREFILL_FLOP / (pf_ms / 1e3) / 1e12
         line["prefill"] = {"value": PREFILL_T / (pf_ms / 1e3), "unit": "tok/s", "ms": pf_ms,
                            "config": "config 3: B=1, T=8192, 16/32 heads, d=128, bf16 q/k/v, fp32 state from 0",
-                           "achieved_tflops": PREFILL_FLOP / (pf_ms / 1e3) / 1e12,
-                           "frac_of_bf16_peak": PREFILL_FLOP / (pf_ms / 1e3) / 1e12 / tc_peak,
-                           "algo": "auto"}
+                           "achieved_tflops": pf_tflops, "frac_of_bf16_peak": pf_tflops / tc_peak, "algo": "auto",
+                           "roofline": {"bound": "tensor", "achieved": pf_tflops, "peak": tc_peak, "unit": "TFLOP/s",
+                                        "frac": pf_tflops / tc_peak,
+                                        "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops, burst)",
+                                        "flop_per_call": PREFILL_FLOP, "bytes_per_call": PREFILL_BYTES,
+                                        **PREFILL_NCU}}
 
         # --- config 4 fused block (secondary) --------------------------------
         blk_ms, blk_tok = measure_block(device)
@@ -928,15 +1096,23 @@ def main():
                       "decode_us: the same layer (Qwen3_5LinearAttention with a RecurrentCache) at one "
                       "decode token, device time of a CUDA-graph replay"}
 
+        # --- the sharded configurations at this world size -----------------
+        line["sharded"] = measure_sharded(world, rank, device)
+
         # --- CPU baseline (rank 0, N=1 only) --------------------------------
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             steps_cpu, secs = cpu_decode_sample()
+            mlx = mlx_probe()
             line["cpu_baseline"] = {
                 "value": DECODE_BYTES * steps_cpu / secs / 1e9, "unit": "GB/s", "cores": os.cpu_count() or 1,
                 "kind": "port",
                 "sample": f"{steps_cpu} decode steps x 64 sequences in {secs:.1f} s: torch-CPU restatement of the "
                           "reference's ops path (qw/gated_delta.py:24-41,93-109), one call per sequence; "
-                          "MLX CPU unavailable on this box"}
+                          f"MLX probe on this host: {mlx}",
+                "mlx_probe": mlx,
+                "prefill_tok_s": cpu_prefill_sample(),
+                "prefill_sample": "the first 512 tokens of a config-3-shaped sequence (16/32 heads of 128, "
+                                  "state from N(0, 0.02)), the same restatement, all threads"}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -210,7 +210,11 @@ gdn_status gdn_fused_block(const gdn_block_args *args, gdn_stream_t stream);
  *    anything runs; split them into calls over fewer tokens.
  *  - The first call on each device looks up the array's device address
  *    (cudaGetSymbolAddress, with that device current) and caches it; make
- *    that first call before any stream capture.
+ *    that first call before any stream capture.  The cache is keyed by the
+ *    device ordinal and is never refreshed: after cudaDeviceReset (or
+ *    anything else that destroys and recreates the device's primary
+ *    context) the cached address is stale, so a process that resets a
+ *    device must not call this entry point on it again.
  *  - All calls share the one array.  Calls that can overlap on the GPU
  *    (different streams, or several host threads) race on it: serialise them,
  *    e.g. on one stream.  The array keeps the last call's data; nothing in it

@@ -7,6 +7,7 @@
 #include <string>
 
 #include "gdn_common.cuh"
+#include "gdn_testing.h"
 
 namespace {
 
@@ -367,6 +368,23 @@ gdn_status gdn_fused_block(const gdn_block_args* args, gdn_stream_t stream) {
   if (st != GDN_OK) return st;
   if (sp.z) return GDN_OK;  // the scan's output stage did the gated norm
   return cuda_status(gdn::launch_block_epilogue(p, s), "block epilogue launch");
+}
+
+gdn_status gdn_test_set_wait_limit(uint64_t ns) {
+  unsigned long long cur = 0;
+  int fault = 0;
+  cudaError_t e = gdn::read_test_hooks(&cur, &fault);
+  if (e == cudaSuccess) e = gdn::set_test_hooks(ns, fault);
+  return cuda_status(e, "setting the wait limit");
+}
+
+gdn_status gdn_test_inject_fault(int32_t fault) {
+  if (fault < 0 || fault > 1) return fail(GDN_EINVAL, "unknown test fault %d", (int)fault);
+  unsigned long long cur = 0;
+  int old = 0;
+  cudaError_t e = gdn::read_test_hooks(&cur, &old);
+  if (e == cudaSuccess) e = gdn::set_test_hooks(cur, fault);
+  return cuda_status(e, "setting the test fault");
 }
 
 gdn_status gdn_check_device_errors(gdn_stream_t stream) {

@@ -745,14 +745,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_mma_kernel(const AttnPara
 
 template <int HD>
 gdn_status launch_mma(const AttnParams& p, cudaStream_t s) {
-  static bool attr = false;
+  static DeviceFlags attr;
   constexpr size_t smem = MmaSmem<HD>::kBytes;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return set_error(GDN_ECUDA, "attention: shared-memory attribute");
-    attr = true;
-  }
+  if (ensure_smem_attr(attn_mma_kernel<HD>, smem, attr) != cudaSuccess)
+    return set_error(GDN_ECUDA, "attention: shared-memory attribute");
   const int64_t qtiles = (p.n_tokens + kMQ - 1) / kMQ;
   if (qtiles > 65535) return set_error(GDN_EUNSUPPORTED, "attention: at most %d tokens per call", 65535 * kMQ);
   const dim3 grid((unsigned)p.heads, (unsigned)qtiles);
@@ -968,14 +964,10 @@ __global__ void __launch_bounds__(kDWarps * 32) attn_dec_mma_kernel(const AttnPa
 
 template <int HD>
 gdn_status launch_dec_mma(const AttnParams& p, cudaStream_t s) {
-  static bool attr = false;
+  static DeviceFlags attr;
   constexpr size_t smem = DecSmem<HD>::kBytes;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_dec_mma_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return set_error(GDN_ECUDA, "attention: shared-memory attribute");
-    attr = true;
-  }
+  if (ensure_smem_attr(attn_dec_mma_kernel<HD>, smem, attr) != cudaSuccess)
+    return set_error(GDN_ECUDA, "attention: shared-memory attribute");
   const dim3 grid((unsigned)((p.splits + kDWarps - 1) / kDWarps), (unsigned)p.kv_heads);
   const cudaError_t e = launch_dependent(attn_dec_mma_kernel<HD>, grid, dim3(kDWarps * 32), smem, s, p);
   if (e != cudaSuccess) return set_error(GDN_ECUDA, "attention launch: %s", cudaGetErrorString(e));
@@ -984,14 +976,10 @@ gdn_status launch_dec_mma(const AttnParams& p, cudaStream_t s) {
 
 template <typename T, int HD>
 gdn_status launch_fwd(const AttnParams& p, dim3 grid, cudaStream_t s) {
-  static bool attr = false;  // set once per instance (a repeat from a racing thread is harmless)
+  static DeviceFlags attr;
   constexpr size_t smem = AttnSmem<T, HD>::kBytes;
-  if (!attr) {
-    if (cudaFuncSetAttribute(attn_fwd_kernel<T, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess)
-      return set_error(GDN_ECUDA, "attention: shared-memory attribute");
-    attr = true;
-  }
+  if (ensure_smem_attr(attn_fwd_kernel<T, HD>, smem, attr) != cudaSuccess)
+    return set_error(GDN_ECUDA, "attention: shared-memory attribute");
   const cudaError_t e = launch_dependent(attn_fwd_kernel<T, HD>, grid, dim3(kWarps * 32), smem, s, p);
   if (e != cudaSuccess) return set_error(GDN_ECUDA, "attention launch: %s", cudaGetErrorString(e));
   return GDN_OK;

@@ -48,6 +48,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 #include "gdn_common.cuh"
 #include "gdn_sm100.cuh"
@@ -57,13 +58,20 @@ namespace gdn {
 // Error word written by bounded device-side waits (0 = no error).
 __device__ unsigned g_device_error = 0;
 
+// Limit of every bounded wait in the chunked kernels (2 s unless a test
+// shortens it through gdn_test_set_wait_limit), and the fault a test may
+// inject (gdn_test_inject_fault; 0 = none).  Both are read once per CTA.
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;
+__device__ unsigned long long g_wait_limit_ns = kDefaultWaitNs;
+__device__ int g_test_fault = 0;
+constexpr int kFaultWithholdV = 1;  // the scan's producer never issues (nor arrives for) chunk 0's V tile
+
 namespace {
 
 using namespace sm100;
 
 constexpr int CH = 64;   // chunk length
 constexpr int DH = 128;  // head dim (Dk = Dv)
-constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr uint32_t kTile64 = 64 * 64 * 2;          // 64 x 64 bf16 operand tile (8 KB)
 constexpr uint32_t kGateBytes = 1024;               // beta[64], exp G[64], exp(G_last - G)[64], gamma
 // Per (chunk, head): T hi, T lo, P hi, P lo, gates.
@@ -250,6 +258,7 @@ __device__ __forceinline__ void prep_level1(float* sA, float* sT, int tid) {
 __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constant__ CUtensorMap qmap,
                                                             const __grid_constant__ CUtensorMap kmap,
                                                             const ChunkParams p) {
+  const uint64_t wait_ns = g_wait_limit_ns;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sKQ = base;                                        // [K;Q] 128 rows x 128, SW128
@@ -326,7 +335,7 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
 
   bool mma_issued = false;
   if (tid == 0) {
-    if (mbar_wait(&bar_load, 0, kWaitNs)) {
+    if (mbar_wait(&bar_load, 0, wait_ns)) {
       tc_fence_after();
       const uint32_t idesc = idesc_bf16_f32(128, 64);
 #pragma unroll
@@ -343,12 +352,12 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
     }
   }
   __syncthreads();
-  const bool ok = !abort_flag && mbar_wait(&bar_mma, 0, kWaitNs);
+  const bool ok = !abort_flag && mbar_wait(&bar_mma, 0, wait_ns);
   if (!ok && tid == 0) record_error(&abort_flag);
   __syncthreads();
   if (abort_flag) {
-    if (tid == 0 && mma_issued) mbar_wait(&bar_mma, 0, kWaitNs);
-    if (tid == 0) mbar_wait(&bar_load, 0, kWaitNs);
+    if (tid == 0 && mma_issued) mbar_wait(&bar_mma, 0, wait_ns);
+    if (tid == 0) mbar_wait(&bar_load, 0, wait_ns);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 64);
@@ -552,6 +561,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
                                                             const __grid_constant__ CUtensorMap omap,
                                                             const __grid_constant__ CUtensorMap zmap,
                                                             const ChunkParams p) {
+  const uint64_t wait_ns = g_wait_limit_ns;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t bars[N_BARS];
@@ -620,13 +630,14 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       }
       // Loads issued per full barrier (each barrier has at most one in flight).
       uint32_t n_kq = 0, n_v = 0, n_t = 0, n_p = 0;
+      const bool withhold_v = g_test_fault == kFaultWithholdV;
       for (int64_t c = 0; c < nch; ++c) {
         const uint32_t par = (uint32_t)((c - 1) & 1);
         if (lane == 0) {
           const int t0 = (int)(start + c * CH);
           const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
           do {
-            if (c > 0 && !mbar_wait(&bars[B_KQ_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+            if (c > 0 && !mbar_wait(&bars[B_KQ_EMPTY], par, wait_ns)) record_error(&abort_flag);
             if (abort_flag) break;
             mbar_arrive_expect_tx(&bars[B_KQ_FULL], 32768 + kGateBytes);
             for (int kb = 0; kb < 2; ++kb) {
@@ -635,22 +646,25 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
             }
             bulk_load(base + OFF_GATES + (c & 1) * kGateBytes, rec + 4 * kTile64, kGateBytes, &bars[B_KQ_FULL]);
             ++n_kq;
-            if (c > 0 && !mbar_wait(&bars[B_V_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+            if (c > 0 && !mbar_wait(&bars[B_V_EMPTY], par, wait_ns)) record_error(&abort_flag);
             if (abort_flag) break;
-            if (flags & kChainZeroV) {
+            if (withhold_v && c == 0) {
+              // test fault: V_FULL never completes, so the waits on it run out
+            } else if (flags & kChainZeroV) {
               mbar_arrive(&bars[B_V_FULL]);
+              ++n_v;
             } else {
               mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
               tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
+              ++n_v;
             }
-            ++n_v;
             // T and P once the previous chunk's Delta and O MMAs have read theirs.
-            if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+            if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, wait_ns)) record_error(&abort_flag);
             if (abort_flag) break;
             mbar_arrive_expect_tx(&bars[B_T_FULL], 2 * kTile64);
             bulk_load(base + OFF_T, rec, 2 * kTile64, &bars[B_T_FULL]);
             ++n_t;
-            if (c > 0 && !mbar_wait(&bars[B_P_EMPTY], par, kWaitNs)) record_error(&abort_flag);
+            if (c > 0 && !mbar_wait(&bars[B_P_EMPTY], par, wait_ns)) record_error(&abort_flag);
             if (abort_flag) break;
             mbar_arrive_expect_tx(&bars[B_P_FULL], 2 * kTile64);
             bulk_load(base + OFF_P, rec + 2 * kTile64, 2 * kTile64, &bars[B_P_FULL]);
@@ -663,8 +677,8 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           if (lane == 0) mbar_arrive(&bars[B_KQ_EMPTY]);
           continue;
         }
-        const bool ok = mbar_wait(&bars[B_KQ_FULL], (uint32_t)(c & 1), kWaitNs) &&
-                        (c == 0 || mbar_wait(&bars[B_U_DONE], par, kWaitNs));
+        const bool ok = mbar_wait(&bars[B_KQ_FULL], (uint32_t)(c & 1), wait_ns) &&
+                        (c == 0 || mbar_wait(&bars[B_U_DONE], par, wait_ns));
         if (!__all_sync(0xffffffffu, ok)) {
           if (lane == 0) record_error(&abort_flag);
           break;
@@ -690,10 +704,10 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       // After an abort, let the copies this thread started land (bounded)
       // before the CTA releases its shared memory.
       if (lane == 0 && abort_flag) {
-        if (n_kq) mbar_wait(&bars[B_KQ_FULL], (n_kq - 1) & 1, kWaitNs);
-        if (n_v) mbar_wait(&bars[B_V_FULL], (n_v - 1) & 1, kWaitNs);
-        if (n_t) mbar_wait(&bars[B_T_FULL], (n_t - 1) & 1, kWaitNs);
-        if (n_p) mbar_wait(&bars[B_P_FULL], (n_p - 1) & 1, kWaitNs);
+        if (n_kq) mbar_wait(&bars[B_KQ_FULL], (n_kq - 1) & 1, wait_ns);
+        if (n_v) mbar_wait(&bars[B_V_FULL], (n_v - 1) & 1, wait_ns);
+        if (n_t) mbar_wait(&bars[B_T_FULL], (n_t - 1) & 1, wait_ns);
+        if (n_p) mbar_wait(&bars[B_P_FULL], (n_p - 1) & 1, wait_ns);
       }
     }
   } else if (warp == 1) {
@@ -712,8 +726,8 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         // [X | Y] = S [K | Q]^T, one K-block (64 of Dk) at a time as the
         // epilogue finishes converting it; Y is free to overwrite once the
         // output warps have read the previous chunk's.
-        if (!mbar_wait(&bars[B_KQ_FULL], par, kWaitNs) ||
-            (c > 0 && !mbar_wait(&bars[B_Y_FREE], (uint32_t)((c - 1) & 1), kWaitNs))) {
+        if (!mbar_wait(&bars[B_KQ_FULL], par, wait_ns) ||
+            (c > 0 && !mbar_wait(&bars[B_Y_FREE], (uint32_t)((c - 1) & 1), wait_ns))) {
           record_error(&abort_flag);
           break;
         }
@@ -721,7 +735,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           bool stop = false;
           int n = 0;
           for (int kb = 0; kb < 2; ++kb) {
-            if (!mbar_wait(&bars[kb == 0 ? B_S_READY0 : B_S_READY1], par, kWaitNs)) {
+            if (!mbar_wait(&bars[kb == 0 ? B_S_READY0 : B_S_READY1], par, wait_ns)) {
               record_error(&abort_flag);
               stop = true;
               break;
@@ -739,14 +753,14 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         // Delta^T = R_hi [T_hi; T_lo]^T (N = 128) + R_lo T_hi^T (N = 64), R from
         // TMEM: K steps {0, 2} (tokens 0-15, 32-47) once the first half of R is
         // in, then {1, 3}.
-        if (!mbar_wait(&bars[B_T_FULL], par, kWaitNs)) {
+        if (!mbar_wait(&bars[B_T_FULL], par, wait_ns)) {
           record_error(&abort_flag);
           break;
         }
         {
           bool stop = false;
           for (int rh = 0; rh < 2; ++rh) {
-            if (!mbar_wait(&bars[rh == 0 ? B_R_READY0 : B_R_READY1], par, kWaitNs)) {
+            if (!mbar_wait(&bars[rh == 0 ? B_R_READY0 : B_R_READY1], par, wait_ns)) {
               record_error(&abort_flag);
               stop = true;
               break;
@@ -763,7 +777,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         }
         mma_commit(&bars[B_D_DONE]);
         mma_commit(&bars[B_T_EMPTY]);
-        if (!mbar_wait(&bars[B_DD_READY], par, kWaitNs) || !mbar_wait(&bars[B_KT_READY], par, kWaitNs)) {
+        if (!mbar_wait(&bars[B_DD_READY], par, wait_ns) || !mbar_wait(&bars[B_KT_READY], par, wait_ns)) {
           record_error(&abort_flag);
           break;
         }
@@ -776,8 +790,8 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
               mma_bf16_ts(tmem + TM_S, tDP[part] + ks * 8, sdesc_sw128(sKt + ks * 32), id128, true);
         }
         mma_commit(&bars[B_U_DONE]);
-        if (!mbar_wait(&bars[B_P_FULL], par, kWaitNs) ||
-            (c > 0 && !mbar_wait(&bars[B_O_FREE], (uint32_t)((c - 1) & 1), kWaitNs))) {
+        if (!mbar_wait(&bars[B_P_FULL], par, wait_ns) ||
+            (c > 0 && !mbar_wait(&bars[B_O_FREE], (uint32_t)((c - 1) & 1), wait_ns))) {
           record_error(&abort_flag);
           break;
         }
@@ -794,7 +808,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       }
       // Wait for every MMA issued so far before the CTA winds down.
       mma_commit(&bars[B_DRAIN]);
-      mbar_wait(&bars[B_DRAIN], 0, kWaitNs);
+      mbar_wait(&bars[B_DRAIN], 0, wait_ns);
     }
   } else if (warp < 10) {
     // ------------------------------------------------------- state-chain epilogue
@@ -846,12 +860,12 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
 
       // Gates of this chunk arrive with K and Q.
-      bool ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
+      bool ok = mbar_wait(&bars[B_KQ_FULL], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
 
       // R = beta (V - X exp(G)), tokens 32*half .. +32 of row dv.
-      ok = mbar_wait(&bars[B_X_DONE], par, kWaitNs) && mbar_wait(&bars[B_V_FULL], par, kWaitNs);
+      ok = mbar_wait(&bars[B_X_DONE], par, wait_ns) && mbar_wait(&bars[B_V_FULL], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
@@ -911,7 +925,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       }
 
       // Delta -> bf16 hi/lo operand.
-      ok = mbar_wait(&bars[B_D_DONE], par, kWaitNs);
+      ok = mbar_wait(&bars[B_D_DONE], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
@@ -948,7 +962,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
 
       // The updated S -> its hi/lo operand for the next chunk, one K-block per
       // pass so that the next X/Y MMA can start on the first.
-      ok = mbar_wait(&bars[B_U_DONE], par, kWaitNs);
+      ok = mbar_wait(&bars[B_U_DONE], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
@@ -1023,7 +1037,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         // 8 dk), four per ldmatrix/stmatrix pair, eight pairs per warp.  The
         // previous state update has read the last K^T: this group passed its
         // output stage, which follows it.
-        ok = mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
+        ok = mbar_wait(&bars[B_KQ_FULL], par, wait_ns);
         if (!ok) record_error(&abort_flag);
         if (named_sync_or(2, kAuxThreads, !ok)) break;
         const int r = lane & 7, m = lane >> 3;
@@ -1040,7 +1054,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         if (leader) mbar_arrive(&bars[B_KT_READY]);
       }
       // Y (the gates, read below, came with K and Q).
-      ok = mbar_wait(&bars[B_X_DONE], par, kWaitNs) && mbar_wait(&bars[B_KQ_FULL], par, kWaitNs);
+      ok = mbar_wait(&bars[B_X_DONE], par, wait_ns) && mbar_wait(&bars[B_KQ_FULL], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(2, kAuxThreads, !ok)) break;
       tc_fence_after();
@@ -1064,7 +1078,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
       }
 
       // Output: y_t += O_t (both accumulator parts), then store.
-      ok = mbar_wait(&bars[B_OU_DONE], par, kWaitNs);
+      ok = mbar_wait(&bars[B_OU_DONE], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(2, kAuxThreads, !ok)) break;
       tc_fence_after();
@@ -1097,7 +1111,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
             st16[i * DH + dv] = (unsigned short)(w2 & 0xFFFFu);
             st16[(i + 1) * DH + dv] = (unsigned short)(w2 >> 16);
           }
-          ok = mbar_wait(&bars[B_Z_FULL0 + (c & 1)], (uint32_t)((c >> 1) & 1), kWaitNs);
+          ok = mbar_wait(&bars[B_Z_FULL0 + (c & 1)], (uint32_t)((c >> 1) & 1), wait_ns);
           if (!ok) record_error(&abort_flag);
           if (named_sync_or(2, kAuxThreads, !ok)) break;  // every row is staged, z has landed
           const int g8 = (e & 15) * 8;
@@ -1212,7 +1226,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     // barrier i & 1; waiting for a completed phase returns at once).
     if (leader)
       for (int64_t i = n_z - 2 < 0 ? 0 : n_z - 2; i < n_z; ++i)
-        mbar_wait(&bars[B_Z_FULL0 + (i & 1)], (uint32_t)((i >> 1) & 1), kWaitNs);
+        mbar_wait(&bars[B_Z_FULL0 + (i & 1)], (uint32_t)((i >> 1) & 1), wait_ns);
   }
 
   tc_fence_before();
@@ -1339,27 +1353,34 @@ __global__ void __launch_bounds__(256) state_combine_kernel(const float* __restr
 }
 
 // A second stream (and its fork / join events) per device, made on first use.
+// Every caller on a device shares them, so a caller holds `lock` from the
+// fork record to its wait on the join: another caller's record of either
+// event cannot then land between this caller's record and its wait (the
+// events are not reused until both waits have been enqueued, and a wait
+// enqueues the event's state at the time of the call).
 struct SideStream {
   cudaStream_t stream;
   cudaEvent_t fork, join;
+  std::mutex lock;
+  bool made;
 };
 SideStream* side_stream() {
-  constexpr int kMaxDevices = 64;
   static SideStream streams[kMaxDevices];
-  static bool made[kMaxDevices];
+  static std::mutex create;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  if (!made[dev]) {
-    SideStream& x = streams[dev];
+  std::lock_guard<std::mutex> g(create);
+  SideStream& x = streams[dev];
+  if (!x.made) {
     int lo = 0, hi = 0;  // numerically greatest = lowest priority
     if (cudaDeviceGetStreamPriorityRange(&lo, &hi) != cudaSuccess ||
         cudaStreamCreateWithPriority(&x.stream, cudaStreamNonBlocking, lo) != cudaSuccess ||
         cudaEventCreateWithFlags(&x.fork, cudaEventDisableTiming) != cudaSuccess ||
         cudaEventCreateWithFlags(&x.join, cudaEventDisableTiming) != cudaSuccess)
       return nullptr;
-    made[dev] = true;
+    x.made = true;
   }
-  return &streams[dev];
+  return &x;
 }
 
 // Segments for one scan (1 = run it whole): only a single dense sequence whose
@@ -1446,15 +1467,14 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   p.norm_w = sp.norm_w;
   p.norm_eps = sp.norm_eps;
 
-  static bool attrs_set = false;
-  if (!attrs_set) {
-    cudaError_t e = cudaFuncSetAttribute(chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPrepSmem);
+  {
+    static DeviceFlags prep_attr, scan_attr, comb_attr;
+    cudaError_t e = ensure_smem_attr(chunk_prep_kernel, kPrepSmem, prep_attr);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kScanSmem);
+    e = ensure_smem_attr(chunk_scan_kernel, kScanSmem, scan_attr);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(state_combine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kCombineSmem);
+    e = ensure_smem_attr(state_combine_kernel, kCombineSmem, comb_attr);
     if (e != cudaSuccess) return e;
-    attrs_set = true;
   }
   p.n_chains = 0;
   const int P = seg_count(sp);
@@ -1487,6 +1507,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   // on the SMs phase 1 leaves free.
   SideStream* side = side_stream();
   if (!side) return cudaErrorNotReady;
+  std::lock_guard<std::mutex> side_guard(side->lock);  // fork record .. join wait
   const int64_t nch_all = (N + CH - 1) / CH;
   const int64_t last0 = (nch_all * (P - 1) / P);  // first chunk of the last segment
   {
@@ -1542,6 +1563,19 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   for (int i = 1; i <= P - 1; ++i) p3.chains[i - 1] = {i, W + (i - 1) * hstate, i == P - 1 ? sp.state_out : nullptr, 0};
   chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p3);
   return cudaGetLastError();
+}
+
+cudaError_t set_test_hooks(unsigned long long wait_ns, int fault) {
+  if (!wait_ns) wait_ns = kDefaultWaitNs;
+  cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &wait_ns, sizeof(wait_ns));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyToSymbol(g_test_fault, &fault, sizeof(fault));
+}
+
+cudaError_t read_test_hooks(unsigned long long* wait_ns, int* fault) {
+  cudaError_t e = cudaMemcpyFromSymbol(wait_ns, g_wait_limit_ns, sizeof(*wait_ns));
+  if (e != cudaSuccess) return e;
+  return cudaMemcpyFromSymbol(fault, g_test_fault, sizeof(*fault));
 }
 
 cudaError_t read_and_clear_device_error(unsigned* code) {

@@ -6,11 +6,36 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 #include "gdn_api.h"
 
 namespace gdn {
+
+// ---------------------------------------------------------------------------
+// Per-device one-time set-up.  Function attributes (the opt-in to more than
+// 48 KB of dynamic shared memory) belong to each device's context, so one
+// process driving several GPUs must set them on every device it launches on.
+// The flags are atomics: host threads may launch concurrently; a repeat of
+// cudaFuncSetAttribute from a racing thread is harmless.
+// ---------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+struct DeviceFlags {
+  std::atomic<bool> set[kMaxDevices];
+};
+
+template <typename K>
+cudaError_t ensure_smem_attr(K* kernel, size_t bytes, DeviceFlags& flags) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const bool cached = dev >= 0 && dev < kMaxDevices;
+  if (cached && flags.set[dev].load(std::memory_order_acquire)) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess && cached) flags.set[dev].store(true, std::memory_order_release);
+  return e;
+}
 
 // ---------------------------------------------------------------------------
 // Element loads/stores with conversion to/from float
@@ -192,6 +217,10 @@ size_t chunked_workspace_bytes(const ScanParams& p);
 cudaError_t launch_chunked_scan(const ScanParams& p, cudaStream_t s);
 // Reads and clears the device error word of the chunked kernels (0 = none).
 cudaError_t read_and_clear_device_error(unsigned* code);
+// Test hooks of the chunked kernels (gdn_testing.h): wait limit (0 = the
+// default) and injected fault, on the current device.
+cudaError_t set_test_hooks(unsigned long long wait_ns, int fault);
+cudaError_t read_test_hooks(unsigned long long* wait_ns, int* fault);
 cudaError_t read_and_clear_qlinear_error(unsigned* code);
 
 }  // namespace gdn

@@ -656,14 +656,10 @@ gdn_status q_cuda(cudaError_t e, const char* what) {
 
 template <int BITS, int WARPS, int NT>
 gdn_status gv_launch_one(const GvParams& g, unsigned grid, size_t smem, cudaStream_t cs) {
-  static bool attr = false;  // set once per instance (a repeat from a racing thread is harmless)
-  if (!attr) {
-    const gdn_status st = q_cuda(cudaFuncSetAttribute(qgemv_kernel<BITS, WARPS, NT>,
-                                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGvMaxSmem),
-                                 "quantized_linear attribute");
-    if (st != GDN_OK) return st;
-    attr = true;
-  }
+  static DeviceFlags attr;
+  const gdn_status st =
+      q_cuda(ensure_smem_attr(qgemv_kernel<BITS, WARPS, NT>, kGvMaxSmem, attr), "quantized_linear attribute");
+  if (st != GDN_OK) return st;
   return q_cuda(launch_dependent(qgemv_kernel<BITS, WARPS, NT>, dim3(grid), dim3(WARPS * 32), smem, cs, g),
                 "quantized_linear launch");
 }
@@ -725,14 +721,9 @@ extern "C" gdn_status gdn_quantized_linear(const gdn_qlinear_args* a, gdn_stream
       !gdn::q_map(&wmap, a->w, CU_TENSOR_MAP_DATA_TYPE_UINT32, kw, a->n, kw * 4, 64 * a->bits / 32, 256, false) ||
       !gdn::q_map(&omap, a->out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, a->n, a->m, a->out_stride_m * 2, 64, 128, true))
     return gdn::set_error(GDN_ECUDA, "quantized_linear: tensor map encoding failed");
-  static bool attr = false;
-  if (!attr) {
-    st = gdn::q_cuda(cudaFuncSetAttribute(gdn::qlinear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)gdn::kQSmem),
-                     "quantized_linear attribute");
-    if (st != GDN_OK) return st;
-    attr = true;
-  }
+  static gdn::DeviceFlags attr;
+  st = gdn::q_cuda(gdn::ensure_smem_attr(gdn::qlinear_kernel, gdn::kQSmem, attr), "quantized_linear attribute");
+  if (st != GDN_OK) return st;
   CUtensorMap smap, bmap;
   std::memset(&smap, 0, sizeof(smap));
   std::memset(&bmap, 0, sizeof(bmap));

@@ -1,4 +1,5 @@
-"""ctypes binding of libgdn_b200.so (the C ABI declared in include/gdn_api.h).
+"""ctypes binding of libgdn_b200.so (the C ABI declared in include/gdn_api.h,
+and the test hooks of include/gdn_testing.h).
 
 The library is the only compute path: if it is missing or CUDA is not usable,
 calls raise; there is no CPU fallback.
@@ -107,6 +108,8 @@ EXPORTS = {
     "gdn_attention_workspace_size": (_enum, [ctypes.POINTER(AttnArgs), ctypes.POINTER(ctypes.c_size_t)]),
     "gdn_attention": (_enum, [ctypes.POINTER(AttnArgs), _p]),
     "gdn_check_device_errors": (_enum, [_p]),
+    "gdn_test_set_wait_limit": (_enum, [ctypes.c_uint64]),
+    "gdn_test_inject_fault": (_enum, [_i32]),
 }
 
 _lib = None

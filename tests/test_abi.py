@@ -1,13 +1,17 @@
 """The C ABI: the library loads on a CPU-only host, exports every function
-include/gdn_api.h declares, its ctypes structs match the C layout, and
+include/*.h declares (the operator interface gdn_api.h and the test hooks
+gdn_testing.h), its ctypes structs match the C layout, and
 argument errors come back as status codes before any CUDA call."""
 
 from __future__ import annotations
 
 import ctypes
+import glob
+import json
 import os
 import re
 import subprocess
+import sys
 
 import pytest
 
@@ -15,12 +19,15 @@ from conftest import ROOT
 from gdn_b200 import _lib
 
 HEADER = os.path.join(ROOT, "include", "gdn_api.h")
+HEADERS = sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
 def declared_functions() -> list[str]:
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(gdn_[a-z_]+)\s*\(", text)))
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names.update(re.findall(r"\b(gdn_[a-z_]+)\s*\(", text))
+    return sorted(names)
 
 
 def test_library_exports_every_declared_function():
@@ -162,27 +169,63 @@ def test_attention_workspace_follows_the_split_rule():
     assert size.value == _align256(4096 * 16 * 256 * 2)
 
 
-@pytest.mark.parametrize(
-    "mutate,fragment",
-    [
-        (lambda a: setattr(a, "head_dim", 96), "head_dim"),
-        (lambda a: setattr(a, "rotary_dim", 63), "rotary_dim"),
-        (lambda a: setattr(a, "kv_heads", 3), "multiple of kv_heads"),
-        (lambda a: setattr(a, "cache_len", 0), "n_tokens <= cache_len"),
-        (lambda a: setattr(a, "k_cache", 0x50008), "16-byte aligned"),
-        (lambda a: setattr(a, "qg", None), "non-NULL"),
-        (lambda a: setattr(a, "act_dtype", _lib.GDN_F16), "float32 or bf16"),
-        (lambda a: setattr(a, "workspace_bytes", 64), "workspace too small"),
-        (lambda a: setattr(a, "workspace", 0x80008), "workspace must be 16-byte aligned"),
-    ],
-)
-def test_attention_rejects_bad_arguments_before_any_launch(mutate, fragment):
-    lib = _lib.load()
-    a = _attn_args()
+# Rejection cases of gdn_attention as (field, value, message fragment).
+_ATTN_BAD = [
+    ("head_dim", 96, "head_dim"),
+    ("rotary_dim", 63, "rotary_dim"),
+    ("kv_heads", 3, "multiple of kv_heads"),
+    ("cache_len", 0, "n_tokens <= cache_len"),
+    ("k_cache", 0x50008, "16-byte aligned"),
+    ("qg", None, "non-NULL"),
+    ("act_dtype", _lib.GDN_F16, "float32 or bf16"),
+    ("workspace_bytes", 64, "workspace too small"),
+    ("workspace", 0x80008, "workspace must be 16-byte aligned"),
+]
+
+# The cases pass made-up device addresses, so they run in a child process
+# that sees no GPU: if an argument check ever regressed, the launch behind it
+# would fail there with a CUDA error instead of touching a device.
+_ATTN_CHILD = r"""
+import ctypes, importlib.util, json, sys
+spec = importlib.util.spec_from_file_location("gdn_lib", sys.argv[1])
+L = importlib.util.module_from_spec(spec)
+spec.loader.exec_module(L)
+lib = L.load()
+cases = json.loads(sys.argv[2])
+res = []
+for field, value in cases:
+    a = L.AttnArgs()
+    a.n_tokens, a.cache_len, a.capacity = 1, 4097, 4352
+    a.heads, a.kv_heads, a.head_dim, a.rotary_dim = 16, 2, 256, 64
+    a.rope_base, a.eps, a.scale = 1e7, 1e-6, 256 ** -0.5
+    a.qg, a.qg_stride_t = 0x10000, 16 * 512
+    a.k_new, a.k_stride_t, a.v_new, a.v_stride_t = 0x20000, 512, 0x30000, 512
+    a.q_norm = a.k_norm = 0x40000
+    a.k_cache, a.v_cache = 0x50000, 0x60000
+    a.act_dtype = L.GDN_BF16
+    a.out, a.out_stride_t = 0x70000, 16 * 256
     size = ctypes.c_size_t(0)
-    assert lib.gdn_attention_workspace_size(ctypes.byref(a), ctypes.byref(size)) == _lib.GDN_OK
+    assert lib.gdn_attention_workspace_size(ctypes.byref(a), ctypes.byref(size)) == L.GDN_OK
     a.workspace, a.workspace_bytes = 0x80000, size.value
-    mutate(a)
+    setattr(a, field, value)
     st = lib.gdn_attention(ctypes.byref(a), None)
+    res.append([st, lib.gdn_last_error().decode()])
+print(json.dumps(res))
+"""
+
+
+@pytest.fixture(scope="module")
+def attention_rejections():
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    cases = json.dumps([[f, v] for f, v, _ in _ATTN_BAD])
+    out = subprocess.run([sys.executable, "-c", _ATTN_CHILD, os.path.join(os.path.dirname(_lib.__file__), "_lib.py"),
+                          cases], capture_output=True, text=True, env=env, timeout=120)
+    assert out.returncode == 0, out.stderr
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+@pytest.mark.parametrize("case", range(len(_ATTN_BAD)), ids=[c[0] for c in _ATTN_BAD])
+def test_attention_rejects_bad_arguments_before_any_launch(case, attention_rejections):
+    st, msg = attention_rejections[case]
     assert st in (_lib.GDN_EINVAL, _lib.GDN_EUNSUPPORTED)
-    assert fragment in lib.gdn_last_error().decode()
+    assert _ATTN_BAD[case][2] in msg
