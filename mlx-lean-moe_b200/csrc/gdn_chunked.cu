@@ -14,31 +14,20 @@
 //
 // Two kernels:
 //  * chunk_prep_kernel, parallel over (chunk, value head): one tcgen05 MMA
-//    [K;Q] K^T (M=128, N=64, K=128) gives K K^T and Q K^T in TMEM; the
-//    epilogue builds A and P, a forward substitution gives T, and T and P are
-//    written to the workspace as bf16 hi/lo pairs in the SW128 operand layout.
-//    The same kernel stores the chunk's gate vectors (beta, exp G,
-//    exp(G_last - G), gamma) next to T and P.
+//    [K;Q] K^T (M=128, N=64, K=128, bf16 inputs exact) gives K K^T and Q K^T
+//    in TMEM; the epilogue builds A and P, a forward substitution gives T, and
+//    T and P are written to the workspace as tf32 tiles in the SW128 K-major
+//    operand layout.  The same kernel stores the chunk's gate vectors (beta,
+//    exp G, exp(G_last - G), gamma) next to T and P.
 //  * chunk_scan_kernel, one CTA per (sequence, value head), serial over the
-//    chunks with the float32 state S resident in TMEM.  Warp roles: warp 0
-//    loads (TMA tensor loads of K, Q, V; bulk copies of T, P and the gates),
-//    warp 1 issues the MMAs, warps 2-9 run the state-chain epilogues (two
-//    per TMEM lane quarter: each thread owns one state row and half of its
-//    columns), warps 10-13 transpose K and write the output, off the chain.  Per
-//    chunk, in the transposed orientation (M = Dv state rows):
-//      [X | Y] = S [K | Q]^T       (N = 128, K = Dk)    2 passes (S hi, lo)
-//      Delta^T = R^T T^T           (N = 128 + 64, K = C) R_hi [T_hi; T_lo]^T + R_lo T_hi^T
-//      U       = Delta'^T K        (N = 128, K = C)     2 passes, Delta' = Delta diag(exp(G_last - G))
-//      O^T     = Delta^T P^T       (N = 128 + 64, K = C) as Delta
-//    (an M = 128 MMA costs about the same for N = 64 and N = 128, so the
-//    hi*lo term rides along as the second half of a 128-wide product).
-//    then S <- gamma S + U (the chain into the next chunk) and, off that
-//    chain, y = exp(G) Y + O.  Delta reuses the S lo operand buffer, which is
-//    dead between the X/Y MMAs and the state update.
-//  Operands that are not exact in bf16 (S, R, T, Delta, Delta', P) are split into
-//  bf16 hi + lo parts; the products then carry ~16 mantissa bits (rel-L2
-//  ~5e-6 against the float64 recurrence at T = 4096, versus ~3e-3 with plain
-//  bf16 operands and ~4e-4 with tf32).
+//    chunks with the float32 state S resident in TMEM, read there as the tf32
+//    A operand of the products that need it (no conversion of S on the
+//    chain); see the kernel's own comment for the products and operands.
+//  Precision: tf32 operands (S read with its low mantissa bits dropped, the
+//  other tf32 operands rounded to nearest) and a bf16 hi + lo Delta' in the
+//  state update give rel-L2 ~3e-4 to 5e-4 against the float64 recurrence at
+//  T = 2048 in an emulation of these roundings, for slow, moderate and
+//  strong decay.
 //
 // Every wait is bounded (2 s): on a timeout the kernel records an error in
 // g_device_error (read by gdn_check_device_errors), stops issuing work, lets
@@ -72,10 +61,11 @@ using namespace sm100;
 
 constexpr int CH = 64;   // chunk length
 constexpr int DH = 128;  // head dim (Dk = Dv)
-constexpr uint32_t kTile64 = 64 * 64 * 2;          // 64 x 64 bf16 operand tile (8 KB)
+constexpr uint32_t kTileTf32 = 64 * 64 * 4;        // 64 x 64 tf32 operand tile (16 KB)
 constexpr uint32_t kGateBytes = 1024;               // beta[64], exp G[64], exp(G_last - G)[64], gamma
-// Per (chunk, head): T hi, T lo, P hi, P lo, gates.
-constexpr size_t kRecBytes = 4 * (size_t)kTile64 + kGateBytes;
+// Per (chunk, head): T, P (tf32 [t][s], SW128 K-major), gates.
+constexpr uint32_t kRecT = 0, kRecP = kTileTf32, kRecGates = 2 * kTileTf32;
+constexpr size_t kRecBytes = 2 * (size_t)kTileTf32 + kGateBytes;
 constexpr uint32_t GATE_BETA = 0, GATE_EG = 64, GATE_DG = 128, GATE_GAMMA = 192;  // float offsets
 
 // A chain of the serial kernel other than "sequence b from state_in[b]":
@@ -111,6 +101,8 @@ struct ChunkParams {
   int gated;
   const float* norm_w;
   float norm_eps;
+  const __nv_bfloat16* z;  // [N, Hv, Dv] bf16, token stride z_st, head stride Dv
+  int64_t z_st;
   // n_chains > 0: CTA row blockIdx.x / hv runs chains[row] instead of sequence
   // blockIdx.x / hv with state_in / state_out.
   int n_chains;
@@ -212,7 +204,7 @@ __device__ __forceinline__ void chunk_cumsum(int lane, const float* sl, float* s
 }
 
 // ===========================================================================
-// Kernel A: per (chunk, value head) -- T = (I + A)^-1 and P, as bf16 hi/lo.
+// Kernel A: per (chunk, value head) -- T = (I + A)^-1 and P, as tf32 tiles.
 // ===========================================================================
 constexpr int kPrepAStride = 68;  // floats per row of the A / T scratch (16-byte rows)
 // A and T scratch; it takes the place of the [K;Q] tile once the MMA has read it.
@@ -324,7 +316,7 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
   if (warp == 1) {
     chunk_cumsum(lane, sl, sG, seG, sdG, &sgamma);
     __syncwarp();
-    float* gates = reinterpret_cast<float*>(p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes + 4 * kTile64);
+    float* gates = reinterpret_cast<float*>(p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes + kRecGates);
     for (int i = lane; i < CH; i += 32) {
       gates[GATE_BETA + i] = sb[i];
       gates[GATE_EG + i] = seG[i];
@@ -377,7 +369,7 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
   }
   // Decay groups of four columns past the warp's last row are all masked
   // and skipped (warp-uniform).  ex2.approx (relative error ~2^-22) is far
-  // below the bf16 hi/lo resolution of the records.
+  // below the tf32 resolution of the records.
   const int s_lim = (warp & 1) * 32 + 32;
   if (row < CH) {
     const int t = row;
@@ -410,14 +402,12 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
         v[s4] = v[s4 + 1] = v[s4 + 2] = v[s4 + 3] = 0.f;
       }
     }
-    unsigned char* rec = p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes;
+    // Row t of P as tf32: 16 chunks of 4, K-block j >> 3 (s in [32 kb, 32 kb + 32)).
+    unsigned char* rec = p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes + kRecP;
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 hi, lo;
-      split8(v + 8 * c, hi, lo);
-      *reinterpret_cast<uint4*>(rec + 2 * kTile64 + sw128_chunk(64, t, 0, c)) = hi;
-      *reinterpret_cast<uint4*>(rec + 3 * kTile64 + sw128_chunk(64, t, 0, c)) = lo;
-    }
+    for (int j = 0; j < 16; ++j)
+      *reinterpret_cast<float4*>(rec + sw128_chunk(64, t, j >> 3, j & 7)) =
+          make_float4(tf32_rn(v[4 * j]), tf32_rn(v[4 * j + 1]), tf32_rn(v[4 * j + 2]), tf32_rn(v[4 * j + 3]));
   }
   tc_fence_before();
   __syncthreads();
@@ -493,18 +483,15 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
   }
   __syncthreads();
   {
-    const int t = tid & 63;
-    const bool lo_half = tid >= 64;
-    unsigned char* rec = p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes + (lo_half ? kTile64 : 0);
-    const float* trow = sT + t * kPrepAStride;
+    // Row t, K-block kb (s in [32 kb, 32 kb + 32)) of T as tf32.
+    const int t = tid & 63, kb = tid >> 6;
+    unsigned char* rec = p.ws + ((size_t)(p.rec0 + slot) * p.hv + h) * kRecBytes + kRecT;
+    const float* trow = sT + t * kPrepAStride + 32 * kb;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      float x8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x8[i] = trow[8 * c + i];
-      uint4 hi, lo;
-      split8(x8, hi, lo);
-      *reinterpret_cast<uint4*>(rec + sw128_chunk(64, t, 0, c)) = lo_half ? lo : hi;
+      const float4 x = *reinterpret_cast<const float4*>(trow + 4 * c);
+      *reinterpret_cast<float4*>(rec + sw128_chunk(64, t, kb, c)) =
+          make_float4(tf32_rn(x.x), tf32_rn(x.y), tf32_rn(x.z), tf32_rn(x.w));
     }
   }
 }
@@ -512,55 +499,95 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
 // ===========================================================================
 // Kernel B: per (sequence, value head) -- serial over chunks, S in TMEM.
 // ===========================================================================
-// Dynamic shared memory map (offsets from the 1024-aligned base).
-constexpr uint32_t OFF_SHI = 0, OFF_SLO = 32768;   // S hi/lo: 128 x 128, two K-blocks each
-constexpr uint32_t OFF_KQ = 65536;                 // [K;Q]: 128 x 128, two K-blocks
-constexpr uint32_t OFF_V = 98304;                  // V: [64][128] bf16 row-major
-constexpr uint32_t OFF_T = 114688;                 // T hi, T lo: 64 x 64 each
-constexpr uint32_t OFF_P = 131072;                 // P hi, P lo
-constexpr uint32_t OFF_KT = 147456;                // K^T: 128 (dk) x 64 (t), exact in bf16
-constexpr uint32_t OFF_GATES = OFF_KT + 16384;     // two 1 KB gate buffers (chunk parity)
-// Output staging for the TMA store: [64 t][128 dv] in the output dtype (its
-// own buffer, so that the next chunk's T and P loads need not wait for the
-// store to drain).
-constexpr uint32_t OFF_OSTAGE = OFF_GATES + 2 * kGateBytes;
-// z tiles [64 t][128 dv] bf16 of the gated output, double-buffered: the
-// second one in the upper half of the staging buffer (the gated output is
-// bf16, so the staging needs only its lower half).
-constexpr uint32_t OFF_Z = OFF_OSTAGE + 64 * DH * 4;
-constexpr uint32_t OFF_Z2 = OFF_OSTAGE + 64 * DH * 2;
-constexpr uint32_t SCAN_SMEM_USED = OFF_Z + 64 * DH * 2;
+// The float32 state S lives in TMEM and never leaves it during the scan: the
+// products that need S read it there as a tf32 A operand (kind::tf32 with a
+// TMEM A operand).  Per chunk, in the transposed orientation (M = 128 state
+// rows dv):
+//   X   = S K^T                  tf32, N = 64, K = Dk   -> R = diag(beta)(V - diag(e^G) X), over X
+//   Y_b = S Q~^T                 tf32, N = 64, K = Dk   Q~ = diag(e^G) Q, so y = Y + O
+//   D_b = R^T T^T  (= Delta^T)   tf32, N = 64, K = C
+//   S   = gamma S + Delta'^T K   bf16, N = Dk, K = C: Delta' = Delta diag(e^(G_last - G)) as
+//                                bf16 hi + lo, K (exact in bf16) read MN-major from its TMA tile
+//   Y_b += D_b P^T               tf32, N = 64, K = C    issued one chunk later, off the chain
+// The chain per chunk is X -> R -> Delta -> Delta' -> S.  Y and Delta are
+// double-buffered by chunk parity (b), so neither the output warps nor the
+// late O product hold the chain up.  Operands the epilogue writes (R, Delta)
+// are rounded to the nearest tf32; K and Q are widened from their bf16 tiles
+// into tf32 tiles by four converter warps (Q scaled by e^G on the way).
+//
+// Dynamic shared memory (offsets from the 1024-aligned base).  The fp32 tiles
+// are SW128 K-major: per K-block of 32 floats, 64 rows of 128 bytes (8 KB).
+constexpr uint32_t kKTile = 64 * DH * 4;            // fp32 [64 t][128] tile (32 KB)
+constexpr uint32_t kBTile = 64 * DH * 2;            // bf16 [64 t][128] tile (16 KB)
+constexpr uint32_t OFF_KB = 0;                       // bf16 K tiles (TMA, SW128), chunk parity
+constexpr uint32_t OFF_K = 2 * kBTile;               // fp32 K tiles, chunk parity
+constexpr uint32_t OFF_Q = OFF_K + 2 * kKTile;       // fp32 Q~ (the bf16 TMA tile lands in its
+                                                     // first 16 KB and is widened in place)
+constexpr uint32_t OFF_V = OFF_Q + kKTile;           // V bf16 [64 t][128 dv] row-major
+constexpr uint32_t OFF_T = OFF_V + kBTile;           // T [t][s] tf32 (16 KB)
+constexpr uint32_t OFF_P = OFF_T + kTileTf32;        // P [t][s] tf32 (16 KB)
+constexpr uint32_t OFF_GATES = OFF_P + kTileTf32;    // two 1 KB gate buffers (chunk parity)
+constexpr uint32_t OFF_OSTAGE = OFF_GATES + 2 * kGateBytes;  // gated output: y bf16 [64 t][128 dv]
+constexpr uint32_t SCAN_SMEM_USED = OFF_OSTAGE + kBTile;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
+static_assert(OFF_Q % 1024 == 0 && OFF_T % 1024 == 0 && OFF_P % 1024 == 0 && OFF_V % 1024 == 0,
+              "operand tiles on 1 KB boundaries");
+constexpr int kScanThreads = 576;
 constexpr int kEpiThreads = 256;                   // warps 2-9: the state chain
-constexpr int kAuxThreads = 128;                   // warps 10-13: K^T and the output
+constexpr int kOutThreads = 128;                   // warps 10-13: the output
+constexpr int kCvtThreads = 128;                   // warps 14-17: bf16 -> tf32 operand tiles
 
-// TMEM columns.
-// The state update accumulates straight onto S (S is scaled by gamma in TMEM
-// while the Delta MMA runs), so there is no separate U accumulator.
-// Delta and O take 128 columns each: their hi*hi + lo*hi part in the first 64,
-// the hi*lo part (one N = 128 MMA against [hi; lo] of T or P) in the second.
-// R and Delta, the A operands of the next MMAs, are written back as packed
-// bf16 hi/lo in place of the accumulators they come from (X, Delta).
-constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y = 192, TM_D = 256, TM_O = 384;
-constexpr uint32_t TM_RHI = TM_X, TM_RLO = TM_X + 32;   // 64 tokens -> 32 packed columns each
-constexpr uint32_t TM_DHI = TM_D, TM_DLO = TM_D + 32;
-// Delta' = Delta diag(exp(G_last - G)) for the state update, in the second
-// half of the Delta region (its hi*lo accumulator part is read first).
-constexpr uint32_t TM_DPHI = TM_D + 64, TM_DPLO = TM_D + 96;
+// TMEM columns (512).  R overwrites X in place; O accumulates onto Y_b.
+constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y0 = 192, TM_D0 = 320, TM_DPHI = 448, TM_DPLO = 480;
 
 enum Bar {
-  B_KQ_FULL, B_KQ_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_P_FULL,
-  B_S_READY0, B_S_READY1, B_X_DONE, B_R_READY0, B_R_READY1, B_D_DONE, B_DD_READY, B_KT_READY, B_U_DONE, B_OU_DONE, B_Y_FREE, B_O_FREE, B_T_EMPTY, B_P_EMPTY, B_Z_FULL0, B_Z_FULL1,
+  B_K_FULL0, B_K_FULL1, B_K_READY0, B_K_READY1, B_K_EMPTY0, B_K_EMPTY1,
+  B_Q_FULL, B_Q_READY, B_Q_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
+  B_S_INIT, B_X_DONE, B_Y_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_U_DONE,
+  B_OU_DONE0, B_OU_DONE1, B_Y_FREE0, B_Y_FREE1,
   B_DRAIN,
   N_BARS
 };
 
-__global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                            const __grid_constant__ CUtensorMap kmap,
-                                                            const __grid_constant__ CUtensorMap vmap,
-                                                            const __grid_constant__ CUtensorMap omap,
-                                                            const __grid_constant__ CUtensorMap zmap,
-                                                            const ChunkParams p) {
+// Widens a bf16 [64 t][128] SW128 tile (two 64-wide K-blocks, 16 KB at src)
+// into the fp32 SW128 K-major tile (four 32-wide K-blocks, 32 KB at dst), row
+// t scaled by scale[t] and rounded to tf32 when scale is given.  128 threads
+// (thread e), named barrier bar_id; dst may equal src (every thread reads its
+// eight 16-byte chunks before any thread writes).
+__device__ __forceinline__ void widen_tile(const unsigned char* src, unsigned char* dst, const float* scale, int e,
+                                           int bar_id) {
+  uint4 raw[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) raw[j] = reinterpret_cast<const uint4*>(src)[e + 128 * j];
+  if (src == dst) named_sync(bar_id, kCvtThreads);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int i = e + 128 * j;                  // physical 16-byte chunk of the bf16 tile
+    const int kb = i >> 9, r = (i >> 3) & 63;   // 64-wide K-block, row
+    const int c = (i & 7) ^ (r & 7);            // logical chunk: elements 64 kb + 8 c .. + 7
+    const uint32_t w[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
+    float f[8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      f[2 * u] = bf16_lo_f(w[u]);
+      f[2 * u + 1] = bf16_hi_f(w[u]);
+    }
+    if (scale) {
+      const float s = scale[r];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) f[u] = tf32_rn(f[u] * s);
+    }
+    const int fb = 2 * kb + (c >> 2), cc = 2 * (c & 3);
+    *reinterpret_cast<float4*>(dst + sw128_chunk(64, r, fb, cc)) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(dst + sw128_chunk(64, r, fb, cc + 1)) = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                     const __grid_constant__ CUtensorMap kmap,
+                                                                     const __grid_constant__ CUtensorMap vmap,
+                                                                     const __grid_constant__ CUtensorMap zmap,
+                                                                     const ChunkParams p) {
   const uint64_t wait_ns = g_wait_limit_ns;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -592,7 +619,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     flags = 0;
   }
   if (flags & kChainZeroV) {  // V = 0 for a transition chain: a zero tile, never loaded
-    for (int i = tid; i < 16384 / 16; i += blockDim.x)
+    for (int i = tid; i < (int)(kBTile / 16); i += blockDim.x)
       reinterpret_cast<uint4*>(base + OFF_V)[i] = make_uint4(0u, 0u, 0u, 0u);
   }
 
@@ -603,8 +630,7 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     s_end = en;
     s_cbase = chunk_base_of(p, b);
     abort_flag = 0;
-    // KQ_EMPTY: the X/Y MMA, the K^T transpose and the output warps (done with the gates).
-    for (int i = 0; i < N_BARS; ++i) mbar_init(&bars[i], (i == B_KQ_EMPTY) ? 3 : 1);
+    for (int i = 0; i < N_BARS; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
   }
   if (warp == 0) tmem_alloc(&tmem_base, 512);
@@ -617,195 +643,168 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Lane 0 issues the loads.  With the gated output (whose norm keeps the
-    // output warps busy) the whole warp then transposes the chunk's K into
-    // K^T (the state update's operand) once it has landed and the previous
-    // state update has read the last K^T: 128 blocks of (8 tokens x 8 dk),
-    // four per ldmatrix/stmatrix pair.  Otherwise the output warps do it.
-    if (nch > 0) {
+    // Lanes 0-4 each own one operand stream and issue its loads in chunk
+    // order, each into its buffer as soon as the chunk before is done with
+    // it: lane 0 K (bf16, two buffers) with the gates, and the L2 prefetch
+    // of chunk c + 2's tiles and records (so the loads arrive at L2
+    // latency); lane 1 Q; lane 2 V; lane 3 T; lane 4 P.
+    if (nch > 0 && lane < 5) {
       if (lane == 0) {
         prefetch_tensormap(&qmap);
         prefetch_tensormap(&kmap);
         prefetch_tensormap(&vmap);
+        if (p.gated) prefetch_tensormap(&zmap);
       }
-      // Loads issued per full barrier (each barrier has at most one in flight).
-      uint32_t n_kq = 0, n_v = 0, n_t = 0, n_p = 0;
       const bool withhold_v = g_test_fault == kFaultWithholdV;
-      for (int64_t c = 0; c < nch; ++c) {
+      uint32_t n_issued[2] = {0, 0};  // loads issued (lane 0: per K buffer)
+      for (int64_t c = 0; c < nch && !abort_flag; ++c) {
+        const int bb = (int)(c & 1);
         const uint32_t par = (uint32_t)((c - 1) & 1);
+        const int t0 = (int)(start + c * CH);
+        const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
+        bool ok = true;
         if (lane == 0) {
-          const int t0 = (int)(start + c * CH);
-          const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
-          do {
-            if (c > 0 && !mbar_wait(&bars[B_KQ_EMPTY], par, wait_ns)) record_error(&abort_flag);
-            if (abort_flag) break;
-            mbar_arrive_expect_tx(&bars[B_KQ_FULL], 32768 + kGateBytes);
-            for (int kb = 0; kb < 2; ++kb) {
-              tma_load_3d(base + OFF_KQ + kb * 16384, &kmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
-              tma_load_3d(base + OFF_KQ + kb * 16384 + 8192, &qmap, &bars[B_KQ_FULL], kb * 64, kh, t0);
-            }
-            bulk_load(base + OFF_GATES + (c & 1) * kGateBytes, rec + 4 * kTile64, kGateBytes, &bars[B_KQ_FULL]);
-            ++n_kq;
-            if (c > 0 && !mbar_wait(&bars[B_V_EMPTY], par, wait_ns)) record_error(&abort_flag);
-            if (abort_flag) break;
-            if (withhold_v && c == 0) {
-              // test fault: V_FULL never completes, so the waits on it run out
-            } else if (flags & kChainZeroV) {
-              mbar_arrive(&bars[B_V_FULL]);
-              ++n_v;
-            } else {
-              mbar_arrive_expect_tx(&bars[B_V_FULL], 16384);
-              tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
-              ++n_v;
-            }
-            // T and P once the previous chunk's Delta and O MMAs have read theirs.
-            if (c > 0 && !mbar_wait(&bars[B_T_EMPTY], par, wait_ns)) record_error(&abort_flag);
-            if (abort_flag) break;
-            mbar_arrive_expect_tx(&bars[B_T_FULL], 2 * kTile64);
-            bulk_load(base + OFF_T, rec, 2 * kTile64, &bars[B_T_FULL]);
-            ++n_t;
-            if (c > 0 && !mbar_wait(&bars[B_P_EMPTY], par, wait_ns)) record_error(&abort_flag);
-            if (abort_flag) break;
-            mbar_arrive_expect_tx(&bars[B_P_FULL], 2 * kTile64);
-            bulk_load(base + OFF_P, rec + 2 * kTile64, 2 * kTile64, &bars[B_P_FULL]);
-            ++n_p;
-          } while (false);
-        }
-        __syncwarp();
-        if (abort_flag) break;
-        if (!p.gated) {  // the output warps have the time for K^T
-          if (lane == 0) mbar_arrive(&bars[B_KQ_EMPTY]);
-          continue;
-        }
-        const bool ok = mbar_wait(&bars[B_KQ_FULL], (uint32_t)(c & 1), wait_ns) &&
-                        (c == 0 || mbar_wait(&bars[B_U_DONE], par, wait_ns));
-        if (!__all_sync(0xffffffffu, ok)) {
-          if (lane == 0) record_error(&abort_flag);
-          break;
-        }
-        {
-          const int r = lane & 7, m = lane >> 3;
-#pragma unroll 4
-          for (int it = 0; it < 32; ++it) {
-            const int bi = it * 4 + m;                  // 0..127
-            const int cidx = bi >> 3, tb = bi & 7;      // dk chunk (0..15), token block
-            uint32_t f[4];
-            ldmatrix_x4_trans(smem_u32(base + OFF_KQ + sw128_chunk(128, tb * 8 + r, cidx >> 3, cidx & 7)), f);
-            stmatrix_x4(smem_u32(base + OFF_KT + sw128_chunk(128, cidx * 8 + r, 0, tb)), f);
+          if (c + 2 < nch) {
+            const int t2 = t0 + 2 * CH;
+            tma_prefetch_3d(&kmap, 0, kh, t2);
+            tma_prefetch_3d(&kmap, 64, kh, t2);
+            tma_prefetch_3d(&qmap, 0, kh, t2);
+            tma_prefetch_3d(&qmap, 64, kh, t2);
+            if (!(flags & kChainZeroV)) tma_prefetch_3d(&vmap, 0, h, t2);
+            if (p.gated && !(flags & kChainNoOut)) tma_prefetch_3d(&zmap, 0, h, t2);
+            bulk_prefetch_l2(rec + 2 * (size_t)p.hv * kRecBytes, (uint32_t)kRecBytes);
+          }
+          ok = c < 2 || mbar_wait(&bars[B_K_EMPTY0 + bb], (uint32_t)(((c >> 1) - 1) & 1), wait_ns);
+          if (ok) {
+            mbar_arrive_expect_tx(&bars[B_K_FULL0 + bb], kBTile + kGateBytes);
+            tma_load_3d(base + OFF_KB + bb * kBTile, &kmap, &bars[B_K_FULL0 + bb], 0, kh, t0);
+            tma_load_3d(base + OFF_KB + bb * kBTile + 8192, &kmap, &bars[B_K_FULL0 + bb], 64, kh, t0);
+            bulk_load(base + OFF_GATES + bb * kGateBytes, rec + kRecGates, kGateBytes, &bars[B_K_FULL0 + bb]);
+            ++n_issued[bb];
+          }
+        } else if (lane == 1) {
+          ok = c < 1 || mbar_wait(&bars[B_Q_EMPTY], par, wait_ns);
+          if (ok) {
+            mbar_arrive_expect_tx(&bars[B_Q_FULL], kBTile);
+            tma_load_3d(base + OFF_Q, &qmap, &bars[B_Q_FULL], 0, kh, t0);
+            tma_load_3d(base + OFF_Q + 8192, &qmap, &bars[B_Q_FULL], 64, kh, t0);
+            ++n_issued[0];
+          }
+        } else if (lane == 2) {
+          ok = c < 1 || mbar_wait(&bars[B_V_EMPTY], par, wait_ns);
+          if (!ok || (withhold_v && c == 0)) {
+            // (test fault: V_FULL never completes, so the waits on it run out)
+          } else if (flags & kChainZeroV) {
+            mbar_arrive(&bars[B_V_FULL]);
+            ++n_issued[0];
+          } else {
+            mbar_arrive_expect_tx(&bars[B_V_FULL], kBTile);
+            tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
+            ++n_issued[0];
+          }
+        } else if (lane == 3) {
+          ok = c < 1 || mbar_wait(&bars[B_T_EMPTY], par, wait_ns);
+          if (ok) {
+            mbar_arrive_expect_tx(&bars[B_T_FULL], kTileTf32);
+            bulk_load(base + OFF_T, rec + kRecT, kTileTf32, &bars[B_T_FULL]);
+            ++n_issued[0];
+          }
+        } else {
+          ok = c < 1 || mbar_wait(&bars[B_P_EMPTY], par, wait_ns);
+          if (ok) {
+            mbar_arrive_expect_tx(&bars[B_P_FULL], kTileTf32);
+            bulk_load(base + OFF_P, rec + kRecP, kTileTf32, &bars[B_P_FULL]);
+            ++n_issued[0];
           }
         }
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&bars[B_KT_READY]);
-          mbar_arrive(&bars[B_KQ_EMPTY]);
+        if (!ok) {
+          record_error(&abort_flag);
+          break;
         }
       }
-      // After an abort, let the copies this thread started land (bounded)
+      // After an abort, let the copies this lane started land (bounded)
       // before the CTA releases its shared memory.
-      if (lane == 0 && abort_flag) {
-        if (n_kq) mbar_wait(&bars[B_KQ_FULL], (n_kq - 1) & 1, wait_ns);
-        if (n_v) mbar_wait(&bars[B_V_FULL], (n_v - 1) & 1, wait_ns);
-        if (n_t) mbar_wait(&bars[B_T_FULL], (n_t - 1) & 1, wait_ns);
-        if (n_p) mbar_wait(&bars[B_P_FULL], (n_p - 1) & 1, wait_ns);
+      if (abort_flag) {
+        if (lane == 0) {
+          for (int bb = 0; bb < 2; ++bb)
+            if (n_issued[bb]) mbar_wait(&bars[B_K_FULL0 + bb], (n_issued[bb] - 1) & 1, wait_ns);
+        } else if (n_issued[0]) {
+          const int bar = lane == 1 ? B_Q_FULL : lane == 2 ? B_V_FULL : lane == 3 ? B_T_FULL : B_P_FULL;
+          mbar_wait(&bars[bar], (n_issued[0] - 1) & 1, wait_ns);
+        }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Per chunk: X_c (the chain), Y_c, Delta_c, O_(c-1), U_c.  A product that
+    // reads a TMEM operand written by the epilogue or by an earlier product is
+    // issued after the barrier that says that operand is complete.
     if (lane == 0 && nch > 0) {
-      const uint32_t id128 = idesc_bf16_f32(128, 128);
-      const uint32_t id64 = idesc_bf16_f32(128, 64);
-      const uint32_t sS[2] = {smem_u32(base + OFF_SHI), smem_u32(base + OFF_SLO)};
-      const uint32_t sK = smem_u32(base + OFF_KQ);
-      const uint32_t sT[2] = {smem_u32(base + OFF_T), smem_u32(base + OFF_T + kTile64)};
-      const uint32_t sP[2] = {smem_u32(base + OFF_P), smem_u32(base + OFF_P + kTile64)};
-      const uint32_t tD[2] = {tmem + TM_DHI, tmem + TM_DLO};
-      const uint32_t sKt = smem_u32(base + OFF_KT);
-      for (int64_t c = 0; c < nch; ++c) {
+      const uint32_t id64 = idesc_tf32_f32(128, 64);
+      const uint32_t idu = idesc_bf16_f32_bmn(128, 128);
+      const uint32_t sK[2] = {smem_u32(base + OFF_K), smem_u32(base + OFF_K + kKTile)};
+      const uint32_t sKb[2] = {smem_u32(base + OFF_KB), smem_u32(base + OFF_KB + kBTile)};
+      const uint32_t sQ = smem_u32(base + OFF_Q), sT = smem_u32(base + OFF_T), sP = smem_u32(base + OFF_P);
+      // O_c^T += Delta_c^T P_c^T onto Y of chunk c's parity.
+      auto issue_o = [&](int64_t c) -> bool {
+        if (!mbar_wait(&bars[B_P_FULL], (uint32_t)(c & 1), wait_ns)) return false;
+        tc_fence_after();
+        const uint32_t cb = (uint32_t)(c & 1);
+        for (int ks = 0; ks < 8; ++ks)
+          mma_tf32_ts(tmem + TM_Y0 + 64 * cb, tmem + TM_D0 + 64 * cb + 8 * ks,
+                      sdesc_sw128(sP + (ks >> 2) * 8192 + (ks & 3) * 32), id64, true);
+        mma_commit(&bars[B_OU_DONE0 + cb]);
+        mma_commit(&bars[B_P_EMPTY]);
+        return true;
+      };
+      bool ok = mbar_wait(&bars[B_S_INIT], 0, wait_ns);
+      for (int64_t c = 0; ok && c < nch; ++c) {
+        const int bb = (int)(c & 1);
         const uint32_t par = (uint32_t)(c & 1);
-        // [X | Y] = S [K | Q]^T, one K-block (64 of Dk) at a time as the
-        // epilogue finishes converting it; Y is free to overwrite once the
-        // output warps have read the previous chunk's.
-        if (!mbar_wait(&bars[B_KQ_FULL], par, wait_ns) ||
-            (c > 0 && !mbar_wait(&bars[B_Y_FREE], (uint32_t)((c - 1) & 1), wait_ns))) {
-          record_error(&abort_flag);
-          break;
-        }
-        {
-          bool stop = false;
-          int n = 0;
-          for (int kb = 0; kb < 2; ++kb) {
-            if (!mbar_wait(&bars[kb == 0 ? B_S_READY0 : B_S_READY1], par, wait_ns)) {
-              record_error(&abort_flag);
-              stop = true;
-              break;
-            }
-            tc_fence_after();
-            for (int part = 0; part < 2; ++part)
-              for (int ks = 0; ks < 4; ++ks, ++n)
-                mma_bf16(tmem + TM_X, sdesc_sw128(sS[part] + kb * 16384 + ks * 32),
-                         sdesc_sw128(sK + kb * 16384 + ks * 32), id128, n > 0);
-          }
-          if (stop || abort_flag) break;
-        }
+        // X_c = S K_c^T, S as left by U_(c-1)
+        ok = mbar_wait(&bars[B_K_READY0 + bb], (uint32_t)((c >> 1) & 1), wait_ns) &&
+             (c == 0 || mbar_wait(&bars[B_U_DONE], (uint32_t)((c - 1) & 1), wait_ns));
+        if (!ok || abort_flag) break;
+        tc_fence_after();
+        for (int ks = 0; ks < 16; ++ks)
+          mma_tf32_ts(tmem + TM_X, tmem + TM_S + 8 * ks, sdesc_sw128(sK[bb] + (ks >> 2) * 8192 + (ks & 3) * 32), id64,
+                      ks > 0);
         mma_commit(&bars[B_X_DONE]);
-        mma_commit(&bars[B_KQ_EMPTY]);
-        // Delta^T = R_hi [T_hi; T_lo]^T (N = 128) + R_lo T_hi^T (N = 64), R from
-        // TMEM: K steps {0, 2} (tokens 0-15, 32-47) once the first half of R is
-        // in, then {1, 3}.
-        if (!mbar_wait(&bars[B_T_FULL], par, wait_ns)) {
-          record_error(&abort_flag);
-          break;
-        }
-        {
-          bool stop = false;
-          for (int rh = 0; rh < 2; ++rh) {
-            if (!mbar_wait(&bars[rh == 0 ? B_R_READY0 : B_R_READY1], par, wait_ns)) {
-              record_error(&abort_flag);
-              stop = true;
-              break;
-            }
-            tc_fence_after();
-            for (int kk = 0; kk < 2; ++kk) {
-              const int ks = rh + 2 * kk;
-              mma_bf16_ts(tmem + TM_D, tmem + TM_RHI + ks * 8, sdesc_sw128(sT[0] + ks * 32), id128,
-                          !(rh == 0 && kk == 0));
-              mma_bf16_ts(tmem + TM_D, tmem + TM_RLO + ks * 8, sdesc_sw128(sT[0] + ks * 32), id64, true);
-            }
-          }
-          if (stop || abort_flag) break;
-        }
+        // Y_c = S Q~_c^T into Y_b, once the output warps have read chunk c - 2's
+        ok = mbar_wait(&bars[B_Q_READY], par, wait_ns) &&
+             (c < 2 || mbar_wait(&bars[B_Y_FREE0 + bb], (uint32_t)(((c >> 1) - 1) & 1), wait_ns));
+        if (!ok || abort_flag) break;
+        tc_fence_after();
+        for (int ks = 0; ks < 16; ++ks)
+          mma_tf32_ts(tmem + TM_Y0 + 64 * bb, tmem + TM_S + 8 * ks, sdesc_sw128(sQ + (ks >> 2) * 8192 + (ks & 3) * 32),
+                      id64, ks > 0);
+        mma_commit(&bars[B_Y_DONE]);
+        mma_commit(&bars[B_Q_EMPTY]);
+        // D_b = Delta_c^T = R^T T^T (R over X)
+        ok = mbar_wait(&bars[B_T_FULL], par, wait_ns) && mbar_wait(&bars[B_R_READY], par, wait_ns);
+        if (!ok || abort_flag) break;
+        tc_fence_after();
+        for (int ks = 0; ks < 8; ++ks)
+          mma_tf32_ts(tmem + TM_D0 + 64 * bb, tmem + TM_X + 8 * ks, sdesc_sw128(sT + (ks >> 2) * 8192 + (ks & 3) * 32),
+                      id64, ks > 0);
         mma_commit(&bars[B_D_DONE]);
         mma_commit(&bars[B_T_EMPTY]);
-        if (!mbar_wait(&bars[B_DD_READY], par, wait_ns) || !mbar_wait(&bars[B_KT_READY], par, wait_ns)) {
-          record_error(&abort_flag);
-          break;
-        }
-        if (abort_flag) break;
+        // O_(c-1), off the chain
+        if (c > 0 && !(ok = issue_o(c - 1))) break;
+        // S = gamma S + Delta'^T K: Delta' hi then lo (packed bf16 in TMEM),
+        // K from its bf16 TMA tile read MN-major (N = Dk contiguous)
+        ok = mbar_wait(&bars[B_DD_READY], par, wait_ns);
+        if (!ok || abort_flag) break;
         tc_fence_after();
-        {  // S <- (gamma S) + Delta'^T K   (state chain first), Delta' from TMEM, K exact
-          const uint32_t tDP[2] = {tmem + TM_DPHI, tmem + TM_DPLO};
-          for (int part = 0; part < 2; ++part)
-            for (int ks = 0; ks < 4; ++ks)
-              mma_bf16_ts(tmem + TM_S, tDP[part] + ks * 8, sdesc_sw128(sKt + ks * 32), id128, true);
-        }
+        for (int part = 0; part < 2; ++part)
+          for (int ks = 0; ks < 4; ++ks)
+            mma_bf16_ts(tmem + TM_S, tmem + (part ? TM_DPLO : TM_DPHI) + 8 * ks,
+                        sdesc_sw128_mn(sKb[bb] + ks * 2048, 8192, 1024), idu, true);
         mma_commit(&bars[B_U_DONE]);
-        if (!mbar_wait(&bars[B_P_FULL], par, wait_ns) ||
-            (c > 0 && !mbar_wait(&bars[B_O_FREE], (uint32_t)((c - 1) & 1), wait_ns))) {
-          record_error(&abort_flag);
-          break;
-        }
-        if (abort_flag) break;
-        tc_fence_after();
-        {  // O^T = Delta_hi [P_hi; P_lo]^T (N = 128) + Delta_lo P_hi^T (N = 64)
-          for (int ks = 0; ks < 4; ++ks)
-            mma_bf16_ts(tmem + TM_O, tD[0] + ks * 8, sdesc_sw128(sP[0] + ks * 32), id128, ks > 0);
-          for (int ks = 0; ks < 4; ++ks)
-            mma_bf16_ts(tmem + TM_O, tD[1] + ks * 8, sdesc_sw128(sP[0] + ks * 32), id64, true);
-        }
-        mma_commit(&bars[B_OU_DONE]);
-        mma_commit(&bars[B_P_EMPTY]);
+        mma_commit(&bars[B_K_EMPTY0 + bb]);
       }
+      if (ok && !abort_flag) ok = issue_o(nch - 1);
+      if (!ok) record_error(&abort_flag);
       // Wait for every MMA issued so far before the CTA winds down.
       mma_commit(&bars[B_DRAIN]);
       mbar_wait(&bars[B_DRAIN], 0, wait_ns);
@@ -820,52 +819,41 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
     const bool leader = e == 0;
     unsigned char* sm = base;
 
-    // S_0 -> TMEM and its bf16 hi/lo operand, one K-block per pass (columns
-    // 64*kb + 32*half .. +32 of row dv in pass kb).
-    for (int kb = 0; kb < 2; ++kb) {
-      const int col = kb * 64 + half * 32;
+    // S_0 -> TMEM: columns 64 half .. + 63 of row dv.
+    {
       const float* srow = chain_in ? chain_in + (size_t)dv * DH : nullptr;
       const float diag = (flags & kChainIdentity) ? 1.f : 0.f;
-      float x[32];
+      for (int cc = 0; cc < 2; ++cc) {
+        const int col = half * 64 + cc * 32;
+        float x[32];
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 v4 = srow ? *reinterpret_cast<const float4*>(srow + col + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-        x[i] = v4.x;
-        x[i + 1] = v4.y;
-        x[i + 2] = v4.z;
-        x[i + 3] = v4.w;
-      }
-      if (!srow) {
+        for (int i = 0; i < 32; i += 4) {
+          const float4 v4 = srow ? *reinterpret_cast<const float4*>(srow + col + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+          x[i] = v4.x;
+          x[i + 1] = v4.y;
+          x[i + 2] = v4.z;
+          x[i + 3] = v4.w;
+        }
+        if (!srow) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[i] = (col + i == dv) ? diag : 0.f;
-      }
-      tmem_st32(tq + TM_S + col, x);
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        uint4 hi, lo;
-        split8(x + 8 * c4, hi, lo);
-        const int cidx = half * 4 + c4;
-        *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, kb, cidx)) = hi;
-        *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, kb, cidx)) = lo;
+          for (int i = 0; i < 32; ++i) x[i] = (col + i == dv) ? diag : 0.f;
+        }
+        tmem_st32(tq + TM_S + col, x);
       }
       tmem_wait_st();
-      fence_async_smem();
       tc_fence_before();
       named_sync(1, kEpiThreads);
-      if (leader) mbar_arrive(&bars[kb == 0 ? B_S_READY0 : B_S_READY1]);
+      if (leader) mbar_arrive(&bars[B_S_INIT]);
     }
 
     for (int64_t c = 0; c < nch; ++c) {
       const uint32_t par = (uint32_t)(c & 1);
-      const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
+      const uint32_t cb = (uint32_t)(c & 1);
+      const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + cb * kGateBytes);
 
-      // Gates of this chunk arrive with K and Q.
-      bool ok = mbar_wait(&bars[B_KQ_FULL], par, wait_ns);
-      if (!ok) record_error(&abort_flag);
-      if (named_sync_or(1, kEpiThreads, !ok)) break;
-
-      // R = beta (V - X exp(G)), tokens 32*half .. +32 of row dv.
-      ok = mbar_wait(&bars[B_X_DONE], par, wait_ns) && mbar_wait(&bars[B_V_FULL], par, wait_ns);
+      // R = beta (V - e^G X) over X: tokens 32 half .. + 31 of row dv.
+      bool ok = mbar_wait(&bars[B_K_FULL0 + cb], (uint32_t)((c >> 1) & 1), wait_ns) &&  // the gates
+                mbar_wait(&bars[B_X_DONE], par, wait_ns) && mbar_wait(&bars[B_V_FULL], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
@@ -874,42 +862,32 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
         float x[32];
         tmem_ld32(tq + TM_X + half * 32, x);
         tmem_wait_ld();
-        // Tokens 32*half + [0, 16) first (K steps 0 and 2 of the Delta MMA),
-        // then 32*half + [16, 32).
 #pragma unroll
-        for (int rh = 0; rh < 2; ++rh) {
-          float r16[16];
-#pragma unroll
-          for (int i4 = 0; i4 < 16; i4 += 4) {
-            const int j = rh * 16 + i4;
-            const float4 b4 = *reinterpret_cast<const float4*>(gates + GATE_BETA + half * 32 + j);
-            const float4 e4 = *reinterpret_cast<const float4*>(gates + GATE_EG + half * 32 + j);
-            const int t = half * 32 + j;
-            r16[i4] = b4.x * (__bfloat162float(V[t * DH + dv]) - x[j] * e4.x);
-            r16[i4 + 1] = b4.y * (__bfloat162float(V[(t + 1) * DH + dv]) - x[j + 1] * e4.y);
-            r16[i4 + 2] = b4.z * (__bfloat162float(V[(t + 2) * DH + dv]) - x[j + 2] * e4.z);
-            r16[i4 + 3] = b4.w * (__bfloat162float(V[(t + 3) * DH + dv]) - x[j + 3] * e4.w);
-          }
-          uint32_t hi[8], lo[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            hi[j] = pack_bf16(r16[2 * j], r16[2 * j + 1]);
-            lo[j] = pack_bf16(r16[2 * j] - bf16_lo_f(hi[j]), r16[2 * j + 1] - bf16_hi_f(hi[j]));
-          }
-          // R hi/lo overwrite X in place: every X column must be read first.
-          if (rh == 0) named_sync(1, kEpiThreads);
-          tmem_st8(tq + TM_RHI + half * 16 + rh * 8, hi);
-          tmem_st8(tq + TM_RLO + half * 16 + rh * 8, lo);
-          tmem_wait_st();
-          tc_fence_before();
-          named_sync(1, kEpiThreads);
-          if (leader) mbar_arrive(&bars[rh == 0 ? B_R_READY0 : B_R_READY1]);
+        for (int i4 = 0; i4 < 32; i4 += 4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(gates + GATE_BETA + half * 32 + i4);
+          const float4 e4 = *reinterpret_cast<const float4*>(gates + GATE_EG + half * 32 + i4);
+          const int t = half * 32 + i4;
+          x[i4] = tf32_rn(b4.x * (__bfloat162float(V[t * DH + dv]) - x[i4] * e4.x));
+          x[i4 + 1] = tf32_rn(b4.y * (__bfloat162float(V[(t + 1) * DH + dv]) - x[i4 + 1] * e4.y));
+          x[i4 + 2] = tf32_rn(b4.z * (__bfloat162float(V[(t + 2) * DH + dv]) - x[i4 + 2] * e4.z));
+          x[i4 + 3] = tf32_rn(b4.w * (__bfloat162float(V[(t + 3) * DH + dv]) - x[i4 + 3] * e4.w));
         }
+        tmem_st32(tq + TM_X + half * 32, x);
+        tmem_wait_st();
       }
-      if (leader) mbar_arrive(&bars[B_V_EMPTY]);
+      tc_fence_before();
+      named_sync(1, kEpiThreads);
+      if (leader) {
+        mbar_arrive(&bars[B_R_READY]);
+        mbar_arrive(&bars[B_V_EMPTY]);
+      }
 
-      // While the Delta MMA runs: S <- gamma S in TMEM (the state update MMA
-      // then accumulates onto it).  Ordered before the U MMA by DD_READY.
+      // gamma S once X_c and Y_c (which read S) are done; the state update
+      // then accumulates onto it.
+      ok = mbar_wait(&bars[B_Y_DONE], par, wait_ns);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(1, kEpiThreads, !ok)) break;
+      tc_fence_after();
       {
         const float gamma = gates[GATE_GAMMA];
         for (int cc = 0; cc < 2; ++cc) {
@@ -921,73 +899,41 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           for (int i = 0; i < 32; ++i) sv[i] *= gamma;
           tmem_st32(tq + TM_S + col, sv);
         }
-        tmem_wait_st();
       }
 
-      // Delta -> bf16 hi/lo operand.
+      // Delta rounded to tf32 in place (the O product's operand), and
+      // Delta' = Delta diag(e^(G_last - G)) as packed bf16 hi / lo (the state
+      // update's operand).
       ok = mbar_wait(&bars[B_D_DONE], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
       {
-        float x[32], x2[32];
-        tmem_ld32(tq + TM_D + half * 32, x);
-        tmem_ld32(tq + TM_D + 64 + half * 32, x2);
+        float x[32], dg[32];
+        tmem_ld32(tq + TM_D0 + 64 * cb + half * 32, x);
+        load_gate32(gates + GATE_DG + half * 32, dg);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[i] += x2[i];
-        // Delta and Delta' hi/lo overwrite the accumulator in place: read it all first.
-        named_sync(1, kEpiThreads);
-        {
-          uint32_t hi[16], lo[16];
-          split32_packed(x, hi, lo);
-          tmem_st16(tq + TM_DHI + half * 16, hi);
-          tmem_st16(tq + TM_DLO + half * 16, lo);
+        for (int i = 0; i < 32; ++i) {
+          dg[i] *= x[i];
+          x[i] = tf32_rn(x[i]);
         }
-        {
-          float dg[32];
-          load_gate32(gates + GATE_DG + half * 32, dg);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] *= dg[i];
-          uint32_t hi[16], lo[16];
-          split32_packed(x, hi, lo);
-          tmem_st16(tq + TM_DPHI + half * 16, hi);
-          tmem_st16(tq + TM_DPLO + half * 16, lo);
-        }
+        tmem_st32(tq + TM_D0 + 64 * cb + half * 32, x);
+        uint32_t hi[16], lo[16];
+        split32_packed(dg, hi, lo);
+        tmem_st16(tq + TM_DPHI + half * 16, hi);
+        tmem_st16(tq + TM_DPLO + half * 16, lo);
         tmem_wait_st();
       }
       tc_fence_before();
       named_sync(1, kEpiThreads);
       if (leader) mbar_arrive(&bars[B_DD_READY]);
-
-      // The updated S -> its hi/lo operand for the next chunk, one K-block per
-      // pass so that the next X/Y MMA can start on the first.
-      ok = mbar_wait(&bars[B_U_DONE], par, wait_ns);
-      if (!ok) record_error(&abort_flag);
-      if (named_sync_or(1, kEpiThreads, !ok)) break;
-      tc_fence_after();
-      for (int kb = 0; kb < 2; ++kb) {
-        const int col = kb * 64 + half * 32;
-        float sv[32];
-        tmem_ld32(tq + TM_S + col, sv);
-        tmem_wait_ld();
-#pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint4 hi, lo;
-          split8(sv + 8 * c4, hi, lo);
-          const int cidx = half * 4 + c4;
-          *reinterpret_cast<uint4*>(sm + OFF_SHI + sw128_chunk(128, dv, kb, cidx)) = hi;
-          *reinterpret_cast<uint4*>(sm + OFF_SLO + sw128_chunk(128, dv, kb, cidx)) = lo;
-        }
-        fence_async_smem();
-        tc_fence_before();
-        named_sync(1, kEpiThreads);
-        if (leader) mbar_arrive(&bars[kb == 0 ? B_S_READY0 : B_S_READY1]);
-      }
     }
 
     // Final state (or the initial one for an empty sequence) -> state_out.
-    if (!named_sync_or(1, kEpiThreads, abort_flag != 0) && chain_out) {
+    bool ok = !abort_flag && (nch == 0 || mbar_wait(&bars[B_U_DONE], (uint32_t)((nch - 1) & 1), wait_ns));
+    if (!ok && !abort_flag) record_error(&abort_flag);
+    if (!named_sync_or(1, kEpiThreads, !ok) && chain_out) {
       tc_fence_after();
       float* orow = chain_out + (size_t)dv * DH;
       for (int cc = 0; cc < 2; ++cc) {
@@ -1000,233 +946,137 @@ __global__ void __launch_bounds__(448, 1) chunk_scan_kernel(const __grid_constan
           *reinterpret_cast<float4*>(orow + col + i) = make_float4(sv[i], sv[i + 1], sv[i + 2], sv[i + 3]);
       }
     }
-  } else {
-    // ------------------------------------------------- K^T (ungated) and output (aux)
+  } else if (warp < 14) {
+    // ------------------------------------------------------------- output
     const int e = tid - 320;                  // 0..127 (warps 10-13)
     const int q = warp & 3;                   // TMEM lane quarter of this warp
     const int dv = q * 32 + lane;             // output row (value dim)
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     const bool leader = e == 0;
     unsigned char* sm = base;
-    float nw[8];  // gated output: the norm weights of this lane's 8 dv
+    const int g8 = (e & 15) * 8;  // gated output: the 8 dv of this lane
+    float nw[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) nw[j] = p.gated ? p.norm_w[(e & 15) * 8 + j] : 0.f;
-    // The z tiles are loaded by this group's leader into two buffers, chunk c
-    // into buffer c & 1, each as soon as chunk c - 2 is done with it.
-    const bool zload = p.gated && !(flags & kChainNoOut);
-    const uint32_t zoff[2] = {OFF_Z2, OFF_Z};
-    int64_t n_z = 0;  // z tiles issued
-    if (zload && leader) {
-      prefetch_tensormap(&zmap);
-      for (; n_z < 2 && n_z < nch; ++n_z) {
-        mbar_arrive_expect_tx(&bars[B_Z_FULL0 + (n_z & 1)], 64 * DH * 2);
-        tma_load_3d(base + zoff[n_z & 1], &zmap, &bars[B_Z_FULL0 + (n_z & 1)], 0, h, (int)(start + n_z * CH));
-      }
-    }
+    for (int j = 0; j < 8; ++j) nw[j] = p.gated ? p.norm_w[g8 + j] : 0.f;
+    const size_t ostride = (size_t)p.hv * DH;
     for (int64_t c = 0; c < nch; ++c) {
-      const uint32_t par = (uint32_t)(c & 1);
       const int64_t t0 = start + c * CH;
       const int n = (int)(end - t0 < CH ? end - t0 : CH);
-      const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + (c & 1) * kGateBytes);
-
-      // y = exp(G) Y for all 64 tokens of row dv, read out of TMEM as soon as
-      // the X/Y MMA is done so that the next chunk's can start early.
-      bool ok;
-      if (!p.gated) {
-        // K^T (exact bf16 transpose) by 8x8 blocks: 128 blocks of (8 tokens x
-        // 8 dk), four per ldmatrix/stmatrix pair, eight pairs per warp.  The
-        // previous state update has read the last K^T: this group passed its
-        // output stage, which follows it.
-        ok = mbar_wait(&bars[B_KQ_FULL], par, wait_ns);
-        if (!ok) record_error(&abort_flag);
-        if (named_sync_or(2, kAuxThreads, !ok)) break;
-        const int r = lane & 7, m = lane >> 3;
-#pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const int bi = ((e >> 5) * 8 + it) * 4 + m;  // 0..127
-          const int cidx = bi >> 3, tb = bi & 7;      // dk chunk (0..15), token block
-          uint32_t f[4];
-          ldmatrix_x4_trans(smem_u32(sm + OFF_KQ + sw128_chunk(128, tb * 8 + r, cidx >> 3, cidx & 7)), f);
-          stmatrix_x4(smem_u32(sm + OFF_KT + sw128_chunk(128, cidx * 8 + r, 0, tb)), f);
-        }
-        fence_async_smem();
-        named_sync(2, kAuxThreads);
-        if (leader) mbar_arrive(&bars[B_KT_READY]);
-      }
-      // Y (the gates, read below, came with K and Q).
-      ok = mbar_wait(&bars[B_X_DONE], par, wait_ns) && mbar_wait(&bars[B_KQ_FULL], par, wait_ns);
+      const uint32_t cb = (uint32_t)(c & 1);
+      // y = Y + O of this chunk (e^G is in Q~): all 64 tokens of row dv.
+      bool ok = mbar_wait(&bars[B_OU_DONE0 + cb], (uint32_t)((c >> 1) & 1), wait_ns);
       if (!ok) record_error(&abort_flag);
-      if (named_sync_or(2, kAuxThreads, !ok)) break;
+      if (named_sync_or(2, kOutThreads, !ok)) break;
       tc_fence_after();
       float y[64];
-      tmem_ld32(tq + TM_Y, *reinterpret_cast<float(*)[32]>(y));
-      tmem_ld32(tq + TM_Y + 32, *reinterpret_cast<float(*)[32]>(y + 32));
+      tmem_ld32(tq + TM_Y0 + 64 * cb, *reinterpret_cast<float(*)[32]>(y));
+      tmem_ld32(tq + TM_Y0 + 64 * cb + 32, *reinterpret_cast<float(*)[32]>(y + 32));
       tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 64; i += 4) {
-        const float4 g4 = *reinterpret_cast<const float4*>(gates + GATE_EG + i);
-        y[i] *= g4.x;
-        y[i + 1] *= g4.y;
-        y[i + 2] *= g4.z;
-        y[i + 3] *= g4.w;
-      }
       tc_fence_before();
-      named_sync(2, kAuxThreads);
-      if (leader) {
-        mbar_arrive(&bars[B_Y_FREE]);
-        mbar_arrive(&bars[B_KQ_EMPTY]);  // this chunk's gates are no longer needed here
-      }
-
-      // Output: y_t += O_t (both accumulator parts), then store.
-      ok = mbar_wait(&bars[B_OU_DONE], par, wait_ns);
-      if (!ok) record_error(&abort_flag);
-      if (named_sync_or(2, kAuxThreads, !ok)) break;
-      tc_fence_after();
-      {
+      named_sync(2, kOutThreads);  // every thread has read Y_b (and the last chunk's staging)
+      if (leader) mbar_arrive(&bars[B_Y_FREE0 + cb]);
+      if (flags & kChainNoOut) continue;  // a transition chain: only its final state is wanted
+      if (!p.gated) {
+        // One token row per store: 32 lanes write 32 consecutive dv.
+        if (p.out_dtype == GDN_BF16) {
+          __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + dv;
 #pragma unroll
-        for (int hh = 0; hh < 4; ++hh) {
-          float o[32];
-          tmem_ld32(tq + TM_O + hh * 32, o);
-          tmem_wait_ld();
-          const int yb = (hh & 1) * 32;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) y[yb + i] += o[i];
-        }
-        // The previous chunk's tile store must have left the staging buffer.
-        if (leader) bulk_wait_group_read0();
-        tc_fence_before();
-        named_sync(2, kAuxThreads);
-        if (leader) mbar_arrive(&bars[B_O_FREE]);
-        if (flags & kChainNoOut) {
-          // a transition chain: only its final state is wanted
-        } else if (p.gated) {
-          // Fused-block output: y rounded to bf16 is staged [t][dv]; then the
-          // 16 lanes of a token (8 dv each) reduce its row, gate it with z
-          // and overwrite it in place: out = silu(z) * rms_norm(y, w, eps).
-          __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
-          unsigned short* st16 = reinterpret_cast<unsigned short*>(st);
-#pragma unroll
-          for (int i = 0; i < 64; i += 2) {
-            const uint32_t w2 = cvt_bf16x2(y[i], y[i + 1]);
-            st16[i * DH + dv] = (unsigned short)(w2 & 0xFFFFu);
-            st16[(i + 1) * DH + dv] = (unsigned short)(w2 >> 16);
-          }
-          ok = mbar_wait(&bars[B_Z_FULL0 + (c & 1)], (uint32_t)((c >> 1) & 1), wait_ns);
-          if (!ok) record_error(&abort_flag);
-          if (named_sync_or(2, kAuxThreads, !ok)) break;  // every row is staged, z has landed
-          const int g8 = (e & 15) * 8;
-          const __nv_bfloat16* zt = reinterpret_cast<const __nv_bfloat16*>(sm + zoff[c & 1]);
-          // The 8 items (tokens (e >> 4) + 8 it) four at a time, phase by phase,
-          // so that the shuffle and special-function latencies overlap.
-#pragma unroll 1
-          for (int i0 = 0; i0 < 8; i0 += 4) {
-            uint4 yu[4], zu[4];
-            float ss[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int tt = (e >> 4) + 8 * (i0 + k);
-              yu[k] = *reinterpret_cast<const uint4*>(st + tt * DH + g8);
-              zu[k] = *reinterpret_cast<const uint4*>(zt + tt * DH + g8);
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t yw[4] = {yu[k].x, yu[k].y, yu[k].z, yu[k].w};
-              float acc = 0.f;
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float y0 = bf16_lo_f(yw[j]), y1 = bf16_hi_f(yw[j]);
-                acc = fmaf(y0, y0, acc);
-                acc = fmaf(y1, y1, acc);
-              }
-              ss[k] = acc;
-            }
-#pragma unroll
-            for (int off = 8; off >= 1; off >>= 1)
-#pragma unroll
-              for (int k = 0; k < 4; ++k) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], off);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int tt = (e >> 4) + 8 * (i0 + k);
-              const float inv = rsqrtf(ss[k] * (1.f / DH) + p.norm_eps);
-              const uint32_t yw[4] = {yu[k].x, yu[k].y, yu[k].z, yu[k].w};
-              const uint32_t zw[4] = {zu[k].x, zu[k].y, zu[k].z, zu[k].w};
-              uint32_t ow[4];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                float n0 = bf16_lo_f(yw[j]) * inv * nw[2 * j], n1 = bf16_hi_f(yw[j]) * inv * nw[2 * j + 1];
-                round2_bf16(n0, n1);
-                ow[j] = pack_bf16(silu_fast(bf16_lo_f(zw[j])) * n0, silu_fast(bf16_hi_f(zw[j])) * n1);
-              }
-              *reinterpret_cast<uint4*>(st + tt * DH + g8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
-            }
-          }
-          fence_async_smem();
-          named_sync(2, kAuxThreads);
-          if (leader && c + 2 < nch) {  // z of chunk c + 2 into the tile just read
-            mbar_arrive_expect_tx(&bars[B_Z_FULL0 + (c & 1)], 64 * DH * 2);
-            tma_load_3d(base + zoff[c & 1], &zmap, &bars[B_Z_FULL0 + (c & 1)], 0, h, (int)(t0 + 2 * CH));
-            n_z = c + 3;
-          }
-          if (n == CH) {
-            if (leader) {
-              tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
-              bulk_commit_group();
-            }
-          } else {  // ragged last chunk: the valid rows, 16 bytes per lane
-            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + g8;
-            for (int it = 0; it < 8; ++it) {
-              const int tt = (e >> 4) + 8 * it;
-              if (tt < n)
-                *reinterpret_cast<uint4*>(op + (size_t)tt * p.hv * DH) =
-                    *reinterpret_cast<const uint4*>(st + tt * DH + g8);
-            }
-          }
-        } else if (n == CH) {
-          // Whole chunk: stage [t][dv] in shared memory, one TMA tensor store.
-          if (p.out_dtype == GDN_BF16) {
-            unsigned short* st16 = reinterpret_cast<unsigned short*>(sm + OFF_OSTAGE);
-#pragma unroll
-            for (int i = 0; i < 64; i += 2) {
-              const uint32_t w2 = cvt_bf16x2(y[i], y[i + 1]);
-              st16[i * DH + dv] = (unsigned short)(w2 & 0xFFFFu);
-              st16[(i + 1) * DH + dv] = (unsigned short)(w2 >> 16);
-            }
-          } else {
-            float* st = reinterpret_cast<float*>(sm + OFF_OSTAGE);
-#pragma unroll
-            for (int i = 0; i < 64; ++i) st[i * DH + dv] = y[i];
-          }
-          fence_async_smem();
-          named_sync(2, kAuxThreads);
-          if (leader) {
-            tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
-            bulk_commit_group();
-          }
+          for (int i = 0; i < 64; ++i)
+            if (i < n) op[i * ostride] = __float2bfloat16_rn(y[i]);
         } else {
-          // Ragged last chunk of a sequence: plain stores of the valid rows.
-          const size_t ostride = (size_t)p.hv * DH;
-          const size_t obase = ((size_t)t0 * p.hv + h) * DH + dv;
-          if (p.out_dtype == GDN_BF16) {
-            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + obase;
+          float* op = static_cast<float*>(p.out) + ((size_t)t0 * p.hv + h) * DH + dv;
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (i < n) op[i * ostride] = __float2bfloat16_rn(y[i]);
-          } else {
-            float* op = static_cast<float*>(p.out) + obase;
+          for (int i = 0; i < 64; ++i)
+            if (i < n) op[i * ostride] = y[i];
+        }
+        continue;
+      }
+      // Fused-block output: y rounded to bf16 is staged [t][dv]; then the 16
+      // lanes of a token (8 dv each) reduce its row, gate it with z (read
+      // from global memory, prefetched into L2 two chunks ahead) and store:
+      // out = silu(z) * rms_norm(y, w, eps).
+      __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
+      unsigned short* st16 = reinterpret_cast<unsigned short*>(st);
 #pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (i < n) op[i * ostride] = y[i];
+      for (int i = 0; i < 64; i += 2) {
+        const uint32_t w2 = cvt_bf16x2(y[i], y[i + 1]);
+        st16[i * DH + dv] = (unsigned short)(w2 & 0xFFFFu);
+        st16[(i + 1) * DH + dv] = (unsigned short)(w2 >> 16);
+      }
+      uint4 zu[8];  // items it: token (e >> 4) + 8 it
+      const __nv_bfloat16* zb = p.z + (size_t)t0 * p.z_st + (size_t)h * DH + g8;
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int tt = (e >> 4) + 8 * it;
+        zu[it] = tt < n ? *reinterpret_cast<const uint4*>(zb + (size_t)tt * p.z_st) : make_uint4(0u, 0u, 0u, 0u);
+      }
+      named_sync(2, kOutThreads);  // every row is staged
+      __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + g8;
+      // The 8 items four at a time, phase by phase, so that the shuffle and
+      // special-function latencies overlap.
+#pragma unroll
+      for (int i0 = 0; i0 < 8; i0 += 4) {
+        uint4 yu[4];
+        float ss[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) yu[k] = *reinterpret_cast<const uint4*>(st + ((e >> 4) + 8 * (i0 + k)) * DH + g8);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t yw[4] = {yu[k].x, yu[k].y, yu[k].z, yu[k].w};
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float y0 = bf16_lo_f(yw[j]), y1 = bf16_hi_f(yw[j]);
+            acc = fmaf(y0, y0, acc);
+            acc = fmaf(y1, y1, acc);
           }
+          ss[k] = acc;
+        }
+#pragma unroll
+        for (int off = 8; off >= 1; off >>= 1)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) ss[k] += __shfl_xor_sync(0xffffffffu, ss[k], off);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int tt = (e >> 4) + 8 * (i0 + k);
+          const float inv = rsqrtf(ss[k] * (1.f / DH) + p.norm_eps);
+          const uint32_t yw[4] = {yu[k].x, yu[k].y, yu[k].z, yu[k].w};
+          const uint32_t zw[4] = {zu[i0 + k].x, zu[i0 + k].y, zu[i0 + k].z, zu[i0 + k].w};
+          uint32_t ow[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float n0 = bf16_lo_f(yw[j]) * inv * nw[2 * j], n1 = bf16_hi_f(yw[j]) * inv * nw[2 * j + 1];
+            round2_bf16(n0, n1);
+            ow[j] = pack_bf16(silu_fast(bf16_lo_f(zw[j])) * n0, silu_fast(bf16_hi_f(zw[j])) * n1);
+          }
+          if (tt < n) *reinterpret_cast<uint4*>(ob + (size_t)tt * ostride) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
         }
       }
     }
-    if (leader) bulk_wait_group0();  // every output tile has reached global memory
-    // After an abort, let the z loads still in flight land (bounded) before
-    // the CTA releases its shared memory (tile i completes phase i >> 1 of
-    // barrier i & 1; waiting for a completed phase returns at once).
-    if (leader)
-      for (int64_t i = n_z - 2 < 0 ? 0 : n_z - 2; i < n_z; ++i)
-        mbar_wait(&bars[B_Z_FULL0 + (i & 1)], (uint32_t)((i >> 1) & 1), wait_ns);
+  } else {
+    // ------------------------------------------------- bf16 -> tf32 operands
+    // K_c from its bf16 tile into the fp32 tile of its parity, and
+    // Q~_c = diag(e^G) Q_c widened in place.
+    const int e = tid - 448;                  // 0..127 (warps 14-17)
+    const bool leader = e == 0;
+    for (int64_t c = 0; c < nch; ++c) {
+      const int bb = (int)(c & 1);
+      bool ok = !abort_flag && mbar_wait(&bars[B_K_FULL0 + bb], (uint32_t)((c >> 1) & 1), wait_ns);
+      if (!ok && !abort_flag) record_error(&abort_flag);
+      if (named_sync_or(3, kCvtThreads, !ok)) break;
+      widen_tile(base + OFF_KB + bb * kBTile, base + OFF_K + bb * kKTile, nullptr, e, 3);
+      fence_async_smem();
+      named_sync(3, kCvtThreads);
+      if (leader) mbar_arrive(&bars[B_K_READY0 + bb]);
+      ok = !abort_flag && mbar_wait(&bars[B_Q_FULL], (uint32_t)(c & 1), wait_ns);
+      if (!ok && !abort_flag) record_error(&abort_flag);
+      if (named_sync_or(3, kCvtThreads, !ok)) break;
+      widen_tile(base + OFF_Q, base + OFF_Q, reinterpret_cast<const float*>(base + OFF_GATES + bb * kGateBytes) + GATE_EG,
+                 e, 3);
+      fence_async_smem();
+      named_sync(3, kCvtThreads);
+      if (leader) mbar_arrive(&bars[B_Q_READY]);
+    }
   }
 
   tc_fence_before();
@@ -1263,22 +1113,6 @@ bool make_map(CUtensorMap* map, const void* ptr, int64_t n_tokens, int heads, in
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-// 3-D map over the contiguous output [N, Hv, 128] (fp32 or bf16), box {128, 1, 64}.
-bool make_out_map(CUtensorMap* map, void* ptr, int64_t n_tokens, int heads, gdn_dtype dt) {
-  auto enc = tensor_map_encoder();
-  if (!enc) return false;
-  std::memset(map, 0, sizeof(*map));
-  const cuuint64_t es = dt == GDN_BF16 ? 2 : 4;
-  cuuint64_t dims[3] = {(cuuint64_t)DH, (cuuint64_t)heads, (cuuint64_t)n_tokens};
-  cuuint64_t strides[2] = {DH * es, (cuuint64_t)heads * DH * es};
-  cuuint32_t box[3] = {(cuuint32_t)DH, 1, (cuuint32_t)CH};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, dt == GDN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr,
-                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1428,7 +1262,7 @@ size_t chunked_workspace_bytes(const ScanParams& p) { return seg_layout(p, seg_c
 cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   if (!aligned_ptr16(sp.q) || !aligned_ptr16(sp.k) || !aligned_ptr16(sp.v) || !aligned_ptr16(sp.workspace))
     return cudaErrorMisalignedAddress;
-  CUtensorMap qmap, kmap, vmap, omap, zmap;
+  CUtensorMap qmap, kmap, vmap, zmap;
   const int64_t N = sp.n_tokens;
   const bool gated = sp.z != nullptr;
   if (gated && (sp.out_dtype != GDN_BF16 || !aligned_ptr16(sp.z) || !aligned_elems(sp.z_st) || !sp.norm_w))
@@ -1438,12 +1272,11 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     if (!make_map(&qmap, sp.q, N, sp.hk, sp.q_st, sp.q_sh, 64, true) ||
         !make_map(&kmap, sp.k, N, sp.hk, sp.k_st, sp.k_sh, 64, true) ||
         !make_map(&vmap, sp.v, N, sp.hv, sp.v_st, sp.v_sh, 128, false) ||
-        !make_out_map(&omap, sp.out, N, sp.hv, sp.out_dtype) ||
         (gated && !make_map(&zmap, sp.z, N, sp.hv, sp.z_st, DH, 128, false)))
       return cudaErrorInvalidValue;
   } else {
     std::memset(&qmap, 0, sizeof(qmap));
-    kmap = vmap = omap = qmap;
+    kmap = vmap = qmap;
   }
   ChunkParams p;
   p.n_tokens = N;
@@ -1466,6 +1299,8 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   p.gated = gated ? 1 : 0;
   p.norm_w = sp.norm_w;
   p.norm_eps = sp.norm_eps;
+  p.z = static_cast<const __nv_bfloat16*>(sp.z);
+  p.z_st = sp.z_st;
 
   {
     static DeviceFlags prep_attr, scan_attr, comb_attr;
@@ -1499,7 +1334,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     }
     const int64_t ctas = sp.n_seqs * sp.hv;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    chunk_scan_kernel<<<(unsigned)ctas, 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p);
+    chunk_scan_kernel<<<(unsigned)ctas, kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, zmap, p);
     return cudaGetLastError();
   }
   // Chunk records: segments 0..P-2 before phase 1; the last segment's (needed
@@ -1545,7 +1380,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     p1.chains[i] = {i, nullptr, W + i * hstate, kChainNoOut};
     p1.chains[P - 2 + i] = {i, nullptr, Mt + (i - 1) * hstate, kChainIdentity | kChainZeroV | kChainNoOut};
   }
-  chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p1);
+  chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, zmap, p1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // phase 2: start states, W[j] = W[j-1] M_j + U_j
@@ -1561,7 +1396,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   ChunkParams p3 = p;
   p3.n_chains = P - 1;
   for (int i = 1; i <= P - 1; ++i) p3.chains[i - 1] = {i, W + (i - 1) * hstate, i == P - 1 ? sp.state_out : nullptr, 0};
-  chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), 448, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p3);
+  chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, zmap, p3);
   return cudaGetLastError();
 }
 

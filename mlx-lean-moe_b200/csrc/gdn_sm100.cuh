@@ -296,6 +296,71 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::tf32: A float32 in TMEM (lane = row,
+// column j = K element j; the MMA uses the top 19 bits), B a K-major tf32
+// smem tile.  One instruction covers K = 8: A advances 8 columns and B 32
+// bytes per K step.  (A tf32 B operand must be K-major here: an MN-major tf32
+// B tile in the plain 128-byte swizzle contributes nothing, measured.)
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            bool accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      : "memory");
+}
+
+// Instruction descriptor: tf32 x tf32 -> f32, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
+  return (1u << 4)                       // D format: f32
+         | (2u << 7)                     // A format: tf32
+         | (2u << 10)                    // B format: tf32
+         | ((uint32_t)(N >> 3) << 17)    // N / 8
+         | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+// Instruction descriptor: bf16 x bf16 -> f32, A K-major, B MN-major (N
+// contiguous in smem).
+__host__ __device__ constexpr uint32_t idesc_bf16_f32_bmn(int M, int N) {
+  return idesc_bf16_f32(M, N) | (1u << 16);
+}
+
+// Shared-memory descriptor of a SWIZZLE_128B MN-major bf16 tile: 128-byte
+// rows run along N (64 elements), 8 consecutive rows (8 K values) form a
+// 1024-byte swizzle atom; `lbo` bytes between atoms along N, `sbo` bytes
+// between groups of 8 K rows.  A K step of 16 advances the start address by
+// two row groups.
+__device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// float32 rounded to the nearest tf32 (10-bit mantissa, ties away from 0).
+__device__ __forceinline__ float tf32_rn(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Fire-and-forget L2 prefetches: a 3-D tensor tile, or `bytes` (multiple of
+// 16) of plain global memory.
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 

@@ -2,9 +2,12 @@
 Dk = Dv = 128, bf16 q/k/v, fp32 state) against the C oracle's float64
 recurrence on the same bf16 inputs.
 
-Bound: the north star's rel-L2 <= 2e-3 for bf16 inputs; the design (bf16
-hi/lo split operands) is held to 1e-4 here so that a precision regression
-shows long before the bound is reached."""
+Bound: the north star's rel-L2 <= 2e-3 for bf16 inputs. The design (tf32
+tensor-core operands: the float32 state read as tf32 from tensor memory, the
+other tf32 operands rounded to nearest, the state update's Delta' as bf16
+hi + lo against exact bf16 K) gives ~3e-4 to 5e-4 in a float64 emulation at
+T = 2048 for the decays below; it is held to 1e-3 here, half the bound, so
+that a precision regression shows before the bound is reached."""
 
 from __future__ import annotations
 
@@ -19,7 +22,7 @@ from oracle import oracle_c
 
 pytestmark = pytest.mark.gpu
 BOUND = 2e-3
-DESIGN = 1e-4
+DESIGN = 1e-3
 
 
 def _inputs(lengths, hk, hv, seed, decay="cfg", state_std=0.02):

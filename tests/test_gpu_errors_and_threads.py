@@ -32,7 +32,7 @@ from oracle import gdn_oracle as O
 from oracle import oracle_c
 
 pytestmark = pytest.mark.gpu
-DESIGN = 1e-4  # rel-L2 the chunked tests hold the tensor-core path to
+DESIGN = 1e-3  # rel-L2 the chunked tests hold the tensor-core path to
 
 
 def _prefill(lengths, hk, hv, seed):
