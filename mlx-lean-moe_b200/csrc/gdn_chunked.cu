@@ -643,95 +643,97 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Lanes 0-4 each own one operand stream and issue its loads in chunk
-    // order, each into its buffer as soon as the chunk before is done with
-    // it: lane 0 K (bf16, two buffers) with the gates, and the L2 prefetch
-    // of chunk c + 2's tiles and records (so the loads arrive at L2
-    // latency); lane 1 Q; lane 2 V; lane 3 T; lane 4 P.
-    if (nch > 0 && lane < 5) {
-      if (lane == 0) {
-        prefetch_tensormap(&qmap);
-        prefetch_tensormap(&kmap);
-        prefetch_tensormap(&vmap);
-        if (p.gated) prefetch_tensormap(&zmap);
-      }
+    // Lane 0 keeps five operand streams going -- K (bf16, two buffers) with
+    // the gates, Q, V, T, P -- each in chunk order, each load issued as soon
+    // as the chunk before is done with that buffer.  It polls the streams
+    // round-robin without blocking on any one of them (a late consumer of
+    // one buffer must not hold up the loads of the others), and gives up
+    // (recording a timeout) once no stream has advanced for the wait limit.
+    // With each K load it prefetches chunk c + 2's tiles and records into L2,
+    // so the loads themselves arrive at L2 latency.
+    if (nch > 0 && lane == 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      if (p.gated) prefetch_tensormap(&zmap);
       const bool withhold_v = g_test_fault == kFaultWithholdV;
-      uint32_t n_issued[2] = {0, 0};  // loads issued (lane 0: per K buffer)
-      for (int64_t c = 0; c < nch && !abort_flag; ++c) {
-        const int bb = (int)(c & 1);
-        const uint32_t par = (uint32_t)((c - 1) & 1);
-        const int t0 = (int)(start + c * CH);
-        const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
-        bool ok = true;
-        if (lane == 0) {
-          if (c + 2 < nch) {
-            const int t2 = t0 + 2 * CH;
-            tma_prefetch_3d(&kmap, 0, kh, t2);
-            tma_prefetch_3d(&kmap, 64, kh, t2);
-            tma_prefetch_3d(&qmap, 0, kh, t2);
-            tma_prefetch_3d(&qmap, 64, kh, t2);
-            if (!(flags & kChainZeroV)) tma_prefetch_3d(&vmap, 0, h, t2);
-            if (p.gated && !(flags & kChainNoOut)) tma_prefetch_3d(&zmap, 0, h, t2);
-            bulk_prefetch_l2(rec + 2 * (size_t)p.hv * kRecBytes, (uint32_t)kRecBytes);
-          }
-          ok = c < 2 || mbar_wait(&bars[B_K_EMPTY0 + bb], (uint32_t)(((c >> 1) - 1) & 1), wait_ns);
-          if (ok) {
+      int64_t next[5] = {0, 0, 0, 0, 0};   // next chunk to load, per stream
+      uint32_t n_k[2] = {0, 0};            // K loads issued per buffer
+      uint64_t last = globaltimer_ns();
+      while (!abort_flag) {
+        bool progress = false, pending = false;
+        for (int sidx = 0; sidx < 5; ++sidx) {
+          const int64_t c = next[sidx];
+          if (c >= nch) continue;
+          pending = true;
+          const int bb = (int)(c & 1);
+          const uint32_t par = (uint32_t)((c - 1) & 1);
+          const int t0 = (int)(start + c * CH);
+          const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
+          if (sidx == 0) {  // K_c and the gates into buffer c & 1, free once U_(c-2) is done
+            if (c >= 2 && !mbar_try_wait(&bars[B_K_EMPTY0 + bb], (uint32_t)(((c >> 1) - 1) & 1))) continue;
+            if (c + 2 < nch) {
+              const int t2 = t0 + 2 * CH;
+              tma_prefetch_3d(&kmap, 0, kh, t2);
+              tma_prefetch_3d(&kmap, 64, kh, t2);
+              tma_prefetch_3d(&qmap, 0, kh, t2);
+              tma_prefetch_3d(&qmap, 64, kh, t2);
+              if (!(flags & kChainZeroV)) tma_prefetch_3d(&vmap, 0, h, t2);
+              if (p.gated && !(flags & kChainNoOut)) tma_prefetch_3d(&zmap, 0, h, t2);
+              bulk_prefetch_l2(rec + 2 * (size_t)p.hv * kRecBytes, (uint32_t)kRecBytes);
+            }
             mbar_arrive_expect_tx(&bars[B_K_FULL0 + bb], kBTile + kGateBytes);
             tma_load_3d(base + OFF_KB + bb * kBTile, &kmap, &bars[B_K_FULL0 + bb], 0, kh, t0);
             tma_load_3d(base + OFF_KB + bb * kBTile + 8192, &kmap, &bars[B_K_FULL0 + bb], 64, kh, t0);
             bulk_load(base + OFF_GATES + bb * kGateBytes, rec + kRecGates, kGateBytes, &bars[B_K_FULL0 + bb]);
-            ++n_issued[bb];
-          }
-        } else if (lane == 1) {
-          ok = c < 1 || mbar_wait(&bars[B_Q_EMPTY], par, wait_ns);
-          if (ok) {
+            ++n_k[bb];
+          } else if (sidx == 1) {  // Q_c once Y_(c-1) has read Q~_(c-1)
+            if (c >= 1 && !mbar_try_wait(&bars[B_Q_EMPTY], par)) continue;
             mbar_arrive_expect_tx(&bars[B_Q_FULL], kBTile);
             tma_load_3d(base + OFF_Q, &qmap, &bars[B_Q_FULL], 0, kh, t0);
             tma_load_3d(base + OFF_Q + 8192, &qmap, &bars[B_Q_FULL], 64, kh, t0);
-            ++n_issued[0];
-          }
-        } else if (lane == 2) {
-          ok = c < 1 || mbar_wait(&bars[B_V_EMPTY], par, wait_ns);
-          if (!ok || (withhold_v && c == 0)) {
-            // (test fault: V_FULL never completes, so the waits on it run out)
-          } else if (flags & kChainZeroV) {
-            mbar_arrive(&bars[B_V_FULL]);
-            ++n_issued[0];
-          } else {
-            mbar_arrive_expect_tx(&bars[B_V_FULL], kBTile);
-            tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
-            ++n_issued[0];
-          }
-        } else if (lane == 3) {
-          ok = c < 1 || mbar_wait(&bars[B_T_EMPTY], par, wait_ns);
-          if (ok) {
+          } else if (sidx == 2) {  // V_c once R_(c-1) has read V_(c-1)
+            if (c >= 1 && !mbar_try_wait(&bars[B_V_EMPTY], par)) continue;
+            if (withhold_v && c == 0) {
+              // test fault: V_FULL never completes, so the waits on it run out
+            } else if (flags & kChainZeroV) {
+              mbar_arrive(&bars[B_V_FULL]);
+            } else {
+              mbar_arrive_expect_tx(&bars[B_V_FULL], kBTile);
+              tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
+            }
+          } else if (sidx == 3) {  // T_c once Delta_(c-1) has read T_(c-1)
+            if (c >= 1 && !mbar_try_wait(&bars[B_T_EMPTY], par)) continue;
             mbar_arrive_expect_tx(&bars[B_T_FULL], kTileTf32);
             bulk_load(base + OFF_T, rec + kRecT, kTileTf32, &bars[B_T_FULL]);
-            ++n_issued[0];
-          }
-        } else {
-          ok = c < 1 || mbar_wait(&bars[B_P_EMPTY], par, wait_ns);
-          if (ok) {
+          } else {  // P_c once O_(c-1) has read P_(c-1)
+            if (c >= 1 && !mbar_try_wait(&bars[B_P_EMPTY], par)) continue;
             mbar_arrive_expect_tx(&bars[B_P_FULL], kTileTf32);
             bulk_load(base + OFF_P, rec + kRecP, kTileTf32, &bars[B_P_FULL]);
-            ++n_issued[0];
           }
+          next[sidx] = c + 1;
+          progress = true;
         }
-        if (!ok) {
+        if (!pending) break;
+        const uint64_t now = globaltimer_ns();
+        if (progress) {
+          last = now;
+        } else if (now - last > wait_ns) {
           record_error(&abort_flag);
           break;
         }
       }
-      // After an abort, let the copies this lane started land (bounded)
-      // before the CTA releases its shared memory.
+      // After an abort, let the copies this thread started land (bounded)
+      // before the CTA releases its shared memory.  Stream s has issued
+      // next[s] loads (V one fewer when the test fault withheld chunk 0's).
       if (abort_flag) {
-        if (lane == 0) {
-          for (int bb = 0; bb < 2; ++bb)
-            if (n_issued[bb]) mbar_wait(&bars[B_K_FULL0 + bb], (n_issued[bb] - 1) & 1, wait_ns);
-        } else if (n_issued[0]) {
-          const int bar = lane == 1 ? B_Q_FULL : lane == 2 ? B_V_FULL : lane == 3 ? B_T_FULL : B_P_FULL;
-          mbar_wait(&bars[bar], (n_issued[0] - 1) & 1, wait_ns);
-        }
+        for (int bb = 0; bb < 2; ++bb)
+          if (n_k[bb]) mbar_wait(&bars[B_K_FULL0 + bb], (n_k[bb] - 1) & 1, wait_ns);
+        if (next[1]) mbar_wait(&bars[B_Q_FULL], (uint32_t)((next[1] - 1) & 1), wait_ns);
+        const int64_t nv = next[2] - (withhold_v && next[2] > 0 ? 1 : 0);
+        if (nv > 0) mbar_wait(&bars[B_V_FULL], (uint32_t)((nv - 1) & 1), wait_ns);
+        if (next[3]) mbar_wait(&bars[B_T_FULL], (uint32_t)((next[3] - 1) & 1), wait_ns);
+        if (next[4]) mbar_wait(&bars[B_P_FULL], (uint32_t)((next[4] - 1) & 1), wait_ns);
       }
     }
   } else if (warp == 1) {
