@@ -500,66 +500,64 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
 // Kernel B: per (sequence, value head) -- serial over chunks, S in TMEM.
 // ===========================================================================
 // The float32 state S lives in TMEM and never leaves it during the scan: the
-// products that need S read it there as a tf32 A operand (kind::tf32 with a
-// TMEM A operand).  Per chunk, in the transposed orientation (M = 128 state
-// rows dv):
-//   X   = S K^T                  tf32, N = 64, K = Dk   -> R = diag(beta)(V - diag(e^G) X), over X
-//   Y_b = S Q~^T                 tf32, N = 64, K = Dk   Q~ = diag(e^G) Q, so y = Y + O
-//   D_b = R^T T^T  (= Delta^T)   tf32, N = 64, K = C
+// X|Y product reads it there as its tf32 A operand (kind::tf32 with a TMEM A
+// operand).  Per chunk, in the transposed orientation (M = 128 state rows
+// dv), with b the chunk's parity:
+//   [X | Y]_b = S [K ; Q~]^T     tf32, N = 128, K = Dk   Q~ = diag(e^G) Q, so y = Y + O
+//   R   = diag(beta)(V - diag(e^G) X)                     over X, rounded to tf32
+//   D_b = R^T T^T (= Delta^T)    tf32, N = 64, K = C
 //   S   = gamma S + Delta'^T K   bf16, N = Dk, K = C: Delta' = Delta diag(e^(G_last - G)) as
-//                                bf16 hi + lo, K (exact in bf16) read MN-major from its TMA tile
-//   Y_b += D_b P^T               tf32, N = 64, K = C    issued one chunk later, off the chain
-// The chain per chunk is X -> R -> Delta -> Delta' -> S.  Y and Delta are
-// double-buffered by chunk parity (b), so neither the output warps nor the
-// late O product hold the chain up.  Operands the epilogue writes (R, Delta)
-// are rounded to the nearest tf32; K and Q are widened from their bf16 tiles
-// into tf32 tiles by four converter warps (Q scaled by e^G on the way).
+//                                bf16 hi + lo over the dead R; K (exact in bf16) read
+//                                MN-major from its TMA tile
+//   Y_b += D_b P^T               tf32, N = 64, K = C     issued a chunk later, off the chain
+// The chain per chunk is X|Y -> R -> Delta -> Delta' -> S.  [X|Y] and Delta
+// are double-buffered by parity, so neither the output warps nor the late O
+// product hold the chain up.  Four converter warps widen K and Q from their
+// bf16 tiles into the one fp32 [K ; Q~] operand tile (Q scaled by e^G).
 //
-// Dynamic shared memory (offsets from the 1024-aligned base).  The fp32 tiles
-// are SW128 K-major: per K-block of 32 floats, 64 rows of 128 bytes (8 KB).
-constexpr uint32_t kKTile = 64 * DH * 4;            // fp32 [64 t][128] tile (32 KB)
-constexpr uint32_t kBTile = 64 * DH * 2;            // bf16 [64 t][128] tile (16 KB)
-constexpr uint32_t OFF_KB = 0;                       // bf16 K tiles (TMA, SW128), chunk parity
-constexpr uint32_t OFF_K = 2 * kBTile;               // fp32 K tiles, chunk parity
-constexpr uint32_t OFF_Q = OFF_K + 2 * kKTile;       // fp32 Q~ (the bf16 TMA tile lands in its
-                                                     // first 16 KB and is widened in place)
-constexpr uint32_t OFF_V = OFF_Q + kKTile;           // V bf16 [64 t][128 dv] row-major
-constexpr uint32_t OFF_T = OFF_V + kBTile;           // T [t][s] tf32 (16 KB)
-constexpr uint32_t OFF_P = OFF_T + kTileTf32;        // P [t][s] tf32 (16 KB)
-constexpr uint32_t OFF_GATES = OFF_P + kTileTf32;    // two 1 KB gate buffers (chunk parity)
-constexpr uint32_t OFF_OSTAGE = OFF_GATES + 2 * kGateBytes;  // gated output: y bf16 [64 t][128 dv]
-constexpr uint32_t SCAN_SMEM_USED = OFF_OSTAGE + kBTile;
+// Dynamic shared memory (offsets from the 1024-aligned base).  fp32 operand
+// tiles are SW128 K-major: per K-block of 32 floats, one 128-byte row each.
+constexpr uint32_t kBTile = 64 * DH * 2;             // bf16 [64 t][128] tile (16 KB)
+constexpr uint32_t OFF_KQ = 0;                        // fp32 [K ; Q~] 128 rows x 128: 4 K-blocks of 16 KB
+constexpr uint32_t OFF_KB = 4 * 128 * 128;            // bf16 K TMA tiles (SW128), chunk parity
+constexpr uint32_t OFF_QB = OFF_KB + 2 * kBTile;      // bf16 Q TMA tile (SW128)
+constexpr uint32_t OFF_V = OFF_QB + kBTile;           // V bf16 [64 t][128 dv] row-major
+constexpr uint32_t OFF_T = OFF_V + kBTile;            // T [t][s] tf32 (16 KB)
+constexpr uint32_t OFF_P = OFF_T + kTileTf32;         // P [t][s] tf32 (16 KB)
+constexpr uint32_t OFF_GATES = OFF_P + kTileTf32;     // two 1 KB gate buffers (chunk parity)
+constexpr uint32_t OFF_OSTAGE = OFF_GATES + 2 * kGateBytes;  // output staging [64 t][128 dv], out dtype
+constexpr uint32_t SCAN_SMEM_USED = OFF_OSTAGE + 64 * DH * 4;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
-static_assert(OFF_Q % 1024 == 0 && OFF_T % 1024 == 0 && OFF_P % 1024 == 0 && OFF_V % 1024 == 0,
+static_assert(OFF_KB % 1024 == 0 && OFF_QB % 1024 == 0 && OFF_T % 1024 == 0 && OFF_P % 1024 == 0,
               "operand tiles on 1 KB boundaries");
+static_assert(OFF_OSTAGE % 128 == 0, "TMA store source on 128 B");
 constexpr int kScanThreads = 576;
 constexpr int kEpiThreads = 256;                   // warps 2-9: the state chain
 constexpr int kOutThreads = 128;                   // warps 10-13: the output
-constexpr int kCvtThreads = 128;                   // warps 14-17: bf16 -> tf32 operand tiles
+constexpr int kCvtThreads = 128;                   // warps 14-17: bf16 -> tf32 operand tile
 
-// TMEM columns (512).  R overwrites X in place; O accumulates onto Y_b.
-constexpr uint32_t TM_S = 0, TM_X = 128, TM_Y0 = 192, TM_D0 = 320, TM_DPHI = 448, TM_DPLO = 480;
+// TMEM columns (512): S, then [X | Y] of each parity (X's 64 columns hold R,
+// then Delta' hi / lo), then Delta of each parity.
+constexpr uint32_t TM_S = 0, TM_XY = 128, TM_D = 384;
 
 enum Bar {
-  B_K_FULL0, B_K_FULL1, B_K_READY0, B_K_READY1, B_K_EMPTY0, B_K_EMPTY1,
-  B_Q_FULL, B_Q_READY, B_Q_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
-  B_S_INIT, B_X_DONE, B_Y_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_U_DONE,
+  B_K_FULL0, B_K_FULL1, B_K_EMPTY0, B_K_EMPTY1, B_KQ_READY,
+  B_Q_FULL, B_Q_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
+  B_S_INIT, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_U_DONE,
   B_OU_DONE0, B_OU_DONE1, B_Y_FREE0, B_Y_FREE1,
   B_DRAIN,
   N_BARS
 };
 
 // Widens a bf16 [64 t][128] SW128 tile (two 64-wide K-blocks, 16 KB at src)
-// into the fp32 SW128 K-major tile (four 32-wide K-blocks, 32 KB at dst), row
-// t scaled by scale[t] and rounded to tf32 when scale is given.  128 threads
-// (thread e), named barrier bar_id; dst may equal src (every thread reads its
-// eight 16-byte chunks before any thread writes).
-__device__ __forceinline__ void widen_tile(const unsigned char* src, unsigned char* dst, const float* scale, int e,
-                                           int bar_id) {
+// into rows row0 .. row0 + 63 of the 128-row fp32 SW128 K-major tile at dst,
+// row t scaled by scale[t] and rounded to tf32 when scale is given.  128
+// threads, thread e; each moves eight 16-byte chunks.
+__device__ __forceinline__ void widen_tile(const unsigned char* src, unsigned char* dst, int row0, const float* scale,
+                                           int e) {
   uint4 raw[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) raw[j] = reinterpret_cast<const uint4*>(src)[e + 128 * j];
-  if (src == dst) named_sync(bar_id, kCvtThreads);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const int i = e + 128 * j;                  // physical 16-byte chunk of the bf16 tile
@@ -578,14 +576,15 @@ __device__ __forceinline__ void widen_tile(const unsigned char* src, unsigned ch
       for (int u = 0; u < 8; ++u) f[u] = tf32_rn(f[u] * s);
     }
     const int fb = 2 * kb + (c >> 2), cc = 2 * (c & 3);
-    *reinterpret_cast<float4*>(dst + sw128_chunk(64, r, fb, cc)) = make_float4(f[0], f[1], f[2], f[3]);
-    *reinterpret_cast<float4*>(dst + sw128_chunk(64, r, fb, cc + 1)) = make_float4(f[4], f[5], f[6], f[7]);
+    *reinterpret_cast<float4*>(dst + sw128_chunk(128, row0 + r, fb, cc)) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(dst + sw128_chunk(128, row0 + r, fb, cc + 1)) = make_float4(f[4], f[5], f[6], f[7]);
   }
 }
 
-__global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                      const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
+                                                                     const __grid_constant__ CUtensorMap omap,
                                                                      const __grid_constant__ CUtensorMap zmap,
                                                                      const ChunkParams p) {
   const uint64_t wait_ns = g_wait_limit_ns;
@@ -646,15 +645,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     // Lane 0 keeps five operand streams going -- K (bf16, two buffers) with
     // the gates, Q, V, T, P -- each in chunk order, each load issued as soon
     // as the chunk before is done with that buffer.  It polls the streams
-    // round-robin without blocking on any one of them (a late consumer of
-    // one buffer must not hold up the loads of the others), and gives up
-    // (recording a timeout) once no stream has advanced for the wait limit.
-    // With each K load it prefetches chunk c + 2's tiles and records into L2,
-    // so the loads themselves arrive at L2 latency.
+    // round-robin with non-blocking tests, never waiting on any one of them (a
+    // late consumer of one buffer must not hold up the loads of the others),
+    // and gives up (recording a timeout) once no stream has advanced for the
+    // wait limit.  With each K load it prefetches chunk c + 2's tiles and
+    // records into L2, so the loads themselves arrive at L2 latency.
     if (nch > 0 && lane == 0) {
       prefetch_tensormap(&qmap);
       prefetch_tensormap(&kmap);
       prefetch_tensormap(&vmap);
+      prefetch_tensormap(&omap);
       if (p.gated) prefetch_tensormap(&zmap);
       const bool withhold_v = g_test_fault == kFaultWithholdV;
       int64_t next[5] = {0, 0, 0, 0, 0};   // next chunk to load, per stream
@@ -671,7 +671,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
           const int t0 = (int)(start + c * CH);
           const unsigned char* rec = p.ws + ((size_t)(s_cbase + c) * p.hv + h) * kRecBytes;
           if (sidx == 0) {  // K_c and the gates into buffer c & 1, free once U_(c-2) is done
-            if (c >= 2 && !mbar_try_wait(&bars[B_K_EMPTY0 + bb], (uint32_t)(((c >> 1) - 1) & 1))) continue;
+            if (c >= 2 && !mbar_test_wait(&bars[B_K_EMPTY0 + bb], (uint32_t)(((c >> 1) - 1) & 1))) continue;
             if (c + 2 < nch) {
               const int t2 = t0 + 2 * CH;
               tma_prefetch_3d(&kmap, 0, kh, t2);
@@ -687,13 +687,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
             tma_load_3d(base + OFF_KB + bb * kBTile + 8192, &kmap, &bars[B_K_FULL0 + bb], 64, kh, t0);
             bulk_load(base + OFF_GATES + bb * kGateBytes, rec + kRecGates, kGateBytes, &bars[B_K_FULL0 + bb]);
             ++n_k[bb];
-          } else if (sidx == 1) {  // Q_c once Y_(c-1) has read Q~_(c-1)
-            if (c >= 1 && !mbar_try_wait(&bars[B_Q_EMPTY], par)) continue;
+          } else if (sidx == 1) {  // Q_c once the converter has read Q_(c-1)
+            if (c >= 1 && !mbar_test_wait(&bars[B_Q_EMPTY], par)) continue;
             mbar_arrive_expect_tx(&bars[B_Q_FULL], kBTile);
-            tma_load_3d(base + OFF_Q, &qmap, &bars[B_Q_FULL], 0, kh, t0);
-            tma_load_3d(base + OFF_Q + 8192, &qmap, &bars[B_Q_FULL], 64, kh, t0);
+            tma_load_3d(base + OFF_QB, &qmap, &bars[B_Q_FULL], 0, kh, t0);
+            tma_load_3d(base + OFF_QB + 8192, &qmap, &bars[B_Q_FULL], 64, kh, t0);
           } else if (sidx == 2) {  // V_c once R_(c-1) has read V_(c-1)
-            if (c >= 1 && !mbar_try_wait(&bars[B_V_EMPTY], par)) continue;
+            if (c >= 1 && !mbar_test_wait(&bars[B_V_EMPTY], par)) continue;
             if (withhold_v && c == 0) {
               // test fault: V_FULL never completes, so the waits on it run out
             } else if (flags & kChainZeroV) {
@@ -703,11 +703,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
               tma_load_3d(base + OFF_V, &vmap, &bars[B_V_FULL], 0, h, t0);
             }
           } else if (sidx == 3) {  // T_c once Delta_(c-1) has read T_(c-1)
-            if (c >= 1 && !mbar_try_wait(&bars[B_T_EMPTY], par)) continue;
+            if (c >= 1 && !mbar_test_wait(&bars[B_T_EMPTY], par)) continue;
             mbar_arrive_expect_tx(&bars[B_T_FULL], kTileTf32);
             bulk_load(base + OFF_T, rec + kRecT, kTileTf32, &bars[B_T_FULL]);
           } else {  // P_c once O_(c-1) has read P_(c-1)
-            if (c >= 1 && !mbar_try_wait(&bars[B_P_EMPTY], par)) continue;
+            if (c >= 1 && !mbar_test_wait(&bars[B_P_EMPTY], par)) continue;
             mbar_arrive_expect_tx(&bars[B_P_FULL], kTileTf32);
             bulk_load(base + OFF_P, rec + kRecP, kTileTf32, &bars[B_P_FULL]);
           }
@@ -738,22 +738,23 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Per chunk: X_c (the chain), Y_c, Delta_c, O_(c-1), U_c.  A product that
+    // Per chunk: [X|Y]_c (the chain), Delta_c, O_(c-1), U_c.  A product that
     // reads a TMEM operand written by the epilogue or by an earlier product is
     // issued after the barrier that says that operand is complete.
     if (lane == 0 && nch > 0) {
+      const uint32_t id128 = idesc_tf32_f32(128, 128);
       const uint32_t id64 = idesc_tf32_f32(128, 64);
       const uint32_t idu = idesc_bf16_f32_bmn(128, 128);
-      const uint32_t sK[2] = {smem_u32(base + OFF_K), smem_u32(base + OFF_K + kKTile)};
+      const uint32_t sKQ = smem_u32(base + OFF_KQ);
       const uint32_t sKb[2] = {smem_u32(base + OFF_KB), smem_u32(base + OFF_KB + kBTile)};
-      const uint32_t sQ = smem_u32(base + OFF_Q), sT = smem_u32(base + OFF_T), sP = smem_u32(base + OFF_P);
+      const uint32_t sT = smem_u32(base + OFF_T), sP = smem_u32(base + OFF_P);
       // O_c^T += Delta_c^T P_c^T onto Y of chunk c's parity.
       auto issue_o = [&](int64_t c) -> bool {
         if (!mbar_wait(&bars[B_P_FULL], (uint32_t)(c & 1), wait_ns)) return false;
         tc_fence_after();
         const uint32_t cb = (uint32_t)(c & 1);
         for (int ks = 0; ks < 8; ++ks)
-          mma_tf32_ts(tmem + TM_Y0 + 64 * cb, tmem + TM_D0 + 64 * cb + 8 * ks,
+          mma_tf32_ts(tmem + TM_XY + 128 * cb + 64, tmem + TM_D + 64 * cb + 8 * ks,
                       sdesc_sw128(sP + (ks >> 2) * 8192 + (ks & 3) * 32), id64, true);
         mma_commit(&bars[B_OU_DONE0 + cb]);
         mma_commit(&bars[B_P_EMPTY]);
@@ -763,45 +764,37 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
       for (int64_t c = 0; ok && c < nch; ++c) {
         const int bb = (int)(c & 1);
         const uint32_t par = (uint32_t)(c & 1);
-        // X_c = S K_c^T, S as left by U_(c-1)
-        ok = mbar_wait(&bars[B_K_READY0 + bb], (uint32_t)((c >> 1) & 1), wait_ns) &&
-             (c == 0 || mbar_wait(&bars[B_U_DONE], (uint32_t)((c - 1) & 1), wait_ns));
-        if (!ok || abort_flag) break;
-        tc_fence_after();
-        for (int ks = 0; ks < 16; ++ks)
-          mma_tf32_ts(tmem + TM_X, tmem + TM_S + 8 * ks, sdesc_sw128(sK[bb] + (ks >> 2) * 8192 + (ks & 3) * 32), id64,
-                      ks > 0);
-        mma_commit(&bars[B_X_DONE]);
-        // Y_c = S Q~_c^T into Y_b, once the output warps have read chunk c - 2's
-        ok = mbar_wait(&bars[B_Q_READY], par, wait_ns) &&
+        const uint32_t xy = tmem + TM_XY + 128 * (uint32_t)bb;
+        // [X|Y]_c = S [K ; Q~]_c^T, S as left by U_(c-1), into the region the
+        // output warps have finished with (chunk c - 2's Y)
+        ok = mbar_wait(&bars[B_KQ_READY], par, wait_ns) &&
+             (c == 0 || mbar_wait(&bars[B_U_DONE], (uint32_t)((c - 1) & 1), wait_ns)) &&
              (c < 2 || mbar_wait(&bars[B_Y_FREE0 + bb], (uint32_t)(((c >> 1) - 1) & 1), wait_ns));
         if (!ok || abort_flag) break;
         tc_fence_after();
         for (int ks = 0; ks < 16; ++ks)
-          mma_tf32_ts(tmem + TM_Y0 + 64 * bb, tmem + TM_S + 8 * ks, sdesc_sw128(sQ + (ks >> 2) * 8192 + (ks & 3) * 32),
-                      id64, ks > 0);
-        mma_commit(&bars[B_Y_DONE]);
-        mma_commit(&bars[B_Q_EMPTY]);
+          mma_tf32_ts(xy, tmem + TM_S + 8 * ks, sdesc_sw128(sKQ + (ks >> 2) * 16384 + (ks & 3) * 32), id128, ks > 0);
+        mma_commit(&bars[B_X_DONE]);
         // D_b = Delta_c^T = R^T T^T (R over X)
         ok = mbar_wait(&bars[B_T_FULL], par, wait_ns) && mbar_wait(&bars[B_R_READY], par, wait_ns);
         if (!ok || abort_flag) break;
         tc_fence_after();
         for (int ks = 0; ks < 8; ++ks)
-          mma_tf32_ts(tmem + TM_D0 + 64 * bb, tmem + TM_X + 8 * ks, sdesc_sw128(sT + (ks >> 2) * 8192 + (ks & 3) * 32),
-                      id64, ks > 0);
+          mma_tf32_ts(tmem + TM_D + 64 * bb, xy + 8 * ks, sdesc_sw128(sT + (ks >> 2) * 8192 + (ks & 3) * 32), id64,
+                      ks > 0);
         mma_commit(&bars[B_D_DONE]);
         mma_commit(&bars[B_T_EMPTY]);
         // O_(c-1), off the chain
         if (c > 0 && !(ok = issue_o(c - 1))) break;
-        // S = gamma S + Delta'^T K: Delta' hi then lo (packed bf16 in TMEM),
+        // S = gamma S + Delta'^T K: Delta' hi then lo (packed bf16 over X),
         // K from its bf16 TMA tile read MN-major (N = Dk contiguous)
         ok = mbar_wait(&bars[B_DD_READY], par, wait_ns);
         if (!ok || abort_flag) break;
         tc_fence_after();
         for (int part = 0; part < 2; ++part)
           for (int ks = 0; ks < 4; ++ks)
-            mma_bf16_ts(tmem + TM_S, tmem + (part ? TM_DPLO : TM_DPHI) + 8 * ks,
-                        sdesc_sw128_mn(sKb[bb] + ks * 2048, 8192, 1024), idu, true);
+            mma_bf16_ts(tmem + TM_S, xy + 32 * part + 8 * ks, sdesc_sw128_mn(sKb[bb] + ks * 2048, 8192, 1024), idu,
+                        true);
         mma_commit(&bars[B_U_DONE]);
         mma_commit(&bars[B_K_EMPTY0 + bb]);
       }
@@ -851,30 +844,46 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     for (int64_t c = 0; c < nch; ++c) {
       const uint32_t par = (uint32_t)(c & 1);
       const uint32_t cb = (uint32_t)(c & 1);
+      const uint32_t xq = tq + TM_XY + 128 * cb;  // this chunk's [X|Y] region, this warp's lanes
       const float* gates = reinterpret_cast<const float*>(sm + OFF_GATES + cb * kGateBytes);
 
-      // R = beta (V - e^G X) over X: tokens 32 half .. + 31 of row dv.
+      // beta V of tokens 32 half .. + 31 ahead of X, then
+      // R = beta V - (beta e^G) X over X.
       bool ok = mbar_wait(&bars[B_K_FULL0 + cb], (uint32_t)((c >> 1) & 1), wait_ns) &&  // the gates
-                mbar_wait(&bars[B_X_DONE], par, wait_ns) && mbar_wait(&bars[B_V_FULL], par, wait_ns);
+                mbar_wait(&bars[B_V_FULL], par, wait_ns);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(1, kEpiThreads, !ok)) break;
+      float bv[32];
+      {
+        const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_V) + dv;
+#pragma unroll
+        for (int i4 = 0; i4 < 32; i4 += 4) {
+          const float4 b4 = *reinterpret_cast<const float4*>(gates + GATE_BETA + half * 32 + i4);
+          const int t = half * 32 + i4;
+          bv[i4] = b4.x * __bfloat162float(V[t * DH]);
+          bv[i4 + 1] = b4.y * __bfloat162float(V[(t + 1) * DH]);
+          bv[i4 + 2] = b4.z * __bfloat162float(V[(t + 2) * DH]);
+          bv[i4 + 3] = b4.w * __bfloat162float(V[(t + 3) * DH]);
+        }
+      }
+      ok = mbar_wait(&bars[B_X_DONE], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
       {
-        const __nv_bfloat16* V = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_V);
         float x[32];
-        tmem_ld32(tq + TM_X + half * 32, x);
+        tmem_ld32(xq + half * 32, x);
         tmem_wait_ld();
 #pragma unroll
         for (int i4 = 0; i4 < 32; i4 += 4) {
           const float4 b4 = *reinterpret_cast<const float4*>(gates + GATE_BETA + half * 32 + i4);
           const float4 e4 = *reinterpret_cast<const float4*>(gates + GATE_EG + half * 32 + i4);
-          const int t = half * 32 + i4;
-          x[i4] = tf32_rn(b4.x * (__bfloat162float(V[t * DH + dv]) - x[i4] * e4.x));
-          x[i4 + 1] = tf32_rn(b4.y * (__bfloat162float(V[(t + 1) * DH + dv]) - x[i4 + 1] * e4.y));
-          x[i4 + 2] = tf32_rn(b4.z * (__bfloat162float(V[(t + 2) * DH + dv]) - x[i4 + 2] * e4.z));
-          x[i4 + 3] = tf32_rn(b4.w * (__bfloat162float(V[(t + 3) * DH + dv]) - x[i4 + 3] * e4.w));
+          x[i4] = tf32_rn(fmaf(-b4.x * e4.x, x[i4], bv[i4]));
+          x[i4 + 1] = tf32_rn(fmaf(-b4.y * e4.y, x[i4 + 1], bv[i4 + 1]));
+          x[i4 + 2] = tf32_rn(fmaf(-b4.z * e4.z, x[i4 + 2], bv[i4 + 2]));
+          x[i4 + 3] = tf32_rn(fmaf(-b4.w * e4.w, x[i4 + 3], bv[i4 + 3]));
         }
-        tmem_st32(tq + TM_X + half * 32, x);
+        tmem_st32(xq + half * 32, x);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -884,12 +893,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         mbar_arrive(&bars[B_V_EMPTY]);
       }
 
-      // gamma S once X_c and Y_c (which read S) are done; the state update
-      // then accumulates onto it.
-      ok = mbar_wait(&bars[B_Y_DONE], par, wait_ns);
-      if (!ok) record_error(&abort_flag);
-      if (named_sync_or(1, kEpiThreads, !ok)) break;
-      tc_fence_after();
+      // gamma S ([X|Y] has read S); the state update then accumulates onto it.
       {
         const float gamma = gates[GATE_GAMMA];
         for (int cc = 0; cc < 2; ++cc) {
@@ -904,27 +908,28 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
       }
 
       // Delta rounded to tf32 in place (the O product's operand), and
-      // Delta' = Delta diag(e^(G_last - G)) as packed bf16 hi / lo (the state
-      // update's operand).
+      // Delta' = Delta diag(e^(G_last - G)) as packed bf16 hi / lo over the
+      // dead R (the state update's operand).
+      float dg[32];
+      load_gate32(gates + GATE_DG + half * 32, dg);
       ok = mbar_wait(&bars[B_D_DONE], par, wait_ns);
       if (!ok) record_error(&abort_flag);
       if (named_sync_or(1, kEpiThreads, !ok)) break;
       tc_fence_after();
       {
-        float x[32], dg[32];
-        tmem_ld32(tq + TM_D0 + 64 * cb + half * 32, x);
-        load_gate32(gates + GATE_DG + half * 32, dg);
+        float x[32];
+        tmem_ld32(tq + TM_D + 64 * cb + half * 32, x);
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           dg[i] *= x[i];
           x[i] = tf32_rn(x[i]);
         }
-        tmem_st32(tq + TM_D0 + 64 * cb + half * 32, x);
+        tmem_st32(tq + TM_D + 64 * cb + half * 32, x);
         uint32_t hi[16], lo[16];
         split32_packed(dg, hi, lo);
-        tmem_st16(tq + TM_DPHI + half * 16, hi);
-        tmem_st16(tq + TM_DPLO + half * 16, lo);
+        tmem_st16(xq + half * 16, hi);
+        tmem_st16(xq + 32 + half * 16, lo);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -971,16 +976,37 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
       if (named_sync_or(2, kOutThreads, !ok)) break;
       tc_fence_after();
       float y[64];
-      tmem_ld32(tq + TM_Y0 + 64 * cb, *reinterpret_cast<float(*)[32]>(y));
-      tmem_ld32(tq + TM_Y0 + 64 * cb + 32, *reinterpret_cast<float(*)[32]>(y + 32));
+      tmem_ld32(tq + TM_XY + 128 * cb + 64, *reinterpret_cast<float(*)[32]>(y));
+      tmem_ld32(tq + TM_XY + 128 * cb + 96, *reinterpret_cast<float(*)[32]>(y + 32));
       tmem_wait_ld();
+      if (leader) bulk_wait_group_read0();  // the previous tile store has left the staging buffer
       tc_fence_before();
-      named_sync(2, kOutThreads);  // every thread has read Y_b (and the last chunk's staging)
+      named_sync(2, kOutThreads);
       if (leader) mbar_arrive(&bars[B_Y_FREE0 + cb]);
       if (flags & kChainNoOut) continue;  // a transition chain: only its final state is wanted
       if (!p.gated) {
-        // One token row per store: 32 lanes write 32 consecutive dv.
-        if (p.out_dtype == GDN_BF16) {
+        if (n == CH) {
+          // Whole chunk: stage [t][dv] in shared memory, one TMA tensor store.
+          if (p.out_dtype == GDN_BF16) {
+            unsigned short* st16 = reinterpret_cast<unsigned short*>(sm + OFF_OSTAGE);
+#pragma unroll
+            for (int i = 0; i < 64; i += 2) {
+              const uint32_t w2 = cvt_bf16x2(y[i], y[i + 1]);
+              st16[i * DH + dv] = (unsigned short)(w2 & 0xFFFFu);
+              st16[(i + 1) * DH + dv] = (unsigned short)(w2 >> 16);
+            }
+          } else {
+            float* st = reinterpret_cast<float*>(sm + OFF_OSTAGE);
+#pragma unroll
+            for (int i = 0; i < 64; ++i) st[i * DH + dv] = y[i];
+          }
+          fence_async_smem();
+          named_sync(2, kOutThreads);
+          if (leader) {
+            tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
+            bulk_commit_group();
+          }
+        } else if (p.out_dtype == GDN_BF16) {  // ragged last chunk: plain stores of the valid rows
           __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + dv;
 #pragma unroll
           for (int i = 0; i < 64; ++i)
@@ -995,8 +1021,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
       }
       // Fused-block output: y rounded to bf16 is staged [t][dv]; then the 16
       // lanes of a token (8 dv each) reduce its row, gate it with z (read
-      // from global memory, prefetched into L2 two chunks ahead) and store:
-      // out = silu(z) * rms_norm(y, w, eps).
+      // from global memory, prefetched into L2 two chunks ahead) and
+      // overwrite it in place: out = silu(z) * rms_norm(y, w, eps).
       __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
       unsigned short* st16 = reinterpret_cast<unsigned short*>(st);
 #pragma unroll
@@ -1013,7 +1039,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         zu[it] = tt < n ? *reinterpret_cast<const uint4*>(zb + (size_t)tt * p.z_st) : make_uint4(0u, 0u, 0u, 0u);
       }
       named_sync(2, kOutThreads);  // every row is staged
-      __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + g8;
       // The 8 items four at a time, phase by phase, so that the shuffle and
       // special-function latencies overlap.
 #pragma unroll
@@ -1051,33 +1076,47 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
             round2_bf16(n0, n1);
             ow[j] = pack_bf16(silu_fast(bf16_lo_f(zw[j])) * n0, silu_fast(bf16_hi_f(zw[j])) * n1);
           }
-          if (tt < n) *reinterpret_cast<uint4*>(ob + (size_t)tt * ostride) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          *reinterpret_cast<uint4*>(st + tt * DH + g8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+      }
+      if (n == CH) {
+        fence_async_smem();
+        named_sync(2, kOutThreads);
+        if (leader) {
+          tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
+          bulk_commit_group();
+        }
+      } else {  // ragged last chunk: the valid rows, 16 bytes per lane
+        __nv_bfloat16* ob = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + g8;
+        for (int it = 0; it < 8; ++it) {
+          const int tt = (e >> 4) + 8 * it;
+          if (tt < n) *reinterpret_cast<uint4*>(ob + (size_t)tt * ostride) = *reinterpret_cast<const uint4*>(st + tt * DH + g8);
         }
       }
     }
+    if (leader) bulk_wait_group0();  // every output tile has reached global memory
   } else {
-    // ------------------------------------------------- bf16 -> tf32 operands
-    // K_c from its bf16 tile into the fp32 tile of its parity, and
-    // Q~_c = diag(e^G) Q_c widened in place.
+    // ------------------------------------------------- bf16 -> tf32 operand tile
+    // [K ; Q~]_c into the fp32 tile once [X|Y]_(c-1) has read it: K_c from its
+    // bf16 tile (rows 0-63), Q~_c = diag(e^G) Q_c (rows 64-127).
     const int e = tid - 448;                  // 0..127 (warps 14-17)
     const bool leader = e == 0;
     for (int64_t c = 0; c < nch; ++c) {
       const int bb = (int)(c & 1);
-      bool ok = !abort_flag && mbar_wait(&bars[B_K_FULL0 + bb], (uint32_t)((c >> 1) & 1), wait_ns);
+      bool ok = !abort_flag && mbar_wait(&bars[B_K_FULL0 + bb], (uint32_t)((c >> 1) & 1), wait_ns) &&
+                mbar_wait(&bars[B_Q_FULL], (uint32_t)(c & 1), wait_ns) &&
+                (c == 0 || mbar_wait(&bars[B_X_DONE], (uint32_t)((c - 1) & 1), wait_ns));
       if (!ok && !abort_flag) record_error(&abort_flag);
       if (named_sync_or(3, kCvtThreads, !ok)) break;
-      widen_tile(base + OFF_KB + bb * kBTile, base + OFF_K + bb * kKTile, nullptr, e, 3);
+      widen_tile(base + OFF_KB + bb * kBTile, base + OFF_KQ, 0, nullptr, e);
+      widen_tile(base + OFF_QB, base + OFF_KQ, 64,
+                 reinterpret_cast<const float*>(base + OFF_GATES + bb * kGateBytes) + GATE_EG, e);
       fence_async_smem();
       named_sync(3, kCvtThreads);
-      if (leader) mbar_arrive(&bars[B_K_READY0 + bb]);
-      ok = !abort_flag && mbar_wait(&bars[B_Q_FULL], (uint32_t)(c & 1), wait_ns);
-      if (!ok && !abort_flag) record_error(&abort_flag);
-      if (named_sync_or(3, kCvtThreads, !ok)) break;
-      widen_tile(base + OFF_Q, base + OFF_Q, reinterpret_cast<const float*>(base + OFF_GATES + bb * kGateBytes) + GATE_EG,
-                 e, 3);
-      fence_async_smem();
-      named_sync(3, kCvtThreads);
-      if (leader) mbar_arrive(&bars[B_Q_READY]);
+      if (leader) {
+        mbar_arrive(&bars[B_Q_EMPTY]);
+        mbar_arrive(&bars[B_KQ_READY]);
+      }
     }
   }
 
@@ -1115,6 +1154,22 @@ bool make_map(CUtensorMap* map, const void* ptr, int64_t n_tokens, int heads, in
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// 3-D map over the contiguous output [N, Hv, 128] (fp32 or bf16), box {128, 1, 64}.
+bool make_out_map(CUtensorMap* map, void* ptr, int64_t n_tokens, int heads, gdn_dtype dt) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  std::memset(map, 0, sizeof(*map));
+  const cuuint64_t es = dt == GDN_BF16 ? 2 : 4;
+  cuuint64_t dims[3] = {(cuuint64_t)DH, (cuuint64_t)heads, (cuuint64_t)n_tokens};
+  cuuint64_t strides[2] = {DH * es, (cuuint64_t)heads * DH * es};
+  cuuint32_t box[3] = {(cuuint32_t)DH, 1, (cuuint32_t)CH};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt == GDN_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr,
+                   dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1264,7 +1319,7 @@ size_t chunked_workspace_bytes(const ScanParams& p) { return seg_layout(p, seg_c
 cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   if (!aligned_ptr16(sp.q) || !aligned_ptr16(sp.k) || !aligned_ptr16(sp.v) || !aligned_ptr16(sp.workspace))
     return cudaErrorMisalignedAddress;
-  CUtensorMap qmap, kmap, vmap, zmap;
+  CUtensorMap qmap, kmap, vmap, omap, zmap;
   const int64_t N = sp.n_tokens;
   const bool gated = sp.z != nullptr;
   if (gated && (sp.out_dtype != GDN_BF16 || !aligned_ptr16(sp.z) || !aligned_elems(sp.z_st) || !sp.norm_w))
@@ -1274,11 +1329,12 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     if (!make_map(&qmap, sp.q, N, sp.hk, sp.q_st, sp.q_sh, 64, true) ||
         !make_map(&kmap, sp.k, N, sp.hk, sp.k_st, sp.k_sh, 64, true) ||
         !make_map(&vmap, sp.v, N, sp.hv, sp.v_st, sp.v_sh, 128, false) ||
+        !make_out_map(&omap, sp.out, N, sp.hv, sp.out_dtype) ||
         (gated && !make_map(&zmap, sp.z, N, sp.hv, sp.z_st, DH, 128, false)))
       return cudaErrorInvalidValue;
   } else {
     std::memset(&qmap, 0, sizeof(qmap));
-    kmap = vmap = qmap;
+    kmap = vmap = omap = qmap;
   }
   ChunkParams p;
   p.n_tokens = N;
@@ -1336,7 +1392,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     }
     const int64_t ctas = sp.n_seqs * sp.hv;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    chunk_scan_kernel<<<(unsigned)ctas, kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, zmap, p);
+    chunk_scan_kernel<<<(unsigned)ctas, kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p);
     return cudaGetLastError();
   }
   // Chunk records: segments 0..P-2 before phase 1; the last segment's (needed
@@ -1382,7 +1438,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     p1.chains[i] = {i, nullptr, W + i * hstate, kChainNoOut};
     p1.chains[P - 2 + i] = {i, nullptr, Mt + (i - 1) * hstate, kChainIdentity | kChainZeroV | kChainNoOut};
   }
-  chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, zmap, p1);
+  chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // phase 2: start states, W[j] = W[j-1] M_j + U_j
@@ -1398,7 +1454,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   ChunkParams p3 = p;
   p3.n_chains = P - 1;
   for (int i = 1; i <= P - 1; ++i) p3.chains[i - 1] = {i, W + (i - 1) * hstate, i == P - 1 ? sp.state_out : nullptr, 0};
-  chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, zmap, p3);
+  chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p3);
   return cudaGetLastError();
 }
 

@@ -69,6 +69,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the same (returns at once; try_wait may suspend the
+// thread for a while when the phase is incomplete, so a thread polling
+// several barriers uses this).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete, for at most
 // `limit_ns` nanoseconds.  Returns false on timeout (the caller records the
 // error and winds down); never spins without bound.
@@ -341,11 +356,12 @@ __device__ __forceinline__ uint64_t sdesc_sw128_mn(uint32_t smem_addr, uint32_t 
   return d;
 }
 
-// float32 rounded to the nearest tf32 (10-bit mantissa, ties away from 0).
+// float32 rounded to the nearest tf32 (10-bit mantissa, ties away from 0 in
+// magnitude) by integer arithmetic on the bit pattern: two full-rate integer
+// instructions instead of a conversion on the special-function pipe.  For
+// finite inputs below the largest tf32 (the operands here are far smaller).
 __device__ __forceinline__ float tf32_rn(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 // Fire-and-forget L2 prefetches: a 3-D tensor tile, or `bytes` (multiple of
