@@ -543,7 +543,7 @@ constexpr uint32_t TM_S = 0, TM_XY = 128, TM_D = 384;
 enum Bar {
   B_K_FULL0, B_K_FULL1, B_K_EMPTY0, B_K_EMPTY1, B_KQ_READY,
   B_Q_FULL, B_Q_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
-  B_S_INIT, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_U_DONE,
+  B_S_INIT, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_DR_READY, B_U_DONE,
   B_OU_DONE0, B_OU_DONE1, B_Y_FREE0, B_Y_FREE1,
   B_DRAIN,
   N_BARS
@@ -581,7 +581,7 @@ __device__ __forceinline__ void widen_tile(const unsigned char* src, unsigned ch
   }
 }
 
-__global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                      const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
                                                                      const __grid_constant__ CUtensorMap omap,
@@ -738,7 +738,7 @@ __global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUten
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Per chunk: [X|Y]_c (the chain), Delta_c, O_(c-1), U_c.  A product that
+    // Per chunk: [X|Y]_c (the chain), O_(c-1), Delta_c, U_c.  A product that
     // reads a TMEM operand written by the epilogue or by an earlier product is
     // issued after the barrier that says that operand is complete.
     if (lane == 0 && nch > 0) {
@@ -748,16 +748,22 @@ __global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUten
       const uint32_t sKQ = smem_u32(base + OFF_KQ);
       const uint32_t sKb[2] = {smem_u32(base + OFF_KB), smem_u32(base + OFF_KB + kBTile)};
       const uint32_t sT = smem_u32(base + OFF_T), sP = smem_u32(base + OFF_P);
-      // O_c^T += Delta_c^T P_c^T onto Y of chunk c's parity.
-      auto issue_o = [&](int64_t c) -> bool {
-        if (!mbar_wait(&bars[B_P_FULL], (uint32_t)(c & 1), wait_ns)) return false;
+      // O_c^T += Delta_c^T P_c^T onto Y of chunk c's parity, in two halves
+      // of K (tokens 0-31, 32-63) placed where the tensor pipe would idle;
+      // the first half waits for the rounded Delta_c and P_c.
+      auto issue_o = [&](int64_t c, int part) -> bool {
+        if (part == 0 && (!mbar_wait(&bars[B_P_FULL], (uint32_t)(c & 1), wait_ns) ||
+                          !mbar_wait(&bars[B_DR_READY], (uint32_t)(c & 1), wait_ns)))
+          return false;
         tc_fence_after();
         const uint32_t cb = (uint32_t)(c & 1);
-        for (int ks = 0; ks < 8; ++ks)
+        for (int ks = 4 * part; ks < 4 * part + 4; ++ks)
           mma_tf32_ts(tmem + TM_XY + 128 * cb + 64, tmem + TM_D + 64 * cb + 8 * ks,
                       sdesc_sw128(sP + (ks >> 2) * 8192 + (ks & 3) * 32), id64, true);
-        mma_commit(&bars[B_OU_DONE0 + cb]);
-        mma_commit(&bars[B_P_EMPTY]);
+        if (part == 1) {
+          mma_commit(&bars[B_OU_DONE0 + cb]);
+          mma_commit(&bars[B_P_EMPTY]);
+        }
         return true;
       };
       bool ok = mbar_wait(&bars[B_S_INIT], 0, wait_ns);
@@ -768,15 +774,18 @@ __global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUten
         // [X|Y]_c = S [K ; Q~]_c^T, S as left by U_(c-1), into the region the
         // output warps have finished with (chunk c - 2's Y)
         ok = mbar_wait(&bars[B_KQ_READY], par, wait_ns) &&
-             (c == 0 || mbar_wait(&bars[B_U_DONE], (uint32_t)((c - 1) & 1), wait_ns)) &&
+             (c == 0 || mbar_wait_spin(&bars[B_U_DONE], (uint32_t)((c - 1) & 1), wait_ns)) &&
              (c < 2 || mbar_wait(&bars[B_Y_FREE0 + bb], (uint32_t)(((c >> 1) - 1) & 1), wait_ns));
         if (!ok || abort_flag) break;
         tc_fence_after();
         for (int ks = 0; ks < 16; ++ks)
           mma_tf32_ts(xy, tmem + TM_S + 8 * ks, sdesc_sw128(sKQ + (ks >> 2) * 16384 + (ks & 3) * 32), id128, ks > 0);
         mma_commit(&bars[B_X_DONE]);
+        // first half of O_(c-1) right behind it: it runs while the epilogue
+        // forms R, when the tensor pipe would otherwise idle
+        if (c > 0 && !(ok = issue_o(c - 1, 0))) break;
         // D_b = Delta_c^T = R^T T^T (R over X)
-        ok = mbar_wait(&bars[B_T_FULL], par, wait_ns) && mbar_wait(&bars[B_R_READY], par, wait_ns);
+        ok = mbar_wait(&bars[B_T_FULL], par, wait_ns) && mbar_wait_spin(&bars[B_R_READY], par, wait_ns);
         if (!ok || abort_flag) break;
         tc_fence_after();
         for (int ks = 0; ks < 8; ++ks)
@@ -784,11 +793,11 @@ __global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUten
                       ks > 0);
         mma_commit(&bars[B_D_DONE]);
         mma_commit(&bars[B_T_EMPTY]);
-        // O_(c-1), off the chain
-        if (c > 0 && !(ok = issue_o(c - 1))) break;
+        // second half of O_(c-1), while the epilogue forms Delta'
+        if (c > 0 && !(ok = issue_o(c - 1, 1))) break;
         // S = gamma S + Delta'^T K: Delta' hi then lo (packed bf16 over X),
         // K from its bf16 TMA tile read MN-major (N = Dk contiguous)
-        ok = mbar_wait(&bars[B_DD_READY], par, wait_ns);
+        ok = mbar_wait_spin(&bars[B_DD_READY], par, wait_ns);
         if (!ok || abort_flag) break;
         tc_fence_after();
         for (int part = 0; part < 2; ++part)
@@ -798,7 +807,7 @@ __global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUten
         mma_commit(&bars[B_U_DONE]);
         mma_commit(&bars[B_K_EMPTY0 + bb]);
       }
-      if (ok && !abort_flag) ok = issue_o(nch - 1);
+      if (ok && !abort_flag) ok = issue_o(nch - 1, 0) && issue_o(nch - 1, 1);
       if (!ok) record_error(&abort_flag);
       // Wait for every MMA issued so far before the CTA winds down.
       mma_commit(&bars[B_DRAIN]);
@@ -907,9 +916,9 @@ __global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUten
         }
       }
 
-      // Delta rounded to tf32 in place (the O product's operand), and
       // Delta' = Delta diag(e^(G_last - G)) as packed bf16 hi / lo over the
-      // dead R (the state update's operand).
+      // dead R (the state update's operand, on the chain), then Delta rounded
+      // to tf32 in place (the O product's operand, off it).
       float dg[32];
       load_gate32(gates + GATE_DG + half * 32, dg);
       ok = mbar_wait(&bars[B_D_DONE], par, wait_ns);
@@ -921,20 +930,23 @@ __global__ void __maxnreg__(112) chunk_scan_kernel(const __grid_constant__ CUten
         tmem_ld32(tq + TM_D + 64 * cb + half * 32, x);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          dg[i] *= x[i];
-          x[i] = tf32_rn(x[i]);
-        }
-        tmem_st32(tq + TM_D + 64 * cb + half * 32, x);
+        for (int i = 0; i < 32; ++i) dg[i] *= x[i];
         uint32_t hi[16], lo[16];
         split32_packed(dg, hi, lo);
         tmem_st16(xq + half * 16, hi);
         tmem_st16(xq + 32 + half * 16, lo);
         tmem_wait_st();
+        tc_fence_before();
+        named_sync(1, kEpiThreads);
+        if (leader) mbar_arrive(&bars[B_DD_READY]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[i] = tf32_rn(x[i]);
+        tmem_st32(tq + TM_D + 64 * cb + half * 32, x);
+        tmem_wait_st();
       }
       tc_fence_before();
       named_sync(1, kEpiThreads);
-      if (leader) mbar_arrive(&bars[B_DD_READY]);
+      if (leader) mbar_arrive(&bars[B_DR_READY]);
     }
 
     // Final state (or the initial one for an empty sequence) -> state_out.

@@ -97,6 +97,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// The same wait by polling with the non-blocking test: no suspend and wake-up
+// between the phase completing and the caller seeing it, for a single thread
+// on a latency-critical chain (it keeps its issue slot busy while it waits).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // TMA: 3-D tiled tensor load and 1-D bulk copy, completing on an mbarrier.
 // ---------------------------------------------------------------------------
