@@ -247,7 +247,7 @@ __device__ __forceinline__ void prep_level1(float* sA, float* sT, int tid) {
   *reinterpret_cast<float4*>(sT + (r1 + ii) * kPrepAStride + r0 + j0) = make_float4(-t[0], -t[1], -t[2], -t[3]);
 }
 
-__global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(128, 6) chunk_prep_kernel(const __grid_constant__ CUtensorMap qmap,
                                                             const __grid_constant__ CUtensorMap kmap,
                                                             const ChunkParams p) {
   const uint64_t wait_ns = g_wait_limit_ns;
@@ -269,18 +269,30 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
   const int kh = h / (p.hv / p.hk);
   const int64_t slot = blockIdx.x;
 
+  // The chunk's [K;Q] tile is requested as soon as its first token is known,
+  // so that the load overlaps the tensor-memory allocation and gate reads.
   if (warp == 0) {
     int64_t b = 0, j = 0;
     const bool valid = slot_to_chunk(p, slot, lane, b, j);
     if (lane == 0) {
       s_valid = valid ? 1 : 0;
+      abort_flag = 0;
       if (valid) {
         int64_t st, en;
         seq_range(p.cu, p.n_tokens, p.n_seqs, b, st, en);
-        s_t0 = st + j * CH;
-        s_n = (int)(en - s_t0 < CH ? en - s_t0 : CH);
+        const int64_t c0 = st + j * CH;
+        s_t0 = c0;
+        s_n = (int)(en - c0 < CH ? en - c0 : CH);
+        mbar_init(&bar_load, 1);
+        mbar_init(&bar_mma, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&bar_load, 32768);
+#pragma unroll
+        for (int kb = 0; kb < 2; ++kb) {
+          tma_load_3d(sKQ + kb * 16384, &kmap, &bar_load, kb * 64, kh, (int)c0);
+          tma_load_3d(sKQ + kb * 16384 + 8192, &qmap, &bar_load, kb * 64, kh, (int)c0);
+        }
       }
-      abort_flag = 0;
     }
   }
   __syncthreads();
@@ -289,11 +301,6 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
   const int n = s_n;
 
   if (warp == 0) tmem_alloc(&tmem_base, 64);
-  if (tid == 0) {
-    mbar_init(&bar_load, 1);
-    mbar_init(&bar_mma, 1);
-    fence_mbar_init();
-  }
   if (tid < CH) {
     const bool ok = tid < n;
     // Decays in log2 units: every exp below is an exp2 of a difference.
@@ -305,14 +312,6 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
   tc_fence_after();
   const uint32_t tmem = tmem_base;
 
-  if (tid == 0) {
-    mbar_arrive_expect_tx(&bar_load, 32768);
-#pragma unroll
-    for (int kb = 0; kb < 2; ++kb) {
-      tma_load_3d(sKQ + kb * 16384, &kmap, &bar_load, kb * 64, kh, (int)t0);
-      tma_load_3d(sKQ + kb * 16384 + 8192, &qmap, &bar_load, kb * 64, kh, (int)t0);
-    }
-  }
   if (warp == 1) {
     chunk_cumsum(lane, sl, sG, seG, sdG, &sgamma);
     __syncwarp();
@@ -455,12 +454,23 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
     const int i = tid >> 2, j0 = (tid & 3) * 8;
     float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const float* arow = sA + (32 + i) * kPrepAStride;
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      const float a = arow[k];
-      const float* trow = sT + k * kPrepAStride + j0;
+#pragma unroll 2
+    for (int k4 = 0; k4 < 32; k4 += 4) {
+      const float4 a4 = *reinterpret_cast<const float4*>(arow + k4);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w};
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) m[jj] = fmaf(a, trow[jj], m[jj]);
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 t0v = *reinterpret_cast<const float4*>(sT + (k4 + kk) * kPrepAStride + j0);
+        const float4 t1v = *reinterpret_cast<const float4*>(sT + (k4 + kk) * kPrepAStride + j0 + 4);
+        m[0] = fmaf(a[kk], t0v.x, m[0]);
+        m[1] = fmaf(a[kk], t0v.y, m[1]);
+        m[2] = fmaf(a[kk], t0v.z, m[2]);
+        m[3] = fmaf(a[kk], t0v.w, m[3]);
+        m[4] = fmaf(a[kk], t1v.x, m[4]);
+        m[5] = fmaf(a[kk], t1v.y, m[5]);
+        m[6] = fmaf(a[kk], t1v.z, m[6]);
+        m[7] = fmaf(a[kk], t1v.w, m[7]);
+      }
     }
     __syncthreads();
 #pragma unroll
@@ -471,12 +481,23 @@ __global__ void __launch_bounds__(128, 5) chunk_prep_kernel(const __grid_constan
     const int i = tid >> 2, j0 = (tid & 3) * 8;
     float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     const float* trow = sT + (32 + i) * kPrepAStride + 32;
-#pragma unroll 8
-    for (int k = 0; k < 32; ++k) {
-      const float tv = trow[k];
-      const float* mrow = sA + k * kPrepAStride + j0;
+#pragma unroll 2
+    for (int k4 = 0; k4 < 32; k4 += 4) {
+      const float4 t4 = *reinterpret_cast<const float4*>(trow + k4);
+      const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) m[jj] = fmaf(tv, mrow[jj], m[jj]);
+      for (int kk = 0; kk < 4; ++kk) {
+        const float4 m0v = *reinterpret_cast<const float4*>(sA + (k4 + kk) * kPrepAStride + j0);
+        const float4 m1v = *reinterpret_cast<const float4*>(sA + (k4 + kk) * kPrepAStride + j0 + 4);
+        m[0] = fmaf(tv[kk], m0v.x, m[0]);
+        m[1] = fmaf(tv[kk], m0v.y, m[1]);
+        m[2] = fmaf(tv[kk], m0v.z, m[2]);
+        m[3] = fmaf(tv[kk], m0v.w, m[3]);
+        m[4] = fmaf(tv[kk], m1v.x, m[4]);
+        m[5] = fmaf(tv[kk], m1v.y, m[5]);
+        m[6] = fmaf(tv[kk], m1v.z, m[6]);
+        m[7] = fmaf(tv[kk], m1v.w, m[7]);
+      }
     }
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) sT[(32 + i) * kPrepAStride + j0 + jj] = -m[jj];
