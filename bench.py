@@ -8,7 +8,7 @@ one decode launch over the batch; ``value`` is the state HBM traffic
 prefill number of config 3 (T=8192) under ``"prefill"``.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload decode|varlen|prefill|qproj|attn|layerdecode] [--tokens M]
+                    [--workload decode|varlen|prefill|block|qproj|attn|layerdecode] [--tokens M]
 
 ``--workload varlen`` is config 5 instead: 64 packed sequences (lengths
 ``default_rng(1).integers(256, 16384, 64, endpoint=True)``, 516,496 tokens)
@@ -599,6 +599,20 @@ def run_prefill(args):
                       "dtype": "bf16", "data": "synthetic"}), flush=True)
 
 
+def run_block(args):
+    """Only config 4 (the fused block over B=8 x T=4096, bf16 mixed
+    projection), K calls; for profiling the block's kernels on their own."""
+    device = torch.device("cuda", 0)
+    ms, tok = measure_block(device, iters=max(args.steps, 1))
+    _, tc_peak, _ = peaks()
+    flop = (PREFILL_FLOP // PREFILL_T) * tok
+    print(json.dumps({"metric": "config-4 fused block tok/s", "value": tok / (ms / 1e3), "unit": "tok/s",
+                      "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
+                      "achieved_tflops": flop / (ms / 1e3) / 1e12, "frac_of_bf16_peak": flop / (ms / 1e3) / 1e12 / tc_peak,
+                      "config": {"workload": "config 4: fused block, B=8 x T=4096, 16/32 heads, d=128"},
+                      "dtype": "bf16", "data": "synthetic"}), flush=True)
+
+
 def run_layerdecode(args):
     """Only the linear-attention layer at one decode token, launched eagerly
     (one kernel after another, as ncu lists them); for profiling the decode
@@ -873,21 +887,21 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="decode only: no e2e, prefill or CPU legs (for profiler runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg (profiler runs)")
-    ap.add_argument("--workload", choices=["decode", "varlen", "prefill", "qproj", "attn", "layerdecode"],
+    ap.add_argument("--workload", choices=["decode", "varlen", "prefill", "block", "qproj", "attn", "layerdecode"],
                     default="decode")
     ap.add_argument("--tokens", type=int, default=4096, help="rows of x for --workload qproj / attn")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.workload in ("qproj", "attn", "layerdecode", "prefill"):
+    if args.workload in ("qproj", "attn", "layerdecode", "prefill", "block"):
         if args.impl == "reference":
             why = ("a profiling workload of this build's own kernels; the reference arm times config 2 (default) "
-                   "and config 5 (--workload varlen)") if args.workload == "prefill" else (
+                   "and config 5 (--workload varlen)") if args.workload in ("prefill", "block") else (
                    "the reference's quantized matmul and attention are MLX's (mx.quantized_matmul, "
                    "mx.fast.scaled_dot_product_attention), not installable on this box")
             print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
             return
         return {"qproj": run_qproj, "attn": run_attn, "layerdecode": run_layerdecode,
-                "prefill": run_prefill}[args.workload](args)
+                "prefill": run_prefill, "block": run_block}[args.workload](args)
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         return run_reference(args, world, rank)

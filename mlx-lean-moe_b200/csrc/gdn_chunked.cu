@@ -547,7 +547,8 @@ constexpr uint32_t OFF_T = OFF_V + kBTile;            // T [t][s] tf32 (16 KB)
 constexpr uint32_t OFF_P = OFF_T + kTileTf32;         // P [t][s] tf32 (16 KB)
 constexpr uint32_t OFF_GATES = OFF_P + kTileTf32;     // two 1 KB gate buffers (chunk parity)
 constexpr uint32_t OFF_OSTAGE = OFF_GATES + 2 * kGateBytes;  // output staging [64 t][128 dv], out dtype
-constexpr uint32_t SCAN_SMEM_USED = OFF_OSTAGE + 64 * DH * 4;
+constexpr uint32_t OFF_Z = OFF_OSTAGE + 64 * DH * 4;          // gated output: z [64 t][128 dv] bf16 (TMA)
+constexpr uint32_t SCAN_SMEM_USED = OFF_Z + kBTile;
 constexpr size_t kScanSmem = 1024 + SCAN_SMEM_USED;
 static_assert(OFF_KB % 1024 == 0 && OFF_QB % 1024 == 0 && OFF_T % 1024 == 0 && OFF_P % 1024 == 0,
               "operand tiles on 1 KB boundaries");
@@ -565,7 +566,7 @@ enum Bar {
   B_K_FULL0, B_K_FULL1, B_K_EMPTY0, B_K_EMPTY1, B_KQ_READY,
   B_Q_FULL, B_Q_EMPTY, B_V_FULL, B_V_EMPTY, B_T_FULL, B_T_EMPTY, B_P_FULL, B_P_EMPTY,
   B_S_INIT, B_X_DONE, B_R_READY, B_D_DONE, B_DD_READY, B_DR_READY, B_U_DONE,
-  B_OU_DONE0, B_OU_DONE1, B_Y_FREE0, B_Y_FREE1,
+  B_OU_DONE0, B_OU_DONE1, B_Y_FREE0, B_Y_FREE1, B_Z_FULL,
   B_DRAIN,
   N_BARS
 };
@@ -999,6 +1000,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
 #pragma unroll
     for (int j = 0; j < 8; ++j) nw[j] = p.gated ? p.norm_w[g8 + j] : 0.f;
     const size_t ostride = (size_t)p.hv * DH;
+    // z of chunk c lands in its tile while chunk c - 1's output is formed:
+    // the leader requests it as soon as the norm of chunk c - 1 has read the
+    // tile (z of chunk 0 at once).
+    const bool zload = p.gated && !(flags & kChainNoOut);
+    int64_t n_z = 0;  // z tiles requested
+    if (zload && leader && nch > 0) {
+      mbar_arrive_expect_tx(&bars[B_Z_FULL], kBTile);
+      tma_load_3d(sm + OFF_Z, &zmap, &bars[B_Z_FULL], 0, h, (int)start);
+      n_z = 1;
+    }
     for (int64_t c = 0; c < nch; ++c) {
       const int64_t t0 = start + c * CH;
       const int n = (int)(end - t0 < CH ? end - t0 : CH);
@@ -1053,9 +1064,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         continue;
       }
       // Fused-block output: y rounded to bf16 is staged [t][dv]; then the 16
-      // lanes of a token (8 dv each) reduce its row, gate it with z (read
-      // from global memory, prefetched into L2 two chunks ahead) and
-      // overwrite it in place: out = silu(z) * rms_norm(y, w, eps).
+      // lanes of a token (8 dv each) reduce its row, gate it with z (from its
+      // tile) and overwrite it in place: out = silu(z) * rms_norm(y, w, eps).
       __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sm + OFF_OSTAGE);
       unsigned short* st16 = reinterpret_cast<unsigned short*>(st);
 #pragma unroll
@@ -1064,14 +1074,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         st16[i * DH + dv] = (unsigned short)(w2 & 0xFFFFu);
         st16[(i + 1) * DH + dv] = (unsigned short)(w2 >> 16);
       }
-      uint4 zu[8];  // items it: token (e >> 4) + 8 it
-      const __nv_bfloat16* zb = p.z + (size_t)t0 * p.z_st + (size_t)h * DH + g8;
-#pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int tt = (e >> 4) + 8 * it;
-        zu[it] = tt < n ? *reinterpret_cast<const uint4*>(zb + (size_t)tt * p.z_st) : make_uint4(0u, 0u, 0u, 0u);
-      }
-      named_sync(2, kOutThreads);  // every row is staged
+      ok = mbar_wait(&bars[B_Z_FULL], (uint32_t)(c & 1), wait_ns);
+      if (!ok) record_error(&abort_flag);
+      if (named_sync_or(2, kOutThreads, !ok)) break;  // every row is staged, z has landed
+      const __nv_bfloat16* zt = reinterpret_cast<const __nv_bfloat16*>(sm + OFF_Z);
       // The 8 items four at a time, phase by phase, so that the shuffle and
       // special-function latencies overlap.
 #pragma unroll
@@ -1079,7 +1085,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         uint4 yu[4];
         float ss[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) yu[k] = *reinterpret_cast<const uint4*>(st + ((e >> 4) + 8 * (i0 + k)) * DH + g8);
+        uint4 zu[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          yu[k] = *reinterpret_cast<const uint4*>(st + ((e >> 4) + 8 * (i0 + k)) * DH + g8);
+          zu[k] = *reinterpret_cast<const uint4*>(zt + ((e >> 4) + 8 * (i0 + k)) * DH + g8);
+        }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint32_t yw[4] = {yu[k].x, yu[k].y, yu[k].z, yu[k].w};
@@ -1101,7 +1112,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
           const int tt = (e >> 4) + 8 * (i0 + k);
           const float inv = rsqrtf(ss[k] * (1.f / DH) + p.norm_eps);
           const uint32_t yw[4] = {yu[k].x, yu[k].y, yu[k].z, yu[k].w};
-          const uint32_t zw[4] = {zu[i0 + k].x, zu[i0 + k].y, zu[i0 + k].z, zu[i0 + k].w};
+          const uint32_t zw[4] = {zu[k].x, zu[k].y, zu[k].z, zu[k].w};
           uint32_t ow[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
@@ -1112,9 +1123,14 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
           *reinterpret_cast<uint4*>(st + tt * DH + g8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
         }
       }
+      fence_async_smem();
+      named_sync(2, kOutThreads);  // every thread is done with z (and with the staged rows)
+      if (leader && c + 1 < nch) {  // z of the next chunk into the tile just read
+        mbar_arrive_expect_tx(&bars[B_Z_FULL], kBTile);
+        tma_load_3d(sm + OFF_Z, &zmap, &bars[B_Z_FULL], 0, h, (int)(t0 + CH));
+        n_z = c + 2;
+      }
       if (n == CH) {
-        fence_async_smem();
-        named_sync(2, kOutThreads);
         if (leader) {
           tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
           bulk_commit_group();
@@ -1128,6 +1144,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
       }
     }
     if (leader) bulk_wait_group0();  // every output tile has reached global memory
+    // After an abort, let the last z load in flight land (bounded) before the
+    // CTA releases its shared memory (tile i completes phase i & 1).
+    if (leader && n_z > 0) mbar_wait(&bars[B_Z_FULL], (uint32_t)((n_z - 1) & 1), wait_ns);
   } else {
     // ------------------------------------------------- bf16 -> tf32 operand tile
     // [K ; Q~]_c into the fp32 tile once [X|Y]_(c-1) has read it: K_c from its
