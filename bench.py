@@ -59,12 +59,13 @@ METRIC = "GDN prefill tok/s & decode state HBM GB/s (% peak) at 1/2/4/8 B200 vs 
 B, HK, HV, D = 64, 16, 32, 128
 STATE_BYTES = 2 * B * HV * D * D * 4  # read + write of the fp32 state
 DECODE_BYTES = STATE_BYTES + 2 * B * HK * D * 2 + B * HV * D * 2 + 2 * B * HV * 4 + B * HV * D * 4
-# DRAM bytes per decode_kernel launch at config 2 (read + write), from an ncu
-# capture of consecutive launches with the cache left alone between them
-# (see profiles/decode_config2.md).
-DECODE_NCU_TRAFFIC = 135_301_120 + 76_251_648
-DECODE_NCU_SOURCE = ("ncu capture of one launch at config 2 after an L2 flush (dram__bytes_read.sum 135,301,120 + "
-                     "dram__bytes_write.sum 76,251,648; the rest of the state write-back leaves L2 after the launch)")
+# DRAM bytes per decode_kernel launch at config 2 (read + write), averaged
+# over three consecutive launches of the back-to-back timed loop captured
+# with the cache left alone between them (profiles/decode_config2.md).
+DECODE_NCU_TRAFFIC = 132_349_781 + 131_684_864
+DECODE_NCU_SOURCE = ("ncu --cache-control none capture of launches 11-13 of the back-to-back loop (mean "
+                     "dram__bytes_read.sum 132,349,781 + dram__bytes_write.sum 131,684,864 per launch; "
+                     "algorithmic 270,548,992)")
 PREFILL_T = 8192
 PREFILL_FLOP = 182_955 * PREFILL_T * HV  # chunked WY count per token-head: (10 C^2 d + 6 C d^2 + 2/3 C^3) / C, C = 64, d = 128
 # Algorithmic bytes of one config-3 call: q, k (bf16) + v (bf16) + g, beta (fp32) + y (fp32) + final state (fp32).
@@ -73,8 +74,12 @@ PREFILL_BYTES = 2 * PREFILL_T * HK * D * 2 + PREFILL_T * HV * D * 2 + 2 * PREFIL
 # Counters of the config-3 prefill kernels from one ncu capture of a call
 # (profiles/chunked_prefill_config3.md): the tensor pipe's share of the scan
 # kernels' active cycles, and the DRAM bytes of all the call's kernels.
-PREFILL_NCU = {"tensor_pipe_frac": None, "traffic": None,
-               "ncu_source": "not captured on this tree yet"}
+PREFILL_NCU = {"tensor_pipe_frac": 0.293, "traffic": 585_521_408,
+               "ncu_source": "ncu --set full capture of one config-3 call (chunk_prep x2, chunk_scan x2, "
+                             "state_combine; profiles/chunked_prefill_config3.md): tensor_pipe_frac = "
+                             "sm__pipe_tensor_cycles_active of the scan launches (29.9 % and 28.8 % of their "
+                             "SMs' active cycles, time-weighted); traffic = dram__bytes_read.sum + "
+                             "dram__bytes_write.sum of the five launches"}
 
 
 def peaks():

@@ -1082,10 +1082,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
       // special-function latencies overlap.
 #pragma unroll
       for (int i0 = 0; i0 < 8; i0 += 4) {
-        uint4 yu[4];
+        uint4 yu[4], zu[4];
         float ss[4];
-#pragma unroll
-        uint4 zu[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           yu[k] = *reinterpret_cast<const uint4*>(st + ((e >> 4) + 8 * (i0 + k)) * DH + g8);
