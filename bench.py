@@ -74,10 +74,10 @@ PREFILL_BYTES = 2 * PREFILL_T * HK * D * 2 + PREFILL_T * HV * D * 2 + 2 * PREFIL
 # Counters of the config-3 prefill kernels from one ncu capture of a call
 # (profiles/chunked_prefill_config3.md): the tensor pipe's share of the scan
 # kernels' active cycles, and the DRAM bytes of all the call's kernels.
-PREFILL_NCU = {"tensor_pipe_frac": 0.293, "traffic": 585_521_408,
+PREFILL_NCU = {"tensor_pipe_frac": 0.296, "traffic": 581_989_376,
                "ncu_source": "ncu --set full capture of one config-3 call (chunk_prep x2, chunk_scan x2, "
                              "state_combine; profiles/chunked_prefill_config3.md): tensor_pipe_frac = "
-                             "sm__pipe_tensor_cycles_active of the scan launches (29.9 % and 28.8 % of their "
+                             "sm__pipe_tensor_cycles_active of the scan launches (30.1 % and 29.2 % of their "
                              "SMs' active cycles, time-weighted); traffic = dram__bytes_read.sum + "
                              "dram__bytes_write.sum of the five launches"}
 
