@@ -219,32 +219,28 @@ constexpr float kLog2e = 1.4426950408889634f;
 __device__ __forceinline__ void prep_level1(float* sA, float* sT, int tid) {
   const int pr = tid >> 6, ii = (tid >> 2) & 15, j0 = (tid & 3) * 4;
   const int r0 = 32 * pr, r1 = r0 + 16;  // first rows of blocks b0 and b1
-  float m[4] = {0.f, 0.f, 0.f, 0.f};
+  float2 m01 = make_float2(0.f, 0.f), m23 = make_float2(0.f, 0.f);
   const float* arow = sA + (r1 + ii) * kPrepAStride + r0;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
-    const float a = arow[k];
+    const float2 a = make_float2(arow[k], arow[k]);
     const float4 t4 = *reinterpret_cast<const float4*>(sT + (r0 + k) * kPrepAStride + r0 + j0);
-    m[0] = fmaf(a, t4.x, m[0]);
-    m[1] = fmaf(a, t4.y, m[1]);
-    m[2] = fmaf(a, t4.z, m[2]);
-    m[3] = fmaf(a, t4.w, m[3]);
+    m01 = ffma2(a, make_float2(t4.x, t4.y), m01);
+    m23 = ffma2(a, make_float2(t4.z, t4.w), m23);
   }
   // M -> the A[b0][b0] block (read only by the level-0 substitution, done).
-  *reinterpret_cast<float4*>(sA + (r0 + ii) * kPrepAStride + r0 + j0) = make_float4(m[0], m[1], m[2], m[3]);
+  *reinterpret_cast<float4*>(sA + (r0 + ii) * kPrepAStride + r0 + j0) = make_float4(m01.x, m01.y, m23.x, m23.y);
   __syncthreads();
-  float t[4] = {0.f, 0.f, 0.f, 0.f};
+  float2 t01 = make_float2(0.f, 0.f), t23 = make_float2(0.f, 0.f);
   const float* trow = sT + (r1 + ii) * kPrepAStride + r1;
 #pragma unroll
   for (int k = 0; k < 16; ++k) {
-    const float tv = trow[k];
+    const float2 tv = make_float2(trow[k], trow[k]);
     const float4 m4 = *reinterpret_cast<const float4*>(sA + (r0 + k) * kPrepAStride + r0 + j0);
-    t[0] = fmaf(tv, m4.x, t[0]);
-    t[1] = fmaf(tv, m4.y, t[1]);
-    t[2] = fmaf(tv, m4.z, t[2]);
-    t[3] = fmaf(tv, m4.w, t[3]);
+    t01 = ffma2(tv, make_float2(m4.x, m4.y), t01);
+    t23 = ffma2(tv, make_float2(m4.z, m4.w), t23);
   }
-  *reinterpret_cast<float4*>(sT + (r1 + ii) * kPrepAStride + r0 + j0) = make_float4(-t[0], -t[1], -t[2], -t[3]);
+  *reinterpret_cast<float4*>(sT + (r1 + ii) * kPrepAStride + r0 + j0) = make_float4(-t01.x, -t01.y, -t23.x, -t23.y);
 }
 
 __global__ void __launch_bounds__(128, 6) chunk_prep_kernel(const __grid_constant__ CUtensorMap qmap,
@@ -379,10 +375,15 @@ __global__ void __launch_bounds__(128, 6) chunk_prep_kernel(const __grid_constan
       float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
       if (s4 < s_lim) {
         const float4 g4 = *reinterpret_cast<const float4*>(sG + s4);
-        a4.x = (s4 < t && t < n) ? bt * ex2_approx(gt - g4.x) * v[s4] : 0.f;
-        a4.y = (s4 + 1 < t && t < n) ? bt * ex2_approx(gt - g4.y) * v[s4 + 1] : 0.f;
-        a4.z = (s4 + 2 < t && t < n) ? bt * ex2_approx(gt - g4.z) * v[s4 + 2] : 0.f;
-        a4.w = (s4 + 3 < t && t < n) ? bt * ex2_approx(gt - g4.w) * v[s4 + 3] : 0.f;
+        const float2 b2 = make_float2(bt, bt);
+        const float2 p01 = fmul2(fmul2(b2, make_float2(ex2_approx(gt - g4.x), ex2_approx(gt - g4.y))),
+                                 make_float2(v[s4], v[s4 + 1]));
+        const float2 p23 = fmul2(fmul2(b2, make_float2(ex2_approx(gt - g4.z), ex2_approx(gt - g4.w))),
+                                 make_float2(v[s4 + 2], v[s4 + 3]));
+        a4.x = (s4 < t && t < n) ? p01.x : 0.f;
+        a4.y = (s4 + 1 < t && t < n) ? p01.y : 0.f;
+        a4.z = (s4 + 2 < t && t < n) ? p23.x : 0.f;
+        a4.w = (s4 + 3 < t && t < n) ? p23.y : 0.f;
       }
       *reinterpret_cast<float4*>(arow + s4) = a4;
     }
@@ -393,10 +394,13 @@ __global__ void __launch_bounds__(128, 6) chunk_prep_kernel(const __grid_constan
     for (int s4 = 0; s4 < CH; s4 += 4) {
       if (s4 < s_lim) {
         const float4 g4 = *reinterpret_cast<const float4*>(sG + s4);
-        v[s4] = (s4 <= t && t < n) ? ex2_approx(gt - g4.x) * v[s4] : 0.f;
-        v[s4 + 1] = (s4 + 1 <= t && t < n) ? ex2_approx(gt - g4.y) * v[s4 + 1] : 0.f;
-        v[s4 + 2] = (s4 + 2 <= t && t < n) ? ex2_approx(gt - g4.z) * v[s4 + 2] : 0.f;
-        v[s4 + 3] = (s4 + 3 <= t && t < n) ? ex2_approx(gt - g4.w) * v[s4 + 3] : 0.f;
+        const float2 p01 = fmul2(make_float2(ex2_approx(gt - g4.x), ex2_approx(gt - g4.y)), make_float2(v[s4], v[s4 + 1]));
+        const float2 p23 =
+            fmul2(make_float2(ex2_approx(gt - g4.z), ex2_approx(gt - g4.w)), make_float2(v[s4 + 2], v[s4 + 3]));
+        v[s4] = (s4 <= t && t < n) ? p01.x : 0.f;
+        v[s4 + 1] = (s4 + 1 <= t && t < n) ? p01.y : 0.f;
+        v[s4 + 2] = (s4 + 2 <= t && t < n) ? p23.x : 0.f;
+        v[s4 + 3] = (s4 + 3 <= t && t < n) ? p23.y : 0.f;
       } else {
         v[s4] = v[s4 + 1] = v[s4 + 2] = v[s4 + 3] = 0.f;
       }
@@ -421,16 +425,16 @@ __global__ void __launch_bounds__(128, 6) chunk_prep_kernel(const __grid_constan
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const float* arow = sA + (off + i) * kPrepAStride + off;
-      float acc0 = 0.f, acc1 = 0.f;
+      // (even, odd) partial sums as one pair; a missing odd term multiplies
+      // 0 (A is finite, so the sum is unchanged)
+      float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
       for (int j4 = 0; j4 < i; j4 += 4) {
         const float4 a4 = *reinterpret_cast<const float4*>(arow + j4);
-        acc0 = fmaf(a4.x, x[j4], acc0);
-        if (j4 + 1 < i) acc1 = fmaf(a4.y, x[j4 + 1], acc1);
-        if (j4 + 2 < i) acc0 = fmaf(a4.z, x[j4 + 2], acc0);
-        if (j4 + 3 < i) acc1 = fmaf(a4.w, x[j4 + 3], acc1);
+        acc = ffma2(make_float2(a4.x, a4.y), make_float2(x[j4], j4 + 1 < i ? x[j4 + 1] : 0.f), acc);
+        if (j4 + 2 < i) acc = ffma2(make_float2(a4.z, a4.w), make_float2(x[j4 + 2], j4 + 3 < i ? x[j4 + 3] : 0.f), acc);
       }
-      x[i] = i < c ? 0.f : (i == c ? 1.f : -(acc0 + acc1));
+      x[i] = i < c ? 0.f : (i == c ? 1.f : -(acc.x + acc.y));
     }
     if (lane < 16) {
 #pragma unroll
@@ -452,7 +456,7 @@ __global__ void __launch_bounds__(128, 6) chunk_prep_kernel(const __grid_constan
   // Level 2: T21 = -T22 (A21 T11) with M = A21 T11 in the (dead) A11 block.
   {
     const int i = tid >> 2, j0 = (tid & 3) * 8;
-    float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float2 m[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     const float* arow = sA + (32 + i) * kPrepAStride;
 #pragma unroll 2
     for (int k4 = 0; k4 < 32; k4 += 4) {
@@ -462,24 +466,21 @@ __global__ void __launch_bounds__(128, 6) chunk_prep_kernel(const __grid_constan
       for (int kk = 0; kk < 4; ++kk) {
         const float4 t0v = *reinterpret_cast<const float4*>(sT + (k4 + kk) * kPrepAStride + j0);
         const float4 t1v = *reinterpret_cast<const float4*>(sT + (k4 + kk) * kPrepAStride + j0 + 4);
-        m[0] = fmaf(a[kk], t0v.x, m[0]);
-        m[1] = fmaf(a[kk], t0v.y, m[1]);
-        m[2] = fmaf(a[kk], t0v.z, m[2]);
-        m[3] = fmaf(a[kk], t0v.w, m[3]);
-        m[4] = fmaf(a[kk], t1v.x, m[4]);
-        m[5] = fmaf(a[kk], t1v.y, m[5]);
-        m[6] = fmaf(a[kk], t1v.z, m[6]);
-        m[7] = fmaf(a[kk], t1v.w, m[7]);
+        const float2 aa = make_float2(a[kk], a[kk]);
+        m[0] = ffma2(aa, make_float2(t0v.x, t0v.y), m[0]);
+        m[1] = ffma2(aa, make_float2(t0v.z, t0v.w), m[1]);
+        m[2] = ffma2(aa, make_float2(t1v.x, t1v.y), m[2]);
+        m[3] = ffma2(aa, make_float2(t1v.z, t1v.w), m[3]);
       }
     }
     __syncthreads();
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) sA[i * kPrepAStride + j0 + jj] = m[jj];
+    *reinterpret_cast<float4*>(sA + i * kPrepAStride + j0) = make_float4(m[0].x, m[0].y, m[1].x, m[1].y);
+    *reinterpret_cast<float4*>(sA + i * kPrepAStride + j0 + 4) = make_float4(m[2].x, m[2].y, m[3].x, m[3].y);
   }
   __syncthreads();
   {
     const int i = tid >> 2, j0 = (tid & 3) * 8;
-    float m[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float2 m[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     const float* trow = sT + (32 + i) * kPrepAStride + 32;
 #pragma unroll 2
     for (int k4 = 0; k4 < 32; k4 += 4) {
@@ -489,18 +490,16 @@ __global__ void __launch_bounds__(128, 6) chunk_prep_kernel(const __grid_constan
       for (int kk = 0; kk < 4; ++kk) {
         const float4 m0v = *reinterpret_cast<const float4*>(sA + (k4 + kk) * kPrepAStride + j0);
         const float4 m1v = *reinterpret_cast<const float4*>(sA + (k4 + kk) * kPrepAStride + j0 + 4);
-        m[0] = fmaf(tv[kk], m0v.x, m[0]);
-        m[1] = fmaf(tv[kk], m0v.y, m[1]);
-        m[2] = fmaf(tv[kk], m0v.z, m[2]);
-        m[3] = fmaf(tv[kk], m0v.w, m[3]);
-        m[4] = fmaf(tv[kk], m1v.x, m[4]);
-        m[5] = fmaf(tv[kk], m1v.y, m[5]);
-        m[6] = fmaf(tv[kk], m1v.z, m[6]);
-        m[7] = fmaf(tv[kk], m1v.w, m[7]);
+        const float2 tt = make_float2(tv[kk], tv[kk]);
+        m[0] = ffma2(tt, make_float2(m0v.x, m0v.y), m[0]);
+        m[1] = ffma2(tt, make_float2(m0v.z, m0v.w), m[1]);
+        m[2] = ffma2(tt, make_float2(m1v.x, m1v.y), m[2]);
+        m[3] = ffma2(tt, make_float2(m1v.z, m1v.w), m[3]);
       }
     }
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj) sT[(32 + i) * kPrepAStride + j0 + jj] = -m[jj];
+    *reinterpret_cast<float4*>(sT + (32 + i) * kPrepAStride + j0) = make_float4(-m[0].x, -m[0].y, -m[1].x, -m[1].y);
+    *reinterpret_cast<float4*>(sT + (32 + i) * kPrepAStride + j0 + 4) =
+        make_float4(-m[2].x, -m[2].y, -m[3].x, -m[3].y);
   }
   __syncthreads();
   {
