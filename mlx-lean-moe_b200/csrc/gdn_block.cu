@@ -396,12 +396,14 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
       if (active && t + PF < t_end) ring[u].load(src + (t + PF) * p.mixed_st);
       float x[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        float acc = 0.f;
+      for (int i = 0; i < 8; i += 2) {  // channel pairs: packed FMAs, the scalar order per channel
+        float2 acc = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < K - 1; ++j) acc += w[i][j] * win[j][i];
-        acc += w[i][K - 1] * cur[i];
-        x[i] = acc;
+        for (int j = 0; j < K - 1; ++j)
+          acc = ffma2(make_float2(w[i][j], w[i + 1][j]), make_float2(win[j][i], win[j][i + 1]), acc);
+        acc = ffma2(make_float2(w[i][K - 1], w[i + 1][K - 1]), make_float2(cur[i], cur[i + 1]), acc);
+        x[i] = acc.x;
+        x[i + 1] = acc.y;
       }
       round8<T>(x);  // the conv output, then SiLU of it, in the activation dtype
 #pragma unroll
@@ -423,10 +425,18 @@ __global__ void __launch_bounds__(256) block_prologue_fast_kernel(const BlockPar
         const float inv = rsqrtf(ss / (float)p.dk + 1e-6f);
         const float scale = is_q ? qscale : kscale;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] *= inv;
+        for (int i = 0; i < 8; i += 2) {
+          const float2 r = fmul2(make_float2(x[i], x[i + 1]), make_float2(inv, inv));
+          x[i] = r.x;
+          x[i + 1] = r.y;
+        }
         round8<T>(x);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] *= scale;
+        for (int i = 0; i < 8; i += 2) {
+          const float2 r = fmul2(make_float2(x[i], x[i + 1]), make_float2(scale, scale));
+          x[i] = r.x;
+          x[i + 1] = r.y;
+        }
         round8<T>(x);
         T* dst = static_cast<T*>(is_q ? p.q : p.k) + t * key_dim + (is_q ? c : c - key_dim);
         if (active) store8<T>(dst, x);
