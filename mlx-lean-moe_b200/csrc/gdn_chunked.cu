@@ -1244,51 +1244,62 @@ __global__ void seg_setup_kernel(const SegCu c, int n, int64_t* cu) {
   if (threadIdx.x <= n) cu[threadIdx.x] = c.cu[threadIdx.x];
 }
 
-// next = prev * M + next for every head (128 x 128 fp32 each).  Grid
-// (Hv, 4): 32 rows of one head per CTA, M (64 KB) and the rows (16 KB) staged
-// in shared memory with every load in flight at once; thread = 2 rows x 8
+// Every start state of a segmented sequence in one launch: W_j = W_(j-1) M_j +
+// U_j for j = 1 .. n and every head (128 x 128 fp32 each; W_j holds U_j on
+// entry).  Grid (Hv, 4): 32 rows of one head per CTA.  A row block of W_j
+// depends only on the same rows of W_(j-1), so each CTA walks j on its own:
+// its rows of W_(j-1) stay in shared memory from the step before, M_j (64 KB)
+// is staged per step with every load in flight at once; thread = 2 rows x 8
 // columns.
 constexpr size_t kCombineSmem = (size_t)(DH + 32) * DH * sizeof(float);
-__global__ void __launch_bounds__(256) state_combine_kernel(const float* __restrict__ prev, const float* __restrict__ M,
-                                                            float* next) {
+__global__ void __launch_bounds__(256) state_combine_kernel(float* W, const float* Mt, int n, size_t hstate) {
   extern __shared__ __align__(16) float csm[];
-  float* sm = csm;            // [128][128] M
-  float* sa = csm + DH * DH;  // [32][128] rows of prev
+  float* sm = csm;            // [128][128] M_j
+  float* sa = csm + DH * DH;  // [32][128] rows of W_(j-1)
   const int tid = threadIdx.x, r = (tid >> 4) * 2, c0 = (tid & 15) * 8;
   const size_t head = (size_t)blockIdx.x * DH * DH;
   const int r0 = blockIdx.y * 32;
-  const float4* Mh = reinterpret_cast<const float4*>(M + head);
-  const float4* A = reinterpret_cast<const float4*>(prev + head + (size_t)r0 * DH);
+  {
+    const float4* A = reinterpret_cast<const float4*>(W + head + (size_t)r0 * DH);
 #pragma unroll 4
-  for (int i = tid; i < DH * DH / 4; i += 256) reinterpret_cast<float4*>(sm)[i] = Mh[i];
-#pragma unroll 4
-  for (int i = tid; i < 32 * DH / 4; i += 256) reinterpret_cast<float4*>(sa)[i] = A[i];
-  float* C = next + head + (size_t)(r0 + r) * DH + c0;
-  float acc[2][8];
-#pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    const float4 x0 = *reinterpret_cast<const float4*>(C + rr * DH);
-    const float4 x1 = *reinterpret_cast<const float4*>(C + rr * DH + 4);
-    acc[rr][0] = x0.x; acc[rr][1] = x0.y; acc[rr][2] = x0.z; acc[rr][3] = x0.w;
-    acc[rr][4] = x1.x; acc[rr][5] = x1.y; acc[rr][6] = x1.z; acc[rr][7] = x1.w;
+    for (int i = tid; i < 32 * DH / 4; i += 256) reinterpret_cast<float4*>(sa)[i] = A[i];
   }
-  __syncthreads();
+  for (int j = 1; j <= n; ++j) {
+    const float4* Mh = reinterpret_cast<const float4*>(Mt + (size_t)(j - 1) * hstate + head);
 #pragma unroll 4
-  for (int k = 0; k < DH; ++k) {
-    const float a0 = sa[r * DH + k], a1 = sa[(r + 1) * DH + k];
-    const float4 m0 = *reinterpret_cast<const float4*>(sm + k * DH + c0);
-    const float4 m1 = *reinterpret_cast<const float4*>(sm + k * DH + c0 + 4);
-    const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+    for (int i = tid; i < DH * DH / 4; i += 256) reinterpret_cast<float4*>(sm)[i] = Mh[i];
+    float* C = W + (size_t)j * hstate + head + (size_t)(r0 + r) * DH + c0;
+    float acc[2][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      acc[0][j] = fmaf(a0, mv[j], acc[0][j]);
-      acc[1][j] = fmaf(a1, mv[j], acc[1][j]);
+    for (int rr = 0; rr < 2; ++rr) {
+      const float4 x0 = *reinterpret_cast<const float4*>(C + rr * DH);
+      const float4 x1 = *reinterpret_cast<const float4*>(C + rr * DH + 4);
+      acc[rr][0] = x0.x; acc[rr][1] = x0.y; acc[rr][2] = x0.z; acc[rr][3] = x0.w;
+      acc[rr][4] = x1.x; acc[rr][5] = x1.y; acc[rr][6] = x1.z; acc[rr][7] = x1.w;
     }
-  }
+    __syncthreads();  // M_j and the rows of W_(j-1) are staged
+#pragma unroll 4
+    for (int k = 0; k < DH; ++k) {
+      const float a0 = sa[r * DH + k], a1 = sa[(r + 1) * DH + k];
+      const float4 m0 = *reinterpret_cast<const float4*>(sm + k * DH + c0);
+      const float4 m1 = *reinterpret_cast<const float4*>(sm + k * DH + c0 + 4);
+      const float mv[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
 #pragma unroll
-  for (int rr = 0; rr < 2; ++rr) {
-    *reinterpret_cast<float4*>(C + rr * DH) = make_float4(acc[rr][0], acc[rr][1], acc[rr][2], acc[rr][3]);
-    *reinterpret_cast<float4*>(C + rr * DH + 4) = make_float4(acc[rr][4], acc[rr][5], acc[rr][6], acc[rr][7]);
+      for (int jj = 0; jj < 8; ++jj) {
+        acc[0][jj] = fmaf(a0, mv[jj], acc[0][jj]);
+        acc[1][jj] = fmaf(a1, mv[jj], acc[1][jj]);
+      }
+    }
+    __syncthreads();  // every thread is done with M_j and with W_(j-1)
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+      const float4 lo = make_float4(acc[rr][0], acc[rr][1], acc[rr][2], acc[rr][3]);
+      const float4 hi = make_float4(acc[rr][4], acc[rr][5], acc[rr][6], acc[rr][7]);
+      *reinterpret_cast<float4*>(C + rr * DH) = lo;
+      *reinterpret_cast<float4*>(C + rr * DH + 4) = hi;
+      *reinterpret_cast<float4*>(sa + (r + rr) * DH + c0) = lo;
+      *reinterpret_cast<float4*>(sa + (r + rr) * DH + c0 + 4) = hi;
+    }
   }
 }
 
@@ -1490,10 +1501,9 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  // phase 2: start states, W[j] = W[j-1] M_j + U_j
-  for (int j = 1; j <= P - 2; ++j) {
-    state_combine_kernel<<<dim3((unsigned)sp.hv, DH / 32), 256, kCombineSmem, s>>>(
-        W + (j - 1) * hstate, Mt + (j - 1) * hstate, W + j * hstate);
+  // phase 2: start states, W[j] = W[j-1] M_j + U_j for j = 1 .. P-2, one launch
+  if (P > 2) {
+    state_combine_kernel<<<dim3((unsigned)sp.hv, DH / 32), 256, kCombineSmem, s>>>(W, Mt, P - 2, hstate);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
