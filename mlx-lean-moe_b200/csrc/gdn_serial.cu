@@ -60,8 +60,13 @@ __device__ __forceinline__ float4 load_vec4(const T* row, int col, int dk) {
 }
 
 // One token for each of B sequences.  Grid: x = B * row tiles, y = Hv.
+// Launched as a programmatic dependent of the kernel before it (typically the
+// previous decode step): its CTAs become resident while that kernel drains
+// and wait here before touching memory.
 template <int DKP, typename T>
 __global__ void __launch_bounds__(128) decode_kernel(const ScanParams p) {
+  griddep_wait();  // launched as a dependent of the kernel before it
+  griddep_launch_dependents();
   using L = Layout<DKP>;
   const int n_tiles = (p.dv + L::ROWS - 1) / L::ROWS;
   const int64_t b = blockIdx.x / n_tiles;
@@ -302,8 +307,7 @@ cudaError_t launch_one(const ScanParams& p, cudaStream_t s, bool decode) {
   if (gx > 0x7fffffffLL || p.hv > 65535) return cudaErrorInvalidConfiguration;
   dim3 grid((unsigned)gx, (unsigned)p.hv);
   if (!decode) return launch_dependent(serial_scan_kernel<DKP, T>, grid, dim3(128), 0, s, p);
-  decode_kernel<DKP, T><<<grid, 128, 0, s>>>(p);
-  return cudaGetLastError();
+  return launch_dependent(decode_kernel<DKP, T>, grid, dim3(128), 0, s, p);
 }
 
 template <typename T>
