@@ -880,6 +880,34 @@ def measure_sharded(world, rank, device, steps=3):
         "all_gather_ms": ag_ms / steps, "heads_per_rank": HV // world, "scaling": "strong",
         "note": "T=8192, value heads split over the ranks with their key heads, bf16 outputs all-gathered "
                 "(NCCL all_gather_into_tensor) into [8192, 32, 128] on every rank"}
+
+    if world > 1:
+        # the same, with the gather fused into the scan: each rank's output
+        # tiles go to every rank's [8192, 32, 128] buffer over NVLink from the
+        # scan kernel (gdn_scan_gathered), then a one-element all-reduce
+        from gdn_b200.sharding import GatheredHeads
+
+        gh = GatheredHeads(PREFILL_T, HV, D, torch.bfloat16, device)
+        for _ in range(2):
+            gh.scan(ql, kl, vl, gl, bl, None, vs.start, g_is_log=True)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            gh.scan(ql, kl, vl, gl, bl, None, vs.start, g_is_log=True)
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1)], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        fused_ms = float(t.item()) / steps
+        gh.close()
+        res["config3_head_sharded_fused_gather"] = {
+            "tok_s": PREFILL_T / (fused_ms / 1e3), "ms": fused_ms, "heads_per_rank": HV // world,
+            "scaling": "strong", "kernel": "chunk_scan_kernel with peer stores (gdn_scan_gathered)",
+            "note": "as config3_head_sharded, but the scan's output stage writes each bf16 output tile into every "
+                    "rank's [8192, 32, 128] buffer (16-byte stores over NVLink to CUDA-IPC mappings), then a "
+                    "one-element NCCL all-reduce orders the readers; no all-gather"}
     return res
 
 

@@ -302,6 +302,41 @@ typedef struct {
 gdn_status gdn_attention_workspace_size(const gdn_attn_args *args, size_t *bytes);
 gdn_status gdn_attention(const gdn_attn_args *args, gdn_stream_t stream);
 
+/* Head-sharded prefill with the output all-gather fused into the scan.
+ *
+ * The reference has no multi-device path; this is the optional all-gather of
+ * head-sharded outputs (one process per GPU, each scanning whole GQA groups,
+ * value heads [head0, head0 + hv) of hv_total) done by the scan kernel itself:
+ * its output stage writes each finished 64-token tile of y into this rank's
+ * gathered output (args->out, [N, hv_total, Dv] contiguous, out_dtype) and,
+ * with 16-byte stores over NVLink, into every other rank's (peer_out: their
+ * gathered outputs as mapped on this device, e.g. by gdn_ipc_import), so the
+ * transfer overlaps the scan instead of following it.  Everything else is
+ * gdn_scan's (the workspace is gdn_scan_workspace_size of the same args);
+ * the chunked path only (bf16 q/k/v, dk == dv == 128).  A rank's buffer is
+ * complete once every rank's call has completed: order its readers after a
+ * cross-rank barrier (e.g. a one-element NCCL all-reduce on the stream). */
+#define GDN_MAX_GATHER_PEERS 7
+typedef struct {
+  int32_t hv_total;            /* value heads of the gathered output          */
+  int32_t head0;               /* first value head of this call within it     */
+  int32_t n_peers;             /* 0 .. GDN_MAX_GATHER_PEERS                   */
+  int32_t reserved;            /* 0                                           */
+  void *peer_out[GDN_MAX_GATHER_PEERS]; /* 16-byte aligned                    */
+} gdn_gather_args;
+
+gdn_status gdn_scan_gathered(const gdn_scan_args *args, const gdn_gather_args *gather, gdn_stream_t stream);
+
+/* CUDA IPC for the peer outputs above (no counterpart in the reference).
+ * gdn_ipc_export writes the handle of the allocation that holds `ptr` and
+ * ptr's byte offset in it; gdn_ipc_import maps a handle exported by another
+ * process of this node into this one (peer access enabled) and returns the
+ * address of the same byte; gdn_ipc_release unmaps it. */
+#define GDN_IPC_HANDLE_BYTES 64
+gdn_status gdn_ipc_export(const void *ptr, unsigned char *handle, uint64_t *offset);
+gdn_status gdn_ipc_import(const unsigned char *handle, uint64_t offset, void **ptr);
+gdn_status gdn_ipc_release(void *ptr, uint64_t offset);
+
 /* Synchronises `stream`, then reports and clears any error a bounded
  * device-side wait recorded since the last call (GDN_ETIMEOUT), or a CUDA
  * error (GDN_ECUDA). */

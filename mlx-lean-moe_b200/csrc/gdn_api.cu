@@ -4,6 +4,9 @@
 // its kernel (src/mlx_lean_moe/model/qwen3_5/gated_delta.py:57-79).
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
+
+#include <cuda.h>
 #include <string>
 
 #include "gdn_common.cuh"
@@ -141,6 +144,27 @@ gdn_status set_error(gdn_status st, const char* fmt, ...) {
   g_last_error = buf;
   return st;
 }
+// Base and size of the device allocation holding ptr (cuMemGetAddressRange,
+// reached through the runtime's driver entry point).
+gdn_status allocation_range(const void* ptr, void** base, size_t* size) {
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !f)
+      return set_error(GDN_ECUDA, "cuMemGetAddressRange is not available");
+    fn = reinterpret_cast<GetRange>(f);
+  }
+  CUdeviceptr b = 0;
+  size_t n = 0;
+  const CUresult r = fn(&b, &n, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return set_error(GDN_EINVAL, "cuMemGetAddressRange failed (%d): not a device allocation", (int)r);
+  *base = reinterpret_cast<void*>(b);
+  *size = n;
+  return GDN_OK;
+}
 }  // namespace gdn
 
 extern "C" {
@@ -176,6 +200,68 @@ gdn_status gdn_scan(const gdn_scan_args* args, gdn_stream_t stream) {
     return cuda_status(gdn::launch_chunked_scan(p, s), "chunked scan launch");
   }
   return cuda_status(gdn::launch_serial_scan(p, s), "serial scan launch");
+}
+
+gdn_status gdn_scan_gathered(const gdn_scan_args* args, const gdn_gather_args* gather, gdn_stream_t stream) {
+  if (!gather) return fail(GDN_EINVAL, "gather is NULL");
+  gdn::ScanParams p;
+  gdn_status st = check_scan(args, &p, args ? args->n_seqs : 0);
+  if (st != GDN_OK) return st;
+  if (gather->hv_total < args->hv || gather->head0 < 0 || gather->head0 > gather->hv_total - args->hv)
+    return fail(GDN_EINVAL, "heads [head0, head0 + hv) = [%d, %d) must lie in [0, hv_total = %d)", gather->head0,
+                gather->head0 + args->hv, gather->hv_total);
+  if (gather->n_peers < 0 || gather->n_peers > GDN_MAX_GATHER_PEERS)
+    return fail(GDN_EINVAL, "n_peers must be in [0, %d] (got %d)", GDN_MAX_GATHER_PEERS, gather->n_peers);
+  if (gather->reserved) return fail(GDN_EINVAL, "gather->reserved must be 0");
+  if (!aligned16(args->out)) return fail(GDN_EINVAL, "out must be 16-byte aligned");
+  for (int j = 0; j < gather->n_peers; ++j)
+    if (!gather->peer_out[j] || !aligned16(gather->peer_out[j]) || gather->peer_out[j] == args->out)
+      return fail(GDN_EINVAL, "peer_out[%d] must be a 16-byte aligned buffer other than out", j);
+  bool chunked = false;
+  st = pick_algo(args, p, &chunked);
+  if (st != GDN_OK) return st;
+  if (!chunked)
+    return fail(GDN_EUNSUPPORTED, "the gathered scan runs on the chunked path only (bf16 q/k/v, dk == dv == 128, "
+                                  "sequences of 128+ tokens on average or algo = CHUNKED)");
+  const size_t need = gdn::chunked_workspace_bytes(p);
+  if (args->workspace_bytes < need || (need && !args->workspace))
+    return fail(GDN_EINVAL, "workspace too small: %zu bytes given, %zu needed", args->workspace_bytes, need);
+  p.out_hv = gather->hv_total;
+  p.head0 = gather->head0;
+  p.n_peers = gather->n_peers;
+  for (int j = 0; j < gather->n_peers; ++j) p.peer_out[j] = gather->peer_out[j];
+  return cuda_status(gdn::launch_chunked_scan(p, static_cast<cudaStream_t>(stream)), "gathered scan launch");
+}
+
+gdn_status gdn_ipc_export(const void* ptr, unsigned char* handle, uint64_t* offset) {
+  if (!ptr || !handle || !offset) return fail(GDN_EINVAL, "ptr, handle and offset must be non-NULL");
+  void* base = nullptr;
+  size_t size = 0;
+  gdn_status st = gdn::allocation_range(ptr, &base, &size);
+  if (st != GDN_OK) return st;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, base);
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == GDN_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  *offset = (uint64_t)(static_cast<const char*>(ptr) - static_cast<const char*>(base));
+  return GDN_OK;
+}
+
+gdn_status gdn_ipc_import(const unsigned char* handle, uint64_t offset, void** ptr) {
+  if (!handle || !ptr) return fail(GDN_EINVAL, "handle and ptr must be non-NULL");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_status(e, "cudaIpcOpenMemHandle");
+  *ptr = static_cast<char*>(base) + offset;
+  return GDN_OK;
+}
+
+gdn_status gdn_ipc_release(void* ptr, uint64_t offset) {
+  if (!ptr) return fail(GDN_EINVAL, "ptr is NULL");
+  return cuda_status(cudaIpcCloseMemHandle(static_cast<char*>(ptr) - offset), "cudaIpcCloseMemHandle");
 }
 
 gdn_status gdn_decode(const gdn_decode_args* args, gdn_stream_t stream) {

@@ -103,6 +103,10 @@ struct ChunkParams {
   float norm_eps;
   const __nv_bfloat16* z;  // [N, Hv, Dv] bf16, token stride z_st, head stride Dv
   int64_t z_st;
+  // The output is [N, out_hv, Dv] with this call's heads at [head0, head0 +
+  // hv); each output tile also goes to the n_peers other ranks' outputs.
+  int out_hv, head0, n_peers;
+  void* peer_out[GDN_MAX_GATHER_PEERS];
   // n_chains > 0: CTA row blockIdx.x / hv runs chains[row] instead of sequence
   // blockIdx.x / hv with state_in / state_out.
   int n_chains;
@@ -570,6 +574,22 @@ enum Bar {
   N_BARS
 };
 
+// Copies rows 0 .. n-1 of a staged output tile ([t][Dv] rows of the out
+// dtype, contiguous) of value head h, tokens t0 .., to every peer's gathered
+// output: 16-byte loads from shared memory, one 16-byte store per peer (over
+// NVLink for another GPU's memory).  The 128 output threads, thread e.
+__device__ __forceinline__ void copy_tile_to_peers(const ChunkParams& p, const unsigned char* stage, int64_t t0,
+                                                   int n, int h, int e) {
+  const int row_chunks = DH * (p.out_dtype == GDN_BF16 ? 2 : 4) / 16;
+  const int total = n * row_chunks;
+  for (int i = e; i < total; i += 128) {
+    const int r = i / row_chunks, c = i - r * row_chunks;
+    const uint4 v = reinterpret_cast<const uint4*>(stage)[i];
+    const size_t off = (((size_t)(t0 + r) * p.out_hv + p.head0 + h) * row_chunks + c) * 16;
+    for (int j = 0; j < p.n_peers; ++j) *reinterpret_cast<uint4*>(static_cast<unsigned char*>(p.peer_out[j]) + off) = v;
+  }
+}
+
 // Widens a bf16 [64 t][128] SW128 tile (two 64-wide K-blocks, 16 KB at src)
 // into rows row0 .. row0 + 63 of the 128-row fp32 SW128 K-major tile at dst,
 // row t scaled by scale[t] and rounded to tf32 when scale is given.  128
@@ -998,7 +1018,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     float nw[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) nw[j] = p.gated ? p.norm_w[g8 + j] : 0.f;
-    const size_t ostride = (size_t)p.hv * DH;
+    const size_t ostride = (size_t)p.out_hv * DH;
     // z of chunk c lands in its tile while chunk c - 1's output is formed:
     // the leader requests it as soon as the norm of chunk c - 1 has read the
     // tile (z of chunk 0 at once).
@@ -1046,19 +1066,26 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
           fence_async_smem();
           named_sync(2, kOutThreads);
           if (leader) {
-            tma_store_3d(&omap, sm + OFF_OSTAGE, 0, h, (int)t0);
+            tma_store_3d(&omap, sm + OFF_OSTAGE, 0, p.head0 + h, (int)t0);
             bulk_commit_group();
           }
-        } else if (p.out_dtype == GDN_BF16) {  // ragged last chunk: plain stores of the valid rows
-          __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + dv;
+          if (p.n_peers) copy_tile_to_peers(p, sm + OFF_OSTAGE, t0, CH, h, e);
+        } else {  // ragged last chunk: plain stores of the valid rows, here and at every peer
+          const size_t obase = ((size_t)t0 * p.out_hv + p.head0 + h) * DH + dv;
+          for (int j = -1; j < p.n_peers; ++j) {
+            void* dst = j < 0 ? p.out : p.peer_out[j];
+            if (p.out_dtype == GDN_BF16) {
+              __nv_bfloat16* op = static_cast<__nv_bfloat16*>(dst) + obase;
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i < n) op[i * ostride] = __float2bfloat16_rn(y[i]);
-        } else {
-          float* op = static_cast<float*>(p.out) + ((size_t)t0 * p.hv + h) * DH + dv;
+              for (int i = 0; i < 64; ++i)
+                if (i < n) op[i * ostride] = __float2bfloat16_rn(y[i]);
+            } else {
+              float* op = static_cast<float*>(dst) + obase;
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i < n) op[i * ostride] = y[i];
+              for (int i = 0; i < 64; ++i)
+                if (i < n) op[i * ostride] = y[i];
+            }
+          }
         }
         continue;
       }
@@ -1141,6 +1168,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
       }
     }
     if (leader) bulk_wait_group0();  // every output tile has reached global memory
+    if (p.n_peers) __threadfence_system();  // the peer stores are visible beyond this GPU
     // After an abort, let the last z load in flight land (bounded) before the
     // CTA releases its shared memory (tile i completes phase i & 1).
     if (leader && n_z > 0) mbar_wait(&bars[B_Z_FULL], (uint32_t)((n_z - 1) & 1), wait_ns);
@@ -1389,7 +1417,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     if (!make_map(&qmap, sp.q, N, sp.hk, sp.q_st, sp.q_sh, 64, true) ||
         !make_map(&kmap, sp.k, N, sp.hk, sp.k_st, sp.k_sh, 64, true) ||
         !make_map(&vmap, sp.v, N, sp.hv, sp.v_st, sp.v_sh, 128, false) ||
-        !make_out_map(&omap, sp.out, N, sp.hv, sp.out_dtype) ||
+        !make_out_map(&omap, sp.out, N, sp.out_hv > 0 ? sp.out_hv : sp.hv, sp.out_dtype) ||
         (gated && !make_map(&zmap, sp.z, N, sp.hv, sp.z_st, DH, 128, false)))
       return cudaErrorInvalidValue;
   } else {
@@ -1419,6 +1447,11 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   p.norm_eps = sp.norm_eps;
   p.z = static_cast<const __nv_bfloat16*>(sp.z);
   p.z_st = sp.z_st;
+  p.out_hv = sp.out_hv > 0 ? sp.out_hv : sp.hv;
+  p.head0 = sp.head0;
+  p.n_peers = sp.n_peers;
+  for (int j = 0; j < GDN_MAX_GATHER_PEERS; ++j) p.peer_out[j] = j < sp.n_peers ? sp.peer_out[j] : nullptr;
+  if (gated && (p.out_hv != sp.hv || p.head0 || p.n_peers)) return cudaErrorInvalidValue;  // the fused block is not gathered
 
   {
     static DeviceFlags prep_attr, scan_attr, comb_attr;

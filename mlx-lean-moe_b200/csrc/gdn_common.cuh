@@ -192,6 +192,13 @@ struct ScanParams {
   int64_t z_st = 0;
   const float* norm_w = nullptr;
   float norm_eps = 0.f;
+  // chunked, optional: `out` is a [N, out_hv, Dv] gathered output holding
+  // this call's heads at [head0, head0 + hv); every output tile is also
+  // written to the n_peers other ranks' gathered outputs (gdn_scan_gathered).
+  int out_hv = 0;  // 0: hv
+  int head0 = 0;
+  int n_peers = 0;
+  void* peer_out[GDN_MAX_GATHER_PEERS] = {};
 };
 
 struct BlockParams {
@@ -217,6 +224,7 @@ struct BlockParams {
 
 // Records a printf-style message for gdn_last_error() and returns st.
 gdn_status set_error(gdn_status st, const char* fmt, ...);
+gdn_status allocation_range(const void* ptr, void** base, size_t* size);
 
 cudaError_t launch_decode(const ScanParams& p, cudaStream_t s);
 cudaError_t launch_serial_scan(const ScanParams& p, cudaStream_t s);

@@ -93,6 +93,19 @@ class AttnArgs(ctypes.Structure):
     ]
 
 
+MAX_GATHER_PEERS = 7
+IPC_HANDLE_BYTES = 64
+
+
+class GatherArgs(ctypes.Structure):
+    """``gdn_gather_args``."""
+
+    _fields_ = [
+        ("hv_total", _i32), ("head0", _i32), ("n_peers", _i32), ("reserved", _i32),
+        ("peer_out", _p * MAX_GATHER_PEERS),
+    ]
+
+
 EXPORTS = {
     "gdn_version": (ctypes.c_int, []),
     "gdn_last_error": (ctypes.c_char_p, []),
@@ -107,6 +120,10 @@ EXPORTS = {
     "gdn_dequantize": (_enum, [ctypes.POINTER(QLinearArgs), _enum, _p, _p]),
     "gdn_attention_workspace_size": (_enum, [ctypes.POINTER(AttnArgs), ctypes.POINTER(ctypes.c_size_t)]),
     "gdn_attention": (_enum, [ctypes.POINTER(AttnArgs), _p]),
+    "gdn_scan_gathered": (_enum, [ctypes.POINTER(ScanArgs), ctypes.POINTER(GatherArgs), _p]),
+    "gdn_ipc_export": (_enum, [_p, ctypes.POINTER(ctypes.c_ubyte), ctypes.POINTER(ctypes.c_uint64)]),
+    "gdn_ipc_import": (_enum, [ctypes.POINTER(ctypes.c_ubyte), ctypes.c_uint64, ctypes.POINTER(_p)]),
+    "gdn_ipc_release": (_enum, [_p, ctypes.c_uint64]),
     "gdn_check_device_errors": (_enum, [_p]),
     "gdn_test_set_wait_limit": (_enum, [ctypes.c_uint64]),
     "gdn_test_inject_fault": (_enum, [_i32]),
