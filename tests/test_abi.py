@@ -61,7 +61,7 @@ def _c_layout(tmp_path, struct: str, fields: list[str]) -> list[int]:
 
 @pytest.mark.parametrize("py,c", [(_lib.ScanArgs, "gdn_scan_args"), (_lib.DecodeArgs, "gdn_decode_args"),
                                   (_lib.BlockArgs, "gdn_block_args"), (_lib.QLinearArgs, "gdn_qlinear_args"),
-                                  (_lib.AttnArgs, "gdn_attn_args")])
+                                  (_lib.AttnArgs, "gdn_attn_args"), (_lib.GatherArgs, "gdn_gather_args")])
 def test_ctypes_structs_match_c_layout(tmp_path, py, c):
     fields = [f[0] for f in py._fields_]
     got = [ctypes.sizeof(py)] + [getattr(py, f).offset for f in fields]
@@ -229,3 +229,68 @@ def test_attention_rejects_bad_arguments_before_any_launch(case, attention_rejec
     st, msg = attention_rejections[case]
     assert st in (_lib.GDN_EINVAL, _lib.GDN_EUNSUPPORTED)
     assert _ATTN_BAD[case][2] in msg
+
+
+# Rejection cases of gdn_scan_gathered as (field, value, message fragment);
+# the scan arguments are valid ones at the model's head shape.
+_GATHER_BAD = [
+    ("head0", 17, "must lie in"),
+    ("head0", -1, "must lie in"),
+    ("hv_total", 8, "must lie in"),
+    ("n_peers", 8, "n_peers"),
+    ("reserved", 1, "reserved"),
+    ("peer0", 0x90008, "16-byte aligned"),
+    ("peer0", 0x70000, "other than out"),
+    ("null", 0, "gather is NULL"),
+]
+
+# Made-up device addresses again, so the child sees no GPU (any launch a
+# regressed check let through would fail with a CUDA error there).
+_GATHER_CHILD = r"""
+import ctypes, importlib.util, json, sys
+spec = importlib.util.spec_from_file_location("gdn_lib", sys.argv[1])
+L = importlib.util.module_from_spec(spec)
+spec.loader.exec_module(L)
+lib = L.load()
+res = []
+for field, value in json.loads(sys.argv[2]):
+    a = L.ScanArgs()
+    a.n_tokens, a.n_seqs = 4096, 1
+    a.hk, a.hv, a.dk, a.dv = 8, 16, 128, 128
+    a.q, a.q_stride_t, a.q_stride_h = 0x10000, 1024, 128
+    a.k, a.k_stride_t, a.k_stride_h = 0x20000, 1024, 128
+    a.v, a.v_stride_t, a.v_stride_h = 0x30000, 2048, 128
+    a.g, a.g_stride_t, a.beta, a.beta_stride_t = 0x40000, 16, 0x50000, 16
+    a.state_out, a.out = 0x60000, 0x70000
+    a.qkv_dtype, a.gate_dtype, a.out_dtype = L.GDN_BF16, L.GDN_F32, L.GDN_BF16
+    a.gate_kind, a.algo = L.GDN_GATE_LOG, L.GDN_ALGO_CHUNKED
+    a.workspace, a.workspace_bytes = 0x80000, 1 << 40
+    ga = L.GatherArgs()
+    ga.hv_total, ga.head0, ga.n_peers = 32, 16, 1
+    ga.peer_out[0] = 0x90000
+    if field == "peer0":
+        ga.peer_out[0] = value
+    elif field != "null":
+        setattr(ga, field, value)
+    st = lib.gdn_scan_gathered(ctypes.byref(a), None if field == "null" else ctypes.byref(ga), None)
+    res.append([st, lib.gdn_last_error().decode()])
+print(json.dumps(res))
+"""
+
+
+@pytest.fixture(scope="module")
+def gather_rejections():
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    cases = json.dumps([[f, v] for f, v, _ in _GATHER_BAD])
+    out = subprocess.run([sys.executable, "-c", _GATHER_CHILD,
+                          os.path.join(os.path.dirname(_lib.__file__), "_lib.py"), cases],
+                         capture_output=True, text=True, env=env, timeout=120)
+    assert out.returncode == 0, out.stderr
+    return json.loads(out.stdout.strip().splitlines()[-1])
+
+
+@pytest.mark.parametrize("case", range(len(_GATHER_BAD)), ids=[f"{c[0]}={c[1]}" for c in _GATHER_BAD])
+def test_gathered_scan_rejects_bad_gather_arguments_before_any_launch(case, gather_rejections):
+    st, msg = gather_rejections[case]
+    assert st == _lib.GDN_EINVAL, msg
+    assert _GATHER_BAD[case][2] in msg
