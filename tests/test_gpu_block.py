@@ -68,7 +68,7 @@ def test_layer_stepwise_and_chunked_calls_carry_both_states(golden):
     assert len(shapes) == 1 and cache.size == 12
 
 
-def _bf16_block_case(lengths, hk, hv, dk, dv, seed, algo="auto", kernel=4):
+def _bf16_block_case(lengths, hk, hv, dk, dv, seed, algo="auto", kernel=4, conv_dtype=torch.bfloat16):
     B = len(lengths)
     cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
     N = int(cu[-1])
@@ -83,7 +83,7 @@ def _bf16_block_case(lengths, hk, hv, dk, dv, seed, algo="auto", kernel=4):
     ssm = (rng.standard_normal((B, hv, dv, dk)) * 0.02).astype(np.float32)
     eps = 1e-6
 
-    cs, ss = t(conv_state, torch.bfloat16), t(ssm)
+    cs, ss = t(conv_state, conv_dtype), t(ssm)
     out, _, _ = gdn_b200.gated_delta_block(
         t(mixed, torch.bfloat16), shape, t(conv_w), t(A_log), t(dt_bias), t(norm_w), eps, cs, ss,
         cu_seqlens=t(cu, torch.int64), algo=algo,
@@ -136,3 +136,18 @@ def test_bf16_block_general_head_dims():
     assert O.rel_l2(go, eo) < 2e-3
     assert O.rel_l2(gs, es) < 2e-3
     np.testing.assert_array_equal(gc, ec)
+
+
+@pytest.mark.parametrize("kernel", [1, 2, 3, 4])
+@pytest.mark.parametrize("conv_dtype", [torch.bfloat16, torch.float32])
+def test_bf16_chunked_block_edges(kernel, conv_dtype):
+    """The chunked block at 128-dim heads, two value heads per key head:
+    sequences of 0, 1 and 5 tokens (ragged single chunks), one whose second
+    chunk starts on its conv history, each conv width and both conv-state
+    dtypes."""
+    go, eo, gc, ec, gs, es = _bf16_block_case([5, 70, 1, 0, 200], 4, 8, 128, 128, seed=30 + kernel, algo="chunked",
+                                              kernel=kernel, conv_dtype=conv_dtype)
+    assert O.rel_l2(go, eo) < 2e-3
+    assert O.rel_l2(gs, es) < 2e-3
+    if kernel > 1:
+        np.testing.assert_array_equal(gc, ec)
