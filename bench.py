@@ -791,7 +791,7 @@ def run_varlen(args, world, rank, local):
                    "global_batch": 64, "seq_len": "256..16384 (packed)", "parallelism": f"sequence-sharded x{world}",
                    "l2": "inputs (4.2 GB of q/k/v) far larger than L2"},
         "prefill": {"ms": pf_ms / args.steps, "achieved_tflops": PREFILL_FLOP / PREFILL_T * total_tok / pf_s / 1e12,
-                    "frac_of_bf16_peak": PREFILL_FLOP / PREFILL_T * total_tok / pf_s / 1e12 / tc_peak,
+                    "frac_of_bf16_peak": PREFILL_FLOP / PREFILL_T * total_tok / pf_s / 1e12 / (tc_peak * world),
                     "lpt_max_over_mean": info["lpt_max_over_mean"]},
         "decode": {"value": dec_bytes / (dec_ms / 1e3 / args.steps) / 1e9, "unit": "GB/s", "steps": n_decode,
                    "ms": dec_ms / args.steps, "peak": hbm_peak, "peak_kind": peak_kind},
@@ -826,7 +826,7 @@ def measure_sharded(world, rank, device, steps=3):
     tflops = PREFILL_FLOP / PREFILL_T * info["tokens"] / pf_s / 1e12
     res["config5"] = {
         "prefill_tok_s": info["tokens"] / pf_s, "prefill_ms": pf_ms / steps, "prefill_tflops": tflops,
-        "prefill_frac_of_bf16_peak": tflops / tc_peak, "lpt_max_over_mean": info["lpt_max_over_mean"],
+        "prefill_frac_of_bf16_peak": tflops / (tc_peak * world), "lpt_max_over_mean": info["lpt_max_over_mean"],
         "decode_gbs": info["n_decode"] * (2 * 64 * HV * D * D * 4) / (dec_ms / 1e3 / steps) / 1e9,
         "decode_ms": dec_ms / steps, "scaling": "strong",
         "note": "64 sequences (516,496 tokens) LPT-packed over the ranks, prefill then 256 decode steps per "
