@@ -21,14 +21,16 @@
 namespace gdn {
 namespace {
 
-template <int DKP>
+// ITER_FIX > 0 sets the row groups per warp (decode at Dk = 128 takes four:
+// sixteen 16-byte state loads in flight per thread).
+template <int DKP, int ITER_FIX = 0>
 struct Layout {
   static constexpr int LPR = DKP >= 32 ? 8 : DKP / 4;  // lanes per state row
   static constexpr int VEC = DKP / (4 * LPR);          // float4 per lane per row
   static constexpr int RPG = 32 / LPR;                 // rows per warp per group
   static constexpr int ITER_REG = VEC >= 8 ? 1 : 8 / VEC;
   static constexpr int ITER_CAP = 128 / (4 * RPG) > 0 ? 128 / (4 * RPG) : 1;
-  static constexpr int ITER = ITER_REG < ITER_CAP ? ITER_REG : ITER_CAP;  // row groups per warp
+  static constexpr int ITER = ITER_FIX > 0 ? ITER_FIX : (ITER_REG < ITER_CAP ? ITER_REG : ITER_CAP);  // row groups per warp
   static constexpr int WARPS = 4;
   static constexpr int ROWS = WARPS * RPG * ITER;  // state rows per CTA
   static_assert(LPR * VEC * 4 == DKP, "layout");
@@ -67,7 +69,7 @@ template <int DKP, typename T>
 __global__ void __launch_bounds__(128) decode_kernel(const ScanParams p) {
   griddep_wait();  // launched as a dependent of the kernel before it
   griddep_launch_dependents();
-  using L = Layout<DKP>;
+  using L = Layout<DKP, DKP == 128 ? 4 : 0>;
   const int n_tiles = (p.dv + L::ROWS - 1) / L::ROWS;
   const int64_t b = blockIdx.x / n_tiles;
   const int tile = blockIdx.x % n_tiles;
@@ -300,8 +302,8 @@ int padded_dk(int dk) {
 
 template <int DKP, typename T>
 cudaError_t launch_one(const ScanParams& p, cudaStream_t s, bool decode) {
-  using L = Layout<DKP>;
-  const int64_t n_tiles = (p.dv + L::ROWS - 1) / L::ROWS;
+  const int rows = decode ? Layout<DKP, DKP == 128 ? 4 : 0>::ROWS : Layout<DKP>::ROWS;
+  const int64_t n_tiles = (p.dv + rows - 1) / rows;
   const int64_t gx = n_tiles * p.n_seqs;
   if (gx <= 0) return cudaSuccess;
   if (gx > 0x7fffffffLL || p.hv > 65535) return cudaErrorInvalidConfiguration;
