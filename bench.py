@@ -62,9 +62,9 @@ DECODE_BYTES = STATE_BYTES + 2 * B * HK * D * 2 + B * HV * D * 2 + 2 * B * HV * 
 # DRAM bytes per decode_kernel launch at config 2 (read + write), averaged
 # over three consecutive launches of the back-to-back timed loop captured
 # with the cache left alone between them (profiles/decode_config2.md).
-DECODE_NCU_TRAFFIC = 132_349_781 + 131_684_864
+DECODE_NCU_TRAFFIC = 132_350_464 + 132_196_352
 DECODE_NCU_SOURCE = ("ncu --cache-control none capture of launches 11-13 of the back-to-back loop (mean "
-                     "dram__bytes_read.sum 132,349,781 + dram__bytes_write.sum 131,684,864 per launch; "
+                     "dram__bytes_read.sum 132,350,464 + dram__bytes_write.sum 132,196,352 per launch; "
                      "algorithmic 270,548,992)")
 PREFILL_T = 8192
 PREFILL_FLOP = 182_955 * PREFILL_T * HV  # chunked WY count per token-head: (10 C^2 d + 6 C d^2 + 2/3 C^3) / C, C = 64, d = 128
