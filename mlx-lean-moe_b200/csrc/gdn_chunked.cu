@@ -622,6 +622,10 @@ __device__ __forceinline__ void widen_tile(const unsigned char* src, unsigned ch
   }
 }
 
+// GATHER: the output goes into a [N, out_hv, Dv] gathered output at head0 and
+// to the peers' (gdn_scan_gathered); a separate instance, so that the plain
+// scan's code is not touched by it.
+template <bool GATHER>
 __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ CUtensorMap qmap,
                                                                      const __grid_constant__ CUtensorMap kmap,
                                                                      const __grid_constant__ CUtensorMap vmap,
@@ -1018,7 +1022,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     float nw[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) nw[j] = p.gated ? p.norm_w[g8 + j] : 0.f;
-    const size_t ostride = (size_t)p.out_hv * DH;
+    const size_t ostride = (size_t)(GATHER ? p.out_hv : p.hv) * DH;
     // z of chunk c lands in its tile while chunk c - 1's output is formed:
     // the leader requests it as soon as the norm of chunk c - 1 has read the
     // tile (z of chunk 0 at once).
@@ -1066,11 +1070,23 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
           fence_async_smem();
           named_sync(2, kOutThreads);
           if (leader) {
-            tma_store_3d(&omap, sm + OFF_OSTAGE, 0, p.head0 + h, (int)t0);
+            tma_store_3d(&omap, sm + OFF_OSTAGE, 0, GATHER ? p.head0 + h : h, (int)t0);
             bulk_commit_group();
           }
-          if (p.n_peers) copy_tile_to_peers(p, sm + OFF_OSTAGE, t0, CH, h, e);
-        } else {  // ragged last chunk: plain stores of the valid rows, here and at every peer
+          if (GATHER) copy_tile_to_peers(p, sm + OFF_OSTAGE, t0, CH, h, e);
+        } else if (!GATHER) {  // ragged last chunk: plain stores of the valid rows
+          if (p.out_dtype == GDN_BF16) {
+            __nv_bfloat16* op = static_cast<__nv_bfloat16*>(p.out) + ((size_t)t0 * p.hv + h) * DH + dv;
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              if (i < n) op[i * ostride] = __float2bfloat16_rn(y[i]);
+          } else {
+            float* op = static_cast<float*>(p.out) + ((size_t)t0 * p.hv + h) * DH + dv;
+#pragma unroll
+            for (int i = 0; i < 64; ++i)
+              if (i < n) op[i * ostride] = y[i];
+          }
+        } else {  // the same, here and at every peer
           const size_t obase = ((size_t)t0 * p.out_hv + p.head0 + h) * DH + dv;
           for (int j = -1; j < p.n_peers; ++j) {
             void* dst = j < 0 ? p.out : p.peer_out[j];
@@ -1168,7 +1184,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
       }
     }
     if (leader) bulk_wait_group0();  // every output tile has reached global memory
-    if (p.n_peers) __threadfence_system();  // the peer stores are visible beyond this GPU
+    if (GATHER) __threadfence_system();  // the peer stores are visible beyond this GPU
     // After an abort, let the last z load in flight land (bounded) before the
     // CTA releases its shared memory (tile i completes phase i & 1).
     if (leader && n_z > 0) mbar_wait(&bars[B_Z_FULL], (uint32_t)((n_z - 1) & 1), wait_ns);
@@ -1391,6 +1407,13 @@ SegLayout seg_layout(const ScanParams& p, int P) {
   return L;
 }
 
+// The scan instance for these parameters (the gathered one only when asked).
+using ScanKernel = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, ChunkParams);
+ScanKernel scan_kernel(const ChunkParams& p) {
+  const bool gather = p.n_peers > 0 || p.head0 != 0 || p.out_hv != p.hv;
+  return gather ? chunk_scan_kernel<true> : chunk_scan_kernel<false>;
+}
+
 bool aligned_elems(int64_t s) { return s >= 0 && s % 8 == 0; }
 bool aligned_ptr16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
@@ -1454,10 +1477,12 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   if (gated && (p.out_hv != sp.hv || p.head0 || p.n_peers)) return cudaErrorInvalidValue;  // the fused block is not gathered
 
   {
-    static DeviceFlags prep_attr, scan_attr, comb_attr;
+    static DeviceFlags prep_attr, scan_attr, gather_attr, comb_attr;
     cudaError_t e = ensure_smem_attr(chunk_prep_kernel, kPrepSmem, prep_attr);
     if (e != cudaSuccess) return e;
-    e = ensure_smem_attr(chunk_scan_kernel, kScanSmem, scan_attr);
+    e = ensure_smem_attr(chunk_scan_kernel<false>, kScanSmem, scan_attr);
+    if (e != cudaSuccess) return e;
+    e = ensure_smem_attr(chunk_scan_kernel<true>, kScanSmem, gather_attr);
     if (e != cudaSuccess) return e;
     e = ensure_smem_attr(state_combine_kernel, kCombineSmem, comb_attr);
     if (e != cudaSuccess) return e;
@@ -1485,7 +1510,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     }
     const int64_t ctas = sp.n_seqs * sp.hv;
     if (ctas > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-    chunk_scan_kernel<<<(unsigned)ctas, kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p);
+    scan_kernel(p)<<<(unsigned)ctas, kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p);
     return cudaGetLastError();
   }
   // Chunk records: segments 0..P-2 before phase 1; the last segment's (needed
@@ -1531,7 +1556,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
     p1.chains[i] = {i, nullptr, W + i * hstate, kChainNoOut};
     p1.chains[P - 2 + i] = {i, nullptr, Mt + (i - 1) * hstate, kChainIdentity | kChainZeroV | kChainNoOut};
   }
-  chunk_scan_kernel<<<(unsigned)(p1.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p1);
+  scan_kernel(p1)<<<(unsigned)(p1.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p1);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // phase 2: start states, W[j] = W[j-1] M_j + U_j for j = 1 .. P-2, one launch
@@ -1546,7 +1571,7 @@ cudaError_t launch_chunked_scan(const ScanParams& sp, cudaStream_t s) {
   ChunkParams p3 = p;
   p3.n_chains = P - 1;
   for (int i = 1; i <= P - 1; ++i) p3.chains[i - 1] = {i, W + (i - 1) * hstate, i == P - 1 ? sp.state_out : nullptr, 0};
-  chunk_scan_kernel<<<(unsigned)(p3.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p3);
+  scan_kernel(p3)<<<(unsigned)(p3.n_chains * sp.hv), kScanThreads, kScanSmem, s>>>(qmap, kmap, vmap, omap, zmap, p3);
   return cudaGetLastError();
 }
 
