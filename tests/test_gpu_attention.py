@@ -249,3 +249,22 @@ def test_attention_bf16_decode_on_tensor_cores(heads, kv_heads, head_dim, rotary
                                        rnd=O.bf16_round)
         assert O.rel_l2(n(got), want) < 1e-2, O.rel_l2(n(got), want)
     gdn_b200.check_device_errors()
+
+
+def test_attention_bf16_long_prefill_at_model_shape():
+    """16 query heads over 2 key/value heads of 256: a 600-token prefill
+    (ten key tiles for the last query rows) and a 203-token chunk after it
+    (queries at an offset that is not a tile multiple), against the oracle."""
+    shape = AttentionShape(16, 2, 256, 64, 10000000.0)
+    hidden, eps = 512, 1e-6
+    rng = np.random.default_rng(23)
+    w = _bf16_weights(_random_weights(rng, shape, hidden, 0.05))
+    layer = _layer(w, shape, eps, torch.bfloat16)
+    cache = _cache(shape, max_context=1024, dtype=torch.bfloat16)
+    keys, values = np.zeros((2, 0, 256)), np.zeros((2, 0, 256))
+    for L in (600, 203):
+        x = O.bf16_round(rng.standard_normal((L, hidden)).astype(np.float32))
+        got = layer(t(x, torch.bfloat16), cache)
+        want, keys, values = O.attention_layer(x, w, keys, values, 16, 2, 256, 64, 10000000.0, eps,
+                                               rnd=O.bf16_round)
+        assert O.rel_l2(n(got), want) < 1e-2, (L, O.rel_l2(n(got), want))
