@@ -164,6 +164,18 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(mine)}
 
 
+def clocks_under_load(fn, device, seconds=1.2):
+    """Clocks while fn() runs back to back for about `seconds` (outside any
+    timed region): the SM clock the chunked kernels actually get under load."""
+    with ClockSampler(device.index or 0) as sampler:
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end:
+            for _ in range(20):
+                fn()
+            torch.cuda.synchronize()
+    return sampler.summary()
+
+
 def cpu_decode_sample(budget_s=10.0):
     """The reference's CPU path for config 2: per sequence, the ops-path
     recurrence for one token (torch CPU, all threads). Runs whole steps over
@@ -270,9 +282,10 @@ def run_reference(args, world, rank):
         print(json.dumps(line), flush=True)
 
 
-def measure_prefill(device, iters=3, warmup=2):
+def measure_prefill(device, iters=3, warmup=2, clocks=False):
     """Config 3: one sequence of 8192 tokens, bf16 q/k/v, fp32 state from 0.
-    Median device time of one call (ms)."""
+    Median device time of one call (ms); with clocks=True also the clocks
+    of the same call run back to back for about a second."""
     import gdn_b200
 
     rng = np.random.default_rng(3)
@@ -296,11 +309,16 @@ def measure_prefill(device, iters=3, warmup=2):
         ev[2 * i + 1].record()
     torch.cuda.synchronize()
     ms = statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(iters))
+    if clocks:
+        return ms, clocks_under_load(lambda: gdn_b200.gated_delta_scan_varlen(
+            q, k, v, g, beta, state, g_is_log=True, state_out=st_out, out=out), device)
     return ms
 
 
-def measure_block(device, iters=3):
-    """Config 4: the fused block, B=8 x T=4096, bf16 mixed projection."""
+def measure_block(device, iters=3, clocks=False):
+    """Config 4: the fused block, B=8 x T=4096, bf16 mixed projection.
+    Returns (ms, tokens), and with clocks=True the clocks of the call run
+    back to back for about a second."""
     import gdn_b200
     from gdn_b200.linear_attention import LinearAttentionShape
 
@@ -331,7 +349,10 @@ def measure_block(device, iters=3):
         run()
         ev[2 * i + 1].record()
     torch.cuda.synchronize()
-    return statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(iters)), Bb * T
+    ms = statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(iters))
+    if clocks:
+        return ms, Bb * T, clocks_under_load(run, device)
+    return ms, Bb * T
 
 
 HIDDEN = 2048
@@ -594,28 +615,28 @@ def run_prefill(args):
     q/k/v, fp32 state from 0), K calls back to back; for profiling the
     prefill kernels on their own."""
     device = torch.device("cuda", 0)
-    ms = measure_prefill(device, iters=max(args.steps, 1), warmup=args.warmup)
+    ms, clk = measure_prefill(device, iters=max(args.steps, 1), warmup=args.warmup, clocks=True)
     _, tc_peak, _ = peaks()
     print(json.dumps({"metric": "config-3 prefill tok/s", "value": PREFILL_T / (ms / 1e3), "unit": "tok/s",
                       "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
                       "achieved_tflops": PREFILL_FLOP / (ms / 1e3) / 1e12,
                       "frac_of_bf16_peak": PREFILL_FLOP / (ms / 1e3) / 1e12 / tc_peak,
                       "config": {"workload": "config 3: B=1, T=8192, 16/32 heads, d=128, bf16 q/k/v, fp32 out"},
-                      "dtype": "bf16", "data": "synthetic"}), flush=True)
+                      "clocks_under_load": clk, "dtype": "bf16", "data": "synthetic"}), flush=True)
 
 
 def run_block(args):
     """Only config 4 (the fused block over B=8 x T=4096, bf16 mixed
     projection), K calls; for profiling the block's kernels on their own."""
     device = torch.device("cuda", 0)
-    ms, tok = measure_block(device, iters=max(args.steps, 1))
+    ms, tok, clk = measure_block(device, iters=max(args.steps, 1), clocks=True)
     _, tc_peak, _ = peaks()
     flop = (PREFILL_FLOP // PREFILL_T) * tok
     print(json.dumps({"metric": "config-4 fused block tok/s", "value": tok / (ms / 1e3), "unit": "tok/s",
                       "ms_per_step": ms, "steps": args.steps, "warmup": args.warmup,
                       "achieved_tflops": flop / (ms / 1e3) / 1e12, "frac_of_bf16_peak": flop / (ms / 1e3) / 1e12 / tc_peak,
                       "config": {"workload": "config 4: fused block, B=8 x T=4096, 16/32 heads, d=128"},
-                      "dtype": "bf16", "data": "synthetic"}), flush=True)
+                      "clocks_under_load": clk, "dtype": "bf16", "data": "synthetic"}), flush=True)
 
 
 def run_layerdecode(args):
@@ -1102,11 +1123,12 @@ def main():
         line["gpu_launches"] = 2 * args.steps
 
         # --- config 3 prefill (secondary metric) --------------------------
-        pf_ms = measure_prefill(device)
+        pf_ms, pf_clk = measure_prefill(device, clocks=True)
         pf_tflops = PREFILL_FLOP / (pf_ms / 1e3) / 1e12
         line["prefill"] = {"value": PREFILL_T / (pf_ms / 1e3), "unit": "tok/s", "ms": pf_ms,
                            "config": "config 3: B=1, T=8192, 16/32 heads, d=128, bf16 q/k/v, fp32 state from 0",
                            "achieved_tflops": pf_tflops, "frac_of_bf16_peak": pf_tflops / tc_peak, "algo": "auto",
+                           "clocks_under_load": pf_clk,
                            "roofline": {"bound": "tensor", "achieved": pf_tflops, "peak": tc_peak, "unit": "TFLOP/s",
                                         "frac": pf_tflops / tc_peak,
                                         "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops, burst)",
@@ -1114,13 +1136,14 @@ def main():
                                         **PREFILL_NCU}}
 
         # --- config 4 fused block (secondary) --------------------------------
-        blk_ms, blk_tok = measure_block(device)
+        blk_ms, blk_tok, blk_clk = measure_block(device, clocks=True)
         blk_flop = (PREFILL_FLOP // PREFILL_T) * blk_tok
         line["block"] = {"value": blk_tok / (blk_ms / 1e3), "unit": "tok/s", "ms": blk_ms,
                          "config": "config 4: fused block, B=8 x T=4096, 16/32 heads, d=128, bf16 mixed "
                                    "projection, conv+norms+gates+scan+gated RMSNorm (two state resets included)",
                          "achieved_tflops": blk_flop / (blk_ms / 1e3) / 1e12,
-                         "frac_of_bf16_peak": blk_flop / (blk_ms / 1e3) / 1e12 / tc_peak}
+                         "frac_of_bf16_peak": blk_flop / (blk_ms / 1e3) / 1e12 / tc_peak,
+                         "clocks_under_load": blk_clk}
         att = measure_attention(device)
         line["attention"] = {
             "prefill_ms": att["prefill_ms"], "prefill_tflops": att["prefill_tflops"],
