@@ -483,6 +483,11 @@ gdn_status gdn_check_device_errors(gdn_stream_t stream) {
     e = gdn::read_and_clear_qlinear_error(&code2);
     code |= code2;
   }
+  if (e == cudaSuccess) {
+    unsigned code3 = 0;
+    e = gdn::read_and_clear_attn_error(&code3);
+    code |= code3;
+  }
   if (e != cudaSuccess) return cuda_status(e, "reading the device error word");
   if (code) return fail(GDN_ETIMEOUT, "a bounded device wait gave up (code 0x%x)", code);
   return GDN_OK;

@@ -23,8 +23,11 @@
 //                      rows (normalization, gate, output); several write
 //                      partial (max, sum, output) rows that
 // attn_combine_kernel  adds up, then gates and writes.
-// attn_mma_kernel      bf16 prefill (calls with enough rows for one key
-//                      split) on the tensor cores: see its comment below.
+// attn_tc_kernel       bf16 prefill (calls with enough rows for one key
+//                      split), head_dim 128 or 256: tcgen05 MMAs into TMEM,
+//                      Q, K and V by TMA; see its comment below.
+// attn_mma_kernel      the same for head_dim 64, or when the tensor maps
+//                      cannot be made: mma.sync on the tensor cores.
 // attn_dec_mma_kernel  bf16 decode (one token, a key/value head's query
 //                      heads within 16 rows) on the tensor cores, one warp
 //                      per key split, into the combine.
@@ -39,8 +42,11 @@
 #include <cstring>
 #include <type_traits>
 
+#include <cudaTypedefs.h>
+
 #include "gdn_api.h"
 #include "gdn_common.cuh"
+#include "gdn_sm100.cuh"
 
 namespace gdn {
 namespace {
@@ -743,6 +749,320 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_mma_kernel(const AttnPara
   }
 }
 
+// ------------------------------------------------------------------ prefill on tcgen05
+// attn_tc_kernel<HD>: bf16 prefill (head_dim 128 or 256), one CTA per (128
+// queries, head), keys in tiles of 64.  Warp 0 lane 0 loads Q once and the K
+// and V tiles (two buffers) by TMA, zero-filled past the cache length; warp 1
+// lane 0 issues
+//   S_j  = Q K_j^T   M = 128 queries, N = 64 keys, K = HD    two TMEM buffers
+//   O   += P_j V_j   M = 128, N = HD, K = 64 keys            P read from TMEM, V MN-major
+// and warps 4-7 (one query row per thread: its TMEM lane) turn S_j into P_j
+// with an online softmax in log2 units, P written as packed bf16 over the
+// first 32 columns of S_j's buffer.  A row's O and running sum l are
+// rescaled only when its maximum grows by more than kTcRescale (until then
+// every p <= 2^kTcRescale); l sums the unrounded p, as attn_mma_kernel does.
+// The end: O / l, the sigmoid gate and the bf16 rounding of attn_mma_kernel.
+// Every wait is bounded; a timeout is recorded in g_attn_error.
+constexpr int kTcQ = 128, kTcK = 64, kTcThreads = 256;
+constexpr float kTcRescale = 8.f;
+constexpr unsigned long long kTcWaitNs = 2000000000ull;
+
+__device__ unsigned g_attn_error = 0;
+
+template <int HD>
+struct TcSmem {
+  static constexpr uint32_t kQBytes = kTcQ * HD * 2;   // HD/64 K-blocks of 128 rows x 128 B, SW128
+  static constexpr uint32_t kKVBytes = kTcK * HD * 2;  // HD/64 blocks of 64 rows x 128 B, SW128
+  static constexpr uint32_t OFF_Q = 0, OFF_K = kQBytes, OFF_V = OFF_K + 2 * kKVBytes;
+  static constexpr size_t kBytes = 1024 + OFF_V + 2 * (size_t)kKVBytes;
+};
+
+enum TcBar { T_Q_FULL, T_KV_FULL0, T_KV_FULL1, T_KV_EMPTY0, T_KV_EMPTY1, T_S_FULL0, T_S_FULL1, T_P_READY0,
+             T_P_READY1, T_PV_DONE, T_DRAIN, T_NBARS };
+
+__device__ __forceinline__ void tc_record_error(volatile int* abort_flag) {
+  *abort_flag = 1;
+  atomicOr(&g_attn_error, sm100::kErrTimeout);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                              const __grid_constant__ CUtensorMap kmap,
+                                                              const __grid_constant__ CUtensorMap vmap,
+                                                              const AttnParams p) {
+  using namespace sm100;
+  using SM = TcSmem<HD>;
+  constexpr int KB = HD / 64;                                   // 64-wide blocks of the head dim
+  constexpr uint32_t kCols = HD + 2 * kTcK <= 256 ? 256 : 512;  // O, then the two S buffers
+  extern __shared__ unsigned char smem_tc[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_tc) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bars[T_NBARS];
+  __shared__ uint32_t tmem_base;
+  __shared__ volatile int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = blockIdx.x, hk = h / p.group;
+  // query tiles in reverse order: the tiles with the most keys start first
+  const int64_t q0 = (int64_t)(gridDim.y - 1 - blockIdx.y) * kTcQ;
+  const int64_t q_last = min(q0 + kTcQ, p.n_tokens) - 1;
+  const int64_t kneed = p.offset + q_last + 1;
+  const int ntiles = (int)((kneed + kTcK - 1) / kTcK);
+
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int i = 0; i < T_NBARS; ++i) mbar_init(&bars[i], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) tmem_alloc(&tmem_base, kCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      prefetch_tensormap(&qmap);
+      prefetch_tensormap(&kmap);
+      prefetch_tensormap(&vmap);
+      mbar_arrive_expect_tx(&bars[T_Q_FULL], SM::kQBytes);
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb)
+        tma_load_3d(base + SM::OFF_Q + kb * (kTcQ * 128), &qmap, &bars[T_Q_FULL], kb * 64, h, (int)q0);
+      uint32_t loads[2] = {0, 0};
+      for (int j = 0; j < ntiles && !abort_flag; ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(&bars[T_KV_EMPTY0 + b], (uint32_t)(((j >> 1) - 1) & 1), kTcWaitNs)) {
+          tc_record_error(&abort_flag);
+          break;
+        }
+        mbar_arrive_expect_tx(&bars[T_KV_FULL0 + b], 2 * SM::kKVBytes);
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb) {
+          tma_load_3d(base + SM::OFF_K + b * SM::kKVBytes + kb * (kTcK * 128), &kmap, &bars[T_KV_FULL0 + b], kb * 64,
+                      j * kTcK, hk);
+          tma_load_3d(base + SM::OFF_V + b * SM::kKVBytes + kb * (kTcK * 128), &vmap, &bars[T_KV_FULL0 + b], kb * 64,
+                      j * kTcK, hk);
+        }
+        ++loads[b];
+      }
+      // every copy this thread started lands before the CTA releases its memory
+      mbar_wait(&bars[T_Q_FULL], 0, kTcWaitNs);
+      for (int b = 0; b < 2; ++b)
+        if (loads[b]) mbar_wait(&bars[T_KV_FULL0 + b], (loads[b] - 1) & 1, kTcWaitNs);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    // S_j, then O += P_(j-1) V_(j-1): the product of tile j runs while the
+    // softmax warps form P_(j-1); products from this thread run in order.
+    if (lane == 0) {
+      const uint32_t id_s = idesc_bf16_f32(128, kTcK);
+      const uint32_t id_o = idesc_bf16_f32_bmn(128, HD);
+      const uint32_t sQ = smem_u32(base + SM::OFF_Q);
+      bool ok = mbar_wait(&bars[T_Q_FULL], 0, kTcWaitNs);
+      for (int j = 0; ok && j <= ntiles; ++j) {
+        if (j < ntiles) {
+          const int b = j & 1;
+          ok = mbar_wait(&bars[T_KV_FULL0 + b], (uint32_t)((j >> 1) & 1), kTcWaitNs);
+          if (!ok || abort_flag) break;
+          tc_fence_after();
+          const uint32_t sK = smem_u32(base + SM::OFF_K + b * SM::kKVBytes);
+#pragma unroll
+          for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              mma_bf16(tmem + HD + kTcK * b, sdesc_sw128(sQ + kb * (kTcQ * 128) + ks * 32),
+                       sdesc_sw128(sK + kb * (kTcK * 128) + ks * 32), id_s, kb + ks > 0);
+          mma_commit(&bars[T_S_FULL0 + b]);
+        }
+        if (j >= 1) {
+          const int jp = j - 1, bp = jp & 1;
+          ok = mbar_wait_spin(&bars[T_P_READY0 + bp], (uint32_t)((jp >> 1) & 1), kTcWaitNs);
+          if (!ok || abort_flag) break;
+          tc_fence_after();
+          const uint32_t sV = smem_u32(base + SM::OFF_V + bp * SM::kKVBytes);
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            mma_bf16_ts(tmem, tmem + HD + kTcK * bp + 8 * ks, sdesc_sw128_mn(sV + ks * 2048, kTcK * 128, 1024), id_o,
+                        jp > 0 || ks > 0);
+          mma_commit(&bars[T_PV_DONE]);
+          mma_commit(&bars[T_KV_EMPTY0 + bp]);
+        }
+      }
+      if (!ok) tc_record_error(&abort_flag);
+      mma_commit(&bars[T_DRAIN]);
+      mbar_wait(&bars[T_DRAIN], 0, kTcWaitNs);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------- softmax and output
+    const int q = warp & 3;                             // TMEM lane quarter
+    const int r = q * 32 + lane;                        // query row of the tile
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    const int64_t qpos = p.offset + q0 + r;             // its position in the sequence
+    const float sl2 = p.scale * 1.4426950408889634f;    // scores in log2 units
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int b = j & 1;
+      ok = mbar_wait(&bars[T_S_FULL0 + b], (uint32_t)((j >> 1) & 1), kTcWaitNs);
+      if (!ok) tc_record_error(&abort_flag);
+      if (named_sync_or(1, 128, !ok || abort_flag)) break;
+      tc_fence_after();
+      float s[64];
+      tmem_ld32(tq + HD + kTcK * b, *reinterpret_cast<float(*)[32]>(s));
+      tmem_ld32(tq + HD + kTcK * b + 32, *reinterpret_cast<float(*)[32]>(s + 32));
+      tmem_wait_ld();
+      const int64_t k0 = (int64_t)j * kTcK;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        s[i] = k0 + i <= qpos ? s[i] * sl2 : -INFINITY;
+        mx = fmaxf(mx, s[i]);
+      }
+      // A row rescales when its maximum grows past the bound (the first
+      // valid keys only set it).  The TMEM accesses are warp-collective, so
+      // the whole warp takes the rescale when any of its rows needs one; the
+      // other rows scale by 1.
+      const bool grow = mx > m + kTcRescale;
+      const bool scale_o = grow && m != -INFINITY;  // O holds products of earlier tiles
+      if (__any_sync(0xffffffffu, scale_o)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars[T_PV_DONE], (uint32_t)((j - 1) & 1), kTcWaitNs))) {
+          tc_record_error(&abort_flag);  // O is left alone; the CTA is aborting
+        } else {
+          tc_fence_after();
+          const float a = scale_o ? exp2f(m - mx) : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < HD; c += 32) {
+            float o[32];
+            tmem_ld32(tq + c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= a;
+            tmem_st32(tq + c, o);
+          }
+          tmem_wait_st();
+          l *= a;
+        }
+      }
+      if (grow) m = mx;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        const float p0 = s[i] == -INFINITY ? 0.f : exp2f(s[i] - m);
+        const float p1 = s[i + 1] == -INFINITY ? 0.f : exp2f(s[i + 1] - m);
+        l += p0 + p1;
+        pk[i >> 1] = cvt_bf16x2(p0, p1);
+      }
+      tmem_st16(tq + HD + kTcK * b, *reinterpret_cast<const uint32_t(*)[16]>(pk));
+      tmem_st16(tq + HD + kTcK * b + 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16));
+      tmem_wait_st();
+      tc_fence_before();
+      named_sync(1, 128);
+      if (r == 0) mbar_arrive(&bars[T_P_READY0 + b]);
+    }
+    // O / l, gated: out = bf16(bf16(O / l) * bf16(sigmoid(gate)))
+    ok = ok && !abort_flag && mbar_wait(&bars[T_PV_DONE], (uint32_t)((ntiles - 1) & 1), kTcWaitNs);
+    if (!ok && !abort_flag) tc_record_error(&abort_flag);
+    // Every lane reads its O row (the loads are warp-collective); rows past
+    // the last token of a ragged tile store nothing.
+    const int64_t t = q0 + r;
+    const bool row_ok = t < p.n_tokens;
+    if (!named_sync_or(1, 128, !ok)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const int64_t tr = row_ok ? t : 0;
+      const __nv_bfloat16* gate = static_cast<const __nv_bfloat16*>(p.qg) + tr * p.qg_st + (int64_t)h * 2 * HD + HD;
+      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + tr * p.out_st + (int64_t)h * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD; c += 32) {
+        float o[32];
+        __syncwarp();
+        tmem_ld32(tq + c, o);
+        tmem_wait_ld();
+#pragma unroll
+        for (int d8 = 0; d8 < 32; d8 += 8) {
+          const uint4 gu = *reinterpret_cast<const uint4*>(gate + c + d8);
+          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
+          uint32_t ow[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float a0 = round_to<__nv_bfloat16>(o[d8 + 2 * u] * inv);
+            const float a1 = round_to<__nv_bfloat16>(o[d8 + 2 * u + 1] * inv);
+            const float g0 = round_to<__nv_bfloat16>(sigmoid_f(sm100::bf16_lo_f(gw[u])));
+            const float g1 = round_to<__nv_bfloat16>(sigmoid_f(sm100::bf16_hi_f(gw[u])));
+            ow[u] = cvt_bf16x2(a0 * g0, a1 * g1);
+          }
+          if (row_ok) *reinterpret_cast<uint4*>(dst + c + d8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, kCols);
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 attn_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+// 3-D bf16 map with 128-byte swizzle over dims {d0 (contiguous), d1, d2}
+// with byte strides {s1, s2}; box {64, b1, b2}.
+bool attn_map(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2,
+              uint32_t b1, uint32_t b2) {
+  auto enc = attn_map_encoder();
+  if (!enc) return false;
+  std::memset(map, 0, sizeof(*map));
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {64, b1, b2};
+  cuuint32_t es[3] = {1, 1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// The tcgen05 prefill: Q from the prepared queries [n_tokens, heads, HD]; K
+// and V from the caches [kv_heads, capacity, HD], their key extent the cache
+// length (keys past it read as zeros).  False when the maps cannot be made
+// (the caller then takes attn_mma_kernel).
+template <int HD>
+bool launch_tc(const AttnParams& p, cudaStream_t s, gdn_status* st) {
+  if ((reinterpret_cast<uintptr_t>(p.qg) & 15u) || p.qg_st % 8 || (reinterpret_cast<uintptr_t>(p.out) & 15u) ||
+      p.out_st % 8)
+    return false;  // the output stage moves 16-byte runs of the gate and the output
+  CUtensorMap qmap, kmap, vmap;
+  if (!attn_map(&qmap, p.q_ws, HD, (uint64_t)p.heads, (uint64_t)p.n_tokens, (uint64_t)HD * 2,
+                (uint64_t)p.heads * HD * 2, 1, kTcQ) ||
+      !attn_map(&kmap, p.k_cache, HD, (uint64_t)p.cache_len, (uint64_t)p.kv_heads, (uint64_t)HD * 2,
+                (uint64_t)p.cache_sh * 2, kTcK, 1) ||
+      !attn_map(&vmap, p.v_cache, HD, (uint64_t)p.cache_len, (uint64_t)p.kv_heads, (uint64_t)HD * 2,
+                (uint64_t)p.cache_sh * 2, kTcK, 1))
+    return false;
+  static DeviceFlags attr;
+  constexpr size_t smem = TcSmem<HD>::kBytes;
+  if (ensure_smem_attr(attn_tc_kernel<HD>, smem, attr) != cudaSuccess) {
+    *st = set_error(GDN_ECUDA, "attention: shared-memory attribute");
+    return true;
+  }
+  const int64_t qtiles = (p.n_tokens + kTcQ - 1) / kTcQ;
+  if (qtiles > 65535) {
+    *st = set_error(GDN_EUNSUPPORTED, "attention: at most %d tokens per call", 65535 * kTcQ);
+    return true;
+  }
+  attn_tc_kernel<HD><<<dim3((unsigned)p.heads, (unsigned)qtiles), kTcThreads, smem, s>>>(qmap, kmap, vmap, p);
+  *st = GDN_OK;
+  return true;
+}
+
 template <int HD>
 gdn_status launch_mma(const AttnParams& p, cudaStream_t s) {
   static DeviceFlags attr;
@@ -1064,6 +1384,16 @@ gdn_status attn_setup(const gdn_attn_args* a, AttnParams* p, size_t* ws_bytes) {
 }
 
 }  // namespace
+
+cudaError_t read_and_clear_attn_error(unsigned* code) {
+  cudaError_t e = cudaMemcpyFromSymbol(code, g_attn_error, sizeof(unsigned));
+  if (e != cudaSuccess) return e;
+  if (*code) {
+    const unsigned zero = 0;
+    e = cudaMemcpyToSymbol(g_attn_error, &zero, sizeof(unsigned));
+  }
+  return e;
+}
 }  // namespace gdn
 
 extern "C" gdn_status gdn_attention_workspace_size(const gdn_attn_args* a, size_t* bytes) {
@@ -1110,8 +1440,12 @@ extern "C" gdn_status gdn_attention(const gdn_attn_args* a, gdn_stream_t stream)
     if (p.splits == 1 && a->head_dim >= 64) {  // prefill: the tensor-core kernel
       switch (a->head_dim) {
         case 64: st = gdn::launch_mma<64>(p, s); break;
-        case 128: st = gdn::launch_mma<128>(p, s); break;
-        default: st = gdn::launch_mma<256>(p, s); break;
+        case 128:
+          if (!gdn::launch_tc<128>(p, s, &st)) st = gdn::launch_mma<128>(p, s);
+          break;
+        default:
+          if (!gdn::launch_tc<256>(p, s, &st)) st = gdn::launch_mma<256>(p, s);
+          break;
       }
     } else if (a->n_tokens == 1 && p.group <= gdn::kDQ && a->head_dim >= 64) {  // decode: tensor cores
       switch (a->head_dim) {

@@ -252,5 +252,7 @@ cudaError_t read_and_clear_device_error(unsigned* code);
 cudaError_t set_test_hooks(unsigned long long wait_ns, int fault);
 cudaError_t read_test_hooks(unsigned long long* wait_ns, int* fault);
 cudaError_t read_and_clear_qlinear_error(unsigned* code);
+// The same for the tcgen05 attention prefill.
+cudaError_t read_and_clear_attn_error(unsigned* code);
 
 }  // namespace gdn
