@@ -756,14 +756,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_mma_kernel(const AttnPara
 // lane 0 issues
 //   S_j  = Q K_j^T   M = 128 queries, N = 64 keys, K = HD    two TMEM buffers
 //   O   += P_j V_j   M = 128, N = HD, K = 64 keys            P read from TMEM, V MN-major
-// and warps 4-7 (one query row per thread: its TMEM lane) turn S_j into P_j
-// with an online softmax in log2 units, P written as packed bf16 over the
-// first 32 columns of S_j's buffer.  A row's O and running sum l are
+// and warps 4-11 turn S_j into P_j with an online softmax in log2 units (a
+// query row per TMEM lane, its 64 keys split between warps 4-7 and 8-11), P
+// written as packed bf16 over the first 32 columns of S_j's buffer.  A row's
+// O and running sum l are
 // rescaled only when its maximum grows by more than kTcRescale (until then
 // every p <= 2^kTcRescale); l sums the unrounded p, as attn_mma_kernel does.
 // The end: O / l, the sigmoid gate and the bf16 rounding of attn_mma_kernel.
 // Every wait is bounded; a timeout is recorded in g_attn_error.
-constexpr int kTcQ = 128, kTcK = 64, kTcThreads = 256;
+constexpr int kTcQ = 128, kTcK = 64, kTcThreads = 384;
 constexpr float kTcRescale = 8.f;
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
@@ -777,8 +778,10 @@ struct TcSmem {
   static constexpr size_t kBytes = 1024 + OFF_V + 2 * (size_t)kKVBytes;
 };
 
-enum TcBar { T_Q_FULL, T_KV_FULL0, T_KV_FULL1, T_KV_EMPTY0, T_KV_EMPTY1, T_S_FULL0, T_S_FULL1, T_P_READY0,
-             T_P_READY1, T_PV_DONE, T_DRAIN, T_NBARS };
+// K and V tiles have barriers of their own: a K buffer is free once S_j has
+// read it, a V buffer once O += P_j V_j has.
+enum TcBar { T_Q_FULL, T_K_FULL0, T_K_FULL1, T_V_FULL0, T_V_FULL1, T_K_EMPTY0, T_K_EMPTY1, T_V_EMPTY0, T_V_EMPTY1,
+             T_S_FULL0, T_S_FULL1, T_P_READY0, T_P_READY1, T_PV_DONE, T_O_FULL, T_DRAIN, T_NBARS };
 
 __device__ __forceinline__ void tc_record_error(volatile int* abort_flag) {
   *abort_flag = 1;
@@ -786,7 +789,7 @@ __device__ __forceinline__ void tc_record_error(volatile int* abort_flag) {
 }
 
 template <int HD>
-__global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(kTcThreads, HD == 128 ? 2 : 1) attn_tc_kernel(const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap vmap,
                                                               const AttnParams p) {
@@ -799,6 +802,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
   __shared__ __align__(8) uint64_t bars[T_NBARS];
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_flag;
+  __shared__ float red_max[2][kTcQ];  // row maxima (then row sums) of the two softmax halves
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x, hk = h / p.group;
   // query tiles in reverse order: the tiles with the most keys start first
@@ -828,27 +832,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
 #pragma unroll
       for (int kb = 0; kb < KB; ++kb)
         tma_load_3d(base + SM::OFF_Q + kb * (kTcQ * 128), &qmap, &bars[T_Q_FULL], kb * 64, h, (int)q0);
-      uint32_t loads[2] = {0, 0};
-      for (int j = 0; j < ntiles && !abort_flag; ++j) {
+      // K_i, then V_(i-1): K_i waits for S_(i-2) to have read its buffer and
+      // V_(i-1) for O += P_(i-3) V_(i-3), in the order the MMAs complete.
+      uint32_t kloads[2] = {0, 0}, vloads[2] = {0, 0};
+      auto load = [&](int j, bool is_v) -> bool {
         const int b = j & 1;
-        if (j >= 2 && !mbar_wait(&bars[T_KV_EMPTY0 + b], (uint32_t)(((j >> 1) - 1) & 1), kTcWaitNs)) {
+        const int empty = (is_v ? T_V_EMPTY0 : T_K_EMPTY0) + b, full = (is_v ? T_V_FULL0 : T_K_FULL0) + b;
+        if (j >= 2 && !mbar_wait(&bars[empty], (uint32_t)(((j >> 1) - 1) & 1), kTcWaitNs)) return false;
+        mbar_arrive_expect_tx(&bars[full], SM::kKVBytes);
+        unsigned char* dst = base + (is_v ? SM::OFF_V : SM::OFF_K) + b * SM::kKVBytes;
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+          tma_load_3d(dst + kb * (kTcK * 128), is_v ? &vmap : &kmap, &bars[full], kb * 64, j * kTcK, hk);
+        ++(is_v ? vloads : kloads)[b];
+        return true;
+      };
+      for (int i = 0; i <= ntiles && !abort_flag; ++i) {
+        if ((i < ntiles && !load(i, false)) || (i >= 1 && !load(i - 1, true))) {
           tc_record_error(&abort_flag);
           break;
         }
-        mbar_arrive_expect_tx(&bars[T_KV_FULL0 + b], 2 * SM::kKVBytes);
-#pragma unroll
-        for (int kb = 0; kb < KB; ++kb) {
-          tma_load_3d(base + SM::OFF_K + b * SM::kKVBytes + kb * (kTcK * 128), &kmap, &bars[T_KV_FULL0 + b], kb * 64,
-                      j * kTcK, hk);
-          tma_load_3d(base + SM::OFF_V + b * SM::kKVBytes + kb * (kTcK * 128), &vmap, &bars[T_KV_FULL0 + b], kb * 64,
-                      j * kTcK, hk);
-        }
-        ++loads[b];
       }
       // every copy this thread started lands before the CTA releases its memory
       mbar_wait(&bars[T_Q_FULL], 0, kTcWaitNs);
-      for (int b = 0; b < 2; ++b)
-        if (loads[b]) mbar_wait(&bars[T_KV_FULL0 + b], (loads[b] - 1) & 1, kTcWaitNs);
+      for (int b = 0; b < 2; ++b) {
+        if (kloads[b]) mbar_wait(&bars[T_K_FULL0 + b], (kloads[b] - 1) & 1, kTcWaitNs);
+        if (vloads[b]) mbar_wait(&bars[T_V_FULL0 + b], (vloads[b] - 1) & 1, kTcWaitNs);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -862,7 +872,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
       for (int j = 0; ok && j <= ntiles; ++j) {
         if (j < ntiles) {
           const int b = j & 1;
-          ok = mbar_wait(&bars[T_KV_FULL0 + b], (uint32_t)((j >> 1) & 1), kTcWaitNs);
+          ok = mbar_wait(&bars[T_K_FULL0 + b], (uint32_t)((j >> 1) & 1), kTcWaitNs);
           if (!ok || abort_flag) break;
           tc_fence_after();
           const uint32_t sK = smem_u32(base + SM::OFF_K + b * SM::kKVBytes);
@@ -873,10 +883,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
               mma_bf16(tmem + HD + kTcK * b, sdesc_sw128(sQ + kb * (kTcQ * 128) + ks * 32),
                        sdesc_sw128(sK + kb * (kTcK * 128) + ks * 32), id_s, kb + ks > 0);
           mma_commit(&bars[T_S_FULL0 + b]);
+          mma_commit(&bars[T_K_EMPTY0 + b]);
         }
         if (j >= 1) {
           const int jp = j - 1, bp = jp & 1;
-          ok = mbar_wait_spin(&bars[T_P_READY0 + bp], (uint32_t)((jp >> 1) & 1), kTcWaitNs);
+          ok = mbar_wait_spin(&bars[T_P_READY0 + bp], (uint32_t)((jp >> 1) & 1), kTcWaitNs) &&
+               mbar_wait_spin(&bars[T_V_FULL0 + bp], (uint32_t)((jp >> 1) & 1), kTcWaitNs);
           if (!ok || abort_flag) break;
           tc_fence_after();
           const uint32_t sV = smem_u32(base + SM::OFF_V + bp * SM::kKVBytes);
@@ -885,7 +897,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
             mma_bf16_ts(tmem, tmem + HD + kTcK * bp + 8 * ks, sdesc_sw128_mn(sV + ks * 2048, kTcK * 128, 1024), id_o,
                         jp > 0 || ks > 0);
           mma_commit(&bars[T_PV_DONE]);
-          mma_commit(&bars[T_KV_EMPTY0 + bp]);
+          mma_commit(&bars[T_V_EMPTY0 + bp]);
+          if (j == ntiles) mma_commit(&bars[T_O_FULL]);  // O complete
         }
       }
       if (!ok) tc_record_error(&abort_flag);
@@ -894,30 +907,45 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------- softmax and output
+    // Warps 4-7 take columns 0-31 of each S tile, warps 8-11 columns 32-63,
+    // of the same rows (a warp's TMEM lane quarter is warp % 4).  The two
+    // halves swap their row maxima through shared memory, keep partial row
+    // sums, and each rescales and finally writes half of the O columns.
+    const int half = (warp - 4) >> 2;
     const int q = warp & 3;                             // TMEM lane quarter
     const int r = q * 32 + lane;                        // query row of the tile
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     const int64_t qpos = p.offset + q0 + r;             // its position in the sequence
+    const int64_t qpos_min = p.offset + q0;             // row 0's: no key of a half tile past it is masked
     const float sl2 = p.scale * 1.4426950408889634f;    // scores in log2 units
-    float m = -INFINITY, l = 0.f;
+    constexpr int OC = HD / 2;                          // O columns of each half
+    float m = -INFINITY, l0 = 0.f, l1 = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1;
       ok = mbar_wait(&bars[T_S_FULL0 + b], (uint32_t)((j >> 1) & 1), kTcWaitNs);
       if (!ok) tc_record_error(&abort_flag);
-      if (named_sync_or(1, 128, !ok || abort_flag)) break;
+      __syncwarp();
       tc_fence_after();
-      float s[64];
-      tmem_ld32(tq + HD + kTcK * b, *reinterpret_cast<float(*)[32]>(s));
-      tmem_ld32(tq + HD + kTcK * b + 32, *reinterpret_cast<float(*)[32]>(s + 32));
+      float s[32];
+      tmem_ld32(tq + HD + kTcK * b + 32 * half, s);
       tmem_wait_ld();
-      const int64_t k0 = (int64_t)j * kTcK;
-      float mx = -INFINITY;
+      const int64_t k0 = (int64_t)j * kTcK + 32 * half;
+      const bool masked = k0 + 31 > qpos_min;  // uniform over the CTA
+      // keys k0 + i with i <= lim are visible to this row
+      const int64_t dpos = qpos - k0;
+      const int lim = !masked ? 31 : dpos < -1 ? -1 : dpos > 31 ? 31 : (int)dpos;
+      float mraw = -INFINITY;
+      if (masked) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        s[i] = k0 + i <= qpos ? s[i] * sl2 : -INFINITY;
-        mx = fmaxf(mx, s[i]);
+        for (int i = 0; i < 32; ++i) mraw = i <= lim ? fmaxf(mraw, s[i]) : mraw;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, s[i]);
       }
+      red_max[half][r] = mraw * sl2;
+      if (named_sync_or(1, 256, !ok || abort_flag)) break;  // the maxima of both halves are in
+      const float mx = fmaxf(red_max[0][r], red_max[1][r]);
       // A row rescales when its maximum grows past the bound (the first
       // valid keys only set it).  The TMEM accesses are warp-collective, so
       // the whole warp takes the rescale when any of its rows needs one; the
@@ -931,7 +959,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
           tc_fence_after();
           const float a = scale_o ? exp2f(m - mx) : 1.f;
 #pragma unroll 1
-          for (int c = 0; c < HD; c += 32) {
+          for (int c = half * OC; c < half * OC + OC; c += 32) {
             float o[32];
             tmem_ld32(tq + c, o);
             tmem_wait_ld();
@@ -940,40 +968,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) attn_tc_kernel(const __grid_con
             tmem_st32(tq + c, o);
           }
           tmem_wait_st();
-          l *= a;
+          l0 *= a;
+          l1 *= a;
         }
       }
       if (grow) m = mx;
-      uint32_t pk[32];
+      // p = 2^(s·scale·log2 e − m); m is finite here (every row sees key 0
+      // in the first tile)
+      uint32_t pk[16];
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
-        const float p0 = s[i] == -INFINITY ? 0.f : exp2f(s[i] - m);
-        const float p1 = s[i + 1] == -INFINITY ? 0.f : exp2f(s[i + 1] - m);
-        l += p0 + p1;
+      for (int i = 0; i < 32; i += 2) {
+        float p0 = exp2f(fmaf(s[i], sl2, -m));
+        float p1 = exp2f(fmaf(s[i + 1], sl2, -m));
+        if (masked) {
+          p0 = i <= lim ? p0 : 0.f;
+          p1 = i + 1 <= lim ? p1 : 0.f;
+        }
+        l0 += p0;
+        l1 += p1;
         pk[i >> 1] = cvt_bf16x2(p0, p1);
       }
-      tmem_st16(tq + HD + kTcK * b, *reinterpret_cast<const uint32_t(*)[16]>(pk));
-      tmem_st16(tq + HD + kTcK * b + 16, *reinterpret_cast<const uint32_t(*)[16]>(pk + 16));
+      // P over the first 32 columns of the S buffer: this half's 32 keys
+      // packed in 16 (both halves' S reads finished before the barrier above)
+      tmem_st16(tq + HD + kTcK * b + 16 * half, pk);
       tmem_wait_st();
       tc_fence_before();
-      named_sync(1, 128);
-      if (r == 0) mbar_arrive(&bars[T_P_READY0 + b]);
+      named_sync(1, 256);
+      if (half == 0 && r == 0) mbar_arrive(&bars[T_P_READY0 + b]);
     }
-    // O / l, gated: out = bf16(bf16(O / l) * bf16(sigmoid(gate)))
-    ok = ok && !abort_flag && mbar_wait(&bars[T_PV_DONE], (uint32_t)((ntiles - 1) & 1), kTcWaitNs);
+    // O / l, gated: out = bf16(bf16(O / l) * bf16(sigmoid(gate))).  O is
+    // complete on a barrier of its own: the last two products of O may both
+    // be pending here (the product of the second-last tile is issued after
+    // S of the last), so a parity wait on PV_DONE could pass a phase early.
+    ok = ok && !abort_flag && mbar_wait(&bars[T_O_FULL], 0, kTcWaitNs);
     if (!ok && !abort_flag) tc_record_error(&abort_flag);
-    // Every lane reads its O row (the loads are warp-collective); rows past
-    // the last token of a ragged tile store nothing.
+    red_max[half][r] = l0 + l1;
+    // Every lane reads its O columns (the loads are warp-collective); rows
+    // past the last token of a ragged tile store nothing.
     const int64_t t = q0 + r;
     const bool row_ok = t < p.n_tokens;
-    if (!named_sync_or(1, 128, !ok)) {
+    if (!named_sync_or(1, 256, !ok)) {
+      __syncwarp();
       tc_fence_after();
-      const float inv = 1.f / l;
+      const float inv = 1.f / (red_max[0][r] + red_max[1][r]);
       const int64_t tr = row_ok ? t : 0;
       const __nv_bfloat16* gate = static_cast<const __nv_bfloat16*>(p.qg) + tr * p.qg_st + (int64_t)h * 2 * HD + HD;
       __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + tr * p.out_st + (int64_t)h * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD; c += 32) {
+      for (int c = half * OC; c < half * OC + OC; c += 32) {
         float o[32];
         __syncwarp();
         tmem_ld32(tq + c, o);
