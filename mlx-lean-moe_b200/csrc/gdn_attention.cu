@@ -781,7 +781,7 @@ struct TcSmem {
 // K and V tiles have barriers of their own: a K buffer is free once S_j has
 // read it, a V buffer once O += P_j V_j has.
 enum TcBar { T_Q_FULL, T_K_FULL0, T_K_FULL1, T_V_FULL0, T_V_FULL1, T_K_EMPTY0, T_K_EMPTY1, T_V_EMPTY0, T_V_EMPTY1,
-             T_S_FULL0, T_S_FULL1, T_P_READY0, T_P_READY1, T_PV_DONE, T_O_FULL, T_DRAIN, T_NBARS };
+             T_S_FULL0, T_S_FULL1, T_P_READY0, T_P_READY1, T_PV_DONE, T_O_FULL, T_QT_READY, T_DRAIN, T_NBARS };
 
 __device__ __forceinline__ void tc_record_error(volatile int* abort_flag) {
   *abort_flag = 1;
@@ -797,6 +797,12 @@ __global__ void __launch_bounds__(kTcThreads, HD == 128 ? 2 : 1) attn_tc_kernel(
   using SM = TcSmem<HD>;
   constexpr int KB = HD / 64;                                   // 64-wide blocks of the head dim
   constexpr uint32_t kCols = HD + 2 * kTcK <= 256 ? 256 : 512;  // O, then the two S buffers
+  // At head_dim 256, Q also lives in TMEM (its last 128 columns, bf16 pairs)
+  // as the A operand of S, so that each S product reads only K from shared
+  // memory.  At 128 it stays in shared memory (two CTAs share an SM's TMEM).
+  constexpr bool QT = HD == 256;
+  constexpr uint32_t QCOL = HD + 2 * kTcK;
+  static_assert(!QT || QCOL + HD / 2 <= kCols, "Q fits the TMEM allocation");
   extern __shared__ unsigned char smem_tc[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_tc) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t bars[T_NBARS];
@@ -868,7 +874,7 @@ __global__ void __launch_bounds__(kTcThreads, HD == 128 ? 2 : 1) attn_tc_kernel(
       const uint32_t id_s = idesc_bf16_f32(128, kTcK);
       const uint32_t id_o = idesc_bf16_f32_bmn(128, HD);
       const uint32_t sQ = smem_u32(base + SM::OFF_Q);
-      bool ok = mbar_wait(&bars[T_Q_FULL], 0, kTcWaitNs);
+      bool ok = mbar_wait(&bars[QT ? T_QT_READY : T_Q_FULL], 0, kTcWaitNs);
       for (int j = 0; ok && j <= ntiles; ++j) {
         if (j < ntiles) {
           const int b = j & 1;
@@ -879,9 +885,14 @@ __global__ void __launch_bounds__(kTcThreads, HD == 128 ? 2 : 1) attn_tc_kernel(
 #pragma unroll
           for (int kb = 0; kb < KB; ++kb)
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              mma_bf16(tmem + HD + kTcK * b, sdesc_sw128(sQ + kb * (kTcQ * 128) + ks * 32),
-                       sdesc_sw128(sK + kb * (kTcK * 128) + ks * 32), id_s, kb + ks > 0);
+            for (int ks = 0; ks < 4; ++ks) {
+              if constexpr (QT)
+                mma_bf16_ts(tmem + HD + kTcK * b, tmem + QCOL + kb * 32 + ks * 8,
+                            sdesc_sw128(sK + kb * (kTcK * 128) + ks * 32), id_s, kb + ks > 0);
+              else
+                mma_bf16(tmem + HD + kTcK * b, sdesc_sw128(sQ + kb * (kTcQ * 128) + ks * 32),
+                         sdesc_sw128(sK + kb * (kTcK * 128) + ks * 32), id_s, kb + ks > 0);
+            }
           mma_commit(&bars[T_S_FULL0 + b]);
           mma_commit(&bars[T_K_EMPTY0 + b]);
         }
@@ -921,6 +932,33 @@ __global__ void __launch_bounds__(kTcThreads, HD == 128 ? 2 : 1) attn_tc_kernel(
     constexpr int OC = HD / 2;                          // O columns of each half
     float m = -INFINITY, l0 = 0.f, l1 = 0.f;
     bool ok = true;
+    if constexpr (QT) {
+      // Q rows into TMEM: this half's two 64-wide K-blocks of row r, read
+      // from the SW128 TMA tile (16-byte chunk c of row r at c ^ (r & 7)).
+      ok = mbar_wait(&bars[T_Q_FULL], 0, kTcWaitNs);
+      if (!ok) tc_record_error(&abort_flag);
+      __syncwarp();
+#pragma unroll 1
+      for (int kbh = 0; kbh < 2; ++kbh) {
+        const int kb = half * 2 + kbh;
+        const unsigned char* row = base + SM::OFF_Q + kb * (kTcQ * 128) + r * 128;
+        float w[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 u = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) * 16));
+          w[4 * c] = __uint_as_float(u.x);
+          w[4 * c + 1] = __uint_as_float(u.y);
+          w[4 * c + 2] = __uint_as_float(u.z);
+          w[4 * c + 3] = __uint_as_float(u.w);
+        }
+        __syncwarp();
+        tmem_st32(tq + QCOL + kb * 32, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      named_sync(1, 256);
+      if (half == 0 && r == 0) mbar_arrive(&bars[T_QT_READY]);
+    }
     for (int j = 0; j < ntiles; ++j) {
       const int b = j & 1;
       ok = mbar_wait(&bars[T_S_FULL0 + b], (uint32_t)((j >> 1) & 1), kTcWaitNs);
@@ -1003,17 +1041,17 @@ __global__ void __launch_bounds__(kTcThreads, HD == 128 ? 2 : 1) attn_tc_kernel(
     ok = ok && !abort_flag && mbar_wait(&bars[T_O_FULL], 0, kTcWaitNs);
     if (!ok && !abort_flag) tc_record_error(&abort_flag);
     red_max[half][r] = l0 + l1;
-    // Every lane reads its O columns (the loads are warp-collective); rows
-    // past the last token of a ragged tile store nothing.
-    const int64_t t = q0 + r;
-    const bool row_ok = t < p.n_tokens;
+    // O / l rounded to bf16 goes through shared memory (the K buffers, idle
+    // once the last S product is done): every lane reads its O columns (the
+    // loads are warp-collective) and writes them into its row, 16-byte chunk
+    // c of row r at chunk c ^ (r & 7); then each warp takes whole rows, so
+    // that the gate loads and the output stores are contiguous runs.
     if (!named_sync_or(1, 256, !ok)) {
       __syncwarp();
       tc_fence_after();
       const float inv = 1.f / (red_max[0][r] + red_max[1][r]);
-      const int64_t tr = row_ok ? t : 0;
-      const __nv_bfloat16* gate = static_cast<const __nv_bfloat16*>(p.qg) + tr * p.qg_st + (int64_t)h * 2 * HD + HD;
-      __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + tr * p.out_st + (int64_t)h * HD;
+      unsigned char* stage = base + SM::OFF_K;  // kTcQ rows of HD bf16
+      constexpr int CPR = HD / 8;               // 16-byte chunks per row
 #pragma unroll 1
       for (int c = half * OC; c < half * OC + OC; c += 32) {
         float o[32];
@@ -1022,23 +1060,42 @@ __global__ void __launch_bounds__(kTcThreads, HD == 128 ? 2 : 1) attn_tc_kernel(
         tmem_wait_ld();
 #pragma unroll
         for (int d8 = 0; d8 < 32; d8 += 8) {
-          const uint4 gu = *reinterpret_cast<const uint4*>(gate + c + d8);
-          const uint32_t gw[4] = {gu.x, gu.y, gu.z, gu.w};
           uint32_t ow[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float a0 = round_to<__nv_bfloat16>(o[d8 + 2 * u] * inv);
-            const float a1 = round_to<__nv_bfloat16>(o[d8 + 2 * u + 1] * inv);
-            const float g0 = round_to<__nv_bfloat16>(sigmoid_f(sm100::bf16_lo_f(gw[u])));
-            const float g1 = round_to<__nv_bfloat16>(sigmoid_f(sm100::bf16_hi_f(gw[u])));
-            ow[u] = cvt_bf16x2(a0 * g0, a1 * g1);
-          }
-          if (row_ok) *reinterpret_cast<uint4*>(dst + c + d8) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+          for (int u = 0; u < 4; ++u) ow[u] = cvt_bf16x2(o[d8 + 2 * u] * inv, o[d8 + 2 * u + 1] * inv);
+          const int chunk = ((c + d8) >> 3) ^ (r & 7);
+          *reinterpret_cast<uint4*>(stage + (size_t)r * HD * 2 + chunk * 16) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
         }
+      }
+      named_sync(1, 256);
+      // out = bf16(a * bf16(sigmoid(gate))), a = bf16(O / l); sigmoid from
+      // the approximate exp2 and divide (relative error ~1e-6, well below
+      // the bf16 rounding of the result)
+      constexpr int RPI = 32 / CPR;  // rows per warp per step
+      const int sw = warp - 4, rl = lane / CPR, cl = lane % CPR;
+#pragma unroll 1
+      for (int r0 = sw * RPI; r0 < kTcQ; r0 += 8 * RPI) {
+        const int rr = r0 + rl;
+        const int64_t t = q0 + rr;
+        if (t >= p.n_tokens) continue;  // rows past the last token of a ragged tile
+        const uint4 au = *reinterpret_cast<const uint4*>(stage + (size_t)rr * HD * 2 + ((cl ^ (rr & 7)) * 16));
+        const uint4 gu = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.qg) + t * p.qg_st +
+                                                         (int64_t)h * 2 * HD + HD + cl * 8);
+        const uint32_t aw[4] = {au.x, au.y, au.z, au.w}, gw[4] = {gu.x, gu.y, gu.z, gu.w};
+        uint32_t ow[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float g0 = round_to<__nv_bfloat16>(
+              __fdividef(1.f, 1.f + ex2_approx(sm100::bf16_lo_f(gw[u]) * -1.4426950408889634f)));
+          const float g1 = round_to<__nv_bfloat16>(
+              __fdividef(1.f, 1.f + ex2_approx(sm100::bf16_hi_f(gw[u]) * -1.4426950408889634f)));
+          ow[u] = cvt_bf16x2(sm100::bf16_lo_f(aw[u]) * g0, sm100::bf16_hi_f(aw[u]) * g1);
+        }
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + t * p.out_st + (int64_t)h * HD + cl * 8) =
+            make_uint4(ow[0], ow[1], ow[2], ow[3]);
       }
     }
   }
-
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, kCols);
