@@ -1150,8 +1150,9 @@ def main():
             "decode_us": att["decode_us"], "decode_kv_gbs": att["decode_kv_gbs"],
             "layer_decode_us": att["layer_decode_us"],
             "config": "softmax-attention core (norms, rotary, cache append, grouped-query causal attention, "
-                      "gate) at 16/2 heads of 256, rotary 64, bf16: 4,096-token prefill; one decode token "
-                      "against 4,096 cached positions (CUDA-core flash-style kernel), timed as a CUDA-graph "
+                      "gate) at 16/2 heads of 256, rotary 64, bf16: 4,096-token prefill (tcgen05 kernel, "
+                      "with the cache set-up); one decode token against 4,096 cached positions (split-key "
+                      "mma.sync kernel and the split combine), timed as a CUDA-graph "
                       "replay with the cache resident in L2; layer_decode_us: the whole layer at that "
                       "token (hidden 2,048: fused 4-bit q|gate|k|v GEMV, the core, 4-bit o_proj GEMV)"}
         lay = measure_layer(device)
