@@ -93,10 +93,13 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // warp takes head rows of the token: rows [0, heads) are queries, then the
 // kv_heads keys, then the kv_heads values, each lane holding head_dim / 32
 // consecutive features.  The norm reduces by shuffles; the rotation reads its
-// partner features from the warp's row in shared memory.  A warp's first
-// row is loaded before the angles are computed.  VEC: every row start is
-// aligned to its lane's run of features (up to 16 bytes), so each lane moves
-// its run in vector accesses.
+// partner features from the warp's row in shared memory.  A warp takes RPW
+// rows (rows warp, warp + nwarps, ...), all loaded before the angles are
+// computed: RPW = 1 (a warp per row) for calls with few tokens, where the
+// latency of one CTA matters; RPW = 4 for prefill, where CTAs of fewer warps
+// fit more per SM and keep more loads in flight.  Further rows, if any, go
+// one at a time.  VEC: every row start is aligned to its lane's run of
+// features (up to 16 bytes), so each lane moves its run in vector accesses.
 constexpr int kPrepMaxWarps = 32;
 
 template <int B>
@@ -172,74 +175,81 @@ __device__ __forceinline__ float rope_angle(int64_t pos, double f) {
   return (float)r;
 }
 
-template <typename T, int HD, bool VEC>
-__global__ void __launch_bounds__(kPrepMaxWarps * 32) attn_prep_kernel(const AttnParams p) {
+template <typename T, int HD, bool VEC, int RPW>
+__global__ void __launch_bounds__(RPW == 1 ? kPrepMaxWarps * 32 : 256) attn_prep_kernel(const AttnParams p) {
   constexpr int DPL = HD / 32;
-  __shared__ float xs[kPrepMaxWarps][HD];
+  __shared__ float xs[RPW == 1 ? kPrepMaxWarps : 8][HD];
   __shared__ float2 rot[HD / 2];  // (cos, sin) of this token's angle per frequency
   griddep_launch_dependents();    // the attention kernel waits for this grid before it reads q or the new keys
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const int64_t t = blockIdx.x;
   const int64_t pos = p.offset + t;
   const int rows = p.heads + 2 * p.kv_heads, half = p.rotary_dim / 2, d0 = lane * DPL;
-  // row r of this token: its source and the norm weights (queries, keys) or nothing (values)
-  auto load = [&](int r, float (&x)[DPL], float (&w)[DPL]) {
-    if (r < p.heads) {
+  // row r of this token
+  auto load = [&](int r, float (&x)[DPL]) {
+    if (r < p.heads)
       ld_run<T, DPL, VEC>(static_cast<const T*>(p.qg) + t * p.qg_st + (int64_t)r * 2 * HD + d0, x);
-      ld_run<float, DPL, VEC>(p.q_norm + d0, w);
-    } else if (r < p.heads + p.kv_heads) {
+    else if (r < p.heads + p.kv_heads)
       ld_run<T, DPL, VEC>(static_cast<const T*>(p.k_new) + t * p.k_st + (int64_t)(r - p.heads) * HD + d0, x);
-      ld_run<float, DPL, VEC>(p.k_norm + d0, w);
-    } else {
+    else
       ld_run<T, DPL, VEC>(
           static_cast<const T*>(p.v_new) + t * p.v_st + (int64_t)(r - p.heads - p.kv_heads) * HD + d0, x);
-    }
   };
-  float x[DPL], w[DPL];
-  int row = warp;
-  if (row < rows) load(row, x, w);  // in flight while the angles are computed
+  float* xr = xs[warp];
+  // row r: RMS norm with its weights and rotation (queries, keys) or a copy into the cache (values)
+  auto process = [&](int row, float (&x)[DPL]) {
+    if (row >= p.heads + p.kv_heads) {
+      st_run<T, DPL, VEC>(static_cast<T*>(p.v_cache) + (row - p.heads - p.kv_heads) * p.cache_sh + pos * HD + d0,
+                          x);
+      return;
+    }
+    const bool is_q = row < p.heads;
+    float w[DPL];
+    ld_run<float, DPL, VEC>((is_q ? p.q_norm : p.k_norm) + d0, w);
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) ss += x[e] * x[e];
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.f / sqrtf(ss / (float)HD + p.eps);
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) x[e] = x[e] * inv * w[e];
+    round_run<T, DPL>(x);
+    __syncwarp();  // the previous row's partner reads are done
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) xr[d0 + e] = x[e];
+    __syncwarp();
+    float y[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+      const int d = d0 + e;
+      y[e] = x[e];
+      if (d < p.rotary_dim) {
+        const float2 cs = rot[d < half ? d : d - half];
+        y[e] = d < half ? x[e] * cs.x - xr[d + half] * cs.y : x[e] * cs.x + xr[d - half] * cs.y;
+      }
+    }
+    T* dst = is_q ? static_cast<T*>(p.q_ws) + (t * p.heads + row) * HD + d0
+                  : static_cast<T*>(p.k_cache) + (row - p.heads) * p.cache_sh + pos * HD + d0;
+    st_run<T, DPL, VEC>(dst, y);
+  };
+  float x[RPW][DPL];
+#pragma unroll
+  for (int i = 0; i < RPW; ++i)  // in flight while the angles are computed
+    if (warp + i * nwarps < rows) load(warp + i * nwarps, x[i]);
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
     float sn, cs;
     sincosf(rope_angle(pos, p.inv_freq[i]), &sn, &cs);
     rot[i] = make_float2(cs, sn);
   }
   __syncthreads();
-  float* xr = xs[warp];
-  while (row < rows) {
-    if (row >= p.heads + p.kv_heads) {  // v: a copy into the cache
-      st_run<T, DPL, VEC>(
-          static_cast<T*>(p.v_cache) + (row - p.heads - p.kv_heads) * p.cache_sh + pos * HD + d0, x);
-    } else {
-      const bool is_q = row < p.heads;
-      float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) ss += x[e] * x[e];
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float inv = 1.f / sqrtf(ss / (float)HD + p.eps);
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) x[e] = x[e] * inv * w[e];
-      round_run<T, DPL>(x);
-      __syncwarp();  // the previous row's partner reads are done
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) xr[d0 + e] = x[e];
-      __syncwarp();
-      float y[DPL];
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) {
-        const int d = d0 + e;
-        y[e] = x[e];
-        if (d < p.rotary_dim) {
-          const float2 cs = rot[d < half ? d : d - half];
-          y[e] = d < half ? x[e] * cs.x - xr[d + half] * cs.y : x[e] * cs.x + xr[d - half] * cs.y;
-        }
-      }
-      T* dst = is_q ? static_cast<T*>(p.q_ws) + (t * p.heads + row) * HD + d0
-                    : static_cast<T*>(p.k_cache) + (row - p.heads) * p.cache_sh + pos * HD + d0;
-      st_run<T, DPL, VEC>(dst, y);
-    }
-    row += nwarps;
-    if (row < rows) load(row, x, w);
+  for (int i = 0; i < RPW; ++i)
+    if (warp + i * nwarps < rows) process(warp + i * nwarps, x[i]);
+  for (int row = warp + RPW * nwarps; row < rows; row += nwarps) {
+    float x1[DPL];
+    load(row, x1);
+    process(row, x1);
   }
 }
 
@@ -1178,11 +1188,20 @@ gdn_status launch_mma(const AttnParams& p, cudaStream_t s) {
 template <typename T, int HD>
 void launch_prep(const AttnParams& p, bool vec, dim3 grid, cudaStream_t s) {
   const int rows = p.heads + 2 * p.kv_heads;
-  const int threads = 32 * (rows < kPrepMaxWarps ? rows : kPrepMaxWarps);
-  if (vec)
-    attn_prep_kernel<T, HD, true><<<grid, threads, 0, s>>>(p);
-  else
-    attn_prep_kernel<T, HD, false><<<grid, threads, 0, s>>>(p);
+  if (p.n_tokens < 2 * (int64_t)sm_count()) {  // few tokens: a warp per row
+    const int threads = 32 * (rows < kPrepMaxWarps ? rows : kPrepMaxWarps);
+    if (vec)
+      attn_prep_kernel<T, HD, true, 1><<<grid, threads, 0, s>>>(p);
+    else
+      attn_prep_kernel<T, HD, false, 1><<<grid, threads, 0, s>>>(p);
+  } else {  // prefill: four rows per warp, at most eight warps
+    const int warps = (rows + 3) / 4;
+    const int threads = 32 * (warps < 8 ? warps : 8);
+    if (vec)
+      attn_prep_kernel<T, HD, true, 4><<<grid, threads, 0, s>>>(p);
+    else
+      attn_prep_kernel<T, HD, false, 4><<<grid, threads, 0, s>>>(p);
+  }
 }
 
 template <typename T>

@@ -37,6 +37,23 @@ cudaError_t ensure_smem_attr(K* kernel, size_t bytes, DeviceFlags& flags) {
   return e;
 }
 
+// The current device's SM count, looked up once per device (148 when the
+// lookup fails, which only sizes grids).
+inline int sm_count() {
+  static std::atomic<int> cached[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  const bool in_range = dev >= 0 && dev < kMaxDevices;
+  if (in_range) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  if (in_range) cached[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
 // ---------------------------------------------------------------------------
 // Element loads/stores with conversion to/from float
 // ---------------------------------------------------------------------------
