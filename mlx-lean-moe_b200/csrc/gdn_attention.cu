@@ -7,7 +7,8 @@
 // attention with the causal mask aligned to the newest query, and the
 // output gate sigmoid(gate) carried in q_proj's second half.
 //
-// attn_prep_kernel     one CTA per token, a warp per row of q / k / v heads: the
+// attn_prep_kernel     one CTA per token, a warp per row of q / k / v heads
+//                      (four rows per warp for prefill): the
 //                      norms and the rotation in float32, rounded to the
 //                      activation dtype where the reference materializes
 //                      arrays; q to the workspace, k and v into the cache.
