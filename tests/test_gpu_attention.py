@@ -268,3 +268,31 @@ def test_attention_bf16_long_prefill_at_model_shape():
         want, keys, values = O.attention_layer(x, w, keys, values, 16, 2, 256, 64, 10000000.0, eps,
                                                rnd=O.bf16_round)
         assert O.rel_l2(n(got), want) < 1e-2, (L, O.rel_l2(n(got), want))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_attention_prefill_with_more_head_rows_than_one_prep_cta_covers(dtype):
+    """40 query heads over 8 key/value heads of 128 (56 head rows per token):
+    a prefill long enough that the prep kernel takes four rows per warp over
+    eight warps (32 rows) and the other 24 one at a time, then a chunk at an
+    offset that is not a tile multiple; bf16 (the tensor-core prefill) and
+    float32 (the CUDA-core kernel) against the oracle."""
+    shape = AttentionShape(40, 8, 128, 32, 1000000.0)
+    hidden, eps = 256, 1e-6
+    rng = np.random.default_rng(41)
+    bf16 = dtype == torch.bfloat16
+    w = _random_weights(rng, shape, hidden, 0.05)
+    if bf16:
+        w = _bf16_weights(w)
+    layer = _layer(w, shape, eps, dtype)
+    cache = _cache(shape, max_context=1024, dtype=dtype)
+    keys, values = np.zeros((8, 0, 128)), np.zeros((8, 0, 128))
+    for L in (400, 150):
+        x = rng.standard_normal((L, hidden)).astype(np.float32)
+        if bf16:
+            x = O.bf16_round(x)
+        got = layer(t(x, dtype), cache)
+        want, keys, values = O.attention_layer(x, w, keys, values, 40, 8, 128, 32, 1000000.0, eps,
+                                               **({"rnd": O.bf16_round} if bf16 else {}))
+        assert O.rel_l2(n(got), want) < (1e-2 if bf16 else 1e-4), (L, O.rel_l2(n(got), want))
+    assert cache.size == 550
