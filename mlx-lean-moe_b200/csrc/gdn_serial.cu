@@ -64,9 +64,11 @@ __device__ __forceinline__ float4 load_vec4(const T* row, int col, int dk) {
 // One token for each of B sequences.  Grid: x = B * row tiles, y = Hv.
 // Launched as a programmatic dependent of the kernel before it (typically the
 // previous decode step): its CTAs become resident while that kernel drains
-// and wait here before touching memory.
+// and wait here before touching memory.  At Dk = 128, registers are capped
+// for four CTAs per SM (128 a thread; 130 uncapped gave three): fewer,
+// fuller waves of the 64-row tiles.
 template <int DKP, typename T>
-__global__ void __launch_bounds__(128) decode_kernel(const ScanParams p) {
+__global__ void __launch_bounds__(128, DKP == 128 ? 4 : 1) decode_kernel(const ScanParams p) {
   griddep_wait();  // launched as a dependent of the kernel before it
   griddep_launch_dependents();
   using L = Layout<DKP, DKP == 128 ? 4 : 0>;
