@@ -1147,6 +1147,7 @@ def main():
         att = measure_attention(device)
         line["attention"] = {
             "prefill_ms": att["prefill_ms"], "prefill_tflops": att["prefill_tflops"],
+            "prefill_frac_of_bf16_peak": att["prefill_tflops"] / tc_peak,
             "decode_us": att["decode_us"], "decode_kv_gbs": att["decode_kv_gbs"],
             "layer_decode_us": att["layer_decode_us"],
             "config": "softmax-attention core (norms, rotary, cache append, grouped-query causal attention, "
