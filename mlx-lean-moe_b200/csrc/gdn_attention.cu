@@ -1062,6 +1062,7 @@ __global__ void __launch_bounds__(kTcThreads, HD == 128 ? 2 : 1) attn_tc_kernel(
       tc_fence_after();
       const float inv = 1.f / (red_max[0][r] + red_max[1][r]);
       unsigned char* stage = base + SM::OFF_K;  // kTcQ rows of HD bf16
+      static_assert(2 * SM::kKVBytes >= (uint32_t)kTcQ * HD * 2, "the O tile fits the two K buffers");
       constexpr int CPR = HD / 8;               // 16-byte chunks per row
 #pragma unroll 1
       for (int c = half * OC; c < half * OC + OC; c += 32) {
