@@ -763,18 +763,21 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attn_mma_kernel(const AttnPara
 // ------------------------------------------------------------------ prefill on tcgen05
 // attn_tc_kernel<HD>: bf16 prefill (head_dim 128 or 256), one CTA per (128
 // queries, head), keys in tiles of 64.  Warp 0 lane 0 loads Q once and the K
-// and V tiles (two buffers) by TMA, zero-filled past the cache length; warp 1
-// lane 0 issues
+// and V tiles (two buffers each, with barriers of their own: a K buffer is
+// refilled once S has read it, a V buffer once P V has) by TMA, zero-filled
+// past the cache length; warp 1 lane 0 issues
 //   S_j  = Q K_j^T   M = 128 queries, N = 64 keys, K = HD    two TMEM buffers
 //   O   += P_j V_j   M = 128, N = HD, K = 64 keys            P read from TMEM, V MN-major
-// and warps 4-11 turn S_j into P_j with an online softmax in log2 units (a
-// query row per TMEM lane, its 64 keys split between warps 4-7 and 8-11), P
-// written as packed bf16 over the first 32 columns of S_j's buffer.  A row's
-// O and running sum l are
-// rescaled only when its maximum grows by more than kTcRescale (until then
-// every p <= 2^kTcRescale); l sums the unrounded p, as attn_mma_kernel does.
-// The end: O / l, the sigmoid gate and the bf16 rounding of attn_mma_kernel.
-// Every wait is bounded; a timeout is recorded in g_attn_error.
+// (at head_dim 256, Q is copied into TMEM first and S reads it there) and
+// warps 4-11 turn S_j into P_j with an online softmax in log2 units (a query
+// row per TMEM lane, its 64 keys split between warps 4-7 and 8-11), P written
+// as packed bf16 over the first 32 columns of S_j's buffer.  A row's O and
+// running sum l are rescaled only when its maximum grows by more than
+// kTcRescale (until then every p <= 2^kTcRescale); l sums the unrounded p, as
+// attn_mma_kernel does.  The end: O / l through shared memory (the idle K
+// buffers), then whole rows per warp for the sigmoid gate and the bf16
+// rounding of attn_mma_kernel.  Every wait is bounded; a timeout is recorded
+// in g_attn_error.
 constexpr int kTcQ = 128, kTcK = 64, kTcThreads = 384;
 constexpr float kTcRescale = 8.f;
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
