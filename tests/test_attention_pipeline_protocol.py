@@ -11,7 +11,8 @@ so they act as one role here):
 - MMA issuer: S_j = Q K_j^T into S buffer j % 2, then O += P_(j-1) V_(j-1);
   commits S_FULL, K_EMPTY after S and PV_DONE, V_EMPTY (and O_FULL after the
   last one) after P V;
-- softmax: waits S_FULL, may rescale O (waits for the product of the tile
+- softmax: at head_dim 256 first copies Q into TMEM (after Q_FULL; then
+  QT_READY, which the issuer waits for instead of Q_FULL); waits S_FULL, may rescale O (waits for the product of the tile
   before on PV_DONE), writes P over its S buffer, arrives P_READY; at the end
   waits O_FULL and reads O.
 
@@ -49,9 +50,9 @@ class Barrier:
 
 
 class Model:
-    def __init__(self, ntiles, rng, final_on_pv_done=False):
-        self.ntiles, self.rng, self.final_on_pv_done = ntiles, rng, final_on_pv_done
-        names = ["Q_FULL", "PV_DONE", "O_FULL"] + [f"{n}{b}" for n in
+    def __init__(self, ntiles, rng, final_on_pv_done=False, q_in_tmem=False):
+        self.ntiles, self.rng, self.final_on_pv_done, self.q_in_tmem = ntiles, rng, final_on_pv_done, q_in_tmem
+        names = ["Q_FULL", "QT_READY", "PV_DONE", "O_FULL"] + [f"{n}{b}" for n in
                                                    ("K_FULL", "V_FULL", "K_EMPTY", "V_EMPTY", "S_FULL", "P_READY")
                                                    for b in (0, 1)]
         self.bar = {n: Barrier(n) for n in names}
@@ -148,8 +149,9 @@ class Model:
                 yield None
 
     def issuer(self):
-        yield ("wait", "Q_FULL", 0)
-        self.check_holds("Q", 0, "S products")
+        q_src = "QT" if self.q_in_tmem else "Q"
+        yield ("wait", "QT_READY" if self.q_in_tmem else "Q_FULL", 0)
+        self.check_holds(q_src, 0, "S products")
         for j in range(self.ntiles + 1):
             if j < self.ntiles:
                 b = j & 1
@@ -159,7 +161,7 @@ class Model:
                 # must have been issued before it (the pipe runs in order)
                 if j >= 2 and self.pv_issued < j - 1:
                     raise ProtocolError(f"S_{j} issued before O += P_{j - 2} V_{j - 2}")
-                self.issue_mma(f"S_{j}", ["Q", f"K{b}"], [f"S{b}"],
+                self.issue_mma(f"S_{j}", [q_src, f"K{b}"], [f"S{b}"],
                                effect=lambda b=b, j=j: self.buf.__setitem__(f"S{b}", ("S", j)))
                 self.commit(f"S_FULL{b}")
                 self.commit(f"K_EMPTY{b}")
@@ -182,6 +184,12 @@ class Model:
                 yield None
 
     def softmax(self):
+        if self.q_in_tmem:  # head_dim 256: Q rows copied into TMEM, then QT_READY
+            yield ("wait", "Q_FULL", 0)
+            self.check_holds("Q", 0, "Q into TMEM")
+            self.buf["QT"] = 0
+            self.bar["QT_READY"].complete()
+            yield None
         for j in range(self.ntiles):
             b = j & 1
             yield ("wait", f"S_FULL{b}", j >> 1)
@@ -231,10 +239,11 @@ class Model:
         raise ProtocolError("no progress within the step budget")
 
 
+@pytest.mark.parametrize("q_in_tmem", [False, True])
 @pytest.mark.parametrize("ntiles", [1, 2, 3, 4, 5, 7])
-def test_attention_pipeline_protocol_holds_over_random_schedules(ntiles):
+def test_attention_pipeline_protocol_holds_over_random_schedules(ntiles, q_in_tmem):
     for seed in range(300):
-        Model(ntiles, random.Random(seed * 31 + ntiles)).run()
+        Model(ntiles, random.Random(seed * 31 + ntiles), q_in_tmem=q_in_tmem).run()
 
 
 def test_the_model_flags_a_final_parity_wait_on_the_shared_product_barrier():
