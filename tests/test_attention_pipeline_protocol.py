@@ -210,6 +210,8 @@ class Model:
             yield ("wait", "O_FULL", 0)
         if self.pv_done < self.ntiles:
             raise ProtocolError(f"O read with {self.ntiles - self.pv_done} products pending")
+        for b in (0, 1):  # O / l is staged over the K buffers
+            self.check_free(f"K{b}", "output staging")
 
     # -- scheduler -----------------------------------------------------------
     def run(self, max_steps=20000):
